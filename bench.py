@@ -1,0 +1,366 @@
+"""Benchmark of the GDN op on B200: BASELINE.json's metric on its config 1 (and config 3 as a side line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one forward + backward of the gated delta rule at config 1 (B=8, T=4096, H=16, dk=dv=128,
+bf16 activations, fp32 g and state, chunk 64) on synthetic seeded inputs with config 0's value
+distributions. Under torchrun every rank runs its own B=8 shard (batch x head sharding, no collective:
+weak scaling); the timed region is bracketed by barrier + synchronize on every rank and the time is the
+max over ranks. Prints one JSON line on rank 0.
+
+``value``: device-timed tokens/s with inputs resident in HBM (inputs total ~0.8 GB per rank, larger than
+the 126 MB L2, so no flush is needed between steps). ``e2e``: the same step through the public API from
+pinned host buffers (inputs copied in, outputs o/dq/dk/dv/dg/dbeta copied out, inside the timed region).
+``--impl reference``: the reference algorithm on the host cores (the C restatement of
+sore/model/gdn_ref.py in ``oracle/``; the Python reference itself is not present on the GPU box), rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CFG1 = dict(B=8, T=4096, H=16, D=128)
+CFG3 = dict(N=256, H=16, D=128)
+METRIC = "GDN fwd+bwd tokens/s (B8 T4096 H16 d128 bf16); decode-step HBM GB/s"
+C = 64
+FWD_FLOP_PER_TOKEN_HEAD = 10 * C * 128 + 6 * 128 * 128 + C * C / 3  # chunked fwd count, 181,589
+PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def make_inputs(B, T, H, D, device, seed):
+    import torch
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(B, T, H, D, device=device, generator=gen).bfloat16()
+    k = torch.randn(B, T, H, D, device=device, generator=gen).bfloat16()
+    v = torch.randn(B, T, H, D, device=device, generator=gen).bfloat16()
+    g = torch.nn.functional.logsigmoid(torch.randn(B, T, H, device=device, generator=gen)) / 16
+    beta = torch.sigmoid(torch.randn(B, T, H, device=device, generator=gen)).bfloat16()
+    do = torch.randn(B, T, H, D, device=device, generator=gen).bfloat16()
+    return dict(q=q, k=k, v=v, g=g, beta=beta, do=do)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = str(gpu_index)
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_ours(args):
+    import torch
+
+    from sorernn_b200 import _lib
+    from sorernn_b200 import chunk_gated_delta_rule, fused_recurrent_gated_delta_rule_step
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    B, T, H, D = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["D"]
+    x = make_inputs(B, T, H, D, dev, seed=1234 + rank)
+    leaf = {n: x[n].clone().requires_grad_(n != "do") for n in ("q", "k", "v", "g", "beta")}
+
+    def step(inp, do, ev=None):
+        if ev is not None:
+            ev[0].record()
+        o, _ = chunk_gated_delta_rule(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"],
+                                      use_qk_l2norm_in_kernel=True)
+        if ev is not None:
+            ev[1].record()
+        o.backward(do)
+        if ev is not None:
+            ev[2].record()
+        return o
+
+    def zero():
+        for t in leaf.values():
+            t.grad = None
+
+    for _ in range(args.warmup):
+        zero()
+        step(leaf, x["do"])
+    barrier(world)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _lib.lib().gdn_kernel_launches()
+    with ClockSampler(local) as clk:
+        barrier(world)
+        start.record()
+        for i in range(args.steps):
+            zero()
+            step(leaf, x["do"], evs[i])
+        end.record()
+        barrier(world)
+    launches = _lib.lib().gdn_kernel_launches() - launches0
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms_local, world)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    tokens = B * T * world
+    value = tokens / (ms / 1e3)
+
+    # e2e through the public API from pinned host memory
+    host = {n: t.detach().cpu().pin_memory() for n, t in x.items()}
+    outs = {n: torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for n, t in x.items() if n != "do"}
+    o_host = torch.empty(x["v"].shape, dtype=x["v"].dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = o_host.numel() * o_host.element_size() + sum(t.numel() * t.element_size() for t in outs.values())
+
+    def e2e_step():
+        inp = {n: host[n].to(dev, non_blocking=True) for n in host}
+        for n in ("q", "k", "v", "g", "beta"):
+            inp[n].requires_grad_(True)
+        o = step(inp, inp["do"])
+        o_host.copy_(o.detach(), non_blocking=True)
+        for n in outs:
+            outs[n].copy_(inp[n].grad, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_steps = max(2, min(args.steps, 5))
+    barrier(world)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record()
+    barrier(world)
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e2e_steps, world)
+
+    # decode (config 3): 256 sequences x 16 heads, fp32 state in HBM, bf16 token inputs
+    N, Hd, Dd = CFG3["N"], CFG3["H"], CFG3["D"]
+    gen = torch.Generator(device=dev).manual_seed(99 + rank)
+    state = torch.randn(N, Hd, Dd, Dd, device=dev, generator=gen) * 0.02
+    dq = torch.nn.functional.normalize(torch.randn(N, Hd, Dd, device=dev, generator=gen), dim=-1).bfloat16()
+    dk = torch.nn.functional.normalize(torch.randn(N, Hd, Dd, device=dev, generator=gen), dim=-1).bfloat16()
+    dv = torch.randn(N, Hd, Dd, device=dev, generator=gen).bfloat16()
+    dg = (torch.nn.functional.logsigmoid(torch.randn(N, Hd, device=dev, generator=gen)) / 16).bfloat16()
+    db = torch.sigmoid(torch.randn(N, Hd, device=dev, generator=gen)).bfloat16()
+    do_buf = torch.empty_like(dv)
+    for _ in range(5):
+        fused_recurrent_gated_delta_rule_step(dq, dk, dv, dg, db, state, out=do_buf)
+    n_dec = 200
+    barrier(world)
+    s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s3.record()
+    for _ in range(n_dec):
+        fused_recurrent_gated_delta_rule_step(dq, dk, dv, dg, db, state, out=do_buf)
+    e3.record()
+    barrier(world)
+    dec_ms = max_over_ranks(s3.elapsed_time(e3) / n_dec, world)
+    dec_bytes = 2 * state.numel() * 4 + 3 * dv.numel() * 2 + do_buf.numel() * 2 + 2 * dg.numel() * 2
+    peaks, peak_kind = load_peaks()
+    dec_gbs = dec_bytes / (dec_ms / 1e3) / 1e9
+
+    # roofline of the dominant kernel (the backward launch): algorithmic flops / measured duration
+    bwd_flop = 2 * FWD_FLOP_PER_TOKEN_HEAD * B * T * H
+    fwd_flop = FWD_FLOP_PER_TOKEN_HEAD * B * T * H
+    peak_tf = peaks["bf16_tflops_sustained"]
+    achieved_bwd = bwd_flop / (bwd_ms / 1e3) / 1e12
+    rec = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; config-0 value distributions)",
+        "config": {"workload": "config1: GDN op fwd+bwd B8 T4096 H16 dk=dv=128 bf16, fp32 g/state, chunk 64, "
+                               "in-kernel qk L2 norm", "per_rank_batch": B, "seq_len": T, "heads": H,
+                   "parallelism": f"batch x head shards, dp{world}",
+                   "l2": "inputs (~0.8 GB/rank) exceed the 126 MB L2; no flush"},
+        "e2e": {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
+        "gpu_launches": int(launches),
+        "kernels": {"fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
+                    "fwd_tflops": round(fwd_flop / (fwd_ms / 1e3) / 1e12, 2)},
+        "roofline": {"bound": "tensor", "kernel": "backward", "achieved": round(achieved_bwd, 2),
+                     "peak": peak_tf, "unit": "TFLOP/s", "frac": round(achieved_bwd / peak_tf, 4),
+                     "peak_source": f"{peak_kind} bf16_tflops_sustained", "traffic": None},
+        "decode": {"metric": "decode-step HBM GB/s (config 3: 256 seq x H16 x 128x128 fp32 state)",
+                   "value": round(dec_gbs, 1), "unit": "GB/s", "us_per_step": round(dec_ms * 1e3, 2),
+                   "roofline": {"bound": "hbm", "achieved": round(dec_gbs, 1), "peak": peaks["hbm_gbs"],
+                                "unit": "GB/s", "frac": round(dec_gbs / peaks["hbm_gbs"], 4),
+                                "peak_source": f"{peak_kind} hbm_gbs", "traffic": None}},
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        rec["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+        print(json.dumps(rec), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline(seconds=15.0, threads=0):
+    """The reference recurrence (C restatement in oracle/, fwd + bwd) on the host cores, on a bounded
+    sample of config 1: one batch row (T=4096, H=16) truncated to the tokens that fit the time budget."""
+    import numpy as np
+
+    from oracle import cgdn
+
+    threads = threads or os.cpu_count() or 1
+    H, D = CFG1["H"], CFG1["D"]
+    T = 256
+    while True:
+        rng = np.random.default_rng(5)
+        q = rng.standard_normal((1, T, H, D)).astype(np.float32)
+        k = rng.standard_normal((1, T, H, D)).astype(np.float32)
+        v = rng.standard_normal((1, T, H, D)).astype(np.float32)
+        g = (-np.logaddexp(0, -rng.standard_normal((1, T, H))) / 16).astype(np.float32)
+        beta = (1 / (1 + np.exp(-rng.standard_normal((1, T, H))))).astype(np.float32)
+        do = rng.standard_normal((1, T, H, D)).astype(np.float32)
+        t0 = time.perf_counter()
+        cgdn.forward(q, k, v, g, beta, D ** -0.5, use_qk_l2norm=True, threads=threads)
+        cgdn.backward(q, k, v, g, beta, do, D ** -0.5, use_qk_l2norm=True, threads=threads)
+        dt = time.perf_counter() - t0
+        if dt * 2 > seconds or T >= CFG1["T"]:
+            break
+        T = min(CFG1["T"], T * 2)
+    return {"value": round(T / dt, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"fwd+bwd of 1 batch row, T={T} of 4096, H=16, d=128, fp32, {dt:.2f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(seconds=args.cpu_seconds / 4)
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(seconds=args.cpu_seconds / 4))
+    v = statistics.median(x["value"] for x in vals)
+    cb = dict(vals[-1])
+    cb["value"] = v
+    rec = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+           "config": {"workload": "config1 sample on host cores: reference recurrence fwd+bwd (C port of "
+                                  "sore/model/gdn_ref.py), 1 batch row of B8 T4096 H16 d128"},
+           "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                       "d2h_bytes_per_step": 0}}
+    print(json.dumps(rec), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

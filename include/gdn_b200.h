@@ -1,0 +1,156 @@
+/*
+ * gdn_b200.h — C ABI of the B200 (sm_100a) Gated DeltaNet token mixer.
+ *
+ * This library replaces the call
+ *     o, final_state = chunk_gated_delta_rule(q, k, v, g, beta, scale=..., initial_state=...,
+ *                                             output_final_state=..., use_qk_l2norm_in_kernel=...,
+ *                                             cu_seqlens=..., cu_seqlens_cpu=...)
+ * made by soreRNN at sore/model/gdn.py:166-169 (flash-linear-attention's Triton op,
+ * fla/ops/gated_delta_rule/chunk.py:365-380, with its autograd backward at chunk.py:117-236),
+ * and adds the single-token decode step (the API shape of fla's fused_recurrent_gated_delta_rule,
+ * fla/ops/gated_delta_rule/fused_recurrent.py:291-308) and the per-segment affine state map used to
+ * split a long prefill by sequence across GPUs.
+ *
+ * Math (soreRNN sore/model/gdn_ref.py:17-21), per sequence n and value head h, state S [DK, DV]:
+ *     S <- exp(g_t) S ;  delta = beta_t (v_t - S^T k_t) ;  S <- S + k_t delta^T ;  o_t = scale S^T q_t
+ * Value head h reads q/k head h / (HV / H) (grouped value attention, gdn.py:153-156).
+ *
+ * Conventions of every entry point:
+ *  - all pointers are device pointers unless named *_host; tensors are C-contiguous:
+ *      q, k, dq, dk      [B, T, H,  DK]        (dtype: act_dtype)
+ *      v, o, do, dv      [B, T, HV, DV]        (dtype: act_dtype)
+ *      g, dg             [B, T, HV]            (g: g_dtype; dg: fp32)
+ *      beta, dbeta       [B, T, HV]            (beta: beta_dtype; dbeta: fp32)
+ *      states            [N, HV, DK, DV] fp32  (initial_state, final_state, dh0, dht)
+ *    With cu_seqlens (int64 [N+1], device) B must be 1 and the state restarts at every
+ *    cu_seqlens[i] (gdn_ref.py:53-61); without it every batch row is one sequence (N = B).
+ *  - the caller allocates every output and the workspace (size from the *_workspace_size query);
+ *    the library never allocates device memory and keeps no device state between calls.
+ *  - every call is stream-ordered on `stream`, does not synchronise the host, and returns a status
+ *    code (GDN_OK = 0); nothing aborts or traps. Shapes, dtypes and alignment are checked on the host
+ *    before any launch.
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* gdn_stream_t; /* same object as cudaStream_t */
+
+enum gdn_status {
+    GDN_OK = 0,
+    GDN_ERR_SHAPE = 1,       /* inconsistent or unsupported sizes */
+    GDN_ERR_DTYPE = 2,       /* unsupported dtype code */
+    GDN_ERR_ALIGN = 3,       /* pointer not aligned as the kernel needs (16 B) */
+    GDN_ERR_LAUNCH = 4,      /* a CUDA launch or tensor-map encode failed */
+    GDN_ERR_TIMEOUT = 5,     /* a device-side bounded wait ran out (see gdn_workspace_error) */
+    GDN_ERR_WORKSPACE = 6,   /* workspace pointer NULL or smaller than the query said */
+    GDN_ERR_ARGUMENT = 7     /* NULL pointer for a required tensor, bad flag */
+};
+
+enum gdn_dtype { GDN_BF16 = 0, GDN_FP16 = 1, GDN_FP32 = 2 };
+
+/* Problem description shared by the chunked forward/backward entry points. */
+typedef struct gdn_problem {
+    int64_t B, T, H, HV, DK, DV;  /* see the layouts above */
+    int64_t N;                    /* number of sequences: B, or len(cu_seqlens) - 1 */
+    const int64_t* cu_seqlens;    /* device [N+1] or NULL */
+    int64_t max_seqlen;           /* longest sequence (host-known, e.g. from cu_seqlens_cpu); <=0: B*T */
+    float scale;                  /* o = scale * S^T q; the reference passes DK^-0.5 (gdn.py:148) */
+    int32_t act_dtype;            /* dtype of q, k, v, o, do, dq, dk, dv */
+    int32_t g_dtype;              /* dtype of g */
+    int32_t beta_dtype;           /* dtype of beta */
+    int32_t use_qk_l2norm;        /* 1: q, k are L2-normalised per head inside the kernel (gdn.py:168) */
+    int32_t ckpt_every;           /* forward keeps one state checkpoint every this many 64-token chunks */
+} gdn_problem;
+
+/* Human-readable text for a status code (static storage). */
+const char* gdn_status_string(int status);
+
+/* Which kernel family a problem runs on: 1 = chunked tcgen05 (bf16/fp16, DK = DV = 128),
+ * 0 = recurrent fp32-accumulating kernels (fp32 inputs, other head sizes). */
+int gdn_uses_chunk_kernels(const gdn_problem* p);
+
+/* Number of fp32 [HV, DK, DV] state checkpoints the forward writes for the backward
+ * (an upper bound when cu_seqlens is given; computed from max_seqlen and N only). */
+int64_t gdn_checkpoint_count(const gdn_problem* p);
+
+/* Workspace bytes for gdn_chunk_fwd / gdn_chunk_bwd (0 is possible). */
+size_t gdn_chunk_fwd_workspace_size(const gdn_problem* p);
+size_t gdn_chunk_bwd_workspace_size(const gdn_problem* p);
+
+/*
+ * Forward: o = GDN(q, k, v, g, beta) from initial_state (NULL = zeros).
+ * final_state (NULL = not wanted) receives S after the last token of each sequence.
+ * checkpoints (NULL = not wanted; needed by gdn_chunk_bwd) receives gdn_checkpoint_count(p)
+ * states [HV, DK, DV] fp32: the state at the start of chunk c of sequence n for c % ckpt_every == 0.
+ * Replaces: fla chunk_gated_delta_rule forward (chunk.py:365-380, as called at gdn.py:166-169).
+ */
+int gdn_chunk_fwd(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                  const void* beta, const float* initial_state, void* o, float* final_state,
+                  float* checkpoints, void* workspace, size_t workspace_bytes, gdn_stream_t stream);
+
+/*
+ * Backward of gdn_chunk_fwd given do (and dht = gradient of final_state, NULL = zero).
+ * Recomputes every chunk state from the forward's checkpoints (nothing per chunk is stored by the
+ * forward). dq, dk, dv are written in act_dtype; dg, dbeta in fp32; dh0 (NULL = not wanted) fp32.
+ * Replaces: ChunkGatedDeltaRuleFunction.backward (fla chunk.py:117-236).
+ */
+int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                  const void* beta, const float* initial_state, const float* checkpoints, const void* dout,
+                  const float* dht, void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0,
+                  void* workspace, size_t workspace_bytes, gdn_stream_t stream);
+
+/*
+ * One decode token for N sequences on a resident fp32 state [N, HV, DK, DV], updated in place:
+ * q, k [N, H, DK], v [N, HV, DV], g, beta [N, HV] (dtypes as in gdn_problem), o [N, HV, DV].
+ * Math: one iteration of gdn_ref.py:18-21. Replaces: fla fused_recurrent_gated_delta_rule
+ * (fused_recurrent.py:291-308) with T = 1, initial_state = state, output_final_state in place.
+ */
+int gdn_decode_step(int64_t N, int64_t H, int64_t HV, int64_t DK, int64_t DV, float scale,
+                    int32_t act_dtype, int32_t g_dtype, int32_t beta_dtype, int32_t use_qk_l2norm,
+                    const void* q, const void* k, const void* v, const void* g, const void* beta,
+                    float* state, void* o, gdn_stream_t stream);
+
+/*
+ * Sequence split (no counterpart in the reference, which has no context parallelism: soreRNN only
+ * grows the context by curriculum, configs/b0_8_pretrain.yaml:18-20). A segment of tokens maps the
+ * state entering it to S_out = M S_in + C, where C is gdn_chunk_fwd's final_state from a zero state
+ * and M = prod_t exp(g_t)(I - beta_t k_t k_t^T) (later tokens on the left).
+ *
+ * gdn_segment_transition writes M as fp32 [N, HV, DK, DK]: it is the final state of the same
+ * recurrence run with v = 0 from the identity state.
+ */
+int gdn_segment_transition(const gdn_problem* p, const void* k, const void* g, const void* beta,
+                           float* transition, void* workspace, size_t workspace_bytes, gdn_stream_t stream);
+
+/*
+ * gdn_segment_apply_state adds the effect of an incoming state S_in [N, HV, DK, DV] to the outputs o of a
+ * segment computed from a zero state:  o_t += scale (M_{<=t} S_in)^T q_t, which is the recurrence run
+ * with v = 0 from S_in (the rule is linear in (S, v)). If final_state is not NULL it receives
+ * final_state += M S_in, so that it becomes the segment's true outgoing state.
+ */
+int gdn_segment_apply_state(const gdn_problem* p, const void* q, const void* k, const void* g,
+                            const void* beta, const float* state_in, void* o, float* final_state,
+                            void* workspace, size_t workspace_bytes, gdn_stream_t stream);
+
+/* Workspace bytes for the two sequence-split calls (same for both). */
+size_t gdn_segment_workspace_size(const gdn_problem* p);
+
+/* Reads the error word that device-side bounded waits leave in `workspace` (0 = none; the word is
+ * cleared at the start of every call that takes the workspace). Synchronises `stream`. */
+int gdn_workspace_error(const void* workspace, gdn_stream_t stream, int32_t* error_out);
+
+/* Number of kernels this library has launched in the process so far (host-side counter, for
+ * benchmark accounting). No counterpart in the reference. */
+uint64_t gdn_kernel_launches(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GDN_B200_H */

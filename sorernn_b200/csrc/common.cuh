@@ -1,0 +1,54 @@
+// Shared device helpers: dtype loads/stores, reductions.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gdn_b200.h"
+
+namespace gdn {
+
+template <typename T> __device__ __forceinline__ float ld(const T* p, int64_t i);
+template <> __device__ __forceinline__ float ld<float>(const float* p, int64_t i) { return p[i]; }
+template <> __device__ __forceinline__ float ld<__nv_bfloat16>(const __nv_bfloat16* p, int64_t i) {
+    return __bfloat162float(p[i]);
+}
+template <> __device__ __forceinline__ float ld<__half>(const __half* p, int64_t i) { return __half2float(p[i]); }
+
+template <typename T> __device__ __forceinline__ void st(T* p, int64_t i, float x);
+template <> __device__ __forceinline__ void st<float>(float* p, int64_t i, float x) { p[i] = x; }
+template <> __device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, int64_t i, float x) {
+    p[i] = __float2bfloat16_rn(x);
+}
+template <> __device__ __forceinline__ void st<__half>(__half* p, int64_t i, float x) { p[i] = __float2half_rn(x); }
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
+// Sequence bounds in the flattened token axis: cu_seqlens if given, else row n of a [B, T] batch.
+__device__ __forceinline__ void seq_bounds(const int64_t* cu, int64_t T, int64_t n, int64_t& bos, int64_t& eos) {
+    if (cu) {
+        bos = cu[n];
+        eos = cu[n + 1];
+    } else {
+        bos = n * T;
+        eos = bos + T;
+    }
+}
+
+constexpr float kL2Eps = 1e-12f;  // F.normalize's eps (gdn.py:177)
+
+}  // namespace gdn
+
+// Dispatch a dtype code to a C++ type.
+#define GDN_DISPATCH_DTYPE(code, TYPE, ...)                  \
+    switch (code) {                                          \
+        case GDN_BF16: { using TYPE = __nv_bfloat16; __VA_ARGS__; } break; \
+        case GDN_FP16: { using TYPE = __half; __VA_ARGS__; } break;        \
+        case GDN_FP32: { using TYPE = float; __VA_ARGS__; } break;         \
+        default: return GDN_ERR_DTYPE;                       \
+    }

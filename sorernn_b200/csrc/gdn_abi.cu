@@ -1,0 +1,215 @@
+// extern "C" entry points declared in include/gdn_b200.h: host-side validation and dispatch.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+#include <atomic>
+
+using namespace gdn;
+
+namespace gdn {
+static std::atomic<uint64_t> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+}  // namespace gdn
+
+namespace {
+
+constexpr int64_t kChunk = 64;
+constexpr size_t kErrBytes = 256;  // head of every workspace: device error word (bounded waits)
+
+bool dtype_ok(int32_t d) { return d == GDN_BF16 || d == GDN_FP16 || d == GDN_FP32; }
+
+int check_problem(const gdn_problem* p) {
+    if (!p) return GDN_ERR_ARGUMENT;
+    if (p->B < 0 || p->T < 0 || p->H <= 0 || p->HV <= 0 || p->DK <= 0 || p->DV <= 0 || p->N < 0) return GDN_ERR_SHAPE;
+    if (p->HV % p->H) return GDN_ERR_SHAPE;
+    if (p->DK > 128 || p->DV > 128) return GDN_ERR_SHAPE;
+    if (p->cu_seqlens) {
+        if (p->B != 1) return GDN_ERR_SHAPE;  // gdn_ref.py:42-43
+    } else if (p->N != p->B) {
+        return GDN_ERR_SHAPE;
+    }
+    if (!dtype_ok(p->act_dtype) || !dtype_ok(p->g_dtype) || !dtype_ok(p->beta_dtype)) return GDN_ERR_DTYPE;
+    if (p->ckpt_every < 1) return GDN_ERR_ARGUMENT;
+    return GDN_OK;
+}
+
+int64_t max_len(const gdn_problem* p) {
+    if (p->max_seqlen > 0) return p->max_seqlen;
+    return p->cu_seqlens ? p->B * p->T : p->T;
+}
+
+RecLaunch rec_launch(const gdn_problem* p) {
+    RecLaunch L{};
+    L.cu = p->cu_seqlens;
+    L.N = p->N;
+    L.T = p->T;
+    L.H = p->H;
+    L.HV = p->HV;
+    L.DK = p->DK;
+    L.DV = p->DV;
+    L.scale = p->scale;
+    L.act_dtype = p->act_dtype;
+    L.g_dtype = p->g_dtype;
+    L.beta_dtype = p->beta_dtype;
+    L.l2norm = p->use_qk_l2norm;
+    return L;
+}
+
+bool aligned16(const void* x) { return ((uintptr_t)x & 15) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* gdn_status_string(int status) {
+    switch (status) {
+        case GDN_OK: return "ok";
+        case GDN_ERR_SHAPE: return "unsupported or inconsistent shape";
+        case GDN_ERR_DTYPE: return "unsupported dtype";
+        case GDN_ERR_ALIGN: return "pointer not 16-byte aligned";
+        case GDN_ERR_LAUNCH: return "CUDA launch failed";
+        case GDN_ERR_TIMEOUT: return "device-side wait timed out";
+        case GDN_ERR_WORKSPACE: return "workspace missing or too small";
+        case GDN_ERR_ARGUMENT: return "invalid argument";
+        default: return "unknown status";
+    }
+}
+
+int gdn_uses_chunk_kernels(const gdn_problem* p) {
+    (void)p;
+    return 0;
+}
+
+int64_t gdn_checkpoint_count(const gdn_problem* p) {
+    if (check_problem(p) != GDN_OK) return -1;
+    const int64_t K = p->ckpt_every;
+    if (!p->cu_seqlens) {
+        const int64_t nc = (p->T + kChunk - 1) / kChunk;
+        return p->N * ((nc + K - 1) / K);
+    }
+    // sum_n ceil(ceil(len_n / 64) / K) <= (sum_n ceil(len_n / 64)) / K + N <= (T + 63 N) / 64 / K + N
+    const int64_t nc = (p->B * p->T + (kChunk - 1) * p->N) / kChunk;
+    return nc / K + p->N + 1;
+}
+
+size_t gdn_chunk_fwd_workspace_size(const gdn_problem* p) {
+    if (check_problem(p) != GDN_OK) return 0;
+    return kErrBytes;
+}
+
+size_t gdn_chunk_bwd_workspace_size(const gdn_problem* p) {
+    if (check_problem(p) != GDN_OK) return 0;
+    return kErrBytes + rec_bwd_workspace(p->N, p->HV, p->DK, p->DV, max_len(p), p->B * p->T, p->H);
+}
+
+int gdn_chunk_fwd(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                  const void* beta, const float* initial_state, void* o, float* final_state, float* checkpoints,
+                  void* workspace, size_t workspace_bytes, gdn_stream_t stream) {
+    int st = check_problem(p);
+    if (st != GDN_OK) return st;
+    if (!q || !k || !v || !g || !beta || !o) return GDN_ERR_ARGUMENT;
+    if (!workspace || workspace_bytes < gdn_chunk_fwd_workspace_size(p)) return GDN_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(workspace, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
+    (void)checkpoints;  // the recurrent backward recomputes from the initial state
+    RecLaunch L = rec_launch(p);
+    L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.o = o;
+    L.h0 = initial_state;
+    L.ht = final_state;
+    return rec_fwd(L, s);
+}
+
+int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                  const void* beta, const float* initial_state, const float* checkpoints, const void* dout,
+                  const float* dht, void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0,
+                  void* workspace, size_t workspace_bytes, gdn_stream_t stream) {
+    int st = check_problem(p);
+    if (st != GDN_OK) return st;
+    if (!q || !k || !v || !g || !beta || !dout || !dq || !dk || !dv || !dg || !dbeta) return GDN_ERR_ARGUMENT;
+    if (!workspace || workspace_bytes < gdn_chunk_bwd_workspace_size(p)) return GDN_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return GDN_ERR_ALIGN;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(workspace, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
+    (void)checkpoints;
+    RecLaunch L = rec_launch(p);
+    L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta;
+    L.h0 = initial_state;
+    return rec_bwd(L, dout, dht, dq, dk, dv, dg, dbeta, dh0, (char*)workspace + kErrBytes, max_len(p),
+                   p->B * p->T, s);
+}
+
+int gdn_decode_step(int64_t N, int64_t H, int64_t HV, int64_t DK, int64_t DV, float scale, int32_t act_dtype,
+                    int32_t g_dtype, int32_t beta_dtype, int32_t use_qk_l2norm, const void* q, const void* k,
+                    const void* v, const void* g, const void* beta, float* state, void* o, gdn_stream_t stream) {
+    if (N < 0 || H <= 0 || HV <= 0 || HV % H || DK <= 0 || DV <= 0 || DK > 128 || DV > 128) return GDN_ERR_SHAPE;
+    if (!dtype_ok(act_dtype) || !dtype_ok(g_dtype) || !dtype_ok(beta_dtype)) return GDN_ERR_DTYPE;
+    if (!q || !k || !v || !g || !beta || !state || !o) return GDN_ERR_ARGUMENT;
+    if (DV == 128 && !aligned16(state)) return GDN_ERR_ALIGN;
+    RecLaunch L{};
+    L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.o = o;
+    L.h0 = state;
+    L.ht = state;  // in place: every CTA reads its whole state into registers before writing it
+    L.cu = nullptr;
+    L.N = N; L.T = 1; L.H = H; L.HV = HV; L.DK = DK; L.DV = DV;
+    L.scale = scale;
+    L.act_dtype = act_dtype; L.g_dtype = g_dtype; L.beta_dtype = beta_dtype;
+    L.l2norm = use_qk_l2norm;
+    return rec_fwd(L, (cudaStream_t)stream);
+}
+
+size_t gdn_segment_workspace_size(const gdn_problem* p) {
+    if (check_problem(p) != GDN_OK) return 0;
+    return kErrBytes;
+}
+
+int gdn_segment_transition(const gdn_problem* p, const void* k, const void* g, const void* beta, float* transition,
+                           void* workspace, size_t workspace_bytes, gdn_stream_t stream) {
+    int st = check_problem(p);
+    if (st != GDN_OK) return st;
+    if (p->DK != p->DV) return GDN_ERR_SHAPE;  // the map is run as a DK x DK state
+    if (!k || !g || !beta || !transition) return GDN_ERR_ARGUMENT;
+    if (!workspace || workspace_bytes < gdn_segment_workspace_size(p)) return GDN_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(workspace, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
+    RecLaunch L = rec_launch(p);
+    L.q = k; L.k = k; L.v = k; L.g = g; L.beta = beta; L.o = nullptr;
+    L.zero_v = 1;
+    L.o_mode = 2;
+    L.h0_identity = 1;
+    L.ht = transition;
+    return rec_fwd(L, s);
+}
+
+int gdn_segment_apply_state(const gdn_problem* p, const void* q, const void* k, const void* g, const void* beta,
+                            const float* state_in, void* o, float* final_state, void* workspace,
+                            size_t workspace_bytes, gdn_stream_t stream) {
+    int st = check_problem(p);
+    if (st != GDN_OK) return st;
+    if (!q || !k || !g || !beta || !state_in || !o) return GDN_ERR_ARGUMENT;
+    if (!workspace || workspace_bytes < gdn_segment_workspace_size(p)) return GDN_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(workspace, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
+    RecLaunch L = rec_launch(p);
+    L.q = q; L.k = k; L.v = q; L.g = g; L.beta = beta; L.o = o;
+    L.zero_v = 1;
+    L.o_mode = 1;
+    L.h0 = state_in;
+    L.ht = final_state;  // final_state += M S_in (may be NULL)
+    L.ht_accumulate = 1;
+    return rec_fwd(L, s);
+}
+
+uint64_t gdn_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int gdn_workspace_error(const void* workspace, gdn_stream_t stream, int32_t* error_out) {
+    if (!workspace || !error_out) return GDN_ERR_ARGUMENT;
+    if (cudaMemcpyAsync(error_out, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, (cudaStream_t)stream) !=
+        cudaSuccess)
+        return GDN_ERR_LAUNCH;
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return GDN_ERR_LAUNCH;
+    return GDN_OK;
+}
+
+}  // extern "C"

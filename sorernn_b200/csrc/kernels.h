@@ -1,0 +1,30 @@
+// Internal launch interfaces between the C ABI (gdn_abi.cu) and the kernel files.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+// Host-side count of kernel launches made by the library (gdn_kernel_launches()).
+void count_launch(int n = 1);
+
+// Arguments of the recurrent (token-by-token) kernels.
+struct RecLaunch {
+    const void *q, *k, *v, *g, *beta;
+    void* o;
+    const float* h0;
+    float* ht;
+    const int64_t* cu;
+    int64_t N, T, H, HV, DK, DV;
+    float scale;
+    int act_dtype, g_dtype, beta_dtype;
+    int l2norm, zero_v, o_mode, h0_identity, ht_accumulate;
+};
+
+int rec_fwd(const RecLaunch& L, cudaStream_t s);
+size_t rec_bwd_workspace(int64_t N, int64_t HV, int64_t DK, int64_t DV, int64_t max_len, int64_t total_tokens,
+                         int64_t H);
+int rec_bwd(const RecLaunch& L, const void* dout, const float* dht, void* dq, void* dk, void* dv, float* dg,
+            float* dbeta, float* dh0, void* ws, int64_t max_len, int64_t total_tokens, cudaStream_t s);
+
+}  // namespace gdn

@@ -1,0 +1,206 @@
+"""PyTorch-facing API: the drop-in for ``fla.ops.gated_delta_rule.chunk_gated_delta_rule``.
+
+soreRNN calls (sore/model/gdn.py:166-169)::
+
+    o, _ = chunk_gated_delta_rule(q, k, v, g, beta, scale=scale, cu_seqlens=cu_seqlens,
+                                  cu_seqlens_cpu=cu_seqlens_cpu, use_qk_l2norm_in_kernel=True)
+
+:func:`chunk_gated_delta_rule` here takes the same arguments (FLA 0.5.x signature,
+fla/ops/gated_delta_rule/chunk.py:365-380, minus ``cp_context``/``transpose_state_layout``) and returns
+``(o, final_state or None)``. It is built from two ``torch.library`` custom ops (``sorernn_b200::gdn_fwd``,
+``sorernn_b200::gdn_bwd``) with a registered autograd formula and fake (meta) kernels, so
+``torch.compile`` treats the mixer as one opaque op and activation checkpointing sees it. Each op is a
+thin ctypes call into the C ABI (include/gdn_b200.h); there is no Triton and no CPU fallback: on a
+CPU tensor, or without the built library, the call raises.
+
+:func:`fused_recurrent_gated_delta_rule_step` is the single-token decode step on a resident fp32 state.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+_DT = {torch.bfloat16: _lib.BF16, torch.float16: _lib.FP16, torch.float32: _lib.FP32}
+DEFAULT_CKPT_EVERY = 4  # chunks of 64 tokens between forward state checkpoints kept for the backward
+
+
+def _ptr(t: Optional[Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t: Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _problem(q, k, v, g, beta, scale, cu_seqlens, max_seqlen, use_qk_l2norm, ckpt_every) -> _lib.Problem:
+    B, T, H, DK = q.shape
+    HV, DV = v.shape[2], v.shape[3]
+    N = B if cu_seqlens is None else cu_seqlens.numel() - 1
+    return _lib.Problem(B=B, T=T, H=H, HV=HV, DK=DK, DV=DV, N=N,
+                        cu_seqlens=None if cu_seqlens is None else cu_seqlens.data_ptr(),
+                        max_seqlen=max_seqlen, scale=scale, act_dtype=_DT[q.dtype], g_dtype=_DT[g.dtype],
+                        beta_dtype=_DT[beta.dtype], use_qk_l2norm=int(use_qk_l2norm), ckpt_every=ckpt_every)
+
+
+def _check_inputs(q, k, v, g, beta, cu_seqlens):
+    if not q.is_cuda:
+        raise RuntimeError("sorernn_b200 runs on CUDA tensors only (no CPU fallback)")
+    if q.shape != k.shape or q.dim() != 4:
+        raise ValueError(f"q and k must be [B,T,H,K] with equal shapes, got {tuple(q.shape)} and {tuple(k.shape)}")
+    B, T, H, _ = q.shape
+    if v.dim() != 4 or v.shape[:2] != (B, T) or v.shape[2] % H:
+        raise ValueError(f"v must be [B,T,HV,V] with HV a multiple of H, got {tuple(v.shape)}")
+    HV = v.shape[2]
+    for name, x in (("g", g), ("beta", beta)):
+        if x.shape != (B, T, HV):
+            raise ValueError(f"{name} must be [B,T,HV] = {(B, T, HV)}, got {tuple(x.shape)}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k and v must share one dtype")
+    if cu_seqlens is not None and B != 1:  # gdn_ref.py:42-43
+        raise ValueError(f"cu_seqlens requires B == 1, got B = {B}")
+
+
+# ------------------------------------------------------------------------------------------------
+# custom ops
+# ------------------------------------------------------------------------------------------------
+@torch.library.custom_op("sorernn_b200::gdn_fwd", mutates_args=())
+def gdn_fwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, initial_state: Optional[Tensor],
+            cu_seqlens: Optional[Tensor], scale: float, use_qk_l2norm: bool, max_seqlen: int,
+            ckpt_every: int) -> tuple[Tensor, Tensor, Tensor]:
+    """Returns ``(o, final_state, checkpoints)``; checkpoints feed :func:`gdn_bwd`."""
+    p = _problem(q, k, v, g, beta, scale, cu_seqlens, max_seqlen, use_qk_l2norm, ckpt_every)
+    L = _lib.lib()
+    o = torch.empty_like(v)
+    final = torch.empty(p.N, p.HV, p.DK, p.DV, dtype=torch.float32, device=q.device)
+    n_ck = L.gdn_checkpoint_count(ctypes.byref(p))
+    ck = torch.empty(max(n_ck, 0), p.HV, p.DK, p.DV, dtype=torch.float32, device=q.device)
+    ws_bytes = L.gdn_chunk_fwd_workspace_size(ctypes.byref(p))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+    h0 = None if initial_state is None else initial_state.float().contiguous()
+    _lib.check(L.gdn_chunk_fwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0), _ptr(o),
+                               _ptr(final), _ptr(ck), _ptr(ws), ws_bytes, _stream(q)), "gdn_chunk_fwd")
+    return o, final, ck
+
+
+@gdn_fwd.register_fake
+def _(q, k, v, g, beta, initial_state, cu_seqlens, scale, use_qk_l2norm, max_seqlen, ckpt_every):
+    B, T, H, DK = q.shape
+    HV, DV = v.shape[2], v.shape[3]
+    N = B if cu_seqlens is None else cu_seqlens.shape[0] - 1
+    p = _problem(q, k, v, g, beta, scale, None, max_seqlen, use_qk_l2norm, ckpt_every)
+    p.N = N
+    if cu_seqlens is not None:
+        p.cu_seqlens = 1  # only its presence matters for the count
+    n_ck = _lib.lib().gdn_checkpoint_count(ctypes.byref(p))
+    return (torch.empty_like(v), q.new_empty(N, HV, DK, DV, dtype=torch.float32),
+            q.new_empty(max(n_ck, 0), HV, DK, DV, dtype=torch.float32))
+
+
+@torch.library.custom_op("sorernn_b200::gdn_bwd", mutates_args=())
+def gdn_bwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, initial_state: Optional[Tensor],
+            checkpoints: Tensor, do: Tensor, dht: Optional[Tensor], cu_seqlens: Optional[Tensor], scale: float,
+            use_qk_l2norm: bool, max_seqlen: int, ckpt_every: int) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor,
+                                                                             Tensor]:
+    """Returns ``(dq, dk, dv, dg, dbeta, dh0)``; dg, dbeta in the dtypes of g, beta; dh0 fp32."""
+    p = _problem(q, k, v, g, beta, scale, cu_seqlens, max_seqlen, use_qk_l2norm, ckpt_every)
+    L = _lib.lib()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg = torch.empty(g.shape, dtype=torch.float32, device=q.device)
+    db = torch.empty(beta.shape, dtype=torch.float32, device=q.device)
+    dh0 = torch.empty(p.N, p.HV, p.DK, p.DV, dtype=torch.float32, device=q.device)
+    ws_bytes = L.gdn_chunk_bwd_workspace_size(ctypes.byref(p))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+    h0 = None if initial_state is None else initial_state.float().contiguous()
+    dht_ = None if dht is None else dht.float().contiguous()
+    _lib.check(L.gdn_chunk_bwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0),
+                               _ptr(checkpoints), _ptr(do.contiguous()), _ptr(dht_), _ptr(dq), _ptr(dk), _ptr(dv),
+                               _ptr(dg), _ptr(db), _ptr(dh0), _ptr(ws), ws_bytes, _stream(q)), "gdn_chunk_bwd")
+    return dq, dk, dv, dg.to(g.dtype), db.to(beta.dtype), dh0
+
+
+@gdn_bwd.register_fake
+def _(q, k, v, g, beta, initial_state, checkpoints, do, dht, cu_seqlens, scale, use_qk_l2norm, max_seqlen,
+      ckpt_every):
+    N = q.shape[0] if cu_seqlens is None else cu_seqlens.shape[0] - 1
+    HV, DK, DV = v.shape[2], q.shape[3], v.shape[3]
+    return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(g),
+            torch.empty_like(beta), q.new_empty(N, HV, DK, DV, dtype=torch.float32))
+
+
+def _setup_context(ctx, inputs, output):
+    q, k, v, g, beta, initial_state, cu_seqlens, scale, use_qk_l2norm, max_seqlen, ckpt_every = inputs
+    _, _, ck = output
+    ctx.save_for_backward(q, k, v, g, beta, initial_state, ck, cu_seqlens)
+    ctx.args = (scale, use_qk_l2norm, max_seqlen, ckpt_every)
+    ctx.has_h0 = initial_state is not None
+
+
+def _backward(ctx, do, dht, _dck):
+    q, k, v, g, beta, initial_state, ck, cu_seqlens = ctx.saved_tensors
+    scale, l2, max_seqlen, ckpt_every = ctx.args
+    dq, dk, dv, dg, db, dh0 = gdn_bwd(q, k, v, g, beta, initial_state, ck, do, dht, cu_seqlens, scale, l2,
+                                      max_seqlen, ckpt_every)
+    return dq, dk, dv, dg, db, (dh0 if ctx.has_h0 else None), None, None, None, None, None
+
+
+torch.library.register_autograd("sorernn_b200::gdn_fwd", _backward, setup_context=_setup_context)
+
+
+# ------------------------------------------------------------------------------------------------
+# public API
+# ------------------------------------------------------------------------------------------------
+def chunk_gated_delta_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: Optional[float] = None,
+                           initial_state: Optional[Tensor] = None, output_final_state: bool = False,
+                           use_qk_l2norm_in_kernel: bool = False, cu_seqlens: Optional[Tensor] = None,
+                           cu_seqlens_cpu: Optional[Tensor] = None, ckpt_every: int = DEFAULT_CKPT_EVERY,
+                           **kwargs):
+    """Gated delta rule, same contract as FLA's ``chunk_gated_delta_rule`` (q, k, v, g, beta order).
+
+    q, k ``[B,T,H,K]``; v ``[B,T,HV,V]`` (HV a multiple of H: grouped value attention); g (log decay) and
+    beta ``[B,T,HV]``; initial_state ``[N,HV,K,V]``. Returns ``(o [B,T,HV,V], final_state [N,HV,K,V] fp32 or
+    None)``. ``cu_seqlens`` (int64 ``[N+1]``, B == 1) resets the state at each document start;
+    ``cu_seqlens_cpu`` (same values on the host) is read only to size buffers, never to synchronise.
+    """
+    if kwargs.get("use_gate_in_kernel") or kwargs.get("cp_context") is not None:
+        raise NotImplementedError("use_gate_in_kernel / cp_context are not supported by this op")
+    _check_inputs(q, k, v, g, beta, cu_seqlens)
+    scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
+    if cu_seqlens is not None:
+        cu_seqlens = cu_seqlens.to(device=q.device, dtype=torch.int64).contiguous()
+        if cu_seqlens_cpu is not None:
+            max_seqlen = int((cu_seqlens_cpu[1:] - cu_seqlens_cpu[:-1]).max()) if cu_seqlens_cpu.numel() > 1 else 0
+        else:
+            max_seqlen = q.shape[1]
+    else:
+        max_seqlen = q.shape[1]
+    q, k, v, g, beta = (x.contiguous() for x in (q, k, v, g, beta))
+    o, final, _ = gdn_fwd(q, k, v, g, beta, initial_state, cu_seqlens, scale, bool(use_qk_l2norm_in_kernel),
+                          int(max_seqlen), int(ckpt_every))
+    return o, (final if output_final_state else None)
+
+
+def fused_recurrent_gated_delta_rule_step(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, state: Tensor,
+                                          scale: Optional[float] = None, use_qk_l2norm_in_kernel: bool = False,
+                                          out: Optional[Tensor] = None) -> Tensor:
+    """One decode token: ``q, k [N,H,K]``, ``v [N,HV,V]``, ``g, beta [N,HV]``, ``state [N,HV,K,V]`` fp32
+    (updated in place). Returns ``o [N,HV,V]`` in v's dtype (written into ``out`` if given)."""
+    if not q.is_cuda:
+        raise RuntimeError("sorernn_b200 runs on CUDA tensors only (no CPU fallback)")
+    if state.dtype != torch.float32 or not state.is_contiguous():
+        raise ValueError("state must be a contiguous fp32 tensor")
+    N, H, DK = q.shape
+    HV, DV = v.shape[1], v.shape[2]
+    if state.shape != (N, HV, DK, DV):
+        raise ValueError(f"state must be {(N, HV, DK, DV)}, got {tuple(state.shape)}")
+    scale = DK ** -0.5 if scale is None else float(scale)
+    o = torch.empty_like(v) if out is None else out
+    _lib.check(_lib.lib().gdn_decode_step(N, H, HV, DK, DV, scale, _DT[q.dtype], _DT[g.dtype], _DT[beta.dtype],
+                                          int(use_qk_l2norm_in_kernel), _ptr(q.contiguous()), _ptr(k.contiguous()),
+                                          _ptr(v.contiguous()), _ptr(g.contiguous()), _ptr(beta.contiguous()),
+                                          _ptr(state), _ptr(o), _stream(q)), "gdn_decode_step")
+    return o

@@ -1,0 +1,80 @@
+"""CPU checks of the C-ABI library: it loads, exports every declared symbol, validates arguments.
+
+No kernel runs here (no GPU in this container); argument checks return before any launch.
+"""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from sorernn_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "gdn_b200.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(gdn_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared_functions()
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in gdn_b200.h but not exported"
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_status_strings():
+    lib = _lib.lib()
+    assert lib.gdn_status_string(0) == b"ok"
+    assert b"shape" in lib.gdn_status_string(1)
+    assert lib.gdn_status_string(999) == b"unknown status"
+
+
+def _problem(**kw):
+    base = dict(B=2, T=256, H=4, HV=4, DK=64, DV=64, N=2, cu_seqlens=None, max_seqlen=256, scale=0.125,
+                act_dtype=_lib.FP32, g_dtype=_lib.FP32, beta_dtype=_lib.FP32, use_qk_l2norm=0, ckpt_every=4)
+    base.update(kw)
+    return _lib.Problem(**base)
+
+
+def test_checkpoint_count_and_workspace_queries():
+    lib = _lib.lib()
+    p = _problem()
+    assert lib.gdn_checkpoint_count(ctypes.byref(p)) == 2 * 1  # ceil(ceil(256/64)/4) per sequence
+    p = _problem(T=4096, B=8, N=8, DK=128, DV=128, H=16, HV=16, act_dtype=_lib.BF16)
+    assert lib.gdn_checkpoint_count(ctypes.byref(p)) == 8 * 16
+    assert lib.gdn_chunk_fwd_workspace_size(ctypes.byref(p)) >= 256
+    assert lib.gdn_chunk_bwd_workspace_size(ctypes.byref(p)) >= 256
+    # varlen: an upper bound computed without reading the device cu_seqlens
+    p = _problem(B=1, T=1000, N=5, cu_seqlens=16)
+    assert lib.gdn_checkpoint_count(ctypes.byref(p)) >= 5
+
+
+@pytest.mark.parametrize("bad", [dict(HV=6), dict(DK=256), dict(act_dtype=7), dict(N=3), dict(ckpt_every=0),
+                                 dict(B=2, cu_seqlens=16)])
+def test_invalid_problems_are_rejected_before_launch(bad):
+    lib = _lib.lib()
+    p = _problem(**bad)
+    st = lib.gdn_chunk_fwd(ctypes.byref(p), *([ctypes.c_void_p(16)] * 5), None, ctypes.c_void_p(16), None, None,
+                           ctypes.c_void_p(16), 1 << 20, None)
+    assert st in (1, 2, 7), lib.gdn_status_string(st)
+
+
+def test_missing_workspace_is_rejected():
+    lib = _lib.lib()
+    p = _problem()
+    st = lib.gdn_chunk_fwd(ctypes.byref(p), *([ctypes.c_void_p(16)] * 5), None, ctypes.c_void_p(16), None, None,
+                           None, 0, None)
+    assert st == 6
+
+
+def test_decode_rejects_bad_shapes():
+    lib = _lib.lib()
+    vp = ctypes.c_void_p(16)
+    assert lib.gdn_decode_step(4, 3, 4, 128, 128, 0.1, 0, 0, 0, 0, vp, vp, vp, vp, vp, vp, vp, None) == 1
+    assert lib.gdn_decode_step(4, 4, 4, 128, 128, 0.1, 9, 0, 0, 0, vp, vp, vp, vp, vp, vp, vp, None) == 2
+    assert lib.gdn_decode_step(4, 4, 4, 128, 128, 0.1, 0, 0, 0, 0, vp, vp, vp, vp, vp, None, vp, None) == 7

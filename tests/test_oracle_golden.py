@@ -88,3 +88,39 @@ def test_validation_errors_match_reference():
     x = make_inputs(1, 1, 6, 1, 1, 4, 4)
     with pytest.raises(ValueError, match="cu_seqlens"):
         orc.gdn_forward(x["q"], x["k"], x["v"], x["g"], x["beta"], 1.0, cu_seqlens=[0, 3, 5])
+
+
+@pytest.mark.parametrize("name", CASES + ["initial_state"])
+def test_c_oracle_matches_numpy_oracle(name):
+    from oracle import cgdn
+
+    m = META[name]
+    x = make_inputs(m["seed"], m["B"], m["T"], m["H"], m["HV"], m["dk"], m["dv"],
+                    normalized=not m["l2norm"], g_mode=m["g_mode"])
+    h0 = dht = None
+    if name == "initial_state":
+        h0, dht = make_state_inputs(m["seed"], m["B"], m["HV"], m["dk"], m["dv"])
+    kw = dict(cu_seqlens=m["cu"], use_qk_l2norm=m["l2norm"])
+    o, ht = orc.gdn_forward(x["q"], x["k"], x["v"], x["g"], x["beta"], m["scale"], initial_state=h0, **kw)
+    o_c, ht_c = cgdn.forward(x["q"], x["k"], x["v"], x["g"], x["beta"], m["scale"], initial_state=h0, **kw)
+    np.testing.assert_allclose(o_c, o, atol=2e-6 * max(1, np.abs(o).max()))
+    np.testing.assert_allclose(ht_c, ht, atol=2e-6 * max(1, np.abs(ht).max()))
+    ref = orc.gdn_backward(x["q"], x["k"], x["v"], x["g"], x["beta"], x["do"], m["scale"], initial_state=h0,
+                           dht=dht, **kw)
+    got = cgdn.backward(x["q"], x["k"], x["v"], x["g"], x["beta"], x["do"], m["scale"], initial_state=h0,
+                        dht=dht, **kw)
+    for n, a, b in zip(("dq", "dk", "dv", "dg", "dbeta", "dh0"), got, ref):
+        np.testing.assert_allclose(a, b, atol=1e-5 * max(1, np.abs(b).max()), err_msg=n)
+
+
+def test_c_oracle_decode_step():
+    from oracle import cgdn
+
+    x = make_inputs(5, 3, 1, 2, 4, 16, 8)
+    h0, _ = make_state_inputs(5, 3, 4, 16, 8)
+    st = h0.copy()
+    o = orc.gdn_decode_step(x["q"][:, 0], x["k"][:, 0], x["v"][:, 0], x["g"][:, 0], x["beta"][:, 0], st, 0.25)
+    st_c = h0.astype(np.float32)
+    o_c = cgdn.decode_step(x["q"][:, 0], x["k"][:, 0], x["v"][:, 0], x["g"][:, 0], x["beta"][:, 0], st_c, 0.25)
+    np.testing.assert_allclose(o_c, o, atol=1e-5)
+    np.testing.assert_allclose(st_c, st, atol=1e-5)
