@@ -301,25 +301,29 @@ def cpu_baseline(seconds=15.0, threads=0):
     from oracle import cgdn
 
     threads = threads or os.cpu_count() or 1
-    H, D = CFG1["H"], CFG1["D"]
-    T = 256
+    H, D, T = CFG1["H"], CFG1["D"], CFG1["T"]
+    B, T_s = 1, 512
     while True:
         rng = np.random.default_rng(5)
-        q = rng.standard_normal((1, T, H, D)).astype(np.float32)
-        k = rng.standard_normal((1, T, H, D)).astype(np.float32)
-        v = rng.standard_normal((1, T, H, D)).astype(np.float32)
-        g = (-np.logaddexp(0, -rng.standard_normal((1, T, H))) / 16).astype(np.float32)
-        beta = (1 / (1 + np.exp(-rng.standard_normal((1, T, H))))).astype(np.float32)
-        do = rng.standard_normal((1, T, H, D)).astype(np.float32)
+        q = rng.standard_normal((B, T_s, H, D)).astype(np.float32)
+        k = rng.standard_normal((B, T_s, H, D)).astype(np.float32)
+        v = rng.standard_normal((B, T_s, H, D)).astype(np.float32)
+        g = (-np.logaddexp(0, -rng.standard_normal((B, T_s, H))) / 16).astype(np.float32)
+        beta = (1 / (1 + np.exp(-rng.standard_normal((B, T_s, H))))).astype(np.float32)
+        do = rng.standard_normal((B, T_s, H, D)).astype(np.float32)
         t0 = time.perf_counter()
         cgdn.forward(q, k, v, g, beta, D ** -0.5, use_qk_l2norm=True, threads=threads)
         cgdn.backward(q, k, v, g, beta, do, D ** -0.5, use_qk_l2norm=True, threads=threads)
         dt = time.perf_counter() - t0
-        if dt * 2 > seconds or T >= CFG1["T"]:
+        if dt * 2.2 > seconds or (B >= CFG1["B"] and T_s >= T):
             break
-        T = min(CFG1["T"], T * 2)
-    return {"value": round(T / dt, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"fwd+bwd of 1 batch row, T={T} of 4096, H=16, d=128, fp32, {dt:.2f} s"}
+        if T_s < T:
+            T_s *= 2
+        else:
+            B *= 2
+    return {"value": round(B * T_s / dt, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"fwd+bwd of B={B} rows x T={T_s} tokens (config 1 is B=8 x T=4096), H=16, d=128, fp32, "
+                      f"{dt:.2f} s"}
 
 
 def run_reference(args):

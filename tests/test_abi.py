@@ -27,6 +27,15 @@ def test_library_exports_every_declared_symbol():
     assert set(names) == set(_lib.SIGNATURES), "ctypes signature table out of sync with the header"
 
 
+def test_ctypes_signatures_match_header_arity():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    for name, (_, argtypes) in _lib.SIGNATURES.items():
+        m = re.search(rf"\b{name}\s*\(([^)]*)\)", text)
+        assert m, name
+        params = [x for x in m.group(1).split(",") if x.strip() and x.strip() != "void"]
+        assert len(params) == len(argtypes), f"{name}: header has {len(params)} params, ctypes {len(argtypes)}"
+
+
 def test_status_strings():
     lib = _lib.lib()
     assert lib.gdn_status_string(0) == b"ok"
