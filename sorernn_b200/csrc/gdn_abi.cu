@@ -78,8 +78,21 @@ const char* gdn_status_string(int status) {
 }
 
 int gdn_uses_chunk_kernels(const gdn_problem* p) {
-    (void)p;
-    return 0;
+    return check_problem(p) == GDN_OK && chunk_fwd_supported(p->DK, p->DV, p->act_dtype) ? 1 : 0;
+}
+
+// Forward-type pass (plain forward, transition map, incoming-state correction): the chunked tcgen05
+// kernel when the problem fits it, else the recurrent kernel.
+static int dispatch_forward(const gdn_problem* p, const RecLaunch& L, float* ckpt, void* workspace, cudaStream_t s) {
+    if (!gdn_uses_chunk_kernels(p)) return rec_fwd(L, s);
+    ChunkLaunch C{};
+    C.q = L.q; C.k = L.k; C.v = L.v; C.g = L.g; C.beta = L.beta; C.o = L.o;
+    C.h0 = L.h0; C.ht = L.ht; C.ckpt = ckpt; C.cu = L.cu; C.err = (int*)workspace;
+    C.B = p->B; C.T = p->T; C.N = p->N; C.H = p->H; C.HV = p->HV;
+    C.scale = L.scale; C.g_dtype = L.g_dtype; C.beta_dtype = L.beta_dtype; C.l2norm = L.l2norm;
+    C.zero_v = L.zero_v; C.o_mode = L.o_mode; C.h0_identity = L.h0_identity; C.ht_accumulate = L.ht_accumulate;
+    C.ckpt_every = p->ckpt_every;
+    return chunk_fwd(C, s);
 }
 
 int64_t gdn_checkpoint_count(const gdn_problem* p) {
@@ -113,12 +126,11 @@ int gdn_chunk_fwd(const gdn_problem* p, const void* q, const void* k, const void
     if (!workspace || workspace_bytes < gdn_chunk_fwd_workspace_size(p)) return GDN_ERR_WORKSPACE;
     cudaStream_t s = (cudaStream_t)stream;
     if (cudaMemsetAsync(workspace, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
-    (void)checkpoints;  // the recurrent backward recomputes from the initial state
     RecLaunch L = rec_launch(p);
     L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.o = o;
     L.h0 = initial_state;
     L.ht = final_state;
-    return rec_fwd(L, s);
+    return dispatch_forward(p, L, checkpoints, workspace, s);
 }
 
 int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
@@ -179,7 +191,7 @@ int gdn_segment_transition(const gdn_problem* p, const void* k, const void* g, c
     L.o_mode = 2;
     L.h0_identity = 1;
     L.ht = transition;
-    return rec_fwd(L, s);
+    return dispatch_forward(p, L, nullptr, workspace, s);
 }
 
 int gdn_segment_apply_state(const gdn_problem* p, const void* q, const void* k, const void* g, const void* beta,
@@ -198,7 +210,7 @@ int gdn_segment_apply_state(const gdn_problem* p, const void* q, const void* k, 
     L.h0 = state_in;
     L.ht = final_state;  // final_state += M S_in (may be NULL)
     L.ht_accumulate = 1;
-    return rec_fwd(L, s);
+    return dispatch_forward(p, L, nullptr, workspace, s);
 }
 
 uint64_t gdn_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }

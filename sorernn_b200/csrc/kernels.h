@@ -21,6 +21,23 @@ struct RecLaunch {
     int l2norm, zero_v, o_mode, h0_identity, ht_accumulate;
 };
 
+// Arguments of the chunked tcgen05 kernels (bf16 activations, DK = DV = 128).
+struct ChunkLaunch {
+    const void *q, *k, *v, *g, *beta;
+    void* o;
+    const float* h0;
+    float* ht;
+    float* ckpt;
+    const int64_t* cu;
+    int* err;  // device error word (bounded waits)
+    int64_t B, T, N, H, HV;
+    float scale;
+    int g_dtype, beta_dtype, l2norm, zero_v, o_mode, h0_identity, ht_accumulate, ckpt_every;
+};
+
+bool chunk_fwd_supported(int64_t DK, int64_t DV, int act_dtype);
+int chunk_fwd(const ChunkLaunch& L, cudaStream_t s);
+
 int rec_fwd(const RecLaunch& L, cudaStream_t s);
 size_t rec_bwd_workspace(int64_t N, int64_t HV, int64_t DK, int64_t DV, int64_t max_len, int64_t total_tokens,
                          int64_t H);

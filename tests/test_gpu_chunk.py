@@ -1,0 +1,154 @@
+"""GPU parity of the chunked tcgen05 path (bf16 activations, dk = dv = 128) through the C ABI.
+
+Expected values: the C oracle (the reference recurrence, gdn_ref.py:17-22, restated and pinned by
+test_oracle_golden.py) run in fp32 on exactly the bf16-rounded inputs the GPU sees. Bar: max-abs error
+<= 2e-2 x RMS(reference) for outputs and states, 3e-2 for gradients (bf16).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_rms_close, to_np
+from oracle import cgdn
+
+pytestmark = pytest.mark.gpu
+D = 128
+
+
+def _inputs(seed, B, T, H, HV, normalized=True, g_scale=16.0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn(B, T, H, D, device="cuda", generator=g)
+    k = torch.randn(B, T, H, D, device="cuda", generator=g)
+    if normalized:
+        q, k = torch.nn.functional.normalize(q, dim=-1), torch.nn.functional.normalize(k, dim=-1)
+    v = torch.randn(B, T, HV, D, device="cuda", generator=g)
+    gg = torch.nn.functional.logsigmoid(torch.randn(B, T, HV, device="cuda", generator=g)) / g_scale
+    beta = torch.sigmoid(torch.randn(B, T, HV, device="cuda", generator=g))
+    do = torch.randn(B, T, HV, D, device="cuda", generator=g)
+    bf = lambda x: x.bfloat16()  # noqa: E731
+    return dict(q=bf(q), k=bf(k), v=bf(v), g=gg.float(), beta=bf(beta), do=bf(do))
+
+
+def _np(x):
+    return {n: to_np(t) for n, t in x.items()}
+
+
+def test_chunk_kernels_selected_for_bf16_d128():
+    from sorernn_b200 import _lib
+
+    p = _lib.Problem(B=1, T=64, H=1, HV=1, DK=128, DV=128, N=1, cu_seqlens=None, max_seqlen=64, scale=1.0,
+                     act_dtype=_lib.BF16, g_dtype=_lib.FP32, beta_dtype=_lib.BF16, use_qk_l2norm=1, ckpt_every=4)
+    assert _lib.lib().gdn_uses_chunk_kernels(ctypes.byref(p)) == 1
+
+
+@pytest.mark.parametrize("B,T,H,HV,l2", [(1, 64, 1, 1, False), (2, 300, 2, 2, True), (1, 130, 1, 2, True),
+                                         (3, 1, 2, 2, False), (1, 1000, 2, 4, True)])
+def test_chunk_forward_matches_oracle(B, T, H, HV, l2):
+    from sorernn_b200 import chunk_gated_delta_rule
+
+    x = _inputs(B * 1000 + T, B, T, H, HV, normalized=not l2)
+    h0 = torch.randn(B, HV, D, D, device="cuda") * 0.05
+    o, ht = chunk_gated_delta_rule(x["q"], x["k"], x["v"], x["g"], x["beta"], initial_state=h0,
+                                   output_final_state=True, use_qk_l2norm_in_kernel=l2)
+    xn = _np(x)
+    o_ref, ht_ref = cgdn.forward(xn["q"], xn["k"], xn["v"], xn["g"], xn["beta"], D ** -0.5,
+                                 initial_state=to_np(h0), use_qk_l2norm=l2)
+    assert_rms_close(to_np(o), o_ref, 2e-2, "o")
+    assert_rms_close(to_np(ht), ht_ref, 2e-2, "final_state")
+
+
+def test_chunk_forward_varlen_short_documents():
+    from sorernn_b200 import chunk_gated_delta_rule
+
+    cu = [0, 1, 3, 4, 70, 200, 512]
+    x = _inputs(7, 1, 512, 2, 2, normalized=False)
+    cu_t = torch.tensor(cu, device="cuda")
+    o, ht = chunk_gated_delta_rule(x["q"], x["k"], x["v"], x["g"], x["beta"], output_final_state=True,
+                                   use_qk_l2norm_in_kernel=True, cu_seqlens=cu_t, cu_seqlens_cpu=torch.tensor(cu))
+    xn = _np(x)
+    o_ref, ht_ref = cgdn.forward(xn["q"], xn["k"], xn["v"], xn["g"], xn["beta"], D ** -0.5, cu_seqlens=cu,
+                                 use_qk_l2norm=True)
+    assert_rms_close(to_np(o), o_ref, 2e-2, "o")
+    assert_rms_close(to_np(ht), ht_ref, 2e-2, "final_state")
+    # documents are isolated: changing document [4, 70) leaves later documents bit-identical
+    x2 = dict(x)
+    x2["v"] = x["v"].clone()
+    x2["v"][:, 4:70] = torch.randn_like(x2["v"][:, 4:70].float()).bfloat16()
+    o2, _ = chunk_gated_delta_rule(x2["q"], x2["k"], x2["v"], x2["g"], x2["beta"], use_qk_l2norm_in_kernel=True,
+                                   cu_seqlens=cu_t)
+    assert torch.equal(o2[:, 70:], o[:, 70:]) and torch.equal(o2[:, :4], o[:, :4])
+    assert not torch.equal(o2[:, 4:70], o[:, 4:70])
+
+
+def test_chunk_forward_checkpoints_are_chunk_start_states():
+    from sorernn_b200.gated_delta_rule import gdn_fwd
+
+    T, K = 700, 2  # checkpoints at chunks 0, 2, 4, ... -> tokens 0, 128, 256, ...
+    x = _inputs(11, 1, T, 1, 1)
+    h0 = torch.randn(1, 1, D, D, device="cuda") * 0.05
+    _, _, ck = gdn_fwd(x["q"], x["k"], x["v"], x["g"], x["beta"], h0, None, D ** -0.5, False, T, K)
+    xn = _np(x)
+    n_ck = (T + 63) // 64
+    n_ck = (n_ck + K - 1) // K
+    assert ck.shape[0] == n_ck
+    assert_rms_close(to_np(ck[0]), to_np(h0), 1e-6, "ckpt 0 = h0")
+    for m in range(1, n_ck):
+        t = 64 * K * m
+        _, st = cgdn.forward(xn["q"][:, :t], xn["k"][:, :t], xn["v"][:, :t], xn["g"][:, :t], xn["beta"][:, :t],
+                             D ** -0.5, initial_state=to_np(h0))
+        assert_rms_close(to_np(ck[m]), st[0], 2e-2, f"ckpt {m}")
+
+
+def test_chunk_forward_large_row_config1_shape():
+    """One batch row of config 1 (T = 4096, H = 16) against the oracle (all 64 chunks of a sequence)."""
+    from sorernn_b200 import chunk_gated_delta_rule
+
+    x = _inputs(12, 1, 4096, 16, 16, normalized=False)
+    o, ht = chunk_gated_delta_rule(x["q"], x["k"], x["v"], x["g"], x["beta"], output_final_state=True,
+                                   use_qk_l2norm_in_kernel=True)
+    xn = _np(x)
+    o_ref, ht_ref = cgdn.forward(xn["q"], xn["k"], xn["v"], xn["g"], xn["beta"], D ** -0.5, use_qk_l2norm=True)
+    assert_rms_close(to_np(o), o_ref, 2e-2, "o")
+    assert_rms_close(to_np(ht), ht_ref, 2e-2, "final_state")
+
+
+def test_chunk_forward_strong_decay_stays_finite():
+    """Large |g| (e.g. -exp(A_log) softplus(.) with A up to 16) must not overflow inside a chunk."""
+    from sorernn_b200 import chunk_gated_delta_rule
+
+    x = _inputs(13, 1, 256, 2, 2, g_scale=0.05)  # g ~ -20 x logsigmoid magnitude
+    o, ht = chunk_gated_delta_rule(x["q"], x["k"], x["v"], x["g"], x["beta"], output_final_state=True)
+    xn = _np(x)
+    o_ref, ht_ref = cgdn.forward(xn["q"], xn["k"], xn["v"], xn["g"], xn["beta"], D ** -0.5)
+    assert torch.isfinite(o.float()).all() and torch.isfinite(ht).all()
+    assert_rms_close(to_np(o), o_ref, 2e-2, "o")
+
+
+def test_sequence_split_passes_bf16():
+    from sorernn_b200 import chunk_gated_delta_rule, seqsplit
+
+    B, T, H = 1, 640, 2
+    x = _inputs(14, B, T, H, H)
+    o_full, ht_full = chunk_gated_delta_rule(x["q"], x["k"], x["v"], x["g"], x["beta"], output_final_state=True)
+    cut = 320
+    segs = [{n: t[:, a:b].contiguous() for n, t in x.items()} for a, b in ((0, cut), (cut, T))]
+    o1, c1 = chunk_gated_delta_rule(segs[0]["q"], segs[0]["k"], segs[0]["v"], segs[0]["g"], segs[0]["beta"],
+                                    output_final_state=True)
+    o2, c2 = chunk_gated_delta_rule(segs[1]["q"], segs[1]["k"], segs[1]["v"], segs[1]["g"], segs[1]["beta"],
+                                    output_final_state=True)
+    M = seqsplit.segment_transition(segs[1]["k"], segs[1]["g"], segs[1]["beta"])
+    # M against the product of the per-token transitions (fp64, host)
+    xn = {n: to_np(t).astype(np.float64) for n, t in segs[1].items()}
+    Mref = np.broadcast_to(np.eye(D), (B, H, D, D)).copy()
+    for t in range(T - cut):
+        kk = xn["k"][:, t]
+        Mt = np.exp(xn["g"][:, t])[..., None, None] * (np.eye(D) - xn["beta"][:, t][..., None, None]
+                                                       * kk[..., :, None] * kk[..., None, :])
+        Mref = Mt @ Mref
+    assert_rms_close(to_np(M), Mref, 2e-2, "transition")
+    s_out = seqsplit.combine(M, c2, c1)
+    assert_rms_close(to_np(s_out), to_np(ht_full), 2e-2, "combined state")
+    seqsplit.apply_incoming_state(segs[1]["q"], segs[1]["k"], segs[1]["g"], segs[1]["beta"], c1, o2, D ** -0.5)
+    assert_rms_close(to_np(torch.cat([o1, o2], 1)), to_np(o_full), 2e-2, "o")
