@@ -2,19 +2,23 @@
 // fp32 state resident in tensor memory (TMEM) for the whole sequence.
 //
 // One CTA (256 threads) per (sequence, value head) walks the sequence in chunks of C = 64 tokens.
-// With Gamma = in-chunk inclusive cumsum of g, E_ij = exp(Gamma_i - Gamma_j), and S0 the state at the
-// chunk start (the algebra checked against the per-token recurrence in tests/test_chunk_algebra.py):
-//   A   = strict_lower(diag(beta) K K^T . E)             T = (I + A)^-1   (fp32, blocked 16x16 solve)
-//   W   = T diag(beta e^Gamma) K        U = T diag(beta) V        Delta = U - W S0
-//   O   = scale e^Gamma Q S0 + P Delta,  P = scale lower_incl(Q K^T . E)
-//   S1  = e^Gamma_C S0 + (diag(e^(Gamma_C - Gamma)) K)^T Delta
-// Every GEMM is issued as an M = 128 UMMA with the feature dimension (d = 128) on the TMEM lanes:
-//   MMA1  D1[128x64]  = [Q;K] K^T              (rows 0-63: Q K^T, rows 64-127: K K^T)
-//   MMA2  W^T[dk x i] = K^T (T diag(beta e^G))^T            MMA3  U^T[dv x i] = V^T (T diag(beta))^T
-//   MMA4  U^T        += S0^T (-W)^T   -> Delta^T          MMA5  O^T = S0^T (scale e^G Q)^T
-//   MMA6  O^T        += Delta^T P^T                       MMA7  S^T += (Delta^T diag(e^(G_C-G))) K
-// S^T (fp32, 128 TMEM columns) is never written to HBM except as checkpoints for the backward
-// (every ckpt_every chunks) and the final state.
+// With Gamma = in-chunk inclusive cumsum of g, E_ij = exp(Gamma_i - Gamma_j), S0 the state at the chunk
+// start, and nq_i, nk_j the L2 norms of the raw q/k rows (1 when the norm is off), the chunk computes
+// (algebra checked against the per-token recurrence in tests/test_chunk_algebra.py):
+//   A   = strict_lower(diag(beta) (K K^T / nk nk^T) . E)    T = (I + A)^-1   (fp32, blocked 16x16 solve)
+//   W   = T diag(beta e^Gamma / nk) K     U = T diag(beta) V     Delta = U - W S0
+//   O_i = [ scale e^Gamma_i (S0^T q_i) + (P' Delta)_i ] / nq_i,   P' = scale lower_incl(Q K^T / nk^T . E)
+//   S1  = e^Gamma_C S0 + K^T diag(e^(Gamma_C - Gamma) / nk) Delta
+// The raw bf16 q/k tiles feed the tensor cores unmodified (the norms are applied in fp32), and Delta and
+// P' are split into bf16 hi + lo parts, so the only bf16 roundings left are those of T, W, S0 (whose
+// effect is below the output's own rounding) and the output itself.
+// Every GEMM is an M = 128 UMMA with a 128-wide dimension on the TMEM lanes:
+//   MMA1  D1[128x64] = [Q;K] K^T                 (rows 0-63: Q K^T, rows 64-127: K K^T)
+//   MMA2  W^T  = K^T TB^T,  TB = T diag(beta e^G / nk)     MMA3  U^T = V^T TV^T,  TV = T diag(beta)
+//   MMA4  U^T += S0^T (-W)^T  -> Delta^T                   MMA5  O1^T = S0^T Q^T
+//   MMA6  O2^T = Delta^T P'^T  (hi.hi + lo.hi + hi.lo)     MMA7  S^T += Dd^T K,  Dd = diag(e^(G_C-G)/nk) Delta
+// S^T (fp32, 128 TMEM columns) reaches HBM only as checkpoints for the backward (every ckpt_every
+// chunks) and as the final state.
 #include <cstring>
 
 #include "common.cuh"
@@ -28,25 +32,31 @@ using namespace sm100;
 namespace cf {
 constexpr int NTHR = 256;
 // shared memory carve (bytes from a 1024-aligned base)
-constexpr uint32_t OFF_QK = 0;                 // 2 stages x 32 KB: per d-block kb: [Q 8 KB | K 8 KB]
-constexpr uint32_t OFF_V = 65536;              // 2 stages x 16 KB: [kb][V 8 KB]
-constexpr uint32_t OFF_S = 98304;              // S0^T bf16 [dv][dk] K-major, 2 dk-blocks x 16 KB
-constexpr uint32_t OFF_W = 131072;             // -W bf16 [i][d] K-major, 2 d-blocks x 8 KB
-constexpr uint32_t OFF_D = 147456;             // Delta^T bf16 [dv][j], 16 KB
-constexpr uint32_t OFF_DD = 163840;            // Delta^T diag(exp(G_C - G_j)), 16 KB
-constexpr uint32_t OFF_TB = 180224;            // T diag(beta e^G) bf16 [i][j], 8 KB
-constexpr uint32_t OFF_TV = 188416;            // T diag(beta) bf16 [i][j], 8 KB
-constexpr uint32_t OFF_P = 196608;             // P bf16 [i][j], 8 KB
-constexpr uint32_t OFF_A = 204800;             // A -> T in place, fp32 [64][AST]
-constexpr int AST = 68;                        // padded fp32 row stride (conflict-free float4 rows)
-constexpr uint32_t OFF_Y = OFF_A + 64 * AST * 4;   // Y blocks, fp32 3 x 16 x 16
-constexpr uint32_t OFF_VEC = OFF_Y + 3 * 256 * 4;  // G, e^G, beta, e^(G_C-G), misc: 5 x 64 fp32
-constexpr uint32_t OFF_BAR = OFF_VEC + 5 * 64 * 4;
+constexpr uint32_t OFF_QK = 0;        // 2 stages x 32 KB; per d-block kb: [Q 8 KB | K 8 KB] (64 rows x 128 B)
+constexpr uint32_t OFF_V = 65536;     // V, single stage, [kb][8 KB]
+constexpr uint32_t OFF_S = 81920;     // S0^T bf16 [dv][dk] K-major, 2 dk-blocks x 16 KB
+constexpr uint32_t OFF_W = 114688;    // -W bf16 [i][d] K-major, 2 d-blocks x 8 KB
+constexpr uint32_t OFF_D = 131072;    // Delta^T hi bf16 [dv][j], 16 KB
+constexpr uint32_t OFF_DL = 147456;   // Delta^T lo
+constexpr uint32_t OFF_DD = 163840;   // Dd^T hi
+constexpr uint32_t OFF_DDL = 180224;  // Dd^T lo
+constexpr uint32_t OFF_TB = 196608;   // TB bf16 [i][j], 8 KB
+constexpr uint32_t OFF_TV = 204800;   // TV bf16 [i][j], 8 KB
+constexpr uint32_t OFF_P = 212992;    // P' hi bf16 [i][j], 8 KB
+constexpr uint32_t OFF_PL = 221184;   // P' lo
+constexpr uint32_t OFF_VEC = 229376;  // G, e^G, beta, e^(G_C-G), 1/nq, 1/nk, misc: 7 x 64 fp32
+constexpr uint32_t OFF_BAR = OFF_VEC + 7 * 64 * 4;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 64 + 1024;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+// The fp32 triangular-solve scratch lives in the Delta region, which is dead between MMA7 of one chunk
+// and step (l) of the next.
+constexpr int AST = 68;  // padded fp32 row stride (conflict-free float4 rows)
+constexpr uint32_t OFF_A = OFF_D;
+constexpr uint32_t OFF_Y = OFF_A + 64 * AST * 4;
+static_assert(OFF_Y + 3 * 256 * 4 <= OFF_DD, "solve scratch overlaps live tiles");
 // TMEM columns
-constexpr uint32_t T_D1 = 0, T_W = 64, T_U = 128, T_O = 192, T_S = 256, T_COLS = 512;
-constexpr uint32_t TX_QKV = 6 * 8192, TX_QK = 4 * 8192;
+constexpr uint32_t T_D1 = 0, T_W = 64, T_U = 128, T_O1 = 192, T_O2 = 256, T_S = 320, T_COLS = 512;
+constexpr uint32_t TX_QK = 4 * 8192, TX_V = 2 * 8192;
 }  // namespace cf
 
 struct ChunkFwdArgs {
@@ -85,6 +95,17 @@ __device__ __forceinline__ void st_chunk8(uint8_t* dst, const float* v) {
     u.w = pack_bf16(v[6], v[7]);
     *reinterpret_cast<uint4*>(dst) = u;
 }
+// hi = bf16(v), lo = bf16(v - hi): two chunks whose sum carries ~16 significant bits
+__device__ __forceinline__ void st_chunk8_split(uint8_t* hi, uint8_t* lo, const float* v) {
+    float h[8], l[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        h[e] = __bfloat162float(__float2bfloat16_rn(v[e]));
+        l[e] = v[e] - h[e];
+    }
+    st_chunk8(hi, h);
+    st_chunk8(lo, l);
+}
 
 __device__ __forceinline__ void block_sync_tc() {
     tc_fence_before();
@@ -92,11 +113,22 @@ __device__ __forceinline__ void block_sync_tc() {
     tc_fence_after();
 }
 
-__device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t& phase, int* err, int code) {
-    const bool ok = mbar_wait(bar, phase, err, code);
+// Bounded waits never make threads leave the chunk loop (a divergent exit would strand the others at the
+// next barrier): a timeout records an error code and every later wait of the CTA polls only once, so a
+// broken launch still ends in bounded time.
+__device__ __forceinline__ void wait_bar(uint64_t* bar, uint32_t parity, int* err, int code, bool& ok) {
+    ok = mbar_wait(bar, parity, err, code, ok ? (1u << 22) : 1u) && ok;
+}
+__device__ __forceinline__ void wait_mma(uint64_t* bar, uint32_t& phase, int* err, int code, bool& ok) {
+    wait_bar(bar, phase, err, code, ok);
     phase ^= 1u;
     tc_fence_after();
-    return ok;
+}
+
+__device__ __forceinline__ void ld32(uint32_t taddr, float (&v)[32]) {
+    tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(v));
+    tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+    tmem_wait_ld();
 }
 
 __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_constant__ ChunkFwdArgs a) {
@@ -109,10 +141,13 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     float* vEG = vG + 64;
     float* vB = vG + 128;
     float* vX = vG + 192;
-    float* vMisc = vG + 256;
-    uint64_t* bar_tma = (uint64_t*)(sm + OFF_BAR);
-    uint64_t* bar_mma = bar_tma + 2;
-    uint32_t* tmem_slot = (uint32_t*)(bar_tma + 3);
+    float* vNQ = vG + 256;  // 1/nq (0 on padded rows)
+    float* vNK = vG + 320;  // 1/nk (0 on padded rows)
+    float* vMisc = vG + 384;
+    uint64_t* bar_qk = (uint64_t*)(sm + OFF_BAR);  // [2]
+    uint64_t* bar_v = bar_qk + 2;
+    uint64_t* bar_mma = bar_qk + 3;
+    uint32_t* tmem_slot = (uint32_t*)(bar_qk + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int lg = warp & 3, chh = warp >> 2;  // TMEM lane group, column half
@@ -144,8 +179,9 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     }
 
     if (tid == 0) {
-        mbar_init(&bar_tma[0], 1);
-        mbar_init(&bar_tma[1], 1);
+        mbar_init(&bar_qk[0], 1);
+        mbar_init(&bar_qk[1], 1);
+        mbar_init(bar_v, 1);
         mbar_init(bar_mma, 1);
         fence_barrier_init();
         prefetch_tmap(&a.tq);
@@ -154,11 +190,12 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     }
     if (warp == 0) tmem_alloc(tmem_slot, T_COLS);
     if (a.zero_v) {
-        for (int e = tid; e < 2 * 16384 / 16; e += NTHR) ((uint4*)(sm + OFF_V))[e] = make_uint4(0, 0, 0, 0);
+        for (int e = tid; e < 16384 / 16; e += NTHR) ((uint4*)(sm + OFF_V))[e] = make_uint4(0, 0, 0, 0);
+        fence_async_smem();
     }
     block_sync_tc();
     const uint32_t tm = *tmem_slot;
-    const uint32_t tD1 = tm + T_D1, tW = tm + T_W, tU = tm + T_U, tO = tm + T_O, tS = tm + T_S;
+    const uint32_t tD1 = tm + T_D1, tW = tm + T_W, tU = tm + T_U, tO1 = tm + T_O1, tO2 = tm + T_O2, tS = tm + T_S;
     const uint32_t lane_base = (uint32_t)(32 * lg) << 16;
     uint32_t mma_phase = 0;
     bool ok = true;
@@ -179,29 +216,34 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         tmem_wait_st();
     }
 
-    auto issue_tma = [&](int c, int s) {
+    auto issue_qk = [&](int c, int s) {
         const int tok0 = (int)(bos + 64 * c);
         uint8_t* sQK = sm + OFF_QK + s * 32768;
-        uint8_t* sV = sm + OFF_V + s * 16384;
-        mbar_arrive_expect_tx(&bar_tma[s], a.zero_v ? TX_QK : TX_QKV);
+        mbar_arrive_expect_tx(&bar_qk[s], TX_QK);
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb) {
-            tma_load_3d(sQK + kb * 16384, &a.tq, &bar_tma[s], kb * 64, hq, tok0);
-            tma_load_3d(sQK + kb * 16384 + 8192, &a.tk, &bar_tma[s], kb * 64, hq, tok0);
-            if (!a.zero_v) tma_load_3d(sV + kb * 8192, &a.tv, &bar_tma[s], kb * 64, hv, tok0);
+            tma_load_3d(sQK + kb * 16384, &a.tq, &bar_qk[s], kb * 64, hq, tok0);
+            tma_load_3d(sQK + kb * 16384 + 8192, &a.tk, &bar_qk[s], kb * 64, hq, tok0);
         }
     };
-    if (tid == 0 && nchunks > 0) issue_tma(0, 0);
-    int tma_pending = nchunks > 0 ? 1 : 0;
+    auto issue_v = [&](int c) {
+        const int tok0 = (int)(bos + 64 * c);
+        mbar_arrive_expect_tx(bar_v, TX_V);
+        tma_load_3d(sm + OFF_V, &a.tv, bar_v, 0, hv, tok0);
+        tma_load_3d(sm + OFF_V + 8192, &a.tv, bar_v, 64, hv, tok0);
+    };
+    if (tid == 0 && nchunks > 0) {
+        issue_qk(0, 0);
+        if (!a.zero_v) issue_v(0);
+    }
 
     const uint32_t sbase = smem_u32(sm);
-    for (int c = 0; c < nchunks && ok; ++c) {
+    for (int c = 0; c < nchunks; ++c) {
         const int s = c & 1;
         const int64_t tok0 = bos + 64 * (int64_t)c;
         const int nv = (len - 64 * (int64_t)c) < 64 ? (int)(len - 64 * (int64_t)c) : 64;
         uint8_t* sQK = sm + OFF_QK + s * 32768;
-        uint8_t* sV = sm + OFF_V + s * 16384;
-        const uint32_t aQK = sbase + OFF_QK + s * 32768, aV = sbase + OFF_V + s * 16384;
+        const uint32_t aQK = sbase + OFF_QK + s * 32768, aV = sbase + OFF_V;
 
         // (a) gates: Gamma = cumsum(g) inside the chunk, beta; padded rows carry g = 0, beta = 0
         if (tid < 64) {
@@ -216,66 +258,14 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             }
             vG[tid] = x;
         }
-        __syncthreads();
-        if (tid >= 32 && tid < 64) vG[tid] += vG[31];
-        __syncthreads();
-        if (tid < 64) {
-            vEG[tid] = __expf(vG[tid]);
-            vX[tid] = __expf(vG[63] - vG[tid]);
-        }
-        if (tid == 64) vMisc[0] = __expf(vG[63]);
 
-        // (b) this chunk's Q, K, V tiles; then prefetch the next chunk into the other stage
-        ok = mbar_wait(&bar_tma[s], (uint32_t)(c >> 1) & 1u, a.err, 1);
-        if (!ok) break;
-        tma_pending = 0;
-        if (tid == 0 && c + 1 < nchunks) {
-            issue_tma(c + 1, s ^ 1);
-        }
-        if (c + 1 < nchunks) tma_pending = 1;
+        // (b) this chunk's Q, K tiles; prefetch the next chunk's into the other stage
+        wait_bar(&bar_qk[s], (uint32_t)(c >> 1) & 1u, a.err, 1, ok);
+        if (tid == 0 && c + 1 < nchunks) issue_qk(c + 1, s ^ 1);
 
-        // (c) L2-normalise q/k rows in place (2 threads per row); zero rows past the sequence end
-        {
-            const int r = tid >> 1, half = tid & 1, i = r & 63;
-            uint8_t* rowp = sQK + half * 16384 + (r < 64 ? 0 : 8192) + i * 128;
-            float x[64];
-            float ss = 0.f;
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((cc ^ (i & 7)) << 4));
-                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __bfloat1622float2(h[e]);
-                    x[cc * 8 + 2 * e] = f.x;
-                    x[cc * 8 + 2 * e + 1] = f.y;
-                    ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
-                }
-            }
-            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-            float inv = a.l2norm ? 1.f / fmaxf(sqrtf(ss), kL2Eps) : 1.f;
-            if (i >= nv) inv = 0.f;
-            if (a.l2norm || i >= nv) {
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) {
-                    float y[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) y[e] = x[cc * 8 + e] * inv;
-                    st_chunk8(rowp + ((cc ^ (i & 7)) << 4), y);
-                }
-            }
-            if (!a.zero_v && tid < 128 && (tid >> 1) >= nv) {
-                const int vi = tid >> 1;
-                uint8_t* vrow = sV + (tid & 1) * 8192 + vi * 128;
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) *reinterpret_cast<uint4*>(vrow + cc * 16) = make_uint4(0, 0, 0, 0);
-            }
-        }
-        fence_async_smem();
-        block_sync_tc();
-
-        // (d) MMA1: D1 = [Q;K] K^T  (M=128, N=64, K=128)
+        // (c) MMA1: D1 = [Q;K] K^T on the raw tiles (M=128, N=64, K=128)
         if (tid == 0) {
+            tc_fence_after();
             const uint32_t id = idesc_bf16(128, 64, 0, 0);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
@@ -285,8 +275,37 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             }
             umma_commit(bar_mma);
         }
+        __syncthreads();
+        if (tid >= 32 && tid < 64) vG[tid] += vG[31];
+        // (d) meanwhile: row norms of q and k (2 threads per row)
+        {
+            const int r = tid >> 1, half = tid & 1, i = r & 63;
+            const uint8_t* rowp = sQK + half * 16384 + (r < 64 ? 0 : 8192) + i * 128;
+            float ss = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                const uint4 u = *reinterpret_cast<const uint4*>(rowp + cc * 16);
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __bfloat1622float2(h[e]);
+                    ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+                }
+            }
+            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+            float inv = a.l2norm ? 1.f / fmaxf(sqrtf(ss), kL2Eps) : 1.f;
+            if (i >= nv) inv = 0.f;
+            if (half == 0) (r < 64 ? vNQ : vNK)[i] = inv;
+        }
+        __syncthreads();
+        if (tid < 64) {
+            vEG[tid] = __expf(vG[tid]);
+            vX[tid] = __expf(vG[63] - vG[tid]) * vNK[tid];  // includes 1/nk: Dd = diag(e^(G_C-G)/nk) Delta
+        }
+        if (tid == 64) vMisc[0] = __expf(vG[63]);
+        __syncthreads();
 
-        // (e) meanwhile: S0 -> bf16 S0^T operand, TMEM state <- e^G_C S0, checkpoint
+        // (e) S0 -> bf16 S0^T operand, TMEM state <- e^G_C S0, checkpoint
         {
             const float eGC = vMisc[0];
             const bool ck = a.ckpt && (c % a.ckpt_every == 0);
@@ -309,32 +328,31 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             }
             tmem_wait_st();
         }
-        ok = wait_mma(bar_mma, mma_phase, a.err, 2);
-        if (!ok) break;
+        wait_mma(bar_mma, mma_phase, a.err, 2, ok);
 
-        // (f) D1 -> P (bf16) for rows 0-63 and A (fp32) for rows 64-127
+        // (f) D1 -> P' (hi/lo bf16) for rows 0-63 and A (fp32) for rows 64-127
         {
             float v[32];
-            tmem_ld16(tD1 + lane_base + 32 * chh, *reinterpret_cast<float(*)[16]>(v));
-            tmem_ld16(tD1 + lane_base + 32 * chh + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-            tmem_wait_ld();
+            ld32(tD1 + lane_base + 32 * chh, v);
             if (lg < 2) {  // Q K^T row i
                 const int i = row;
                 const float gi = vG[i];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int jj = 32 * chh + j;
-                    v[j] = (jj <= i) ? a.scale * v[j] * __expf(gi - vG[jj]) : 0.f;
+                    v[j] = (jj <= i) ? a.scale * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q) st_chunk8(sm + OFF_P + sw128_off(i, 32 * chh + 8 * q), v + 8 * q);
+                for (int q = 0; q < 4; ++q)
+                    st_chunk8_split(sm + OFF_P + sw128_off(i, 32 * chh + 8 * q),
+                                    sm + OFF_PL + sw128_off(i, 32 * chh + 8 * q), v + 8 * q);
             } else {  // K K^T row i
                 const int i = row - 64;
-                const float gi = vG[i], bi = vB[i];
+                const float gi = vG[i], bi = vB[i] * vNK[i];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int jj = 32 * chh + j;
-                    v[j] = (jj < i) ? bi * v[j] * __expf(gi - vG[jj]) : 0.f;
+                    v[j] = (jj < i) ? bi * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
                 }
                 float4* dst = reinterpret_cast<float4*>(Am + i * AST + 32 * chh);
 #pragma unroll
@@ -388,7 +406,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             __syncthreads();
         }
 
-        // (h) TB = T diag(beta e^G), TV = T diag(beta)  (bf16, K-major [i][j])
+        // (h) TB = T diag(beta e^G / nk), TV = T diag(beta)  (bf16, K-major [i][j])
         {
             const int i = tid >> 2, q = tid & 3;
             float tb[16], tv[16];
@@ -397,7 +415,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 const int jj = 16 * q + j;
                 const float t = Am[i * AST + jj];
                 tv[j] = t * vB[jj];
-                tb[j] = tv[j] * vEG[jj];
+                tb[j] = tv[j] * vEG[jj] * vNK[jj];
             }
             st_chunk8(sm + OFF_TB + sw128_off(i, 16 * q), tb);
             st_chunk8(sm + OFF_TB + sw128_off(i, 16 * q + 8), tb + 8);
@@ -409,6 +427,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (i) MMA2: W^T = K^T TB^T ; MMA3: U^T = V^T TV^T   (M=128, N=64, K=64 tokens)
         if (tid == 0) {
+            if (!a.zero_v) wait_bar(bar_v, (uint32_t)c & 1u, a.err, 6, ok);
             const uint32_t id = idesc_bf16(128, 64, 1, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
@@ -418,31 +437,14 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             }
             umma_commit(bar_mma);
         }
-        // meanwhile: Q <- scale e^Gamma_i Q (Q is no longer read by MMA2/MMA3)
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-            const int e = tid + it * NTHR;
-            const int i = e >> 4, cc = e & 15;
-            uint8_t* p = sQK + (cc >> 3) * 16384 + i * 128 + (((cc & 7) ^ (i & 7)) << 4);
-            uint4 u = *reinterpret_cast<uint4*>(p);
-            const float f = a.scale * vEG[i];
-            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-            for (int k2 = 0; k2 < 4; ++k2) {
-                float2 z = __bfloat1622float2(h[k2]);
-                h[k2] = __floats2bfloat162_rn(z.x * f, z.y * f);
-            }
-            *reinterpret_cast<uint4*>(p) = u;
-        }
-        ok = wait_mma(bar_mma, mma_phase, a.err, 3);
-        if (!ok) break;
+        wait_mma(bar_mma, mma_phase, a.err, 3, ok);
+        // V is consumed: load the next chunk's V
+        if (tid == 0 && !a.zero_v && c + 1 < nchunks) issue_v(c + 1);
 
         // (j) W^T (TMEM, lane = d) -> -W bf16 [i][d] (K-major B operand of MMA4)
         {
             float v[32];
-            tmem_ld16(tW + lane_base + 32 * chh, *reinterpret_cast<float(*)[16]>(v));
-            tmem_ld16(tW + lane_base + 32 * chh + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-            tmem_wait_ld();
+            ld32(tW + lane_base + 32 * chh, v);
             const int d = row;
             uint8_t* dst = sm + OFF_W + (d >> 6) * 8192;
 #pragma unroll
@@ -452,7 +454,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         fence_async_smem();
         block_sync_tc();
 
-        // (k) MMA4: U^T += S0^T (-W)^T  -> Delta^T ; MMA5: O^T = S0^T Qg^T   (K = dk = 128)
+        // (k) MMA4: U^T += S0^T (-W)^T -> Delta^T ; MMA5: O1^T = S0^T Q^T   (K = dk = 128)
         if (tid == 0) {
             const uint32_t id = idesc_bf16(128, 64, 0, 0);
 #pragma unroll
@@ -460,57 +462,58 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 const uint64_t ad = desc_kmajor(sbase + OFF_S + kb * 16384 + ko);
                 umma_bf16(tU, ad, desc_kmajor(sbase + OFF_W + kb * 8192 + ko), id, 1);
-                umma_bf16(tO, ad, desc_kmajor(aQK + kb * 16384 + ko), id, ks > 0);
+                umma_bf16(tO1, ad, desc_kmajor(aQK + kb * 16384 + ko), id, ks > 0);
             }
             umma_commit(bar_mma);
         }
-        ok = wait_mma(bar_mma, mma_phase, a.err, 4);
-        if (!ok) break;
+        wait_mma(bar_mma, mma_phase, a.err, 4, ok);
 
-        // (l) Delta^T (TMEM, lane = dv) -> bf16 Delta^T and Delta^T diag(exp(G_C - G)) (K-major A operands)
+        // (l) Delta^T (TMEM, lane = dv) -> hi/lo bf16 Delta^T and Dd^T (K-major A operands)
         {
             float v[32], w2[32];
-            tmem_ld16(tU + lane_base + 32 * chh, *reinterpret_cast<float(*)[16]>(v));
-            tmem_ld16(tU + lane_base + 32 * chh + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-            tmem_wait_ld();
+            ld32(tU + lane_base + 32 * chh, v);
 #pragma unroll
             for (int j = 0; j < 32; ++j) w2[j] = v[j] * vX[32 * chh + j];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                st_chunk8(sm + OFF_D + sw128_off(row, 32 * chh + 8 * q), v + 8 * q);
-                st_chunk8(sm + OFF_DD + sw128_off(row, 32 * chh + 8 * q), w2 + 8 * q);
+                const uint32_t off = sw128_off(row, 32 * chh + 8 * q);
+                st_chunk8_split(sm + OFF_D + off, sm + OFF_DL + off, v + 8 * q);
+                st_chunk8_split(sm + OFF_DD + off, sm + OFF_DDL + off, w2 + 8 * q);
             }
         }
         fence_async_smem();
         block_sync_tc();
 
-        // (m) MMA6: O^T += Delta^T P^T (K = 64) ; MMA7: S^T += DeltaD^T K (N = 128, K = 64)
+        // (m) MMA6: O2^T = Delta^T P'^T (hi.hi + lo.hi + hi.lo) ; MMA7: S^T += Dd^T K (hi + lo), N = 128
         if (tid == 0) {
             const uint32_t id6 = idesc_bf16(128, 64, 0, 0), id7 = idesc_bf16(128, 128, 0, 1);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-                umma_bf16(tO, desc_kmajor(sbase + OFF_D + ks * 32), desc_kmajor(sbase + OFF_P + ks * 32), id6, 1);
-                umma_bf16(tS, desc_kmajor(sbase + OFF_DD + ks * 32), desc_mnmajor(aQK + 8192 + ks * 2048, 16384), id7,
-                          1);
+                const uint64_t dh = desc_kmajor(sbase + OFF_D + ks * 32), dl = desc_kmajor(sbase + OFF_DL + ks * 32);
+                const uint64_t ph = desc_kmajor(sbase + OFF_P + ks * 32), pl = desc_kmajor(sbase + OFF_PL + ks * 32);
+                umma_bf16(tO2, dh, ph, id6, ks > 0);
+                umma_bf16(tO2, dl, ph, id6, 1);
+                umma_bf16(tO2, dh, pl, id6, 1);
+                const uint64_t kd = desc_mnmajor(aQK + 8192 + ks * 2048, 16384);
+                umma_bf16(tS, desc_kmajor(sbase + OFF_DD + ks * 32), kd, id7, 1);
+                umma_bf16(tS, desc_kmajor(sbase + OFF_DDL + ks * 32), kd, id7, 1);
             }
             umma_commit(bar_mma);
         }
-        ok = wait_mma(bar_mma, mma_phase, a.err, 5);
-        if (!ok) break;
+        wait_mma(bar_mma, mma_phase, a.err, 5, ok);
 
-        // (n) O^T (TMEM, lane = dv) -> o[token][hv][dv]
+        // (n) O = (scale e^G O1 + O2) / nq -> o[token][hv][dv]
         if (a.o_mode != 2) {
-            float v[32];
-            tmem_ld16(tO + lane_base + 32 * chh, *reinterpret_cast<float(*)[16]>(v));
-            tmem_ld16(tO + lane_base + 32 * chh + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-            tmem_wait_ld();
+            float v1[32], v2[32];
+            ld32(tO1 + lane_base + 32 * chh, v1);
+            ld32(tO2 + lane_base + 32 * chh, v2);
             __nv_bfloat16* o = (__nv_bfloat16*)a.o;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 const int i = 32 * chh + j;
                 if (i < nv) {
                     const int64_t idx = ((tok0 + i) * a.HV + hv) * 128 + row;
-                    float val = v[j];
+                    float val = (a.scale * vEG[i] * v1[j] + v2[j]) * vNQ[i];
                     if (a.o_mode == 1) val += __bfloat162float(o[idx]);
                     o[idx] = __float2bfloat16_rn(val);
                 }
@@ -533,10 +536,6 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 *p = a.ht_accumulate ? *p + v[i] : v[i];
             }
         }
-    }
-    if (!ok && tma_pending) {
-        // a wait gave up: let the outstanding tile load land before the CTA's shared memory goes away
-        mbar_wait(&bar_tma[0], 0, nullptr, 0, 1u << 20);
     }
     block_sync_tc();
     if (warp == 0) tmem_dealloc(tm, T_COLS);

@@ -21,3 +21,19 @@ def assert_rms_close(actual, ref, tol, name=""):
 
 def to_np(t):
     return t.detach().float().cpu().numpy()
+
+
+def assert_bf16_close(actual, ref, tol, name=""):
+    """Parity bar for a bf16 output: the error beyond the output's own rounding (half an ulp of a bf16,
+    at most 2^-8 |ref|, which the reference's fp32 -> bf16 cast at gdn_ref.py:52 carries too) is at most
+    tol x RMS(ref). Returns (strict max-abs/RMS, excess/RMS) for reporting."""
+    a = np.asarray(actual, dtype=np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    assert a.shape == r.shape, f"{name}: shape {a.shape} != {r.shape}"
+    assert np.isfinite(a).all(), f"{name}: non-finite values"
+    rr = max(rms(r), 1e-30)
+    err = np.abs(a - r)
+    excess = float((err - 2.0 ** -8 * np.abs(r)).max()) if a.size else 0.0
+    assert excess <= tol * rr, (f"{name}: error beyond bf16 output rounding {excess:.3e} > {tol} * RMS(ref) = "
+                                f"{tol * rr:.3e} (strict max-abs/RMS {err.max() / rr:.4f})")
+    return float(err.max() / rr), excess / rr

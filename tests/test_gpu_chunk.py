@@ -1,8 +1,9 @@
 """GPU parity of the chunked tcgen05 path (bf16 activations, dk = dv = 128) through the C ABI.
 
 Expected values: the C oracle (the reference recurrence, gdn_ref.py:17-22, restated and pinned by
-test_oracle_golden.py) run in fp32 on exactly the bf16-rounded inputs the GPU sees. Bar: max-abs error
-<= 2e-2 x RMS(reference) for outputs and states, 3e-2 for gradients (bf16).
+test_oracle_golden.py) run in fp32 on exactly the bf16-rounded inputs the GPU sees. Bars: fp32 outputs
+(states, transition maps) max-abs error <= 2e-2 x RMS(reference); bf16 outputs: the same bound on the
+error beyond the output's own bf16 rounding (helpers.assert_bf16_close); gradients 3e-2.
 """
 import ctypes
 
@@ -10,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import assert_rms_close, to_np
+from helpers import assert_bf16_close, assert_rms_close, to_np
 from oracle import cgdn
 
 pytestmark = pytest.mark.gpu
@@ -55,7 +56,7 @@ def test_chunk_forward_matches_oracle(B, T, H, HV, l2):
     xn = _np(x)
     o_ref, ht_ref = cgdn.forward(xn["q"], xn["k"], xn["v"], xn["g"], xn["beta"], D ** -0.5,
                                  initial_state=to_np(h0), use_qk_l2norm=l2)
-    assert_rms_close(to_np(o), o_ref, 2e-2, "o")
+    assert_bf16_close(to_np(o), o_ref, 2e-2, "o")
     assert_rms_close(to_np(ht), ht_ref, 2e-2, "final_state")
 
 
@@ -70,7 +71,7 @@ def test_chunk_forward_varlen_short_documents():
     xn = _np(x)
     o_ref, ht_ref = cgdn.forward(xn["q"], xn["k"], xn["v"], xn["g"], xn["beta"], D ** -0.5, cu_seqlens=cu,
                                  use_qk_l2norm=True)
-    assert_rms_close(to_np(o), o_ref, 2e-2, "o")
+    assert_bf16_close(to_np(o), o_ref, 2e-2, "o")
     assert_rms_close(to_np(ht), ht_ref, 2e-2, "final_state")
     # documents are isolated: changing document [4, 70) leaves later documents bit-identical
     x2 = dict(x)
@@ -93,7 +94,7 @@ def test_chunk_forward_checkpoints_are_chunk_start_states():
     n_ck = (T + 63) // 64
     n_ck = (n_ck + K - 1) // K
     assert ck.shape[0] == n_ck
-    assert_rms_close(to_np(ck[0]), to_np(h0), 1e-6, "ckpt 0 = h0")
+    assert_rms_close(to_np(ck[0]), to_np(h0[0]), 1e-6, "ckpt 0 = h0")
     for m in range(1, n_ck):
         t = 64 * K * m
         _, st = cgdn.forward(xn["q"][:, :t], xn["k"][:, :t], xn["v"][:, :t], xn["g"][:, :t], xn["beta"][:, :t],
@@ -110,7 +111,7 @@ def test_chunk_forward_large_row_config1_shape():
                                    use_qk_l2norm_in_kernel=True)
     xn = _np(x)
     o_ref, ht_ref = cgdn.forward(xn["q"], xn["k"], xn["v"], xn["g"], xn["beta"], D ** -0.5, use_qk_l2norm=True)
-    assert_rms_close(to_np(o), o_ref, 2e-2, "o")
+    assert_bf16_close(to_np(o), o_ref, 2e-2, "o")
     assert_rms_close(to_np(ht), ht_ref, 2e-2, "final_state")
 
 
@@ -123,7 +124,7 @@ def test_chunk_forward_strong_decay_stays_finite():
     xn = _np(x)
     o_ref, ht_ref = cgdn.forward(xn["q"], xn["k"], xn["v"], xn["g"], xn["beta"], D ** -0.5)
     assert torch.isfinite(o.float()).all() and torch.isfinite(ht).all()
-    assert_rms_close(to_np(o), o_ref, 2e-2, "o")
+    assert_bf16_close(to_np(o), o_ref, 2e-2, "o")
 
 
 def test_sequence_split_passes_bf16():
@@ -151,4 +152,4 @@ def test_sequence_split_passes_bf16():
     s_out = seqsplit.combine(M, c2, c1)
     assert_rms_close(to_np(s_out), to_np(ht_full), 2e-2, "combined state")
     seqsplit.apply_incoming_state(segs[1]["q"], segs[1]["k"], segs[1]["g"], segs[1]["beta"], c1, o2, D ** -0.5)
-    assert_rms_close(to_np(torch.cat([o1, o2], 1)), to_np(o_full), 2e-2, "o")
+    assert_bf16_close(to_np(torch.cat([o1, o2], 1)), to_np(o_full), 2e-2, "o")
