@@ -32,10 +32,14 @@ using namespace sm100;
 namespace cf {
 constexpr int NTHR = 256;
 // shared memory carve (bytes from a 1024-aligned base)
-constexpr uint32_t OFF_QK = 0;        // 2 stages x 32 KB; per d-block kb: [Q 8 KB | K 8 KB] (64 rows x 128 B)
-constexpr uint32_t OFF_V = 65536;     // V, single stage, [kb][8 KB]
-constexpr uint32_t OFF_S = 81920;     // S0^T bf16 [dv][dk] K-major, 2 dk-blocks x 16 KB
-constexpr uint32_t OFF_W = 114688;    // -W bf16 [i][d] K-major, 2 d-blocks x 8 KB
+// Q/K: per d-block kb (24 KB apart): [K odd chunks 8 KB | Q 8 KB | K even chunks 8 KB], 64 rows x 128 B
+// each. K is double-buffered, Q single-buffered; either way [Q;K] (even) or [K;Q] (odd) is one
+// contiguous 128-row K-major operand for MMA1.
+constexpr uint32_t OFF_QK = 0;
+constexpr uint32_t QK_BLK = 24576;
+constexpr uint32_t OFF_V = 49152;     // V, single stage, [kb][8 KB]
+constexpr uint32_t OFF_S = 65536;     // S0^T hi bf16 [dv][dk] K-major, 2 dk-blocks x 16 KB
+constexpr uint32_t OFF_SL = 98304;    // S0^T lo
 constexpr uint32_t OFF_D = 131072;    // Delta^T hi bf16 [dv][j], 16 KB
 constexpr uint32_t OFF_DL = 147456;   // Delta^T lo
 constexpr uint32_t OFF_DD = 163840;   // Dd^T hi
@@ -44,6 +48,7 @@ constexpr uint32_t OFF_TB = 196608;   // TB bf16 [i][j], 8 KB
 constexpr uint32_t OFF_TV = 204800;   // TV bf16 [i][j], 8 KB
 constexpr uint32_t OFF_P = 212992;    // P' hi bf16 [i][j], 8 KB
 constexpr uint32_t OFF_PL = 221184;   // P' lo
+constexpr uint32_t OFF_W = OFF_TB;    // -W bf16 [i][d] K-major, 2 d-blocks x 8 KB: reuses TB/TV once MMA2/3 ran
 constexpr uint32_t OFF_VEC = 229376;  // G, e^G, beta, e^(G_C-G), 1/nq, 1/nk, misc: 7 x 64 fp32
 constexpr uint32_t OFF_BAR = OFF_VEC + 7 * 64 * 4;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 64 + 1024;
@@ -144,10 +149,11 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     float* vNQ = vG + 256;  // 1/nq (0 on padded rows)
     float* vNK = vG + 320;  // 1/nk (0 on padded rows)
     float* vMisc = vG + 384;
-    uint64_t* bar_qk = (uint64_t*)(sm + OFF_BAR);  // [2]
-    uint64_t* bar_v = bar_qk + 2;
-    uint64_t* bar_mma = bar_qk + 3;
-    uint32_t* tmem_slot = (uint32_t*)(bar_qk + 4);
+    uint64_t* bar_k = (uint64_t*)(sm + OFF_BAR);  // [2]: K tile of even / odd chunks
+    uint64_t* bar_q = bar_k + 2;
+    uint64_t* bar_v = bar_k + 3;
+    uint64_t* bar_mma = bar_k + 4;
+    uint32_t* tmem_slot = (uint32_t*)(bar_k + 5);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int lg = warp & 3, chh = warp >> 2;  // TMEM lane group, column half
@@ -179,8 +185,9 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     }
 
     if (tid == 0) {
-        mbar_init(&bar_qk[0], 1);
-        mbar_init(&bar_qk[1], 1);
+        mbar_init(&bar_k[0], 1);
+        mbar_init(&bar_k[1], 1);
+        mbar_init(bar_q, 1);
         mbar_init(bar_v, 1);
         mbar_init(bar_mma, 1);
         fence_barrier_init();
@@ -216,15 +223,19 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         tmem_wait_st();
     }
 
-    auto issue_qk = [&](int c, int s) {
-        const int tok0 = (int)(bos + 64 * c);
-        uint8_t* sQK = sm + OFF_QK + s * 32768;
-        mbar_arrive_expect_tx(&bar_qk[s], TX_QK);
+    // K of chunk c goes to slot (c & 1): +16 KB (even) or +0 (odd) inside each d-block; Q to +8 KB
+    auto issue_k = [&](int c) {
+        const int tok0 = (int)(bos + 64 * c), s = c & 1;
+        mbar_arrive_expect_tx(&bar_k[s], TX_QK / 2);
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {
-            tma_load_3d(sQK + kb * 16384, &a.tq, &bar_qk[s], kb * 64, hq, tok0);
-            tma_load_3d(sQK + kb * 16384 + 8192, &a.tk, &bar_qk[s], kb * 64, hq, tok0);
-        }
+        for (int kb = 0; kb < 2; ++kb)
+            tma_load_3d(sm + OFF_QK + kb * QK_BLK + (s ? 0 : 16384), &a.tk, &bar_k[s], kb * 64, hq, tok0);
+    };
+    auto issue_q = [&](int c) {
+        const int tok0 = (int)(bos + 64 * c);
+        mbar_arrive_expect_tx(bar_q, TX_QK / 2);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) tma_load_3d(sm + OFF_QK + kb * QK_BLK + 8192, &a.tq, bar_q, kb * 64, hq, tok0);
     };
     auto issue_v = [&](int c) {
         const int tok0 = (int)(bos + 64 * c);
@@ -233,7 +244,8 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         tma_load_3d(sm + OFF_V + 8192, &a.tv, bar_v, 64, hv, tok0);
     };
     if (tid == 0 && nchunks > 0) {
-        issue_qk(0, 0);
+        issue_k(0);
+        issue_q(0);
         if (!a.zero_v) issue_v(0);
     }
 
@@ -242,8 +254,10 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         const int s = c & 1;
         const int64_t tok0 = bos + 64 * (int64_t)c;
         const int nv = (len - 64 * (int64_t)c) < 64 ? (int)(len - 64 * (int64_t)c) : 64;
-        uint8_t* sQK = sm + OFF_QK + s * 32768;
-        const uint32_t aQK = sbase + OFF_QK + s * 32768, aV = sbase + OFF_V;
+        const uint32_t kofs = s ? 0u : 16384u;              // K slot inside a d-block
+        const uint32_t aBlk = sbase + OFF_QK, aV = sbase + OFF_V;
+        const uint32_t aK = aBlk + kofs, aQ = aBlk + 8192;  // d-block 0 of K and Q
+        const uint32_t aA1 = s ? aK : aQ;                   // MMA1's 128-row A: [Q;K] even, [K;Q] odd
 
         // (a) gates: Gamma = cumsum(g) inside the chunk, beta; padded rows carry g = 0, beta = 0
         if (tid < 64) {
@@ -260,18 +274,18 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
 
         // (b) this chunk's Q, K tiles; prefetch the next chunk's into the other stage
-        wait_bar(&bar_qk[s], (uint32_t)(c >> 1) & 1u, a.err, 1, ok);
-        if (tid == 0 && c + 1 < nchunks) issue_qk(c + 1, s ^ 1);
+        wait_bar(&bar_k[s], (uint32_t)(c >> 1) & 1u, a.err, 1, ok);
+        wait_bar(bar_q, (uint32_t)c & 1u, a.err, 7, ok);
+        if (tid == 0 && c + 1 < nchunks) issue_k(c + 1);  // the other K slot: MMA7 of chunk c-1 is done
 
-        // (c) MMA1: D1 = [Q;K] K^T on the raw tiles (M=128, N=64, K=128)
+        // (c) MMA1: D1 = [Q;K] K^T (even chunks) or [K;Q] K^T (odd) on the raw tiles (M=128, N=64, K=128)
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id = idesc_bf16(128, 64, 0, 0);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tD1, desc_kmajor(aQK + kb * 16384 + ko), desc_kmajor(aQK + kb * 16384 + 8192 + ko), id,
-                          ks > 0);
+                umma_bf16(tD1, desc_kmajor(aA1 + kb * QK_BLK + ko), desc_kmajor(aK + kb * QK_BLK + ko), id, ks > 0);
             }
             umma_commit(bar_mma);
         }
@@ -280,7 +294,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         // (d) meanwhile: row norms of q and k (2 threads per row)
         {
             const int r = tid >> 1, half = tid & 1, i = r & 63;
-            const uint8_t* rowp = sQK + half * 16384 + (r < 64 ? 0 : 8192) + i * 128;
+            const uint8_t* rowp = sm + OFF_QK + half * QK_BLK + (r < 64 ? 8192 : kofs) + i * 128;
             float ss = 0.f;
 #pragma unroll
             for (int cc = 0; cc < 8; ++cc) {
@@ -315,9 +329,9 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 float v[16];
                 tmem_ld16(tS + lane_base + 64 * chh + c0, v);
                 tmem_wait_ld();
-                uint8_t* dst = sm + OFF_S + chh * 16384;
-                st_chunk8(dst + sw128_off(row, c0), v);
-                st_chunk8(dst + sw128_off(row, c0 + 8), v + 8);
+                const uint32_t o0 = chh * 16384 + sw128_off(row, c0), o1 = chh * 16384 + sw128_off(row, c0 + 8);
+                st_chunk8_split(sm + OFF_S + o0, sm + OFF_SL + o0, v);
+                st_chunk8_split(sm + OFF_S + o1, sm + OFF_SL + o1, v + 8);
                 if (ck) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) ckp[(64 * chh + c0 + i) * 128 + row] = v[i];
@@ -334,8 +348,8 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         {
             float v[32];
             ld32(tD1 + lane_base + 32 * chh, v);
-            if (lg < 2) {  // Q K^T row i
-                const int i = row;
+            if ((lg < 2) == (s == 0)) {  // Q K^T row i (rows 0-63 on even chunks, 64-127 on odd)
+                const int i = row & 63;
                 const float gi = vG[i];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
@@ -347,7 +361,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                     st_chunk8_split(sm + OFF_P + sw128_off(i, 32 * chh + 8 * q),
                                     sm + OFF_PL + sw128_off(i, 32 * chh + 8 * q), v + 8 * q);
             } else {  // K K^T row i
-                const int i = row - 64;
+                const int i = row & 63;
                 const float gi = vG[i], bi = vB[i] * vNK[i];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
@@ -431,8 +445,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             const uint32_t id = idesc_bf16(128, 64, 1, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-                umma_bf16(tW, desc_mnmajor(aQK + 8192 + ks * 2048, 16384), desc_kmajor(sbase + OFF_TB + ks * 32), id,
-                          ks > 0);
+                umma_bf16(tW, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sbase + OFF_TB + ks * 32), id, ks > 0);
                 umma_bf16(tU, desc_mnmajor(aV + ks * 2048, 8192), desc_kmajor(sbase + OFF_TV + ks * 32), id, ks > 0);
             }
             umma_commit(bar_mma);
@@ -454,19 +467,24 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         fence_async_smem();
         block_sync_tc();
 
-        // (k) MMA4: U^T += S0^T (-W)^T -> Delta^T ; MMA5: O1^T = S0^T Q^T   (K = dk = 128)
+        // (k) MMA4: U^T += (S0hi + S0lo)^T (-W)^T -> Delta^T ; MMA5: O1^T = S0hi^T Q^T   (K = dk = 128)
         if (tid == 0) {
             const uint32_t id = idesc_bf16(128, 64, 0, 0);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                const uint64_t ad = desc_kmajor(sbase + OFF_S + kb * 16384 + ko);
-                umma_bf16(tU, ad, desc_kmajor(sbase + OFF_W + kb * 8192 + ko), id, 1);
-                umma_bf16(tO1, ad, desc_kmajor(aQK + kb * 16384 + ko), id, ks > 0);
+                const uint64_t ah = desc_kmajor(sbase + OFF_S + kb * 16384 + ko);
+                const uint64_t al = desc_kmajor(sbase + OFF_SL + kb * 16384 + ko);
+                const uint64_t bw = desc_kmajor(sbase + OFF_W + kb * 8192 + ko);
+                umma_bf16(tU, ah, bw, id, 1);
+                umma_bf16(tU, al, bw, id, 1);
+                umma_bf16(tO1, ah, desc_kmajor(aQ + kb * QK_BLK + ko), id, ks > 0);
             }
             umma_commit(bar_mma);
         }
         wait_mma(bar_mma, mma_phase, a.err, 4, ok);
+        // Q is consumed: load the next chunk's Q
+        if (tid == 0 && c + 1 < nchunks) issue_q(c + 1);
 
         // (l) Delta^T (TMEM, lane = dv) -> hi/lo bf16 Delta^T and Dd^T (K-major A operands)
         {
@@ -494,7 +512,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 umma_bf16(tO2, dh, ph, id6, ks > 0);
                 umma_bf16(tO2, dl, ph, id6, 1);
                 umma_bf16(tO2, dh, pl, id6, 1);
-                const uint64_t kd = desc_mnmajor(aQK + 8192 + ks * 2048, 16384);
+                const uint64_t kd = desc_mnmajor(aK + ks * 2048, QK_BLK);
                 umma_bf16(tS, desc_kmajor(sbase + OFF_DD + ks * 32), kd, id7, 1);
                 umma_bf16(tS, desc_kmajor(sbase + OFF_DDL + ks * 32), kd, id7, 1);
             }
