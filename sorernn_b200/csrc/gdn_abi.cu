@@ -114,6 +114,7 @@ size_t gdn_chunk_fwd_workspace_size(const gdn_problem* p) {
 
 size_t gdn_chunk_bwd_workspace_size(const gdn_problem* p) {
     if (check_problem(p) != GDN_OK) return 0;
+    if (gdn_uses_chunk_kernels(p)) return kErrBytes + chunk_bwd_workspace(p->B, p->T, p->N, p->H, p->HV, p->cu_seqlens);
     return kErrBytes + rec_bwd_workspace(p->N, p->HV, p->DK, p->DV, max_len(p), p->B * p->T, p->H);
 }
 
@@ -144,7 +145,18 @@ int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void
     if (!aligned16(workspace)) return GDN_ERR_ALIGN;
     cudaStream_t s = (cudaStream_t)stream;
     if (cudaMemsetAsync(workspace, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
-    (void)checkpoints;
+    if (gdn_uses_chunk_kernels(p)) {
+        if (!checkpoints) return GDN_ERR_ARGUMENT;  // the chunked backward restarts from the forward's checkpoints
+        ChunkBwdLaunch C{};
+        C.q = q; C.k = k; C.v = v; C.g = g; C.beta = beta; C.dout = dout;
+        C.h0 = initial_state; C.ckpt = checkpoints; C.dht = dht;
+        C.dq = dq; C.dk = dk; C.dv = dv; C.dg = dg; C.dbeta = dbeta; C.dh0 = dh0;
+        C.ws = (char*)workspace + kErrBytes; C.cu = p->cu_seqlens; C.err = (int*)workspace;
+        C.B = p->B; C.T = p->T; C.N = p->N; C.H = p->H; C.HV = p->HV; C.max_seqlen = max_len(p);
+        C.scale = p->scale; C.g_dtype = p->g_dtype; C.beta_dtype = p->beta_dtype; C.l2norm = p->use_qk_l2norm;
+        C.ckpt_every = p->ckpt_every;
+        return chunk_bwd(C, s);
+    }
     RecLaunch L = rec_launch(p);
     L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta;
     L.h0 = initial_state;

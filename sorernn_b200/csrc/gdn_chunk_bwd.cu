@@ -1,0 +1,976 @@
+// Chunked gated-delta-rule backward on sm_100a (tcgen05 UMMA, TMA / bulk-copy fed, TMEM accumulators).
+//
+// One CTA (256 threads) per (sequence, value head) walks the chunks in reverse, carrying dS (the gradient
+// of the state at the chunk end, fp32 in TMEM). The chunk-start states S0 are not saved by the forward:
+// a segment-parallel pass of the forward kernel (chunk_fwd in recompute mode) rebuilds them from the
+// forward's checkpoints into the workspace as bf16 operand tiles; this kernel bulk-copies one per chunk.
+//
+// With qn = q/nq, kn = k/nk (the raw bf16 tiles feed the tensor cores; norms are applied in fp32),
+// Gamma = in-chunk cumsum(g), E_ij = exp(Gamma_i - Gamma_j), and the forward's A, T, W, U, Delta, P
+// recomputed per chunk (the algebra of tests/test_chunk_algebra.py::chunked_backward):
+//   dDelta = P^T dO + Kd dS                      Kd = kn e^(Gamma_C - Gamma)
+//   dS0    = scale (qn e^Gamma)^T dO + e^Gamma_C dS - W^T dDelta
+//   dP     = dO Delta^T,  dPs = lower_incl(dP . scale E)
+//   dqn    = scale e^Gamma (dO S0^T) + dPs kn
+//   dkn    = dPs^T qn + (Delta dS^T) e^(Gamma_C-Gamma) + beta e^Gamma dKb + (dG + dG^T) kn
+//   dVb = T^T dDelta, dv = beta dVb;   dW = -dDelta S0^T, dKb = T^T dW
+//   dA  = strict_lower(-Z T^T),  Z = dVb (beta V)^T + dKb (beta e^Gamma kn)^T
+//   dbeta = dVb.v + e^Gamma dKb.kn + rowsum(dA . G E);   dG = dA . beta E
+//   dGamma = rowsum-colsum(dA . A) + rowsum-colsum(dP . P) + scale e^Gamma qn.(S0 dO) + beta e^Gamma dKb.kn
+//            - kn.dKst_j  (+ sum_j kn.dKst_j + e^Gamma_C <dS, S0> on the last row);  dg = reverse cumsum
+//   dq = (dqn - qn (qn.dqn)) / nq,  dk likewise (chain rule through the L2 norm)
+// Every GEMM is an M = 128 UMMA with a 128-wide dimension on the TMEM lanes. The three 64 x 64 x K
+// products (dP, Z, dA) use a 128-row A operand of which one 64-row half is ignored; Z and dA put their
+// rows on lanes 64-127, where the same threads also hold the K K^T rows of the recomputed Gram matrix.
+// Operands are single bf16 (no hi/lo split): measured on the CPU, every gradient stays well inside the
+// bf16 tolerance with the raw q/k tiles exact.
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+#include "tmap.h"
+
+namespace gdn {
+using namespace sm100;
+
+namespace cb {
+constexpr int NTHR = 256;
+// shared memory carve (bytes from a 1024-aligned base)
+constexpr uint32_t OFF_QK = 0, QK_BLK = 16384;  // per d-block kb: [Q 8 KB | K 8 KB] (64 tokens x 128 B)
+constexpr uint32_t OFF_V = 32768;                // [kb][8 KB]
+constexpr uint32_t OFF_DO = 49152;               // [kb][8 KB]
+constexpr uint32_t OFF_S0 = 65536;               // S0^T bf16 [dv][dk], 2 dk-blocks x 16 KB (workspace image)
+constexpr uint32_t OFF_DS = 98304;               // dS^T bf16 [dv][dk]
+constexpr uint32_t OFF_W = 131072;               // -W bf16 [j][dk], 2 d-blocks x 8 KB (TB, TV before)
+constexpr uint32_t OFF_TB = 131072, OFF_TV = 139264;
+constexpr uint32_t OFF_T = 147456;    // T bf16 [i][j]
+constexpr uint32_t OFF_DEL = 155648;  // Delta^T bf16 [dv][j] -> Dd^T; later dG fp32 [64][64]
+constexpr uint32_t OFF_DD = 172032;   // dDelta^T bf16 [dv][j]; solve scratch before
+constexpr uint32_t OFF_PS = 188416;   // P'' bf16 [i][j] -> dPs / nk_j
+constexpr uint32_t OFF_PS2 = 196608;  // dPs / (nq_i nk_j) -> Z bf16 [j][m]
+constexpr uint32_t OFF_A = 204800;    // A -> T fp32 [64][AST]
+constexpr int AST = 68;
+constexpr int NVEC = 10;
+constexpr uint32_t OFF_VEC = OFF_A + 64 * AST * 4;     // NVEC x 64 fp32
+constexpr uint32_t OFF_RED = OFF_VEC + NVEC * 64 * 4;  // 4 reduction buffers of 4 x 64 fp32
+constexpr uint32_t OFF_BAR = OFF_RED + 4 * 256 * 4;    // 2 mbarriers, TMEM slot, scalars
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 128 + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+constexpr uint32_t OFF_DVB = OFF_S0;          // dVb^T bf16 [dv][j]   (S0 dead after step 8)
+constexpr uint32_t OFF_DWT = OFF_S0 + 16384;  // dW^T bf16 [dk][i]
+constexpr uint32_t OFF_DKB = OFF_DS;          // dKb^T bf16 [dk][j]   (dS tile dead after step 8)
+constexpr uint32_t OFF_GS = OFF_DS + 16384;   // (dG + dG^T) / (nk nk) bf16 [j][m]
+constexpr uint32_t OFF_Y = OFF_DD;
+// TMEM columns (fp32, 128 lanes)
+constexpr uint32_t T_S = 0, T_D1 = 128, C192 = 192, C256 = 256, C320 = 320, C384 = 384, C448 = 448, T_COLS = 512;
+}  // namespace cb
+
+struct ChunkBwdArgs {
+    CUtensorMap tq, tk, tv, tdo;
+    const void* g;
+    const void* beta;
+    const uint8_t* s0_tiles;  // per (chunk, head) 32 KB bf16 S0^T images
+    const float* dht;
+    void* dq;  // bf16 [tok][H][128], or fp32 accumulators when accumulate_qk
+    void* dk;
+    void* dv;
+    float* dg;
+    float* dbeta;
+    float* dh0;
+    const int64_t* cu;
+    int* err;
+    int64_t T;
+    int N, H, HV, g_dtype, beta_dtype;
+    float scale;
+    int l2norm, accumulate_qk;
+};
+
+__device__ __forceinline__ float ld_gb(const void* p, int dtype, int64_t i) {
+    if (dtype == GDN_FP32) return ((const float*)p)[i];
+    if (dtype == GDN_BF16) return __bfloat162float(((const __nv_bfloat16*)p)[i]);
+    return __half2float(((const __half*)p)[i]);
+}
+__device__ __forceinline__ uint32_t pk_bf16(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void st8(uint8_t* dst, const float* v) {
+    uint4 u;
+    u.x = pk_bf16(v[0], v[1]);
+    u.y = pk_bf16(v[2], v[3]);
+    u.z = pk_bf16(v[4], v[5]);
+    u.w = pk_bf16(v[6], v[7]);
+    *reinterpret_cast<uint4*>(dst) = u;
+}
+__device__ __forceinline__ float bfv(const uint8_t* base, uint32_t off) {
+    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(base + off));
+}
+// element (row r, col c) of a [rows][128] bf16 tile stored as two 64-column swizzled blocks `blk` bytes apart
+__device__ __forceinline__ float tile128(const uint8_t* base, uint32_t blk, int r, int c) {
+    return bfv(base, (uint32_t)(c >> 6) * blk + sw128_off(r, c & 63));
+}
+__device__ __forceinline__ void sync_tc() {
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+}
+__device__ __forceinline__ void bwait(uint64_t* bar, uint32_t parity, int* err, int code, bool& ok) {
+    ok = mbar_wait(bar, parity, err, code, ok ? (1u << 22) : 1u) && ok;
+}
+__device__ __forceinline__ void mwait(uint64_t* bar, uint32_t& phase, int* err, int code, bool& ok) {
+    bwait(bar, phase, err, code, ok);
+    phase ^= 1u;
+    tc_fence_after();
+}
+__device__ __forceinline__ void ld32c(uint32_t taddr, float (&v)[32]) {
+    tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(v));
+    tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+    tmem_wait_ld();
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"((uint64_t)src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// v[k] holds this thread's value for column 32*chh + k. Afterwards lane l holds the sum over the warp's
+// 32 lanes of column 32*chh + l (recursive halving: 31 shuffles for 32 columns).
+__device__ __forceinline__ float warp_colsum32(float (&v)[32]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const bool up = (lane & off) != 0;
+#pragma unroll
+        for (int k = 0; k < off; ++k) {
+            const float send = up ? v[k] : v[k + off];
+            const float keep = up ? v[k + off] : v[k];
+            v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+    return v[0];
+}
+// Column sums over all 128 TMEM lanes: every warp deposits its 32 column partials in red[lg][col];
+// after a barrier colsum(red, col) is the total. Called by all 8 warps.
+__device__ __forceinline__ void deposit_colsum(float (&v)[32], float* red, int lg, int chh) {
+    const float s = warp_colsum32(v);
+    red[lg * 64 + 32 * chh + (threadIdx.x & 31)] = s;
+}
+__device__ __forceinline__ float colsum(const float* red, int col) {
+    return red[col] + red[64 + col] + red[128 + col] + red[192 + col];
+}
+
+__global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_constant__ ChunkBwdArgs a) {
+    using namespace cb;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    float* Tm = (float*)(sm + OFF_A);
+    float* Yb = (float*)(sm + OFF_Y);
+    float* dGm = (float*)(sm + OFF_DEL);
+    float* vG = (float*)(sm + OFF_VEC);
+    float* vEG = vG + 64;
+    float* vB = vG + 128;
+    float* vX = vG + 192;   // e^(G_C - G) / nk
+    float* vNQ = vG + 256;  // 1/nq (0 on padded rows)
+    float* vNK = vG + 320;  // 1/nk (0 on padded rows)
+    float* vDG = vG + 384;  // dGamma
+    float* vDB = vG + 448;  // dbeta
+    float* vR4 = vG + 512;  // kn_j . dKst_j
+    float* red0 = (float*)(sm + OFF_RED);
+    float* red1 = red0 + 256;
+    float* red2 = red0 + 512;
+    float* red3 = red0 + 768;
+    uint64_t* bar_in = (uint64_t*)(sm + OFF_BAR);
+    uint64_t* bar_mma = bar_in + 1;
+    uint32_t* tmem_slot = (uint32_t*)(bar_in + 2);
+    float* scal = (float*)(bar_in + 3);  // [0] e^G_C, [1..8] <dS, S0> per warp
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int lg = warp & 3, chh = warp >> 2;
+    const int row = 32 * lg + lane;  // TMEM lane of this thread
+    const int n = blockIdx.x / a.HV, hv = blockIdx.x % a.HV, hq = hv / (a.HV / a.H);
+    int64_t bos, eos;
+    seq_bounds(a.cu, a.T, n, bos, eos);
+    const int64_t len = eos - bos;
+    const int nchunks = (int)((len + 63) / 64);
+
+    // index of this sequence's first chunk in the flattened chunk list (S0 tile slots)
+    int64_t cbase = 0;
+    if (!a.cu) {
+        cbase = (int64_t)n * ((a.T + 63) / 64);
+    } else {
+        int64_t part = 0;
+        for (int m = tid; m < n; m += NTHR) part += (a.cu[m + 1] - a.cu[m] + 63) / 64;
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if (lane == 0) ((int64_t*)red0)[warp] = part;
+        __syncthreads();
+        for (int w = 0; w < NTHR / 32; ++w) cbase += ((int64_t*)red0)[w];
+        __syncthreads();
+    }
+
+    if (tid == 0) {
+        mbar_init(bar_in, 1);
+        mbar_init(bar_mma, 1);
+        fence_barrier_init();
+        prefetch_tmap(&a.tq);
+        prefetch_tmap(&a.tk);
+        prefetch_tmap(&a.tv);
+        prefetch_tmap(&a.tdo);
+    }
+    if (warp == 0) tmem_alloc(tmem_slot, T_COLS);
+    sync_tc();
+    const uint32_t tm = *tmem_slot;
+    const uint32_t lb = (uint32_t)(32 * lg) << 16;
+    const uint32_t tS = tm + T_S, tD1 = tm + T_D1;
+    uint32_t mph = 0;
+    bool ok = true;
+    const uint32_t sb = smem_u32(sm);
+
+    // dS^T <- dht^T (TMEM lane = dv, columns dk)
+    {
+        const float* dht = a.dht ? a.dht + ((int64_t)n * a.HV + hv) * 16384 : nullptr;
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = dht ? dht[(64 * chh + c0 + i) * 128 + row] : 0.f;
+            tmem_st16(tS + lb + 64 * chh + c0, v);
+        }
+        tmem_wait_st();
+    }
+
+    auto issue_inputs = [&](int c) {
+        const int tok0 = (int)(bos + 64 * c);
+        mbar_arrive_expect_tx(bar_in, 8 * 8192 + 32768);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+            tma_load_3d(sm + OFF_QK + kb * QK_BLK, &a.tq, bar_in, kb * 64, hq, tok0);
+            tma_load_3d(sm + OFF_QK + kb * QK_BLK + 8192, &a.tk, bar_in, kb * 64, hq, tok0);
+            tma_load_3d(sm + OFF_V + kb * 8192, &a.tv, bar_in, kb * 64, hv, tok0);
+            tma_load_3d(sm + OFF_DO + kb * 8192, &a.tdo, bar_in, kb * 64, hv, tok0);
+        }
+        bulk_load(sm + OFF_S0, a.s0_tiles + ((cbase + c) * a.HV + hv) * 32768, 32768, bar_in);
+    };
+    if (tid == 0 && nchunks > 0) issue_inputs(nchunks - 1);
+    uint32_t in_phase = 0;
+    const uint32_t aQ = sb + OFF_QK, aK = sb + OFF_QK + 8192, aV = sb + OFF_V, aDO = sb + OFF_DO;
+
+    for (int c = nchunks - 1; c >= 0; --c) {
+        const int64_t tok0 = bos + 64 * (int64_t)c;
+        const int nv = (len - 64 * (int64_t)c) < 64 ? (int)(len - 64 * (int64_t)c) : 64;
+
+        // ---- 1. gates; wait for this chunk's tiles ------------------------------------------------------
+        if (tid < 64) {
+            const bool in = tid < nv;
+            const int64_t gi = (tok0 + tid) * a.HV + hv;
+            float x = in ? ld_gb(a.g, a.g_dtype, gi) : 0.f;
+            vB[tid] = in ? ld_gb(a.beta, a.beta_dtype, gi) : 0.f;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            vG[tid] = x;
+            vDG[tid] = 0.f;
+            vDB[tid] = 0.f;
+        }
+        bwait(bar_in, in_phase, a.err, 11, ok);
+        in_phase ^= 1u;
+
+        // ---- 2. R1: D1 = [Q;K] K^T (rows 0-63 Q K^T, 64-127 K K^T; kept for the whole chunk) ----------
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t id = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                umma_bf16(tD1, desc_kmajor(aQ + kb * QK_BLK + ko), desc_kmajor(aK + kb * QK_BLK + ko), id, ks > 0);
+            }
+            umma_commit(bar_mma);
+        }
+        __syncthreads();
+        if (tid >= 32 && tid < 64) vG[tid] += vG[31];
+        {  // row norms (2 threads per row; rows 0-63 q, 64-127 k)
+            const int r = tid >> 1, half = tid & 1, i = r & 63;
+            const uint8_t* rowp = sm + OFF_QK + half * QK_BLK + (r < 64 ? 0 : 8192) + i * 128;
+            float ss = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                const uint4 u = *reinterpret_cast<const uint4*>(rowp + cc * 16);
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __bfloat1622float2(h[e]);
+                    ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+                }
+            }
+            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+            float inv = a.l2norm ? 1.f / fmaxf(sqrtf(ss), kL2Eps) : 1.f;
+            if (i >= nv) inv = 0.f;
+            if (half == 0) (r < 64 ? vNQ : vNK)[i] = inv;
+        }
+        __syncthreads();
+        if (tid < 64) {
+            vEG[tid] = __expf(vG[tid]);
+            vX[tid] = __expf(vG[63] - vG[tid]) * vNK[tid];
+        }
+        if (tid == 64) scal[0] = __expf(vG[63]);
+        __syncthreads();
+        mwait(bar_mma, mph, a.err, 12, ok);
+
+        // ---- 3. D1 -> P'' (bf16) and A (fp32); T = (I + A)^-1; TB, TV, T tiles --------------------------
+        {
+            float v[32];
+            ld32c(tD1 + lb + 32 * chh, v);
+            const int i = row & 63;
+            const float gi = vG[i];
+            if (lg < 2) {  // P''_ij = scale qn_i.kn_j E_ij (j <= i)
+                const float f = a.scale * vNQ[i];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int jj = 32 * chh + j;
+                    v[j] = (jj <= i) ? f * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) st8(sm + OFF_PS + sw128_off(i, 32 * chh + 8 * q), v + 8 * q);
+            } else {  // A_ij = beta_i kn_i.kn_j E_ij (j < i)
+                const float bi = vB[i] * vNK[i];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int jj = 32 * chh + j;
+                    v[j] = (jj < i) ? bi * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
+                }
+                float4* dst = reinterpret_cast<float4*>(Tm + i * AST + 32 * chh);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            }
+        }
+        __syncthreads();
+        {
+            float x[16];
+            const int b = tid >> 4, cidx = tid & 15;
+            if (tid < 64) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float sacc = 0.f;
+#pragma unroll
+                    for (int j = 0; j < i; ++j) sacc = fmaf(Tm[(16 * b + i) * AST + 16 * b + j], x[j], sacc);
+                    x[i] = (i == cidx) ? 1.f : (i < cidx ? 0.f : -sacc);
+                }
+            }
+            __syncthreads();
+            if (tid < 64) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) Tm[(16 * b + i) * AST + 16 * b + cidx] = x[i];
+            }
+            __syncthreads();
+        }
+#pragma unroll 1
+        for (int r = 1; r < 4; ++r) {
+            for (int e = tid; e < r * 256; e += NTHR) {
+                const int s2 = e >> 8, i = (e >> 4) & 15, cc = e & 15;
+                float y = 0.f;
+                for (int m = s2; m < r; ++m) {
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj)
+                        y = fmaf(Tm[(16 * r + i) * AST + 16 * m + jj], Tm[(16 * m + jj) * AST + 16 * s2 + cc], y);
+                }
+                Yb[e] = y;
+            }
+            __syncthreads();
+            for (int e = tid; e < r * 256; e += NTHR) {
+                const int s2 = e >> 8, i = (e >> 4) & 15, cc = e & 15;
+                float t = 0.f;
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj)
+                    t = fmaf(Tm[(16 * r + i) * AST + 16 * r + jj], Yb[s2 * 256 + jj * 16 + cc], t);
+                Tm[(16 * r + i) * AST + 16 * s2 + cc] = -t;
+            }
+            __syncthreads();
+        }
+        {
+            const int i = tid >> 2, q = tid & 3;
+            float tb[16], tv[16], tt[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int jj = 16 * q + j;
+                tt[j] = Tm[i * AST + jj];
+                tv[j] = tt[j] * vB[jj];
+                tb[j] = tv[j] * vEG[jj] * vNK[jj];
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                st8(sm + OFF_TB + sw128_off(i, 16 * q + 8 * h), tb + 8 * h);
+                st8(sm + OFF_TV + sw128_off(i, 16 * q + 8 * h), tv + 8 * h);
+                st8(sm + OFF_T + sw128_off(i, 16 * q + 8 * h), tt + 8 * h);
+            }
+        }
+        fence_async_smem();
+        sync_tc();
+
+        // ---- 4. R2 W^T = K^T TB^T (192), R3 U^T = V^T TV^T (256); meanwhile dS^T -> tile, dS <- e^G_C dS ---
+        if (tid == 0) {
+            const uint32_t id = idesc_bf16(128, 64, 1, 0);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                umma_bf16(tm + C192, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_TB + ks * 32), id,
+                          ks > 0);
+                umma_bf16(tm + C256, desc_mnmajor(aV + ks * 2048, 8192), desc_kmajor(sb + OFF_TV + ks * 32), id,
+                          ks > 0);
+            }
+            umma_commit(bar_mma);
+        }
+        {
+            const float eGC = scal[0];
+            float dss = 0.f;
+#pragma unroll
+            for (int c0 = 0; c0 < 64; c0 += 16) {
+                float v[16];
+                tmem_ld16(tS + lb + 64 * chh + c0, v);
+                tmem_wait_ld();
+                const uint32_t o0 = chh * 16384 + sw128_off(row, c0), o1 = chh * 16384 + sw128_off(row, c0 + 8);
+                st8(sm + OFF_DS + o0, v);
+                st8(sm + OFF_DS + o1, v + 8);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    dss = fmaf(v[e], bfv(sm + OFF_S0, o0 + 2 * e), dss);
+                    dss = fmaf(v[8 + e], bfv(sm + OFF_S0, o1 + 2 * e), dss);
+                }
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] *= eGC;
+                tmem_st16(tS + lb + 64 * chh + c0, v);
+            }
+            tmem_wait_st();
+            dss = warp_sum(dss);
+            if (lane == 0) scal[1 + warp] = dss;
+        }
+        mwait(bar_mma, mph, a.err, 13, ok);
+        {  // W^T (lane = d) -> -W bf16 [j][d]
+            float v[32];
+            ld32c(tm + C192 + lb + 32 * chh, v);
+            const int d = row;
+            uint8_t* dst = sm + OFF_W + (d >> 6) * 8192;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                *reinterpret_cast<__nv_bfloat16*>(dst + sw128_off(32 * chh + j, d & 63)) = __float2bfloat16_rn(-v[j]);
+        }
+        fence_async_smem();
+        sync_tc();
+
+        // ---- 5. R4: Delta^T = U^T + S0^T (-W)^T (256) -------------------------------------------------
+        if (tid == 0) {
+            const uint32_t id = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                umma_bf16(tm + C256, desc_kmajor(sb + OFF_S0 + kb * 16384 + ko),
+                          desc_kmajor(sb + OFF_W + kb * 8192 + ko), id, 1);
+            }
+            umma_commit(bar_mma);
+        }
+        mwait(bar_mma, mph, a.err, 14, ok);
+        {
+            float v[32];
+            ld32c(tm + C256 + lb + 32 * chh, v);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) st8(sm + OFF_DEL + sw128_off(row, 32 * chh + 8 * q), v + 8 * q);
+        }
+        fence_async_smem();
+        sync_tc();
+
+        // ---- 6. dO^T P''^T (320); dS^T K^T (384); dP = [dO;-] Delta^T (448); QA = S0 dO^T (192) ---------
+        if (tid == 0) {
+            const uint32_t id_mm = idesc_bf16(128, 64, 1, 1), id_kk = idesc_bf16(128, 64, 0, 0);
+            const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)  // K = i
+                umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS + ks * 2048, 8192),
+                          id_mm, ks > 0);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                umma_bf16(tm + C384, desc_kmajor(sb + OFF_DS + kb * 16384 + ko), desc_kmajor(aK + kb * QK_BLK + ko),
+                          id_kk, ks > 0);
+                umma_bf16(tm + C448, desc_kmajor(aDO + kb * 8192 + ko), desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192),
+                          id_km, ks > 0);
+                umma_bf16(tm + C192, desc_mnmajor(sb + OFF_S0 + ks * 2048, 16384), desc_kmajor(aDO + kb * 8192 + ko),
+                          id_mk, ks > 0);
+            }
+            umma_commit(bar_mma);
+        }
+        mwait(bar_mma, mph, a.err, 15, ok);
+
+        // ---- 7. dDelta^T = (320) + (384) diag(vX) -> tile; r4; dP -> dPs tiles, X_P sums -------------------
+        {
+            float d1[32], d2[32], de[32];
+            ld32c(tm + C320 + lb + 32 * chh, d1);
+            ld32c(tm + C384 + lb + 32 * chh, d2);
+            ld32c(tm + C256 + lb + 32 * chh, de);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float x = vX[32 * chh + j];
+                de[j] = de[j] * d2[j] * x;  // kn_j . dKst_j partial over this lane (dv)
+                d1[j] = fmaf(d2[j], x, d1[j]);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) st8(sm + OFF_DD + sw128_off(row, 32 * chh + 8 * q), d1 + 8 * q);
+            deposit_colsum(de, red0, lg, chh);
+        }
+        {
+            float v[32], p[32];
+            ld32c(tm + C448 + lb + 32 * chh, v);
+            ld32c(tD1 + lb + 32 * chh, p);
+            if (lg < 2) {
+                const int i = row;
+                const float gi = vG[i], nq = vNQ[i];
+                float d1v[32], d2v[32], rs = 0.f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int jj = 32 * chh + j;
+                    const bool m = jj <= i;
+                    const float e = m ? __expf(gi - vG[jj]) : 0.f;
+                    const float P = a.scale * p[j] * nq * vNK[jj] * e;
+                    const float xp = m ? v[j] * P : 0.f;
+                    rs += xp;
+                    p[j] = xp;
+                    const float dps = m ? v[j] * a.scale * e : 0.f;
+                    d1v[j] = dps * vNK[jj];
+                    d2v[j] = d1v[j] * nq;
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    st8(sm + OFF_PS + sw128_off(i, 32 * chh + 8 * q), d1v + 8 * q);
+                    st8(sm + OFF_PS2 + sw128_off(i, 32 * chh + 8 * q), d2v + 8 * q);
+                }
+                atomicAdd(&vDG[i], rs);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) p[j] = 0.f;
+            }
+            deposit_colsum(p, red1, lg, chh);
+        }
+        __syncthreads();
+        if (tid < 64) {
+            const float r4 = colsum(red0, tid);
+            vR4[tid] = r4;
+            vDG[tid] -= colsum(red1, tid) + r4;
+        }
+        // dO <- dO scale e^G / nq in place (A operand of the dS update; the raw dO readers have finished)
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+            const int e = tid + it * NTHR;
+            const int i = e >> 4, cc = e & 15;
+            uint8_t* pp = sm + OFF_DO + (cc >> 3) * 8192 + i * 128 + (((cc & 7) ^ (i & 7)) << 4);
+            uint4 u = *reinterpret_cast<uint4*>(pp);
+            const float f = a.scale * vEG[i] * vNQ[i];
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+            for (int k2 = 0; k2 < 4; ++k2) {
+                const float2 z = __bfloat1622float2(h[k2]);
+                h[k2] = __floats2bfloat162_rn(z.x * f, z.y * f);
+            }
+            *reinterpret_cast<uint4*>(pp) = u;
+        }
+        {  // Delta^T -> Dd^T = Delta^T diag(vX) in place (thread owns row dv, 32 columns)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t off = sw128_off(row, 32 * chh + 8 * q);
+                uint4 u = *reinterpret_cast<uint4*>(sm + OFF_DEL + off);
+                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+                for (int k2 = 0; k2 < 4; ++k2) {
+                    const float2 z = __bfloat1622float2(h[k2]);
+                    const int j = 32 * chh + 8 * q + 2 * k2;
+                    h[k2] = __floats2bfloat162_rn(z.x * vX[j], z.y * vX[j + 1]);
+                }
+                *reinterpret_cast<uint4*>(sm + OFF_DEL + off) = u;
+            }
+        }
+        fence_async_smem();
+        sync_tc();
+
+        // ---- 8. dVb^T = dDelta^T T (256); S0 dDelta^T = -dW^T (320); QB = K^T dPs1^T (384);
+        //         dK' = Q^T dPs2 + dS Dd^T (448)
+        if (tid == 0) {
+            const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mm = idesc_bf16(128, 64, 1, 1);
+            const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {  // K = tokens
+                umma_bf16(tm + C256, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
+                          id_km, ks > 0);
+                umma_bf16(tm + C384, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_PS + ks * 32), id_mk,
+                          ks > 0);
+                umma_bf16(tm + C448, desc_mnmajor(aQ + ks * 2048, QK_BLK), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
+                          id_mm, ks > 0);
+            }
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {  // K = dv
+                umma_bf16(tm + C320, desc_mnmajor(sb + OFF_S0 + ks * 2048, 16384),
+                          desc_mnmajor(sb + OFF_DD + ks * 2048, 8192), id_mm, ks > 0);
+                umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
+                          desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192), id_mm, 1);
+            }
+            umma_commit(bar_mma);
+        }
+        mwait(bar_mma, mph, a.err, 16, ok);
+
+        // ---- 9. dv, dVb tile, dVb.v; dW^T tile; qn.(S0 dO) and qn.QB -------------------------------------
+        {
+            float v[32], r2[32];
+            ld32c(tm + C256 + lb + 32 * chh, v);  // dVb^T[dv][j]
+            __nv_bfloat16* dvp = (__nv_bfloat16*)a.dv;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int jj = 32 * chh + j;
+                r2[j] = v[j] * tile128(sm + OFF_V, 8192, jj, row);
+                if (jj < nv) dvp[((tok0 + jj) * a.HV + hv) * 128 + row] = __float2bfloat16_rn(v[j] * vB[jj]);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) st8(sm + OFF_DVB + sw128_off(row, 32 * chh + 8 * q), v + 8 * q);
+            deposit_colsum(r2, red0, lg, chh);
+        }
+        {
+            float v[32];
+            ld32c(tm + C320 + lb + 32 * chh, v);  // (S0 dDelta^T)[dk][i] = -dW^T
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = -v[j];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) st8(sm + OFF_DWT + sw128_off(row, 32 * chh + 8 * q), v + 8 * q);
+        }
+        float qa[32], qb[32];  // dqn^T pieces [dk][i] for this thread's 32 tokens
+        {
+            ld32c(tm + C192 + lb + 32 * chh, qa);
+            ld32c(tm + C384 + lb + 32 * chh, qb);
+            float xa[32], xb[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int i = 32 * chh + j;
+                const float qn = tile128(sm + OFF_QK, QK_BLK, i, row) * vNQ[i];
+                xa[j] = qn * qa[j];
+                xb[j] = qn * qb[j];
+            }
+            deposit_colsum(xa, red1, lg, chh);
+            deposit_colsum(xb, red2, lg, chh);
+        }
+        fence_async_smem();
+        sync_tc();
+
+        // ---- 10. dKb^T = dW^T T (192) ; Z1 = [-; dVb] V^T (256, rows j on lanes 64-127) ------------------
+        if (tid == 0) {
+            const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+                umma_bf16(tm + C192, desc_kmajor(sb + OFF_DWT + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
+                          id_km, ks > 0);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                umma_bf16(tm + C256, desc_mnmajor(sb + OFF_DVB - 16384 + ks * 2048, 16384),
+                          desc_kmajor(aV + kb * 8192 + ko), id_mk, ks > 0);
+            }
+            umma_commit(bar_mma);
+        }
+        {  // dq epilogue
+            float xs[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int i = 32 * chh + j;
+                const float sci = a.scale * vEG[i];
+                const float dqn = fmaf(sci, qa[j], qb[j]);
+                float gq = dqn;
+                if (a.l2norm) {
+                    const float qn = tile128(sm + OFF_QK, QK_BLK, i, row) * vNQ[i];
+                    gq = (dqn - qn * fmaf(sci, colsum(red1, i), colsum(red2, i))) * vNQ[i];
+                }
+                xs[j] = gq;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int i = 32 * chh + j;
+                if (i < nv) {
+                    const int64_t idx = ((tok0 + i) * a.H + hq) * 128 + row;
+                    if (a.accumulate_qk) atomicAdd((float*)a.dq + idx, xs[j]);
+                    else ((__nv_bfloat16*)a.dq)[idx] = __float2bfloat16_rn(xs[j]);
+                }
+            }
+        }
+        if (tid < 64) {
+            vDG[tid] += a.scale * vEG[tid] * colsum(red1, tid);  // rowsum(dO . O_inter)
+            vDB[tid] += colsum(red0, tid);                       // dVb . v
+        }
+        mwait(bar_mma, mph, a.err, 17, ok);
+        __syncthreads();  // every reader of red0..red2 above is done before they are reused
+
+        // ---- 11. dKb (kept in registers), dKb.kn, dKb tile ; Z2 = [-; dKb] K^T (320) -------------------
+        float kbr[32];
+        {
+            ld32c(tm + C192 + lb + 32 * chh, kbr);  // dKb^T[dk][j]
+            float r3[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int jj = 32 * chh + j;
+                r3[j] = kbr[j] * tile128(sm + OFF_QK + 8192, QK_BLK, jj, row) * vNK[jj];
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) st8(sm + OFF_DKB + sw128_off(row, 32 * chh + 8 * q), kbr + 8 * q);
+            deposit_colsum(r3, red0, lg, chh);
+        }
+        fence_async_smem();
+        sync_tc();
+        if (tid == 0) {
+            const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                umma_bf16(tm + C320, desc_mnmajor(sb + OFF_DKB - 16384 + ks * 2048, 16384),
+                          desc_kmajor(aK + kb * QK_BLK + ko), id_mk, ks > 0);
+            }
+            umma_commit(bar_mma);
+        }
+        if (tid < 64) {
+            const float r3 = colsum(red0, tid);  // dKb_j . kn_j
+            vDB[tid] += vEG[tid] * r3;
+            vDG[tid] += vB[tid] * vEG[tid] * r3;
+        }
+        mwait(bar_mma, mph, a.err, 18, ok);
+
+        // ---- 12. Z = beta_m (Z1 + e^G_m / nk_m Z2) -> bf16 [j][m] ; dA' = [-; Z] T^T (256) ---------------
+        {
+            float z1[32], z2[32];
+            ld32c(tm + C256 + lb + 32 * chh, z1);
+            ld32c(tm + C320 + lb + 32 * chh, z2);
+            if (lg >= 2) {
+                const int j = row - 64;
+#pragma unroll
+                for (int m = 0; m < 32; ++m) {
+                    const int mm = 32 * chh + m;
+                    z1[m] = vB[mm] * fmaf(vEG[mm] * vNK[mm], z2[m], z1[m]);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) st8(sm + OFF_PS2 + sw128_off(j, 32 * chh + 8 * q), z1 + 8 * q);
+            }
+        }
+        fence_async_smem();
+        sync_tc();
+        if (tid == 0) {
+            const uint32_t id = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)  // A rows 0-63 = the dPs1 tile (ignored), 64-127 = Z
+                umma_bf16(tm + C256, desc_kmajor(sb + OFF_PS + ks * 32), desc_kmajor(sb + OFF_T + ks * 32), id, ks > 0);
+            umma_commit(bar_mma);
+        }
+        mwait(bar_mma, mph, a.err, 19, ok);
+        {  // rows j on lanes 64-127: dA = -dA' (l < j); G E from the K K^T rows of D1
+            float dap[32], kk[32], xa[32];
+            ld32c(tm + C256 + lb + 32 * chh, dap);
+            ld32c(tD1 + lb + 32 * chh, kk);
+            if (lg >= 2) {
+                const int j = row - 64;
+                const float gj = vG[j], bj = vB[j], nkj = vNK[j];
+                float sb_ = 0.f, sx = 0.f;
+#pragma unroll
+                for (int t = 0; t < 32; ++t) {
+                    const int l = 32 * chh + t;
+                    const bool m = l < j;
+                    const float e = m ? __expf(gj - vG[l]) : 0.f;
+                    const float ge = kk[t] * nkj * vNK[l] * e;
+                    const float dA = m ? -dap[t] : 0.f;
+                    sb_ = fmaf(dA, ge, sb_);
+                    xa[t] = dA * bj * ge;
+                    sx += xa[t];
+                    dGm[j * 64 + l] = dA * bj * e;
+                }
+                atomicAdd(&vDB[j], sb_);
+                atomicAdd(&vDG[j], sx);
+            } else {
+#pragma unroll
+                for (int t = 0; t < 32; ++t) xa[t] = 0.f;
+            }
+            deposit_colsum(xa, red1, lg, chh);
+        }
+        __syncthreads();
+        if (tid < 64) vDG[tid] -= colsum(red1, tid);
+        {  // Gs = (dG + dG^T) / (nk nk)  bf16 [j][m]
+            const int j = tid >> 2, q = tid & 3;
+            float gs[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+                const int m = 16 * q + t;
+                gs[t] = (dGm[j * 64 + m] + dGm[m * 64 + j]) * vNK[j] * vNK[m];
+            }
+            st8(sm + OFF_GS + sw128_off(j, 16 * q), gs);
+            st8(sm + OFF_GS + sw128_off(j, 16 * q + 8), gs + 8);
+        }
+        fence_async_smem();
+        sync_tc();
+
+        // ---- 13. dK' += K^T Gs (448) ; dS^T (already x e^G_C) += dOg^T Q + dDelta^T (-W) (0) -----------
+        if (tid == 0) {
+            const uint32_t id_mk = idesc_bf16(128, 64, 1, 0), id_mm = idesc_bf16(128, 128, 1, 1);
+            const uint32_t id_km = idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                umma_bf16(tm + C448, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_GS + ks * 32), id_mk, 1);
+                umma_bf16(tS, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(aQ + ks * 2048, QK_BLK), id_mm, 1);
+                umma_bf16(tS, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_W + ks * 2048, 8192), id_km, 1);
+            }
+            umma_commit(bar_mma);
+        }
+        mwait(bar_mma, mph, a.err, 20, ok);
+
+        // ---- 14. dk = u - kn (kn.u), u = dK' + beta e^G / nk dKb ; dg, dbeta ---------------------------------
+        {
+            float u[32], xk[32];
+            ld32c(tm + C448 + lb + 32 * chh, u);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int jj = 32 * chh + j;
+                u[j] = fmaf(vB[jj] * vEG[jj] * vNK[jj], kbr[j], u[j]);
+                xk[j] = tile128(sm + OFF_QK + 8192, QK_BLK, jj, row) * vNK[jj] * u[j];
+            }
+            deposit_colsum(xk, red3, lg, chh);
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int jj = 32 * chh + j;
+                float gk = u[j];
+                if (a.l2norm) gk = u[j] - tile128(sm + OFF_QK + 8192, QK_BLK, jj, row) * vNK[jj] * colsum(red3, jj);
+                if (jj < nv) {
+                    const int64_t idx = ((tok0 + jj) * a.H + hq) * 128 + row;
+                    if (a.accumulate_qk) atomicAdd((float*)a.dk + idx, gk);
+                    else ((__nv_bfloat16*)a.dk)[idx] = __float2bfloat16_rn(gk);
+                }
+            }
+        }
+        if (tid < 32) {  // last row: + sum_j kn.dKst_j + e^G_C <dS, S0>
+            float s = vR4[tid] + vR4[tid + 32];
+            s = warp_sum(s);
+            float d = (tid < 8) ? scal[1 + tid] : 0.f;
+            d = warp_sum(d);
+            if (tid == 0) vDG[63] += s + scal[0] * d;
+        }
+        __syncthreads();
+        if (tid < 64) {  // dg = reverse cumsum of dGamma
+            float x = vDG[tid];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float y = __shfl_down_sync(0xffffffffu, x, o);
+                if (lane + o < 32) x += y;
+            }
+            red0[tid] = x;
+        }
+        __syncthreads();
+        if (tid < 64 && tid < nv) {
+            const float x = red0[tid] + (tid < 32 ? red0[32] : 0.f);
+            a.dg[(tok0 + tid) * a.HV + hv] = x;
+            a.dbeta[(tok0 + tid) * a.HV + hv] = vDB[tid];
+        }
+        sync_tc();
+        if (tid == 0 && c > 0) issue_inputs(c - 1);
+    }
+
+    if (ok && a.dh0) {
+        float* dh0 = a.dh0 + ((int64_t)n * a.HV + hv) * 16384;
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 16) {
+            float v[16];
+            tmem_ld16(tS + lb + 64 * chh + c0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) dh0[(64 * chh + c0 + i) * 128 + row] = v[i];
+        }
+    }
+    sync_tc();
+    if (warp == 0) tmem_dealloc(tm, T_COLS);
+}
+
+template <typename TO>
+__global__ void qk_convert_kernel(const float* __restrict__ src, TO* __restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+bool chunk_bwd_supported(int64_t DK, int64_t DV, int act_dtype) {
+    return DK == 128 && DV == 128 && act_dtype == GDN_BF16;
+}
+
+size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t HV, bool varlen) {
+    const int64_t chunks = varlen ? (B * T + 63 * N) / 64 + N : N * ((T + 63) / 64);
+    size_t bytes = (size_t)chunks * HV * 32768;  // S0 tiles
+    if (HV > H) bytes += (size_t)B * T * H * 128 * 4 * 2;  // fp32 dq/dk accumulators (grouped value heads)
+    return bytes;
+}
+
+int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s) {
+    using namespace cb;
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(chunk_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+            cudaSuccess)
+            return GDN_ERR_LAUNCH;
+        attr_set = true;
+    }
+    // 1. rebuild every chunk-start state from the checkpoints (segment-parallel forward, no outputs)
+    ChunkLaunch R{};
+    R.q = L.q; R.k = L.k; R.v = L.v; R.g = L.g; R.beta = L.beta; R.o = nullptr;
+    R.h0 = L.h0; R.ht = nullptr; R.ckpt = const_cast<float*>(L.ckpt); R.cu = L.cu; R.err = L.err;
+    R.B = L.B; R.T = L.T; R.N = L.N; R.H = L.H; R.HV = L.HV; R.scale = L.scale;
+    R.g_dtype = L.g_dtype; R.beta_dtype = L.beta_dtype; R.l2norm = L.l2norm; R.o_mode = 2;
+    R.ckpt_every = L.ckpt_every;
+    R.s0_out = L.ws;
+    R.max_seqlen = L.max_seqlen;
+    int st = chunk_fwd(R, s);
+    if (st != GDN_OK) return st;
+
+    // 2. reverse sweep
+    ChunkBwdArgs a;
+    memset(&a, 0, sizeof(a));
+    const int64_t Ttot = L.B * L.T;
+    if (!make_tmap_3d_sw128(&a.tq, L.q, 128, L.H, Ttot, 128, L.H * 128, 64)) return GDN_ERR_ALIGN;
+    if (!make_tmap_3d_sw128(&a.tk, L.k, 128, L.H, Ttot, 128, L.H * 128, 64)) return GDN_ERR_ALIGN;
+    if (!make_tmap_3d_sw128(&a.tv, L.v, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
+    if (!make_tmap_3d_sw128(&a.tdo, L.dout, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
+    const bool acc = L.HV > L.H;
+    const int64_t chunks = L.cu ? (L.B * L.T + 63 * L.N) / 64 + L.N : L.N * ((L.T + 63) / 64);
+    float* acc_q = acc ? (float*)((uint8_t*)L.ws + (size_t)chunks * L.HV * 32768) : nullptr;
+    float* acc_k = acc ? acc_q + Ttot * L.H * 128 : nullptr;
+    if (acc && cudaMemsetAsync(acc_q, 0, (size_t)Ttot * L.H * 128 * 4 * 2, s) != cudaSuccess) return GDN_ERR_LAUNCH;
+    a.g = L.g;
+    a.beta = L.beta;
+    a.s0_tiles = (const uint8_t*)L.ws;
+    a.dht = L.dht;
+    a.dq = acc ? (void*)acc_q : L.dq;
+    a.dk = acc ? (void*)acc_k : L.dk;
+    a.dv = L.dv;
+    a.dg = L.dg;
+    a.dbeta = L.dbeta;
+    a.dh0 = L.dh0;
+    a.cu = L.cu;
+    a.err = L.err;
+    a.T = L.T;
+    a.N = (int)L.N;
+    a.H = (int)L.H;
+    a.HV = (int)L.HV;
+    a.g_dtype = L.g_dtype;
+    a.beta_dtype = L.beta_dtype;
+    a.scale = L.scale;
+    a.l2norm = L.l2norm;
+    a.accumulate_qk = acc ? 1 : 0;
+    const unsigned grid = (unsigned)(L.N * L.HV);
+    if (grid > 0) {
+        chunk_bwd_kernel<<<grid, NTHR, SMEM_BYTES, s>>>(a);
+        count_launch();
+    }
+    if (acc) {
+        const int64_t nqk = Ttot * L.H * 128;
+        const int64_t want = (nqk + 255) / 256;
+        const unsigned blocks = (unsigned)(want < 148 * 16 ? want : 148 * 16);
+        qk_convert_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(acc_q, (__nv_bfloat16*)L.dq, nqk);
+        qk_convert_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(acc_k, (__nv_bfloat16*)L.dk, nqk);
+        count_launch(2);
+    }
+    return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+}  // namespace gdn

@@ -78,6 +78,7 @@ struct ChunkFwdArgs {
     int N, H, HV, g_dtype, beta_dtype;
     float scale;
     int l2norm, zero_v, o_mode, h0_identity, ht_accumulate, ckpt_every;
+    uint8_t* s0_out;  // recompute mode: checkpoints are read, S0^T tiles written here (see ChunkLaunch)
 };
 
 __device__ __forceinline__ float ld_any2(const void* p, int dtype, int64_t i) {
@@ -162,7 +163,28 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     int64_t bos, eos;
     seq_bounds(a.cu, a.T, n, bos, eos);
     const int64_t len = eos - bos;
-    const int nchunks = (int)((len + 63) / 64);
+    const int nchunks_seq = (int)((len + 63) / 64);
+    // recompute mode: this CTA covers chunks [c_begin, c_end) of its sequence, starting from a checkpoint
+    const bool recompute = a.s0_out != nullptr;
+    const int c_begin = recompute ? (int)blockIdx.y * a.ckpt_every : 0;
+    if (c_begin >= nchunks_seq && c_begin > 0) return;
+    const int nchunks = recompute ? min(nchunks_seq, c_begin + a.ckpt_every) : nchunks_seq;
+
+    // first chunk of this sequence in the flattened chunk list (S0 tile slots in recompute mode)
+    int64_t cbase = 0;
+    if (recompute) {
+        if (!a.cu) {
+            cbase = (int64_t)n * ((a.T + 63) / 64);
+        } else {
+            int64_t part = 0;
+            for (int m = tid; m < n; m += NTHR) part += (a.cu[m + 1] - a.cu[m] + 63) / 64;
+            for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+            if (lane == 0) ((int64_t*)Yb)[warp] = part;
+            __syncthreads();
+            for (int w = 0; w < NTHR / 32; ++w) cbase += ((int64_t*)Yb)[w];
+            __syncthreads();
+        }
+    }
 
     // checkpoint slot of this sequence's first checkpoint
     int64_t ck_base = 0;
@@ -210,13 +232,14 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     // initial state -> TMEM: thread (row = dv, half chh) holds S^T[dv][dk] for dk in [64 chh, 64 chh + 64)
     {
         const float* h0 = a.h0 ? a.h0 + ((int64_t)n * a.HV + hv) * 16384 : nullptr;
+        if (recompute) h0 = a.ckpt + ((ck_base + blockIdx.y) * a.HV + hv) * 16384;
 #pragma unroll
         for (int c0 = 0; c0 < 64; c0 += 16) {
             float v[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 const int dk = 64 * chh + c0 + i;
-                v[i] = a.h0_identity ? (dk == row ? 1.f : 0.f) : (h0 ? h0[dk * 128 + row] : 0.f);
+                v[i] = (a.h0_identity && !recompute) ? (dk == row ? 1.f : 0.f) : (h0 ? h0[dk * 128 + row] : 0.f);
             }
             tmem_st16(tS + lane_base + 64 * chh + c0, v);
         }
@@ -224,8 +247,9 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     }
 
     // K of chunk c goes to slot (c & 1): +16 KB (even) or +0 (odd) inside each d-block; Q to +8 KB
-    auto issue_k = [&](int c) {
-        const int tok0 = (int)(bos + 64 * c), s = c & 1;
+    // slots and mbarrier phases follow the CTA-local chunk count cl = c - c_begin
+    auto issue_k = [&](int c, int s) {
+        const int tok0 = (int)(bos + 64 * c);
         mbar_arrive_expect_tx(&bar_k[s], TX_QK / 2);
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
@@ -244,14 +268,15 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         tma_load_3d(sm + OFF_V + 8192, &a.tv, bar_v, 64, hv, tok0);
     };
     if (tid == 0 && nchunks > 0) {
-        issue_k(0);
-        issue_q(0);
-        if (!a.zero_v) issue_v(0);
+        issue_k(c_begin, 0);
+        issue_q(c_begin);
+        if (!a.zero_v) issue_v(c_begin);
     }
 
     const uint32_t sbase = smem_u32(sm);
-    for (int c = 0; c < nchunks; ++c) {
-        const int s = c & 1;
+    for (int c = c_begin; c < nchunks; ++c) {
+        const int cl = c - c_begin;
+        const int s = cl & 1;
         const int64_t tok0 = bos + 64 * (int64_t)c;
         const int nv = (len - 64 * (int64_t)c) < 64 ? (int)(len - 64 * (int64_t)c) : 64;
         const uint32_t kofs = s ? 0u : 16384u;              // K slot inside a d-block
@@ -274,9 +299,9 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
 
         // (b) this chunk's Q, K tiles; prefetch the next chunk's into the other stage
-        wait_bar(&bar_k[s], (uint32_t)(c >> 1) & 1u, a.err, 1, ok);
-        wait_bar(bar_q, (uint32_t)c & 1u, a.err, 7, ok);
-        if (tid == 0 && c + 1 < nchunks) issue_k(c + 1);  // the other K slot: MMA7 of chunk c-1 is done
+        wait_bar(&bar_k[s], (uint32_t)(cl >> 1) & 1u, a.err, 1, ok);
+        wait_bar(bar_q, (uint32_t)cl & 1u, a.err, 7, ok);
+        if (tid == 0 && c + 1 < nchunks) issue_k(c + 1, s ^ 1);  // the other K slot: MMA7 of chunk c-1 is done
 
         // (c) MMA1: D1 = [Q;K] K^T (even chunks) or [K;Q] K^T (odd) on the raw tiles (M=128, N=64, K=128)
         if (tid == 0) {
@@ -322,8 +347,9 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         // (e) S0 -> bf16 S0^T operand, TMEM state <- e^G_C S0, checkpoint
         {
             const float eGC = vMisc[0];
-            const bool ck = a.ckpt && (c % a.ckpt_every == 0);
+            const bool ck = a.ckpt && !recompute && (c % a.ckpt_every == 0);
             float* ckp = ck ? a.ckpt + ((ck_base + c / a.ckpt_every) * a.HV + hv) * 16384 : nullptr;
+            uint8_t* s0g = recompute ? a.s0_out + ((cbase + c) * a.HV + hv) * 32768 : nullptr;
 #pragma unroll
             for (int c0 = 0; c0 < 64; c0 += 16) {
                 float v[16];
@@ -332,6 +358,10 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 const uint32_t o0 = chh * 16384 + sw128_off(row, c0), o1 = chh * 16384 + sw128_off(row, c0 + 8);
                 st_chunk8_split(sm + OFF_S + o0, sm + OFF_SL + o0, v);
                 st_chunk8_split(sm + OFF_S + o1, sm + OFF_SL + o1, v + 8);
+                if (recompute) {  // the backward's S0^T operand tile: the same bytes, in the workspace
+                    *reinterpret_cast<uint4*>(s0g + o0) = *reinterpret_cast<const uint4*>(sm + OFF_S + o0);
+                    *reinterpret_cast<uint4*>(s0g + o1) = *reinterpret_cast<const uint4*>(sm + OFF_S + o1);
+                }
                 if (ck) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) ckp[(64 * chh + c0 + i) * 128 + row] = v[i];
@@ -441,7 +471,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (i) MMA2: W^T = K^T TB^T ; MMA3: U^T = V^T TV^T   (M=128, N=64, K=64 tokens)
         if (tid == 0) {
-            if (!a.zero_v) wait_bar(bar_v, (uint32_t)c & 1u, a.err, 6, ok);
+            if (!a.zero_v) wait_bar(bar_v, (uint32_t)cl & 1u, a.err, 6, ok);
             const uint32_t id = idesc_bf16(128, 64, 1, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
@@ -478,7 +508,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 const uint64_t bw = desc_kmajor(sbase + OFF_W + kb * 8192 + ko);
                 umma_bf16(tU, ah, bw, id, 1);
                 umma_bf16(tU, al, bw, id, 1);
-                umma_bf16(tO1, ah, desc_kmajor(aQ + kb * QK_BLK + ko), id, ks > 0);
+                if (a.o_mode != 2) umma_bf16(tO1, ah, desc_kmajor(aQ + kb * QK_BLK + ko), id, ks > 0);
             }
             umma_commit(bar_mma);
         }
@@ -509,9 +539,11 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             for (int ks = 0; ks < 4; ++ks) {
                 const uint64_t dh = desc_kmajor(sbase + OFF_D + ks * 32), dl = desc_kmajor(sbase + OFF_DL + ks * 32);
                 const uint64_t ph = desc_kmajor(sbase + OFF_P + ks * 32), pl = desc_kmajor(sbase + OFF_PL + ks * 32);
-                umma_bf16(tO2, dh, ph, id6, ks > 0);
-                umma_bf16(tO2, dl, ph, id6, 1);
-                umma_bf16(tO2, dh, pl, id6, 1);
+                if (a.o_mode != 2) {
+                    umma_bf16(tO2, dh, ph, id6, ks > 0);
+                    umma_bf16(tO2, dl, ph, id6, 1);
+                    umma_bf16(tO2, dh, pl, id6, 1);
+                }
                 const uint64_t kd = desc_mnmajor(aK + ks * 2048, QK_BLK);
                 umma_bf16(tS, desc_kmajor(sbase + OFF_DD + ks * 32), kd, id7, 1);
                 umma_bf16(tS, desc_kmajor(sbase + OFF_DDL + ks * 32), kd, id7, 1);
@@ -599,8 +631,17 @@ int chunk_fwd(const ChunkLaunch& L, cudaStream_t s) {
     a.h0_identity = L.h0_identity;
     a.ht_accumulate = L.ht_accumulate;
     a.ckpt_every = L.ckpt_every;
-    const unsigned grid = (unsigned)(L.N * L.HV);
-    if (grid == 0) return GDN_OK;
+    a.s0_out = (uint8_t*)L.s0_out;
+    dim3 grid((unsigned)(L.N * L.HV), 1);
+    if (L.s0_out) {
+        if (!L.ckpt) return GDN_ERR_ARGUMENT;
+        const int64_t maxlen = L.max_seqlen > 0 ? L.max_seqlen : (L.cu ? L.B * L.T : L.T);
+        const int64_t segs = (((maxlen + 63) / 64) + L.ckpt_every - 1) / L.ckpt_every;
+        grid.y = (unsigned)(segs > 0 ? segs : 1);
+        a.ht = nullptr;
+        a.o_mode = 2;
+    }
+    if (grid.x == 0) return GDN_OK;
     chunk_fwd_kernel<<<grid, NTHR, SMEM_BYTES, s>>>(a);
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;

@@ -33,10 +33,32 @@ struct ChunkLaunch {
     int64_t B, T, N, H, HV;
     float scale;
     int g_dtype, beta_dtype, l2norm, zero_v, o_mode, h0_identity, ht_accumulate, ckpt_every;
+    // recompute mode (used by the backward): when s0_out is set, ckpt is READ (the forward's checkpoints),
+    // one CTA per (sequence, head, segment of ckpt_every chunks) restarts from its checkpoint and writes every
+    // chunk's bf16 S0^T operand tile (32 KB) to s0_out; no outputs, no final state.
+    void* s0_out;
+    int64_t max_seqlen;
+};
+
+// Arguments of the chunked backward.
+struct ChunkBwdLaunch {
+    const void *q, *k, *v, *g, *beta, *dout;
+    const float *h0, *ckpt, *dht;
+    void *dq, *dk, *dv;
+    float *dg, *dbeta, *dh0;
+    void* ws;  // chunk_bwd_workspace bytes
+    const int64_t* cu;
+    int* err;
+    int64_t B, T, N, H, HV, max_seqlen;
+    float scale;
+    int g_dtype, beta_dtype, l2norm, ckpt_every;
 };
 
 bool chunk_fwd_supported(int64_t DK, int64_t DV, int act_dtype);
 int chunk_fwd(const ChunkLaunch& L, cudaStream_t s);
+bool chunk_bwd_supported(int64_t DK, int64_t DV, int act_dtype);
+size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t HV, bool varlen);
+int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s);
 
 int rec_fwd(const RecLaunch& L, cudaStream_t s);
 size_t rec_bwd_workspace(int64_t N, int64_t HV, int64_t DK, int64_t DV, int64_t max_len, int64_t total_tokens,

@@ -153,3 +153,48 @@ def test_sequence_split_passes_bf16():
     assert_rms_close(to_np(s_out), to_np(ht_full), 2e-2, "combined state")
     seqsplit.apply_incoming_state(segs[1]["q"], segs[1]["k"], segs[1]["g"], segs[1]["beta"], c1, o2, D ** -0.5)
     assert_bf16_close(to_np(torch.cat([o1, o2], 1)), to_np(o_full), 2e-2, "o")
+
+
+def _grads_vs_oracle(x, h0, dht, l2, cu=None, tol=3e-2):
+    """fwd+bwd through the public op; compare every gradient with the oracle on the same inputs."""
+    from sorernn_b200 import chunk_gated_delta_rule
+
+    t = {n: x[n].clone().requires_grad_(n != "do") for n in x}
+    h0t = None if h0 is None else h0.clone().requires_grad_(True)
+    cu_t = None if cu is None else torch.tensor(cu, device="cuda")
+    o, ht = chunk_gated_delta_rule(t["q"], t["k"], t["v"], t["g"], t["beta"], initial_state=h0t,
+                                   output_final_state=True, use_qk_l2norm_in_kernel=l2, cu_seqlens=cu_t,
+                                   cu_seqlens_cpu=None if cu is None else torch.tensor(cu))
+    loss = (o.float() * t["do"].float()).sum() + (0 if dht is None else (ht * dht).sum())
+    loss.backward()
+    xn = _np(x)
+    ref = cgdn.backward(xn["q"], xn["k"], xn["v"], xn["g"], xn["beta"], xn["do"], D ** -0.5,
+                        initial_state=None if h0 is None else to_np(h0), dht=None if dht is None else to_np(dht),
+                        cu_seqlens=cu, use_qk_l2norm=l2)
+    got = [t["q"].grad, t["k"].grad, t["v"].grad, t["g"].grad, t["beta"].grad]
+    for name, a, r in zip(("dq", "dk", "dv"), got[:3], ref[:3]):
+        assert_bf16_close(to_np(a), r, tol, name)
+    assert_rms_close(to_np(got[3]), ref[3], tol, "dg")
+    assert_rms_close(to_np(got[4]), ref[4], tol, "dbeta")  # beta is bf16: its grad is rounded on return
+    if h0 is not None:
+        assert_rms_close(to_np(h0t.grad), ref[5], tol, "dh0")
+
+
+@pytest.mark.parametrize("B,T,H,HV,l2", [(1, 64, 1, 1, False), (2, 300, 2, 2, True), (1, 200, 1, 2, True),
+                                         (1, 130, 2, 2, False)])
+def test_chunk_backward_matches_oracle(B, T, H, HV, l2):
+    x = _inputs(B * 7 + T, B, T, H, HV, normalized=not l2)
+    h0 = torch.randn(B, HV, D, D, device="cuda") * 0.05
+    dht = torch.randn(B, HV, D, D, device="cuda") * 0.1
+    _grads_vs_oracle(x, h0, dht, l2)
+
+
+def test_chunk_backward_varlen_short_documents():
+    cu = [0, 1, 3, 4, 70, 200, 512]
+    x = _inputs(21, 1, 512, 2, 2, normalized=False)
+    _grads_vs_oracle(x, None, None, True, cu=cu)
+
+
+def test_chunk_backward_large_row_config1_shape():
+    x = _inputs(22, 1, 4096, 16, 16, normalized=False)
+    _grads_vs_oracle(x, None, None, True)
