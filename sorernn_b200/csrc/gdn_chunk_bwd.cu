@@ -421,8 +421,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
             umma_commit(bar_mma);
         }
-        {
-            const float eGC = scal[0];
+        {  // dS^T -> bf16 hi tile (the lo part follows in step 8b), <dS, S0>
             float dss = 0.f;
 #pragma unroll
             for (int c0 = 0; c0 < 64; c0 += 16) {
@@ -437,11 +436,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                     dss = fmaf(v[e], bfv(sm + OFF_S0, o0 + 2 * e), dss);
                     dss = fmaf(v[8 + e], bfv(sm + OFF_S0, o1 + 2 * e), dss);
                 }
-#pragma unroll
-                for (int e = 0; e < 16; ++e) v[e] *= eGC;
-                tmem_st16(tS + lb + 64 * chh + c0, v);
             }
-            tmem_wait_st();
             dss = warp_sum(dss);
             if (lane == 0) scal[1 + warp] = dss;
         }
@@ -614,6 +609,44 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             umma_commit(bar_mma);
         }
         mwait(bar_mma, mph, a.err, 16, ok);
+
+        // ---- 8b. the dS tile's readers (B1b, hi part of dS Dd^T) are done: overwrite it with the lo part
+        //          of dS and finish dS Dd^T; dS (TMEM) <- e^G_C dS + dOg^T Q + dDelta^T (-W). These MMAs
+        //          complete before the step-10 commit, ahead of any write to the tiles they read.
+        {
+            const float eGC = scal[0];
+#pragma unroll
+            for (int c0 = 0; c0 < 64; c0 += 16) {
+                float v[16], lo[16];
+                tmem_ld16(tS + lb + 64 * chh + c0, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    lo[e] = v[e] - __bfloat162float(__float2bfloat16_rn(v[e]));
+                    v[e] *= eGC;
+                }
+                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0), lo);
+                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0 + 8), lo + 8);
+                tmem_st16(tS + lb + 64 * chh + c0, v);
+            }
+            tmem_wait_st();
+        }
+        fence_async_smem();
+        sync_tc();
+        if (tid == 0) {
+            const uint32_t id_mm = idesc_bf16(128, 64, 1, 1), id_mm128 = idesc_bf16(128, 128, 1, 1);
+            const uint32_t id_km128 = idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)  // K = dv
+                umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
+                          desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192), id_mm, 1);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {  // K = tokens
+                umma_bf16(tS, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(aQ + ks * 2048, QK_BLK), id_mm128, 1);
+                umma_bf16(tS, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_W + ks * 2048, 8192), id_km128,
+                          1);
+            }
+        }
 
         // ---- 9. dv, dVb tile, dVb.v; dW^T tile; qn.(S0 dO) and qn.QB -------------------------------------
         {
@@ -805,16 +838,12 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         fence_async_smem();
         sync_tc();
 
-        // ---- 13. dK' += K^T Gs (448) ; dS^T (already x e^G_C) += dOg^T Q + dDelta^T (-W) (0) -----------
+        // ---- 13. dK' += K^T Gs (448) ----------------------------------------------------------------
         if (tid == 0) {
-            const uint32_t id_mk = idesc_bf16(128, 64, 1, 0), id_mm = idesc_bf16(128, 128, 1, 1);
-            const uint32_t id_km = idesc_bf16(128, 128, 0, 1);
+            const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
+            for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tm + C448, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_GS + ks * 32), id_mk, 1);
-                umma_bf16(tS, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(aQ + ks * 2048, QK_BLK), id_mm, 1);
-                umma_bf16(tS, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_W + ks * 2048, 8192), id_km, 1);
-            }
             umma_commit(bar_mma);
         }
         mwait(bar_mma, mph, a.err, 20, ok);
