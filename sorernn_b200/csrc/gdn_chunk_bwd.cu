@@ -62,6 +62,7 @@ constexpr uint32_t OFF_DWT = OFF_S0 + 16384;  // dW^T bf16 [dk][i]
 constexpr uint32_t OFF_DKB = OFF_DS;          // dKb^T bf16 [dk][j]   (dS tile dead after step 8)
 constexpr uint32_t OFF_GS = OFF_DS + 16384;   // (dG + dG^T) / (nk nk) bf16 [j][m]
 constexpr uint32_t OFF_Y = OFF_DD;
+constexpr uint32_t OFF_DDL = OFF_A;  // dDelta^T lo bf16 [dv][j] (16 KB; the fp32 solve area is dead after step 3)
 // TMEM columns (fp32, 128 lanes)
 constexpr uint32_t T_S = 0, T_D1 = 128, C192 = 192, C256 = 256, C320 = 320, C384 = 384, C448 = 448, T_COLS = 512;
 }  // namespace cb
@@ -509,7 +510,13 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 d1[j] = fmaf(d2[j], x, d1[j]);
             }
 #pragma unroll
-            for (int q = 0; q < 4; ++q) st8(sm + OFF_DD + sw128_off(row, 32 * chh + 8 * q), d1 + 8 * q);
+            for (int q = 0; q < 4; ++q) {
+                float lo[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) lo[e] = d1[8 * q + e] - __bfloat162float(__float2bfloat16_rn(d1[8 * q + e]));
+                st8(sm + OFF_DD + sw128_off(row, 32 * chh + 8 * q), d1 + 8 * q);
+                st8(sm + OFF_DDL + sw128_off(row, 32 * chh + 8 * q), lo);
+            }
             deposit_colsum(de, red0, lg, chh);
         }
         {
@@ -594,6 +601,8 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             for (int ks = 0; ks < 4; ++ks) {  // K = tokens
                 umma_bf16(tm + C256, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
                           id_km, ks > 0);
+                umma_bf16(tm + C256, desc_kmajor(sb + OFF_DDL + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
+                          id_km, 1);
                 umma_bf16(tm + C384, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_PS + ks * 32), id_mk,
                           ks > 0);
                 umma_bf16(tm + C448, desc_mnmajor(aQ + ks * 2048, QK_BLK), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
@@ -644,6 +653,8 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             for (int ks = 0; ks < 4; ++ks) {  // K = tokens
                 umma_bf16(tS, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(aQ + ks * 2048, QK_BLK), id_mm128, 1);
                 umma_bf16(tS, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_W + ks * 2048, 8192), id_km128,
+                          1);
+                umma_bf16(tS, desc_kmajor(sb + OFF_DDL + ks * 32), desc_mnmajor(sb + OFF_W + ks * 2048, 8192), id_km128,
                           1);
             }
         }
