@@ -184,8 +184,9 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     float* red3 = red0 + 768;
     uint64_t* bar_in = (uint64_t*)(sm + OFF_BAR);
     uint64_t* bar_mma = bar_in + 1;
-    uint32_t* tmem_slot = (uint32_t*)(bar_in + 2);
-    float* scal = (float*)(bar_in + 3);  // [0] e^G_C, [1..8] <dS, S0> per warp
+    uint64_t* bar_v = bar_in + 2;  // V tile reloaded for Z1 (its region holds the Dd lo tile in steps 5-8)
+    uint32_t* tmem_slot = (uint32_t*)(bar_in + 3);
+    float* scal = (float*)(bar_in + 4);  // [0] e^G_C, [1..8] <dS, S0> per warp
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int lg = warp & 3, chh = warp >> 2;
@@ -213,6 +214,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     if (tid == 0) {
         mbar_init(bar_in, 1);
         mbar_init(bar_mma, 1);
+        mbar_init(bar_v, 1);
         fence_barrier_init();
         prefetch_tmap(&a.tq);
         prefetch_tmap(&a.tk);
@@ -254,7 +256,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         bulk_load(sm + OFF_S0, a.s0_tiles + ((cbase + c) * a.HV + hv) * 32768, 32768, bar_in);
     };
     if (tid == 0 && nchunks > 0) issue_inputs(nchunks - 1);
-    uint32_t in_phase = 0;
+    uint32_t in_phase = 0, v_phase = 0;
     const uint32_t aQ = sb + OFF_QK, aK = sb + OFF_QK + 8192, aV = sb + OFF_V, aDO = sb + OFF_DO;
 
     for (int c = nchunks - 1; c >= 0; --c) {
@@ -334,7 +336,13 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                     v[j] = (jj <= i) ? f * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q) st8(sm + OFF_PS + sw128_off(i, 32 * chh + 8 * q), v + 8 * q);
+                for (int q = 0; q < 4; ++q) {  // hi tile, and its lo part where dPs2 goes later (idle until step 7)
+                    float lo[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) lo[e] = v[8 * q + e] - __bfloat162float(__float2bfloat16_rn(v[8 * q + e]));
+                    st8(sm + OFF_PS + sw128_off(i, 32 * chh + 8 * q), v + 8 * q);
+                    st8(sm + OFF_PS2 + sw128_off(i, 32 * chh + 8 * q), lo);
+                }
             } else {  // A_ij = beta_i kn_i.kn_j E_ij (j < i)
                 const float bi = vB[i] * vNK[i];
 #pragma unroll
@@ -469,8 +477,20 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         {
             float v[32];
             ld32c(tm + C256 + lb + 32 * chh, v);
+            // Delta^T hi tile; and the lo part of Dd = Delta diag(vX) relative to the hi part that step 7
+            // derives in place (bf16(bf16(Delta) vX)), stored where V was (V is reloaded for step 10)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) st8(sm + OFF_DEL + sw128_off(row, 32 * chh + 8 * q), v + 8 * q);
+            for (int q = 0; q < 4; ++q) {
+                float lo[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float x = vX[32 * chh + 8 * q + e];
+                    const float dh = __bfloat162float(__float2bfloat16_rn(v[8 * q + e]));
+                    lo[e] = v[8 * q + e] * x - __bfloat162float(__float2bfloat16_rn(dh * x));
+                }
+                st8(sm + OFF_DEL + sw128_off(row, 32 * chh + 8 * q), v + 8 * q);
+                st8(sm + OFF_V + sw128_off(row, 32 * chh + 8 * q), lo);
+            }
         }
         fence_async_smem();
         sync_tc();
@@ -481,8 +501,12 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)  // K = i
+            {
                 umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS + ks * 2048, 8192),
                           id_mm, ks > 0);
+                umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
+                          id_mm, 1);
+            }
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
@@ -496,6 +520,34 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             umma_commit(bar_mma);
         }
         mwait(bar_mma, mph, a.err, 15, ok);
+
+        // ---- 6b. lo part of dS^T K^T: overwrite the dS tile with dS - bf16(dS) and accumulate into (384);
+        //          step 7 restores the hi tile for the dS Dd^T products of step 8.
+        {
+#pragma unroll
+            for (int c0 = 0; c0 < 64; c0 += 16) {
+                float v[16];
+                tmem_ld16(tS + lb + 64 * chh + c0, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] -= __bfloat162float(__float2bfloat16_rn(v[e]));
+                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0), v);
+                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0 + 8), v + 8);
+            }
+        }
+        fence_async_smem();
+        sync_tc();
+        if (tid == 0) {
+            const uint32_t id_kk = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                umma_bf16(tm + C384, desc_kmajor(sb + OFF_DS + kb * 16384 + ko), desc_kmajor(aK + kb * QK_BLK + ko),
+                          id_kk, 1);
+            }
+            umma_commit(bar_mma);
+        }
+        mwait(bar_mma, mph, a.err, 22, ok);
 
         // ---- 7. dDelta^T = (320) + (384) diag(vX) -> tile; r4; dP -> dPs tiles, X_P sums -------------------
         {
@@ -589,6 +641,16 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 *reinterpret_cast<uint4*>(sm + OFF_DEL + off) = u;
             }
         }
+        {  // restore the dS hi tile (the lo part is in it since step 6b)
+#pragma unroll
+            for (int c0 = 0; c0 < 64; c0 += 16) {
+                float v[16];
+                tmem_ld16(tS + lb + 64 * chh + c0, v);
+                tmem_wait_ld();
+                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0), v);
+                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0 + 8), v + 8);
+            }
+        }
         fence_async_smem();
         sync_tc();
 
@@ -614,10 +676,18 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                           desc_mnmajor(sb + OFF_DD + ks * 2048, 8192), id_mm, ks > 0);
                 umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
                           desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192), id_mm, 1);
+                umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
+                          desc_mnmajor(sb + OFF_V + ks * 2048, 8192), id_mm, 1);  // dS hi . Dd lo
             }
             umma_commit(bar_mma);
         }
         mwait(bar_mma, mph, a.err, 16, ok);
+        if (tid == 0) {  // the Dd lo tile is consumed: bring V back for Z1 (step 10)
+            const int tok0i = (int)tok0;
+            mbar_arrive_expect_tx(bar_v, 2 * 8192);
+            tma_load_3d(sm + OFF_V, &a.tv, bar_v, 0, hv, tok0i);
+            tma_load_3d(sm + OFF_V + 8192, &a.tv, bar_v, 64, hv, tok0i);
+        }
 
         // ---- 8b. the dS tile's readers (B1b, hi part of dS Dd^T) are done: overwrite it with the lo part
         //          of dS and finish dS Dd^T; dS (TMEM) <- e^G_C dS + dOg^T Q + dDelta^T (-W). These MMAs
@@ -660,6 +730,8 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
 
         // ---- 9. dv, dVb tile, dVb.v; dW^T tile; qn.(S0 dO) and qn.QB -------------------------------------
+        bwait(bar_v, v_phase, a.err, 21, ok);  // V is back (reloaded after step 8)
+        v_phase ^= 1u;
         {
             float v[32], r2[32];
             ld32c(tm + C256 + lb + 32 * chh, v);  // dVb^T[dv][j]

@@ -184,8 +184,9 @@ def _grads_vs_oracle(x, h0, dht, l2, cu=None, tol=3e-2):
                                          (1, 130, 2, 2, False)])
 def test_chunk_backward_matches_oracle(B, T, H, HV, l2):
     x = _inputs(B * 7 + T, B, T, H, HV, normalized=not l2)
-    h0 = torch.randn(B, HV, D, D, device="cuda") * 0.05
-    dht = torch.randn(B, HV, D, D, device="cuda") * 0.1
+    gen = torch.Generator(device="cuda").manual_seed(B * 7 + T + 1)
+    h0 = torch.randn(B, HV, D, D, device="cuda", generator=gen) * 0.05
+    dht = torch.randn(B, HV, D, D, device="cuda", generator=gen) * 0.1
     _grads_vs_oracle(x, h0, dht, l2)
 
 
