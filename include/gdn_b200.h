@@ -50,7 +50,8 @@ enum gdn_status {
     GDN_ERR_LAUNCH = 4,      /* a CUDA launch or tensor-map encode failed */
     GDN_ERR_TIMEOUT = 5,     /* a device-side bounded wait ran out (see gdn_workspace_error) */
     GDN_ERR_WORKSPACE = 6,   /* workspace pointer NULL or smaller than the query said */
-    GDN_ERR_ARGUMENT = 7     /* NULL pointer for a required tensor, bad flag */
+    GDN_ERR_ARGUMENT = 7,    /* NULL pointer for a required tensor, bad flag */
+    GDN_ERR_SCRATCH_LIMIT = 8 /* problem needs more scratch than gdn_chunk_bwd_noalloc's fixed array */
 };
 
 enum gdn_dtype { GDN_BF16 = 0, GDN_FP16 = 1, GDN_FP32 = 2 };
@@ -105,6 +106,23 @@ int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void
                   const void* beta, const float* initial_state, const float* checkpoints, const void* dout,
                   const float* dht, void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0,
                   void* workspace, size_t workspace_bytes, gdn_stream_t stream);
+
+/*
+ * gdn_chunk_bwd for callers that cannot allocate device memory. No counterpart in the reference.
+ * Some callers have no device allocator at call time: a host runtime reaching this library over a plain
+ * C FFI without an allocator of its own, or a plugin whose execute hook must not allocate. This variant
+ * takes gdn_chunk_bwd's arguments minus the workspace and allocates nothing (no cudaMalloc/cudaFree);
+ * its scratch is one fixed array of 36 MiB inside the library's device image, held on every GPU that
+ * loads the library until the process exits. Problems whose gdn_chunk_bwd_workspace_size() exceeds
+ * 36 MiB are rejected with GDN_ERR_SCRATCH_LIMIT (one 4,096-token sequence with 16 heads fits). All calls
+ * on a device share the array: calls whose GPU work overlaps (other streams, other host threads) race,
+ * so order them on one stream. The first call on each device looks the array's address up; make that
+ * first call before any stream capture begins.
+ */
+int gdn_chunk_bwd_noalloc(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                          const void* beta, const float* initial_state, const float* checkpoints,
+                          const void* dout, const float* dht, void* dq, void* dk, void* dv, float* dg,
+                          float* dbeta, float* dh0, gdn_stream_t stream);
 
 /*
  * One decode token for N sequences on a resident fp32 state [N, HV, DK, DV], updated in place:

@@ -41,6 +41,7 @@ SIGNATURES = {
     "gdn_segment_workspace_size": (_sz, [_P]),
     "gdn_workspace_error": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_i32)]),
     "gdn_kernel_launches": (ctypes.c_uint64, []),
+    "gdn_chunk_bwd_noalloc": (ctypes.c_int, [_P] + [_vp] * 16),
 }
 
 _lib = None

@@ -73,6 +73,7 @@ const char* gdn_status_string(int status) {
         case GDN_ERR_TIMEOUT: return "device-side wait timed out";
         case GDN_ERR_WORKSPACE: return "workspace missing or too small";
         case GDN_ERR_ARGUMENT: return "invalid argument";
+        case GDN_ERR_SCRATCH_LIMIT: return "problem exceeds the no-allocation scratch limit (36 MiB)";
         default: return "unknown status";
     }
 }
