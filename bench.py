@@ -160,6 +160,8 @@ def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
     B, T, H, D = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["D"]
+    if args.profile_batch:
+        B = args.profile_batch  # profiling mode: a small case, fwd+bwd steps only (no JSON line)
     x = make_inputs(B, T, H, D, dev, seed=1234 + rank)
     leaf = {n: x[n].clone().requires_grad_(n != "do") for n in ("q", "k", "v", "g", "beta")}
 
@@ -183,6 +185,13 @@ def run_ours(args):
         zero()
         step(leaf, x["do"])
     barrier(world)
+    if args.profile_batch:
+        for _ in range(args.steps):
+            zero()
+            step(leaf, x["do"])
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_batch": B, "steps": args.steps, "ok": True}))
+        return
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = _lib.lib().gdn_kernel_launches()
@@ -357,6 +366,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--profile-batch", type=int, default=0,
+                    help="profiling mode: run only fwd+bwd steps of config 1 with this batch (for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
