@@ -26,6 +26,7 @@
 // bf16 tolerance with the raw q/k tiles exact.
 #include <cstring>
 
+#include "chunk_common.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
@@ -259,16 +260,26 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     uint32_t in_phase = 0, v_phase = 0;
     const uint32_t aQ = sb + OFF_QK, aK = sb + OFF_QK + 8192, aV = sb + OFF_V, aDO = sb + OFF_DO;
 
+    float g_next = 0.f, b_next = 0.f;  // gates of the chunk processed next (threads 0-63)
+    if (tid < 64 && nchunks > 0) {
+        const int64_t t0 = bos + 64 * (int64_t)(nchunks - 1);
+        const bool in = tid < len - 64 * (int64_t)(nchunks - 1);
+        g_next = in ? ld_gb(a.g, a.g_dtype, (t0 + tid) * a.HV + hv) : 0.f;
+        b_next = in ? ld_gb(a.beta, a.beta_dtype, (t0 + tid) * a.HV + hv) : 0.f;
+    }
     for (int c = nchunks - 1; c >= 0; --c) {
         const int64_t tok0 = bos + 64 * (int64_t)c;
         const int nv = (len - 64 * (int64_t)c) < 64 ? (int)(len - 64 * (int64_t)c) : 64;
 
         // ---- 1. gates; wait for this chunk's tiles ------------------------------------------------------
         if (tid < 64) {
-            const bool in = tid < nv;
-            const int64_t gi = (tok0 + tid) * a.HV + hv;
-            float x = in ? ld_gb(a.g, a.g_dtype, gi) : 0.f;
-            vB[tid] = in ? ld_gb(a.beta, a.beta_dtype, gi) : 0.f;
+            float x = g_next;
+            vB[tid] = b_next;
+            if (c > 0) {  // gates of chunk c-1 (always 64 tokens): their latency hides behind this chunk
+                const int64_t gi = (tok0 - 64 + tid) * a.HV + hv;
+                g_next = ld_gb(a.g, a.g_dtype, gi);
+                b_next = ld_gb(a.beta, a.beta_dtype, gi);
+            }
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const float y = __shfl_up_sync(0xffffffffu, x, o);
@@ -356,48 +367,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
         }
         __syncthreads();
-        {
-            float x[16];
-            const int b = tid >> 4, cidx = tid & 15;
-            if (tid < 64) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    float sacc = 0.f;
-#pragma unroll
-                    for (int j = 0; j < i; ++j) sacc = fmaf(Tm[(16 * b + i) * AST + 16 * b + j], x[j], sacc);
-                    x[i] = (i == cidx) ? 1.f : (i < cidx ? 0.f : -sacc);
-                }
-            }
-            __syncthreads();
-            if (tid < 64) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) Tm[(16 * b + i) * AST + 16 * b + cidx] = x[i];
-            }
-            __syncthreads();
-        }
-#pragma unroll 1
-        for (int r = 1; r < 4; ++r) {
-            for (int e = tid; e < r * 256; e += NTHR) {
-                const int s2 = e >> 8, i = (e >> 4) & 15, cc = e & 15;
-                float y = 0.f;
-                for (int m = s2; m < r; ++m) {
-#pragma unroll
-                    for (int jj = 0; jj < 16; ++jj)
-                        y = fmaf(Tm[(16 * r + i) * AST + 16 * m + jj], Tm[(16 * m + jj) * AST + 16 * s2 + cc], y);
-                }
-                Yb[e] = y;
-            }
-            __syncthreads();
-            for (int e = tid; e < r * 256; e += NTHR) {
-                const int s2 = e >> 8, i = (e >> 4) & 15, cc = e & 15;
-                float t = 0.f;
-#pragma unroll
-                for (int jj = 0; jj < 16; ++jj)
-                    t = fmaf(Tm[(16 * r + i) * AST + 16 * r + jj], Yb[s2 * 256 + jj * 16 + cc], t);
-                Tm[(16 * r + i) * AST + 16 * s2 + cc] = -t;
-            }
-            __syncthreads();
-        }
+        tri_inverse64<AST>(Tm, Yb);  // T = (I + A)^-1 in place
         {
             const int i = tid >> 2, q = tid & 3;
             float tb[16], tv[16], tt[16];
@@ -418,13 +388,14 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         fence_async_smem();
         sync_tc();
 
-        // ---- 4. R2 W^T = K^T TB^T (192), R3 U^T = V^T TV^T (256); meanwhile dS^T -> tile, dS <- e^G_C dS ---
+        // ---- 4. R2 [W; -] = [TB; TV] K (384-511, W rows on lanes 0-63), R3 U^T = V^T TV^T (256);
+        //         meanwhile dS^T -> hi tile
         if (tid == 0) {
             const uint32_t id = idesc_bf16(128, 64, 1, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-                umma_bf16(tm + C192, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_TB + ks * 32), id,
-                          ks > 0);
+                umma_bf16(tm + C384, desc_kmajor(sb + OFF_TB + ks * 32), desc_mnmajor(aK + ks * 2048, QK_BLK),
+                          idesc_bf16(128, 128, 0, 1), ks > 0);
                 umma_bf16(tm + C256, desc_mnmajor(aV + ks * 2048, 8192), desc_kmajor(sb + OFF_TV + ks * 32), id,
                           ks > 0);
             }
@@ -450,14 +421,17 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             if (lane == 0) scal[1 + warp] = dss;
         }
         mwait(bar_mma, mph, a.err, 13, ok);
-        {  // W^T (lane = d) -> -W bf16 [j][d]
+        if (lg < 2) {  // W rows j (lanes 0-63) -> -W bf16 [j][d], d-block chh, 16-byte stores
             float v[32];
-            ld32c(tm + C192 + lb + 32 * chh, v);
-            const int d = row;
-            uint8_t* dst = sm + OFF_W + (d >> 6) * 8192;
+            uint8_t* dst = sm + OFF_W + chh * 8192;
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-                *reinterpret_cast<__nv_bfloat16*>(dst + sw128_off(32 * chh + j, d & 63)) = __float2bfloat16_rn(-v[j]);
+            for (int h = 0; h < 2; ++h) {
+                ld32c(tm + C384 + lb + 64 * chh + 32 * h, v);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] = -v[e];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) st8(dst + sw128_off(row, 32 * h + 8 * q), v + 8 * q);
+            }
         }
         fence_async_smem();
         sync_tc();

@@ -14,13 +14,17 @@
 // effect is below the output's own rounding) and the output itself.
 // Every GEMM is an M = 128 UMMA with a 128-wide dimension on the TMEM lanes:
 //   MMA1  D1[128x64] = [Q;K] K^T                 (rows 0-63: Q K^T, rows 64-127: K K^T)
-//   MMA2  W^T  = K^T TB^T,  TB = T diag(beta e^G / nk)     MMA3  U^T = V^T TV^T,  TV = T diag(beta)
-//   MMA4  U^T += S0^T (-W)^T  -> Delta^T                   MMA5  O1^T = S0^T Q^T
-//   MMA6  O2^T = Delta^T P'^T  (hi.hi + lo.hi + hi.lo)     MMA7  S^T += Dd^T K,  Dd = diag(e^(G_C-G)/nk) Delta
+//   MMA2  [W; -] = [TB; TV] K  (W rows on lanes 0-63)       MMA3  U^T = V^T TV^T,  TV = T diag(beta)
+//         TB = T diag(beta e^G / nk)
+//   MMA4  U^T += S0^T (-W)^T  -> Delta^T                   MMA5  [-; O1] = [-; Q] S0  (O rows on lanes 64-127)
+//   MMA6  [-; O2] = [-; P'] Delta  (hi.hi + lo.hi + hi.lo) MMA7  S^T += Dd^T K,  Dd = diag(e^(G_C-G)/nk) Delta
+// A 128-row A operand whose half is ignored always takes that half from an allocated tile below or above
+// the real one (never past the end of shared memory).
 // S^T (fp32, 128 TMEM columns) reaches HBM only as checkpoints for the backward (every ckpt_every
 // chunks) and as the final state.
 #include <cstring>
 
+#include "chunk_common.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
@@ -60,7 +64,8 @@ constexpr uint32_t OFF_A = OFF_D;
 constexpr uint32_t OFF_Y = OFF_A + 64 * AST * 4;
 static_assert(OFF_Y + 3 * 256 * 4 <= OFF_DD, "solve scratch overlaps live tiles");
 // TMEM columns
-constexpr uint32_t T_D1 = 0, T_W = 64, T_U = 128, T_O1 = 192, T_O2 = 256, T_S = 320, T_COLS = 512;
+// O2 (128 columns) reuses D1 + U once both are read; O1 reuses W once it is read.
+constexpr uint32_t T_D1 = 0, T_U = 64, T_O2 = 0, T_S = 256, T_W = 384, T_O1 = 384, T_COLS = 512;
 constexpr uint32_t TX_QK = 4 * 8192, TX_V = 2 * 8192;
 }  // namespace cf
 
@@ -274,6 +279,13 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     }
 
     const uint32_t sbase = smem_u32(sm);
+    float g_next = 0.f, b_next = 0.f;  // gates of the next chunk (threads 0-63), loaded one chunk ahead
+    if (tid < 64 && c_begin < nchunks) {
+        const bool in = tid < len - 64 * (int64_t)c_begin;
+        const int64_t gi = (bos + 64 * (int64_t)c_begin + tid) * a.HV + hv;
+        g_next = in ? ld_any2(a.g, a.g_dtype, gi) : 0.f;
+        b_next = in ? ld_any2(a.beta, a.beta_dtype, gi) : 0.f;
+    }
     for (int c = c_begin; c < nchunks; ++c) {
         const int cl = c - c_begin;
         const int s = cl & 1;
@@ -286,10 +298,15 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (a) gates: Gamma = cumsum(g) inside the chunk, beta; padded rows carry g = 0, beta = 0
         if (tid < 64) {
-            const bool in = tid < nv;
-            const int64_t gi = (tok0 + tid) * a.HV + hv;
-            float x = in ? ld_any2(a.g, a.g_dtype, gi) : 0.f;
-            vB[tid] = in ? ld_any2(a.beta, a.beta_dtype, gi) : 0.f;
+            float x = g_next;
+            vB[tid] = b_next;
+            if (c + 1 < nchunks) {  // next chunk's gates: their latency hides behind this chunk
+                const int64_t len1 = len - 64 * (int64_t)(c + 1);
+                const bool in = tid < len1;
+                const int64_t gi = (tok0 + 64 + tid) * a.HV + hv;
+                g_next = in ? ld_any2(a.g, a.g_dtype, gi) : 0.f;
+                b_next = in ? ld_any2(a.beta, a.beta_dtype, gi) : 0.f;
+            }
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const float y = __shfl_up_sync(0xffffffffu, x, o);
@@ -405,50 +422,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
         __syncthreads();
 
-        // (g) T = (I + A)^-1 in place: 16x16 diagonal blocks by column-wise forward substitution ...
-        {
-            float x[16];
-            const int b = tid >> 4, cidx = tid & 15;
-            if (tid < 64) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    float sacc = 0.f;
-#pragma unroll
-                    for (int j = 0; j < i; ++j) sacc = fmaf(Am[(16 * b + i) * AST + 16 * b + j], x[j], sacc);
-                    x[i] = (i == cidx) ? 1.f : (i < cidx ? 0.f : -sacc);
-                }
-            }
-            __syncthreads();
-            if (tid < 64) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) Am[(16 * b + i) * AST + 16 * b + cidx] = x[i];
-            }
-            __syncthreads();
-        }
-        // ... then off-diagonal blocks by block rows: T_rs = -T_rr sum_{m=s}^{r-1} A_rm T_ms
-#pragma unroll 1
-        for (int r = 1; r < 4; ++r) {
-            for (int e = tid; e < r * 256; e += NTHR) {
-                const int s2 = e >> 8, i = (e >> 4) & 15, cc = e & 15;
-                float y = 0.f;
-                for (int m = s2; m < r; ++m) {
-#pragma unroll
-                    for (int jj = 0; jj < 16; ++jj)
-                        y = fmaf(Am[(16 * r + i) * AST + 16 * m + jj], Am[(16 * m + jj) * AST + 16 * s2 + cc], y);
-                }
-                Yb[e] = y;
-            }
-            __syncthreads();
-            for (int e = tid; e < r * 256; e += NTHR) {
-                const int s2 = e >> 8, i = (e >> 4) & 15, cc = e & 15;
-                float t = 0.f;
-#pragma unroll
-                for (int jj = 0; jj < 16; ++jj)
-                    t = fmaf(Am[(16 * r + i) * AST + 16 * r + jj], Yb[s2 * 256 + jj * 16 + cc], t);
-                Am[(16 * r + i) * AST + 16 * s2 + cc] = -t;
-            }
-            __syncthreads();
-        }
+        tri_inverse64<AST>(Am, Yb);  // T = (I + A)^-1 in place
 
         // (h) TB = T diag(beta e^G / nk), TV = T diag(beta)  (bf16, K-major [i][j])
         {
@@ -475,7 +449,8 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             const uint32_t id = idesc_bf16(128, 64, 1, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-                umma_bf16(tW, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sbase + OFF_TB + ks * 32), id, ks > 0);
+                umma_bf16(tW, desc_kmajor(sbase + OFF_TB + ks * 32), desc_mnmajor(aK + ks * 2048, QK_BLK),
+                          idesc_bf16(128, 128, 0, 1), ks > 0);
                 umma_bf16(tU, desc_mnmajor(aV + ks * 2048, 8192), desc_kmajor(sbase + OFF_TV + ks * 32), id, ks > 0);
             }
             umma_commit(bar_mma);
@@ -484,31 +459,40 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         // V is consumed: load the next chunk's V
         if (tid == 0 && !a.zero_v && c + 1 < nchunks) issue_v(c + 1);
 
-        // (j) W^T (TMEM, lane = d) -> -W bf16 [i][d] (K-major B operand of MMA4)
-        {
+        // (j) W (TMEM rows i = lanes 0-63, columns d) -> -W bf16 [i][d] (K-major B operand of MMA4);
+        //     warp column half chh writes d-block chh with 16-byte stores
+        if (lg < 2) {
             float v[32];
-            ld32(tW + lane_base + 32 * chh, v);
-            const int d = row;
-            uint8_t* dst = sm + OFF_W + (d >> 6) * 8192;
+            uint8_t* dst = sm + OFF_W + chh * 8192;
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-                *reinterpret_cast<__nv_bfloat16*>(dst + sw128_off(32 * chh + j, d & 63)) = __float2bfloat16_rn(-v[j]);
+            for (int h = 0; h < 2; ++h) {
+                ld32(tW + lane_base + 64 * chh + 32 * h, v);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] = -v[e];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) st_chunk8(dst + sw128_off(row, 32 * h + 8 * q), v + 8 * q);
+            }
         }
         fence_async_smem();
         block_sync_tc();
 
-        // (k) MMA4: U^T += (S0hi + S0lo)^T (-W)^T -> Delta^T ; MMA5: O1^T = S0hi^T Q^T   (K = dk = 128)
+        // (k) MMA4: U^T += (S0hi + S0lo)^T (-W)^T -> Delta^T ; MMA5: [-; O1] = [-; Q] S0hi (O1 rows on
+        //     lanes 64-127, N = dv = 128)   (K = dk = 128)
         if (tid == 0) {
-            const uint32_t id = idesc_bf16(128, 64, 0, 0);
+            const uint32_t id = idesc_bf16(128, 64, 0, 0), id5 = idesc_bf16(128, 128, 0, 0);
+            // base descriptors; the 14-bit start-address field (bytes >> 4) never carries for smem addresses
+            const uint64_t dS_h = desc_kmajor(sbase + OFF_S), dS_l = desc_kmajor(sbase + OFF_SL);
+            const uint64_t dW_ = desc_kmajor(sbase + OFF_W);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                const uint64_t ah = desc_kmajor(sbase + OFF_S + kb * 16384 + ko);
-                const uint64_t al = desc_kmajor(sbase + OFF_SL + kb * 16384 + ko);
-                const uint64_t bw = desc_kmajor(sbase + OFF_W + kb * 8192 + ko);
+                const uint64_t ah = dS_h + ((kb * 16384 + ko) >> 4);
+                const uint64_t al = dS_l + ((kb * 16384 + ko) >> 4);
+                const uint64_t bw = dW_ + ((kb * 8192 + ko) >> 4);
                 umma_bf16(tU, ah, bw, id, 1);
                 umma_bf16(tU, al, bw, id, 1);
-                if (a.o_mode != 2) umma_bf16(tO1, ah, desc_kmajor(aQ + kb * QK_BLK + ko), id, ks > 0);
+                // A = [K odd slot (ignored); Q]: rows 64-127 are Q, so O1 lands on lanes 64-127
+                if (a.o_mode != 2) umma_bf16(tO1, desc_kmajor(aQ - 8192 + kb * QK_BLK + ko), ah, id5, ks > 0);
             }
             umma_commit(bar_mma);
         }
@@ -533,39 +517,65 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         block_sync_tc();
 
         // (m) MMA6: O2^T = Delta^T P'^T (hi.hi + lo.hi + hi.lo) ; MMA7: S^T += Dd^T K (hi + lo), N = 128
+        // [-; O2] = [-; P'] Delta: the 64 rows below each P' tile (TV for P' hi, P' hi for P' lo, both
+        // allocated and finite) fill the ignored half, so O2 lands on lanes 64-127 like O1
         if (tid == 0) {
-            const uint32_t id6 = idesc_bf16(128, 64, 0, 0), id7 = idesc_bf16(128, 128, 0, 1);
+            const uint32_t id6 = idesc_bf16(128, 128, 0, 0), id7 = idesc_bf16(128, 128, 0, 1);
+            const uint64_t dD_ = desc_kmajor(sbase + OFF_D), dDL_ = desc_kmajor(sbase + OFF_DL);
+            const uint64_t dDD_ = desc_kmajor(sbase + OFF_DD), dDDL_ = desc_kmajor(sbase + OFF_DDL);
+            const uint64_t dP_ = desc_kmajor(sbase + OFF_P - 8192), dPL_ = desc_kmajor(sbase + OFF_PL - 8192);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-                const uint64_t dh = desc_kmajor(sbase + OFF_D + ks * 32), dl = desc_kmajor(sbase + OFF_DL + ks * 32);
-                const uint64_t ph = desc_kmajor(sbase + OFF_P + ks * 32), pl = desc_kmajor(sbase + OFF_PL + ks * 32);
+                const uint64_t dh = dD_ + ks * 2, dl = dDL_ + ks * 2;  // +32 bytes per K step
+                const uint64_t ph = dP_ + ks * 2, pl = dPL_ + ks * 2;
                 if (a.o_mode != 2) {
-                    umma_bf16(tO2, dh, ph, id6, ks > 0);
-                    umma_bf16(tO2, dl, ph, id6, 1);
-                    umma_bf16(tO2, dh, pl, id6, 1);
+                    umma_bf16(tO2, ph, dh, id6, ks > 0);
+                    umma_bf16(tO2, pl, dh, id6, 1);
+                    umma_bf16(tO2, ph, dl, id6, 1);
                 }
                 const uint64_t kd = desc_mnmajor(aK + ks * 2048, QK_BLK);
-                umma_bf16(tS, desc_kmajor(sbase + OFF_DD + ks * 32), kd, id7, 1);
-                umma_bf16(tS, desc_kmajor(sbase + OFF_DDL + ks * 32), kd, id7, 1);
+                umma_bf16(tS, dDD_ + ks * 2, kd, id7, 1);
+                umma_bf16(tS, dDDL_ + ks * 2, kd, id7, 1);
             }
             umma_commit(bar_mma);
         }
         wait_mma(bar_mma, mma_phase, a.err, 5, ok);
 
         // (n) O = (scale e^G O1 + O2) / nq -> o[token][hv][dv]
-        if (a.o_mode != 2) {
-            float v1[32], v2[32];
-            ld32(tO1 + lane_base + 32 * chh, v1);
-            ld32(tO2 + lane_base + 32 * chh, v2);
-            __nv_bfloat16* o = (__nv_bfloat16*)a.o;
+        //     rows i on lanes 64-127: each thread writes 64 contiguous dv of one token (16-byte stores)
+        if (a.o_mode != 2 && lg >= 2) {
+            const int i = row - 64;
+            const float f1 = a.scale * vEG[i] * vNQ[i], f2 = vNQ[i];
+            __nv_bfloat16* orow = (__nv_bfloat16*)a.o + ((tok0 + i) * a.HV + hv) * 128 + 64 * chh;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int i = 32 * chh + j;
+            for (int h = 0; h < 2; ++h) {
+                float v1[32], v2[32];
+                ld32(tO1 + lane_base + 64 * chh + 32 * h, v1);
+                ld32(tO2 + lane_base + 64 * chh + 32 * h, v2);
                 if (i < nv) {
-                    const int64_t idx = ((tok0 + i) * a.HV + hv) * 128 + row;
-                    float val = (a.scale * vEG[i] * v1[j] + v2[j]) * vNQ[i];
-                    if (a.o_mode == 1) val += __bfloat162float(o[idx]);
-                    o[idx] = __float2bfloat16_rn(val);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float y[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) y[e] = fmaf(f1, v1[8 * q + e], f2 * v2[8 * q + e]);
+                        uint4* dst = reinterpret_cast<uint4*>(orow + 32 * h + 8 * q);
+                        if (a.o_mode == 1) {
+                            const uint4 old = *dst;
+                            const __nv_bfloat162* ob = reinterpret_cast<const __nv_bfloat162*>(&old);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float2 z = __bfloat1622float2(ob[e]);
+                                y[2 * e] += z.x;
+                                y[2 * e + 1] += z.y;
+                            }
+                        }
+                        uint4 u;
+                        u.x = pack_bf16(y[0], y[1]);
+                        u.y = pack_bf16(y[2], y[3]);
+                        u.z = pack_bf16(y[4], y[5]);
+                        u.w = pack_bf16(y[6], y[7]);
+                        *dst = u;
+                    }
                 }
             }
         }
