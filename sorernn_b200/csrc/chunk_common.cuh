@@ -32,13 +32,13 @@ __device__ __forceinline__ void tri_inverse64(float* Am, float* Y) {
         }
         __syncthreads();
     }
-#pragma unroll
+#pragma unroll 1
     for (int r = 1; r < 4; ++r) {
         // strips: (s < r, row i, column group c4) -> r * 64 strips
         const int s = tid >> 6, i = (tid >> 2) & 15, c4 = (tid & 3) * 4;
         if (s < r) {
             float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
+#pragma unroll 1
             for (int m = 0; m < 3; ++m) {
                 if (m >= s && m < r) {
 #pragma unroll

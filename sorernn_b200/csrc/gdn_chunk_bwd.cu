@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     // dS^T <- dht^T (TMEM lane = dv, columns dk)
     {
         const float* dht = a.dht ? a.dht + ((int64_t)n * a.HV + hv) * 16384 : nullptr;
-#pragma unroll
+#pragma unroll 1
         for (int c0 = 0; c0 < 64; c0 += 16) {
             float v[16];
 #pragma unroll
@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     auto issue_inputs = [&](int c) {
         const int tok0 = (int)(bos + 64 * c);
         mbar_arrive_expect_tx(bar_in, 8 * 8192 + 32768);
-#pragma unroll
+#pragma unroll 1
         for (int kb = 0; kb < 2; ++kb) {
             tma_load_3d(sm + OFF_QK + kb * QK_BLK, &a.tq, bar_in, kb * 64, hq, tok0);
             tma_load_3d(sm + OFF_QK + kb * QK_BLK + 8192, &a.tk, bar_in, kb * 64, hq, tok0);
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id = idesc_bf16(128, 64, 0, 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 umma_bf16(tD1, desc_kmajor(aQ + kb * QK_BLK + ko), desc_kmajor(aK + kb * QK_BLK + ko), id, ks > 0);
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         //         meanwhile dS^T -> hi tile
         if (tid == 0) {
             const uint32_t id = idesc_bf16(128, 64, 1, 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 4; ++ks) {
                 umma_bf16(tm + C384, desc_kmajor(sb + OFF_TB + ks * 32), desc_mnmajor(aK + ks * 2048, QK_BLK),
                           idesc_bf16(128, 128, 0, 1), ks > 0);
@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         {  // dS^T -> bf16 hi tile (the lo part follows in step 8b), <dS, S0>
             float dss = 0.f;
-#pragma unroll
+#pragma unroll 1
             for (int c0 = 0; c0 < 64; c0 += 16) {
                 float v[16];
                 tmem_ld16(tS + lb + 64 * chh + c0, v);
@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         if (lg < 2) {  // W rows j (lanes 0-63) -> -W bf16 [j][d], d-block chh, 16-byte stores
             float v[32];
             uint8_t* dst = sm + OFF_W + chh * 8192;
-#pragma unroll
+#pragma unroll 1
             for (int h = 0; h < 2; ++h) {
                 ld32c(tm + C384 + lb + 64 * chh + 32 * h, v);
 #pragma unroll
@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         // ---- 5. R4: Delta^T = U^T + S0^T (-W)^T (256) -------------------------------------------------
         if (tid == 0) {
             const uint32_t id = idesc_bf16(128, 64, 0, 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 umma_bf16(tm + C256, desc_kmajor(sb + OFF_S0 + kb * 16384 + ko),
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         if (tid == 0) {
             const uint32_t id_mm = idesc_bf16(128, 64, 1, 1), id_kk = idesc_bf16(128, 64, 0, 0);
             const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 4; ++ks)  // K = i
             {
                 umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS + ks * 2048, 8192),
@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
                           id_mm, 1);
             }
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 umma_bf16(tm + C384, desc_kmajor(sb + OFF_DS + kb * 16384 + ko), desc_kmajor(aK + kb * QK_BLK + ko),
@@ -498,7 +498,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         // ---- 6b. lo part of dS^T K^T: overwrite the dS tile with dS - bf16(dS) and accumulate into (384);
         //          step 7 restores the hi tile for the dS Dd^T products of step 8.
         {
-#pragma unroll
+#pragma unroll 1
             for (int c0 = 0; c0 < 64; c0 += 16) {
                 float v[16];
                 tmem_ld16(tS + lb + 64 * chh + c0, v);
@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         sync_tc();
         if (tid == 0) {
             const uint32_t id_kk = idesc_bf16(128, 64, 0, 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 umma_bf16(tm + C384, desc_kmajor(sb + OFF_DS + kb * 16384 + ko), desc_kmajor(aK + kb * QK_BLK + ko),
@@ -585,7 +585,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             vDG[tid] -= colsum(red1, tid) + r4;
         }
         // dO <- dO scale e^G / nq in place (A operand of the dS update; the raw dO readers have finished)
-#pragma unroll
+#pragma unroll 1
         for (int it = 0; it < 4; ++it) {
             const int e = tid + it * NTHR;
             const int i = e >> 4, cc = e & 15;
@@ -616,7 +616,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
         }
         {  // restore the dS hi tile (the lo part is in it since step 6b)
-#pragma unroll
+#pragma unroll 1
             for (int c0 = 0; c0 < 64; c0 += 16) {
                 float v[16];
                 tmem_ld16(tS + lb + 64 * chh + c0, v);
@@ -633,7 +633,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         if (tid == 0) {
             const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mm = idesc_bf16(128, 64, 1, 1);
             const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 4; ++ks) {  // K = tokens
                 umma_bf16(tm + C256, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
                           id_km, ks > 0);
@@ -644,7 +644,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 umma_bf16(tm + C448, desc_mnmajor(aQ + ks * 2048, QK_BLK), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
                           id_mm, ks > 0);
             }
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {  // K = dv
                 umma_bf16(tm + C320, desc_mnmajor(sb + OFF_S0 + ks * 2048, 16384),
                           desc_mnmajor(sb + OFF_DD + ks * 2048, 8192), id_mm, ks > 0);
@@ -668,7 +668,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         //          complete before the step-10 commit, ahead of any write to the tiles they read.
         {
             const float eGC = scal[0];
-#pragma unroll
+#pragma unroll 1
             for (int c0 = 0; c0 < 64; c0 += 16) {
                 float v[16], lo[16];
                 tmem_ld16(tS + lb + 64 * chh + c0, v);
@@ -689,11 +689,11 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         if (tid == 0) {
             const uint32_t id_mm = idesc_bf16(128, 64, 1, 1), id_mm128 = idesc_bf16(128, 128, 1, 1);
             const uint32_t id_km128 = idesc_bf16(128, 128, 0, 1);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 8; ++ks)  // K = dv
                 umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
                           desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192), id_mm, 1);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 4; ++ks) {  // K = tokens
                 umma_bf16(tS, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(aQ + ks * 2048, QK_BLK), id_mm128, 1);
                 umma_bf16(tS, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_W + ks * 2048, 8192), id_km128,
@@ -749,11 +749,11 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         // ---- 10. dKb^T = dW^T T (192) ; Z1 = [-; dVb] V^T (256, rows j on lanes 64-127) ------------------
         if (tid == 0) {
             const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tm + C192, desc_kmajor(sb + OFF_DWT + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
                           id_km, ks > 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 umma_bf16(tm + C256, desc_mnmajor(sb + OFF_DVB - 16384 + ks * 2048, 16384),
@@ -810,7 +810,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         sync_tc();
         if (tid == 0) {
             const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 umma_bf16(tm + C320, desc_mnmajor(sb + OFF_DKB - 16384 + ks * 2048, 16384),
@@ -845,7 +845,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         sync_tc();
         if (tid == 0) {
             const uint32_t id = idesc_bf16(128, 64, 0, 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 4; ++ks)  // A rows 0-63 = the dPs1 tile (ignored), 64-127 = Z
                 umma_bf16(tm + C256, desc_kmajor(sb + OFF_PS + ks * 32), desc_kmajor(sb + OFF_T + ks * 32), id, ks > 0);
             umma_commit(bar_mma);
@@ -898,7 +898,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         // ---- 13. dK' += K^T Gs (448) ----------------------------------------------------------------
         if (tid == 0) {
             const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
-#pragma unroll
+#pragma unroll 1
             for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tm + C448, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_GS + ks * 32), id_mk, 1);
             umma_commit(bar_mma);
@@ -958,7 +958,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
     if (ok && a.dh0) {
         float* dh0 = a.dh0 + ((int64_t)n * a.HV + hv) * 16384;
-#pragma unroll
+#pragma unroll 1
         for (int c0 = 0; c0 < 64; c0 += 16) {
             float v[16];
             tmem_ld16(tS + lb + 64 * chh + c0, v);

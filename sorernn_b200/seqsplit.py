@@ -7,8 +7,8 @@ A segment of tokens is an affine map on the state entering it (gdn_ref.py:18-21 
 ``S_out = M S_in + C`` with ``M = prod_t exp(g_t)(I - beta_t k_t k_t^T)`` (later tokens on the left,
 ``[dk, dk]``) and ``C`` the segment's final state from a zero state (``[dk, dv]``). Rank r of P:
 
-1. runs the forward of its segment from a zero state: local outputs and ``C_r``;
-   ranks r < P-1 ... r > 0 also compute ``M_r`` (``gdn_segment_transition``);
+1. runs the forward of its segment from a zero state (rank 0: from ``h0``): local outputs and ``C_r``;
+   ranks r > 0 also compute ``M_r`` (``gdn_segment_transition``);
 2. exclusive scan over ranks: rank 0's outgoing state is ``C_0`` (or ``M_0 h0 + C_0``); rank r receives
    ``S_in`` from rank r-1 over NCCL (NVLink), forms ``S_out = M_r S_in + C_r`` and sends it to rank r+1;
 3. ranks r > 0 add the incoming state's contribution to their outputs (``gdn_segment_apply_state``:
@@ -59,7 +59,7 @@ def segment_transition(k: Tensor, g: Tensor, beta: Tensor, use_qk_l2norm: bool =
 
 def combine(M: Tensor, C: Tensor, S_in: Tensor) -> Tensor:
     """``S_out = M S_in + C`` (fp32, batched over [N, HV])."""
-    return torch.matmul(M, S_in.float()) + C
+    return torch.matmul(M, S_in.to(M.dtype)) + C
 
 
 def apply_incoming_state(q: Tensor, k: Tensor, g: Tensor, beta: Tensor, S_in: Tensor, o: Tensor, scale: float,
@@ -73,6 +73,29 @@ def apply_incoming_state(q: Tensor, k: Tensor, g: Tensor, beta: Tensor, S_in: Te
     _lib.check(_lib.lib().gdn_segment_apply_state(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(g), _ptr(beta), _ptr(S_in),
                                                   _ptr(o), _ptr(final_state), _ptr(ws), n, _stream(q)),
                "gdn_segment_apply_state")
+
+
+def exchange_boundary_states(C: Tensor, M: Optional[Tensor], group=None) -> tuple[Optional[Tensor], Tensor]:
+    """Step 2, the only cross-rank step: the exclusive scan of segment maps along the rank chain.
+
+    Rank r receives ``S_in`` (the state entering its segment) from rank r-1, forms ``S_out = M S_in + C``
+    and sends it to rank r+1; rank 0's ``S_out`` is ``C`` (its forward already started from ``h0``).
+    Returns ``(S_in, S_out)``; ``S_in`` is None on rank 0. ``M`` is read on ranks r > 0 only.
+    Every rank issues its receive before its send, so the chain completes in rank order.
+    """
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    glob = (lambda r: dist.get_global_rank(group, r)) if group is not None else (lambda r: r)
+    S_in = None
+    if rank > 0:
+        S_in = torch.empty_like(C)
+        dist.recv(S_in, src=glob(rank - 1), group=group)
+        S_out = combine(M, C, S_in)
+    else:
+        S_out = C
+    if rank < world - 1:
+        dist.send(S_out.contiguous(), dst=glob(rank + 1), group=group)
+    return S_in, S_out
 
 
 def sequence_split_prefill(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: Optional[float] = None,
@@ -92,16 +115,7 @@ def sequence_split_prefill(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Ten
     if world == 1:
         return o, C
     M = segment_transition(k, g, beta, use_qk_l2norm_in_kernel, v.shape[2]) if rank > 0 else None
-    S_in = None
-    if rank > 0:
-        S_in = torch.empty_like(C)
-        dist.recv(S_in, src=dist.get_global_rank(group, rank - 1) if group is not None else rank - 1, group=group)
-        S_out = combine(M, C, S_in)
-    else:
-        S_out = C
-    if rank < world - 1:
-        dist.send(S_out.contiguous(), dst=dist.get_global_rank(group, rank + 1) if group is not None else rank + 1,
-                  group=group)
+    S_in, S_out = exchange_boundary_states(C, M, group)
     if rank > 0:
         apply_incoming_state(q, k, g, beta, S_in, o, scale, use_qk_l2norm_in_kernel)
     return o, (S_out if rank == world - 1 else None)
