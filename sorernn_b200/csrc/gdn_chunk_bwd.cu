@@ -1,6 +1,6 @@
 // Chunked gated-delta-rule backward on sm_100a (tcgen05 UMMA, TMA / bulk-copy fed, TMEM accumulators).
 //
-// One CTA (256 threads) per (sequence, value head) walks the chunks in reverse, carrying dS (the gradient
+// One CTA (512 threads) per (sequence, value head) walks the chunks in reverse, carrying dS (the gradient
 // of the state at the chunk end, fp32 in TMEM). The chunk-start states S0 are not saved by the forward:
 // a segment-parallel pass of the forward kernel (chunk_fwd in recompute mode) rebuilds them from the
 // forward's checkpoints into the workspace as bf16 operand tiles; this kernel bulk-copies one per chunk.
@@ -22,8 +22,10 @@
 // Every GEMM is an M = 128 UMMA with a 128-wide dimension on the TMEM lanes. The three 64 x 64 x K
 // products (dP, Z, dA) use a 128-row A operand of which one 64-row half is ignored; Z and dA put their
 // rows on lanes 64-127, where the same threads also hold the K K^T rows of the recomputed Gram matrix.
-// Operands are single bf16 (no hi/lo split): measured on the CPU, every gradient stays well inside the
-// bf16 tolerance with the raw q/k tiles exact.
+// Operands are bf16 with the raw q/k tiles exact; the products that carry the state gradient's large
+// dynamic range take a second bf16 "lo" operand (x - bf16(x)) for dS (in dS K^T and dS Dd^T), dDelta
+// (in dDelta T, S0 dDelta^T and the dS update) and P'' (in dO^T P''^T), which keeps every gradient
+// within the bf16 tolerance.
 #include <cstring>
 
 #include "chunk_common.cuh"
@@ -36,7 +38,7 @@ namespace gdn {
 using namespace sm100;
 
 namespace cb {
-constexpr int NTHR = 256;
+constexpr int NTHR = 512;  // 16 warps: 4 per TMEM lane quadrant, each owning 16 of 64 columns
 // shared memory carve (bytes from a 1024-aligned base)
 constexpr uint32_t OFF_QK = 0, QK_BLK = 16384;  // per d-block kb: [Q 8 KB | K 8 KB] (64 tokens x 128 B)
 constexpr uint32_t OFF_V = 32768;                // [kb][8 KB]
@@ -130,6 +132,15 @@ __device__ __forceinline__ void ld32c(uint32_t taddr, float (&v)[32]) {
     tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(v + 16));
     tmem_wait_ld();
 }
+__device__ __forceinline__ void ld16c(uint32_t taddr, float (&v)[16]) {
+    tmem_ld16(taddr, v);
+    tmem_wait_ld();
+}
+__device__ __forceinline__ void ld16x2(uint32_t ta, float (&va)[16], uint32_t tb, float (&vb)[16]) {
+    tmem_ld16(ta, va);
+    tmem_ld16(tb, vb);
+    tmem_wait_ld();
+}
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_u32(dst)),
@@ -137,12 +148,13 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  : "memory");
 }
 
-// v[k] holds this thread's value for column 32*chh + k. Afterwards lane l holds the sum over the warp's
-// 32 lanes of column 32*chh + l (recursive halving: 31 shuffles for 32 columns).
-__device__ __forceinline__ float warp_colsum32(float (&v)[32]) {
+// v[k] holds this thread's value for column 16*cq + k. Afterwards lane l holds the sum over the warp's
+// 32 lanes of column 16*cq + (l & 15) (recursive halving over lane bits 3..0, then one exchange across
+// the two half-warps: 16 shuffles for 16 columns).
+__device__ __forceinline__ float warp_colsum16(float (&v)[16]) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
+    for (int off = 8; off >= 1; off >>= 1) {
         const bool up = (lane & off) != 0;
 #pragma unroll
         for (int k = 0; k < off; ++k) {
@@ -151,13 +163,13 @@ __device__ __forceinline__ float warp_colsum32(float (&v)[32]) {
             v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
         }
     }
-    return v[0];
+    return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 16);
 }
-// Column sums over all 128 TMEM lanes: every warp deposits its 32 column partials in red[lg][col];
-// after a barrier colsum(red, col) is the total. Called by all 8 warps.
-__device__ __forceinline__ void deposit_colsum(float (&v)[32], float* red, int lg, int chh) {
-    const float s = warp_colsum32(v);
-    red[lg * 64 + 32 * chh + (threadIdx.x & 31)] = s;
+// Column sums over all 128 TMEM lanes: every warp deposits its 16 column partials in red[lg][col];
+// after a barrier colsum(red, col) is the total. Called by all 16 warps.
+__device__ __forceinline__ void deposit_colsum(float (&v)[16], float* red, int lg, int cq) {
+    const float s = warp_colsum16(v);
+    if ((threadIdx.x & 31) < 16) red[lg * 64 + 16 * cq + (threadIdx.x & 15)] = s;
 }
 __device__ __forceinline__ float colsum(const float* red, int col) {
     return red[col] + red[64 + col] + red[128 + col] + red[192 + col];
@@ -187,10 +199,10 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     uint64_t* bar_mma = bar_in + 1;
     uint64_t* bar_v = bar_in + 2;  // V tile reloaded for Z1 (its region holds the Dd lo tile in steps 5-8)
     uint32_t* tmem_slot = (uint32_t*)(bar_in + 3);
-    float* scal = (float*)(bar_in + 4);  // [0] e^G_C, [1..8] <dS, S0> per warp
+    float* scal = (float*)(bar_in + 4);  // [0] e^G_C, [1..16] <dS, S0> per warp
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int lg = warp & 3, chh = warp >> 2;
+    const int lg = warp & 3, cq = warp >> 2;  // TMEM lane quadrant; column quarter
     const int row = 32 * lg + lane;  // TMEM lane of this thread
     const int n = blockIdx.x / a.HV, hv = blockIdx.x % a.HV, hq = hv / (a.HV / a.H);
     int64_t bos, eos;
@@ -235,11 +247,11 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     {
         const float* dht = a.dht ? a.dht + ((int64_t)n * a.HV + hv) * 16384 : nullptr;
 #pragma unroll 1
-        for (int c0 = 0; c0 < 64; c0 += 16) {
+        for (int c0 = 0; c0 < 32; c0 += 16) {
             float v[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = dht ? dht[(64 * chh + c0 + i) * 128 + row] : 0.f;
-            tmem_st16(tS + lb + 64 * chh + c0, v);
+            for (int i = 0; i < 16; ++i) v[i] = dht ? dht[(32 * cq + c0 + i) * 128 + row] : 0.f;
+            tmem_st16(tS + lb + 32 * cq + c0, v);
         }
         tmem_wait_st();
     }
@@ -305,13 +317,13 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         __syncthreads();
         if (tid >= 32 && tid < 64) vG[tid] += vG[31];
-        {  // row norms (2 threads per row; rows 0-63 q, 64-127 k)
-            const int r = tid >> 1, half = tid & 1, i = r & 63;
-            const uint8_t* rowp = sm + OFF_QK + half * QK_BLK + (r < 64 ? 0 : 8192) + i * 128;
+        {  // row norms (4 threads per row, 32 elements each; rows 0-63 q, 64-127 k)
+            const int r = tid >> 2, part = tid & 3, i = r & 63;
+            const uint8_t* rowp = sm + OFF_QK + (part >> 1) * QK_BLK + (r < 64 ? 0 : 8192) + i * 128;
             float ss = 0.f;
 #pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                const uint4 u = *reinterpret_cast<const uint4*>(rowp + cc * 16);
+            for (int c = 0; c < 4; ++c) {
+                const uint4 u = *reinterpret_cast<const uint4*>(rowp + (4 * (part & 1) + c) * 16);
                 const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -320,9 +332,10 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 }
             }
             ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+            ss += __shfl_xor_sync(0xffffffffu, ss, 2);
             float inv = a.l2norm ? 1.f / fmaxf(sqrtf(ss), kL2Eps) : 1.f;
             if (i >= nv) inv = 0.f;
-            if (half == 0) (r < 64 ? vNQ : vNK)[i] = inv;
+            if (part == 0) (r < 64 ? vNQ : vNK)[i] = inv;
         }
         __syncthreads();
         if (tid < 64) {
@@ -335,55 +348,55 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
         // ---- 3. D1 -> P'' (bf16) and A (fp32); T = (I + A)^-1; TB, TV, T tiles --------------------------
         {
-            float v[32];
-            ld32c(tD1 + lb + 32 * chh, v);
+            float v[16];
+            ld16c(tD1 + lb + 16 * cq, v);
             const int i = row & 63;
             const float gi = vG[i];
             if (lg < 2) {  // P''_ij = scale qn_i.kn_j E_ij (j <= i)
                 const float f = a.scale * vNQ[i];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int jj = 32 * chh + j;
+                for (int j = 0; j < 16; ++j) {
+                    const int jj = 16 * cq + j;
                     v[j] = (jj <= i) ? f * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {  // hi tile, and its lo part where dPs2 goes later (idle until step 7)
+                for (int q = 0; q < 2; ++q) {  // hi tile, and its lo part where dPs2 goes later (idle until step 7)
                     float lo[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) lo[e] = v[8 * q + e] - __bfloat162float(__float2bfloat16_rn(v[8 * q + e]));
-                    st8(sm + OFF_PS + sw128_off(i, 32 * chh + 8 * q), v + 8 * q);
-                    st8(sm + OFF_PS2 + sw128_off(i, 32 * chh + 8 * q), lo);
+                    st8(sm + OFF_PS + sw128_off(i, 16 * cq + 8 * q), v + 8 * q);
+                    st8(sm + OFF_PS2 + sw128_off(i, 16 * cq + 8 * q), lo);
                 }
             } else {  // A_ij = beta_i kn_i.kn_j E_ij (j < i)
                 const float bi = vB[i] * vNK[i];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int jj = 32 * chh + j;
+                for (int j = 0; j < 16; ++j) {
+                    const int jj = 16 * cq + j;
                     v[j] = (jj < i) ? bi * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
                 }
-                float4* dst = reinterpret_cast<float4*>(Tm + i * AST + 32 * chh);
+                float4* dst = reinterpret_cast<float4*>(Tm + i * AST + 16 * cq);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             }
         }
         __syncthreads();
         tri_inverse64<AST>(Tm, Yb);  // T = (I + A)^-1 in place
         {
-            const int i = tid >> 2, q = tid & 3;
-            float tb[16], tv[16], tt[16];
+            const int i = tid >> 3, c8 = 8 * (tid & 7);
+            float tb[8], tv[8], tt[8];
+            const float4 t0 = *reinterpret_cast<const float4*>(Tm + i * AST + c8);
+            const float4 t1 = *reinterpret_cast<const float4*>(Tm + i * AST + c8 + 4);
+            tt[0] = t0.x; tt[1] = t0.y; tt[2] = t0.z; tt[3] = t0.w;
+            tt[4] = t1.x; tt[5] = t1.y; tt[6] = t1.z; tt[7] = t1.w;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int jj = 16 * q + j;
-                tt[j] = Tm[i * AST + jj];
+            for (int j = 0; j < 8; ++j) {
+                const int jj = c8 + j;
                 tv[j] = tt[j] * vB[jj];
                 tb[j] = tv[j] * vEG[jj] * vNK[jj];
             }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                st8(sm + OFF_TB + sw128_off(i, 16 * q + 8 * h), tb + 8 * h);
-                st8(sm + OFF_TV + sw128_off(i, 16 * q + 8 * h), tv + 8 * h);
-                st8(sm + OFF_T + sw128_off(i, 16 * q + 8 * h), tt + 8 * h);
-            }
+            st8(sm + OFF_TB + sw128_off(i, c8), tb);
+            st8(sm + OFF_TV + sw128_off(i, c8), tv);
+            st8(sm + OFF_T + sw128_off(i, c8), tt);
         }
         fence_async_smem();
         sync_tc();
@@ -404,11 +417,12 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         {  // dS^T -> bf16 hi tile (the lo part follows in step 8b), <dS, S0>
             float dss = 0.f;
 #pragma unroll 1
-            for (int c0 = 0; c0 < 64; c0 += 16) {
+            for (int c0 = 0; c0 < 32; c0 += 16) {
                 float v[16];
-                tmem_ld16(tS + lb + 64 * chh + c0, v);
+                tmem_ld16(tS + lb + 32 * cq + c0, v);
                 tmem_wait_ld();
-                const uint32_t o0 = chh * 16384 + sw128_off(row, c0), o1 = chh * 16384 + sw128_off(row, c0 + 8);
+                const uint32_t cb_ = 32 * (cq & 1) + c0;
+                const uint32_t o0 = (cq >> 1) * 16384 + sw128_off(row, cb_), o1 = (cq >> 1) * 16384 + sw128_off(row, cb_ + 8);
                 st8(sm + OFF_DS + o0, v);
                 st8(sm + OFF_DS + o1, v + 8);
 #pragma unroll
@@ -421,17 +435,14 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             if (lane == 0) scal[1 + warp] = dss;
         }
         mwait(bar_mma, mph, a.err, 13, ok);
-        if (lg < 2) {  // W rows j (lanes 0-63) -> -W bf16 [j][d], d-block chh, 16-byte stores
+        if (lg < 2) {  // W rows j (lanes 0-63) -> -W bf16 [j][d], d = 32 cq .. 32 cq + 31, 16-byte stores
             float v[32];
-            uint8_t* dst = sm + OFF_W + chh * 8192;
-#pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-                ld32c(tm + C384 + lb + 64 * chh + 32 * h, v);
+            uint8_t* dst = sm + OFF_W + (cq >> 1) * 8192;
+            ld32c(tm + C384 + lb + 32 * cq, v);
 #pragma unroll
-                for (int e = 0; e < 32; ++e) v[e] = -v[e];
+            for (int e = 0; e < 32; ++e) v[e] = -v[e];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) st8(dst + sw128_off(row, 32 * h + 8 * q), v + 8 * q);
-            }
+            for (int q = 0; q < 4; ++q) st8(dst + sw128_off(row, 32 * (cq & 1) + 8 * q), v + 8 * q);
         }
         fence_async_smem();
         sync_tc();
@@ -449,21 +460,21 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         mwait(bar_mma, mph, a.err, 14, ok);
         {
-            float v[32];
-            ld32c(tm + C256 + lb + 32 * chh, v);
+            float v[16];
+            ld16c(tm + C256 + lb + 16 * cq, v);
             // Delta^T hi tile; and the lo part of Dd = Delta diag(vX) relative to the hi part that step 7
             // derives in place (bf16(bf16(Delta) vX)), stored where V was (V is reloaded for step 10)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < 2; ++q) {
                 float lo[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const float x = vX[32 * chh + 8 * q + e];
+                    const float x = vX[16 * cq + 8 * q + e];
                     const float dh = __bfloat162float(__float2bfloat16_rn(v[8 * q + e]));
                     lo[e] = v[8 * q + e] * x - __bfloat162float(__float2bfloat16_rn(dh * x));
                 }
-                st8(sm + OFF_DEL + sw128_off(row, 32 * chh + 8 * q), v + 8 * q);
-                st8(sm + OFF_V + sw128_off(row, 32 * chh + 8 * q), lo);
+                st8(sm + OFF_DEL + sw128_off(row, 16 * cq + 8 * q), v + 8 * q);
+                st8(sm + OFF_V + sw128_off(row, 16 * cq + 8 * q), lo);
             }
         }
         fence_async_smem();
@@ -499,14 +510,15 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         //          step 7 restores the hi tile for the dS Dd^T products of step 8.
         {
 #pragma unroll 1
-            for (int c0 = 0; c0 < 64; c0 += 16) {
+            for (int c0 = 0; c0 < 32; c0 += 16) {
                 float v[16];
-                tmem_ld16(tS + lb + 64 * chh + c0, v);
+                tmem_ld16(tS + lb + 32 * cq + c0, v);
                 tmem_wait_ld();
 #pragma unroll
                 for (int e = 0; e < 16; ++e) v[e] -= __bfloat162float(__float2bfloat16_rn(v[e]));
-                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0), v);
-                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0 + 8), v + 8);
+                const uint32_t blk = (cq >> 1) * 16384, cb_ = 32 * (cq & 1) + c0;
+                st8(sm + OFF_DS + blk + sw128_off(row, cb_), v);
+                st8(sm + OFF_DS + blk + sw128_off(row, cb_ + 8), v + 8);
             }
         }
         fence_async_smem();
@@ -525,37 +537,37 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
         // ---- 7. dDelta^T = (320) + (384) diag(vX) -> tile; r4; dP -> dPs tiles, X_P sums -------------------
         {
-            float d1[32], d2[32], de[32];
-            ld32c(tm + C320 + lb + 32 * chh, d1);
-            ld32c(tm + C384 + lb + 32 * chh, d2);
-            ld32c(tm + C256 + lb + 32 * chh, de);
+            float d1[16], d2[16], de[16];
+            tmem_ld16(tm + C320 + lb + 16 * cq, d1);
+            tmem_ld16(tm + C384 + lb + 16 * cq, d2);
+            tmem_ld16(tm + C256 + lb + 16 * cq, de);
+            tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float x = vX[32 * chh + j];
+            for (int j = 0; j < 16; ++j) {
+                const float x = vX[16 * cq + j];
                 de[j] = de[j] * d2[j] * x;  // kn_j . dKst_j partial over this lane (dv)
                 d1[j] = fmaf(d2[j], x, d1[j]);
             }
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < 2; ++q) {
                 float lo[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) lo[e] = d1[8 * q + e] - __bfloat162float(__float2bfloat16_rn(d1[8 * q + e]));
-                st8(sm + OFF_DD + sw128_off(row, 32 * chh + 8 * q), d1 + 8 * q);
-                st8(sm + OFF_DDL + sw128_off(row, 32 * chh + 8 * q), lo);
+                st8(sm + OFF_DD + sw128_off(row, 16 * cq + 8 * q), d1 + 8 * q);
+                st8(sm + OFF_DDL + sw128_off(row, 16 * cq + 8 * q), lo);
             }
-            deposit_colsum(de, red0, lg, chh);
+            deposit_colsum(de, red0, lg, cq);
         }
         {
-            float v[32], p[32];
-            ld32c(tm + C448 + lb + 32 * chh, v);
-            ld32c(tD1 + lb + 32 * chh, p);
+            float v[16], p[16];
+            ld16x2(tm + C448 + lb + 16 * cq, v, tD1 + lb + 16 * cq, p);
             if (lg < 2) {
                 const int i = row;
                 const float gi = vG[i], nq = vNQ[i];
-                float d1v[32], d2v[32], rs = 0.f;
+                float d1v[16], d2v[16], rs = 0.f;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int jj = 32 * chh + j;
+                for (int j = 0; j < 16; ++j) {
+                    const int jj = 16 * cq + j;
                     const bool m = jj <= i;
                     const float e = m ? __expf(gi - vG[jj]) : 0.f;
                     const float P = a.scale * p[j] * nq * vNK[jj] * e;
@@ -567,16 +579,16 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                     d2v[j] = d1v[j] * nq;
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    st8(sm + OFF_PS + sw128_off(i, 32 * chh + 8 * q), d1v + 8 * q);
-                    st8(sm + OFF_PS2 + sw128_off(i, 32 * chh + 8 * q), d2v + 8 * q);
+                for (int q = 0; q < 2; ++q) {
+                    st8(sm + OFF_PS + sw128_off(i, 16 * cq + 8 * q), d1v + 8 * q);
+                    st8(sm + OFF_PS2 + sw128_off(i, 16 * cq + 8 * q), d2v + 8 * q);
                 }
                 atomicAdd(&vDG[i], rs);
             } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) p[j] = 0.f;
+                for (int j = 0; j < 16; ++j) p[j] = 0.f;
             }
-            deposit_colsum(p, red1, lg, chh);
+            deposit_colsum(p, red1, lg, cq);
         }
         __syncthreads();
         if (tid < 64) {
@@ -586,7 +598,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         // dO <- dO scale e^G / nq in place (A operand of the dS update; the raw dO readers have finished)
 #pragma unroll 1
-        for (int it = 0; it < 4; ++it) {
+        for (int it = 0; it < 1024 / NTHR; ++it) {
             const int e = tid + it * NTHR;
             const int i = e >> 4, cc = e & 15;
             uint8_t* pp = sm + OFF_DO + (cc >> 3) * 8192 + i * 128 + (((cc & 7) ^ (i & 7)) << 4);
@@ -600,16 +612,16 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
             *reinterpret_cast<uint4*>(pp) = u;
         }
-        {  // Delta^T -> Dd^T = Delta^T diag(vX) in place (thread owns row dv, 32 columns)
+        {  // Delta^T -> Dd^T = Delta^T diag(vX) in place (thread owns row dv, 16 columns)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const uint32_t off = sw128_off(row, 32 * chh + 8 * q);
+            for (int q = 0; q < 2; ++q) {
+                const uint32_t off = sw128_off(row, 16 * cq + 8 * q);
                 uint4 u = *reinterpret_cast<uint4*>(sm + OFF_DEL + off);
                 __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
                 for (int k2 = 0; k2 < 4; ++k2) {
                     const float2 z = __bfloat1622float2(h[k2]);
-                    const int j = 32 * chh + 8 * q + 2 * k2;
+                    const int j = 16 * cq + 8 * q + 2 * k2;
                     h[k2] = __floats2bfloat162_rn(z.x * vX[j], z.y * vX[j + 1]);
                 }
                 *reinterpret_cast<uint4*>(sm + OFF_DEL + off) = u;
@@ -617,12 +629,13 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         {  // restore the dS hi tile (the lo part is in it since step 6b)
 #pragma unroll 1
-            for (int c0 = 0; c0 < 64; c0 += 16) {
+            for (int c0 = 0; c0 < 32; c0 += 16) {
                 float v[16];
-                tmem_ld16(tS + lb + 64 * chh + c0, v);
+                tmem_ld16(tS + lb + 32 * cq + c0, v);
                 tmem_wait_ld();
-                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0), v);
-                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0 + 8), v + 8);
+                const uint32_t blk = (cq >> 1) * 16384, cb_ = 32 * (cq & 1) + c0;
+                st8(sm + OFF_DS + blk + sw128_off(row, cb_), v);
+                st8(sm + OFF_DS + blk + sw128_off(row, cb_ + 8), v + 8);
             }
         }
         fence_async_smem();
@@ -669,18 +682,19 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         {
             const float eGC = scal[0];
 #pragma unroll 1
-            for (int c0 = 0; c0 < 64; c0 += 16) {
+            for (int c0 = 0; c0 < 32; c0 += 16) {
                 float v[16], lo[16];
-                tmem_ld16(tS + lb + 64 * chh + c0, v);
+                tmem_ld16(tS + lb + 32 * cq + c0, v);
                 tmem_wait_ld();
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     lo[e] = v[e] - __bfloat162float(__float2bfloat16_rn(v[e]));
                     v[e] *= eGC;
                 }
-                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0), lo);
-                st8(sm + OFF_DS + chh * 16384 + sw128_off(row, c0 + 8), lo + 8);
-                tmem_st16(tS + lb + 64 * chh + c0, v);
+                const uint32_t blk = (cq >> 1) * 16384, cb_ = 32 * (cq & 1) + c0;
+                st8(sm + OFF_DS + blk + sw128_off(row, cb_), lo);
+                st8(sm + OFF_DS + blk + sw128_off(row, cb_ + 8), lo + 8);
+                tmem_st16(tS + lb + 32 * cq + c0, v);
             }
             tmem_wait_st();
         }
@@ -707,41 +721,36 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         bwait(bar_v, v_phase, a.err, 21, ok);  // V is back (reloaded after step 8)
         v_phase ^= 1u;
         {
-            float v[32], r2[32];
-            ld32c(tm + C256 + lb + 32 * chh, v);  // dVb^T[dv][j]
+            float v[16], r2[16], w[16];
+            ld16x2(tm + C256 + lb + 16 * cq, v, tm + C320 + lb + 16 * cq, w);  // dVb^T[dv][j], -dW^T[dk][i]
             __nv_bfloat16* dvp = (__nv_bfloat16*)a.dv;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int jj = 32 * chh + j;
+            for (int j = 0; j < 16; ++j) {
+                const int jj = 16 * cq + j;
                 r2[j] = v[j] * tile128(sm + OFF_V, 8192, jj, row);
                 if (jj < nv) dvp[((tok0 + jj) * a.HV + hv) * 128 + row] = __float2bfloat16_rn(v[j] * vB[jj]);
+                w[j] = -w[j];
             }
 #pragma unroll
-            for (int q = 0; q < 4; ++q) st8(sm + OFF_DVB + sw128_off(row, 32 * chh + 8 * q), v + 8 * q);
-            deposit_colsum(r2, red0, lg, chh);
+            for (int q = 0; q < 2; ++q) {
+                st8(sm + OFF_DVB + sw128_off(row, 16 * cq + 8 * q), v + 8 * q);
+                st8(sm + OFF_DWT + sw128_off(row, 16 * cq + 8 * q), w + 8 * q);
+            }
+            deposit_colsum(r2, red0, lg, cq);
         }
+        float qa[16], qb[16];  // dqn^T pieces [dk][i] for this thread's 16 tokens
         {
-            float v[32];
-            ld32c(tm + C320 + lb + 32 * chh, v);  // (S0 dDelta^T)[dk][i] = -dW^T
+            ld16x2(tm + C192 + lb + 16 * cq, qa, tm + C384 + lb + 16 * cq, qb);
+            float xa[16], xb[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = -v[j];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) st8(sm + OFF_DWT + sw128_off(row, 32 * chh + 8 * q), v + 8 * q);
-        }
-        float qa[32], qb[32];  // dqn^T pieces [dk][i] for this thread's 32 tokens
-        {
-            ld32c(tm + C192 + lb + 32 * chh, qa);
-            ld32c(tm + C384 + lb + 32 * chh, qb);
-            float xa[32], xb[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int i = 32 * chh + j;
+            for (int j = 0; j < 16; ++j) {
+                const int i = 16 * cq + j;
                 const float qn = tile128(sm + OFF_QK, QK_BLK, i, row) * vNQ[i];
                 xa[j] = qn * qa[j];
                 xb[j] = qn * qb[j];
             }
-            deposit_colsum(xa, red1, lg, chh);
-            deposit_colsum(xb, red2, lg, chh);
+            deposit_colsum(xa, red1, lg, cq);
+            deposit_colsum(xb, red2, lg, cq);
         }
         fence_async_smem();
         sync_tc();
@@ -762,10 +771,10 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             umma_commit(bar_mma);
         }
         {  // dq epilogue
-            float xs[32];
+            float xs[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int i = 32 * chh + j;
+            for (int j = 0; j < 16; ++j) {
+                const int i = 16 * cq + j;
                 const float sci = a.scale * vEG[i];
                 const float dqn = fmaf(sci, qa[j], qb[j]);
                 float gq = dqn;
@@ -776,8 +785,8 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 xs[j] = gq;
             }
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int i = 32 * chh + j;
+            for (int j = 0; j < 16; ++j) {
+                const int i = 16 * cq + j;
                 if (i < nv) {
                     const int64_t idx = ((tok0 + i) * a.H + hq) * 128 + row;
                     if (a.accumulate_qk) atomicAdd((float*)a.dq + idx, xs[j]);
@@ -793,18 +802,18 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         __syncthreads();  // every reader of red0..red2 above is done before they are reused
 
         // ---- 11. dKb (kept in registers), dKb.kn, dKb tile ; Z2 = [-; dKb] K^T (320) -------------------
-        float kbr[32];
+        float kbr[16];
         {
-            ld32c(tm + C192 + lb + 32 * chh, kbr);  // dKb^T[dk][j]
-            float r3[32];
+            ld16c(tm + C192 + lb + 16 * cq, kbr);  // dKb^T[dk][j]
+            float r3[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int jj = 32 * chh + j;
+            for (int j = 0; j < 16; ++j) {
+                const int jj = 16 * cq + j;
                 r3[j] = kbr[j] * tile128(sm + OFF_QK + 8192, QK_BLK, jj, row) * vNK[jj];
             }
 #pragma unroll
-            for (int q = 0; q < 4; ++q) st8(sm + OFF_DKB + sw128_off(row, 32 * chh + 8 * q), kbr + 8 * q);
-            deposit_colsum(r3, red0, lg, chh);
+            for (int q = 0; q < 2; ++q) st8(sm + OFF_DKB + sw128_off(row, 16 * cq + 8 * q), kbr + 8 * q);
+            deposit_colsum(r3, red0, lg, cq);
         }
         fence_async_smem();
         sync_tc();
@@ -826,20 +835,17 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         mwait(bar_mma, mph, a.err, 18, ok);
 
         // ---- 12. Z = beta_m (Z1 + e^G_m / nk_m Z2) -> bf16 [j][m] ; dA' = [-; Z] T^T (256) ---------------
-        {
-            float z1[32], z2[32];
-            ld32c(tm + C256 + lb + 32 * chh, z1);
-            ld32c(tm + C320 + lb + 32 * chh, z2);
-            if (lg >= 2) {
-                const int j = row - 64;
+        if (lg >= 2) {
+            float z1[16], z2[16];
+            ld16x2(tm + C256 + lb + 16 * cq, z1, tm + C320 + lb + 16 * cq, z2);
+            const int j = row - 64;
 #pragma unroll
-                for (int m = 0; m < 32; ++m) {
-                    const int mm = 32 * chh + m;
-                    z1[m] = vB[mm] * fmaf(vEG[mm] * vNK[mm], z2[m], z1[m]);
-                }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) st8(sm + OFF_PS2 + sw128_off(j, 32 * chh + 8 * q), z1 + 8 * q);
+            for (int m = 0; m < 16; ++m) {
+                const int mm = 16 * cq + m;
+                z1[m] = vB[mm] * fmaf(vEG[mm] * vNK[mm], z2[m], z1[m]);
             }
+#pragma unroll
+            for (int q = 0; q < 2; ++q) st8(sm + OFF_PS2 + sw128_off(j, 16 * cq + 8 * q), z1 + 8 * q);
         }
         fence_async_smem();
         sync_tc();
@@ -852,16 +858,16 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         mwait(bar_mma, mph, a.err, 19, ok);
         {  // rows j on lanes 64-127: dA = -dA' (l < j); G E from the K K^T rows of D1
-            float dap[32], kk[32], xa[32];
-            ld32c(tm + C256 + lb + 32 * chh, dap);
-            ld32c(tD1 + lb + 32 * chh, kk);
+            float xa[16];
             if (lg >= 2) {
+                float dap[16], kk[16];
+                ld16x2(tm + C256 + lb + 16 * cq, dap, tD1 + lb + 16 * cq, kk);
                 const int j = row - 64;
                 const float gj = vG[j], bj = vB[j], nkj = vNK[j];
                 float sb_ = 0.f, sx = 0.f;
 #pragma unroll
-                for (int t = 0; t < 32; ++t) {
-                    const int l = 32 * chh + t;
+                for (int t = 0; t < 16; ++t) {
+                    const int l = 16 * cq + t;
                     const bool m = l < j;
                     const float e = m ? __expf(gj - vG[l]) : 0.f;
                     const float ge = kk[t] * nkj * vNK[l] * e;
@@ -869,28 +875,27 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                     sb_ = fmaf(dA, ge, sb_);
                     xa[t] = dA * bj * ge;
                     sx += xa[t];
-                    dGm[j * 64 + l] = dA * bj * e;
+                    dGm[j * 64 + (l ^ (j & 31))] = dA * bj * e;  // column swizzled by the row: conflict-free
                 }
                 atomicAdd(&vDB[j], sb_);
                 atomicAdd(&vDG[j], sx);
             } else {
 #pragma unroll
-                for (int t = 0; t < 32; ++t) xa[t] = 0.f;
+                for (int t = 0; t < 16; ++t) xa[t] = 0.f;
             }
-            deposit_colsum(xa, red1, lg, chh);
+            deposit_colsum(xa, red1, lg, cq);
         }
         __syncthreads();
         if (tid < 64) vDG[tid] -= colsum(red1, tid);
         {  // Gs = (dG + dG^T) / (nk nk)  bf16 [j][m]
-            const int j = tid >> 2, q = tid & 3;
-            float gs[16];
+            const int j = tid >> 3, c8 = 8 * (tid & 7);
+            float gs[8];
 #pragma unroll
-            for (int t = 0; t < 16; ++t) {
-                const int m = 16 * q + t;
-                gs[t] = (dGm[j * 64 + m] + dGm[m * 64 + j]) * vNK[j] * vNK[m];
+            for (int t = 0; t < 8; ++t) {
+                const int m = c8 + t;
+                gs[t] = (dGm[j * 64 + (m ^ (j & 31))] + dGm[m * 64 + (j ^ (m & 31))]) * vNK[j] * vNK[m];
             }
-            st8(sm + OFF_GS + sw128_off(j, 16 * q), gs);
-            st8(sm + OFF_GS + sw128_off(j, 16 * q + 8), gs + 8);
+            st8(sm + OFF_GS + sw128_off(j, c8), gs);
         }
         fence_async_smem();
         sync_tc();
@@ -907,19 +912,19 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
         // ---- 14. dk = u - kn (kn.u), u = dK' + beta e^G / nk dKb ; dg, dbeta ---------------------------------
         {
-            float u[32], xk[32];
-            ld32c(tm + C448 + lb + 32 * chh, u);
+            float u[16], xk[16];
+            ld16c(tm + C448 + lb + 16 * cq, u);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int jj = 32 * chh + j;
+            for (int j = 0; j < 16; ++j) {
+                const int jj = 16 * cq + j;
                 u[j] = fmaf(vB[jj] * vEG[jj] * vNK[jj], kbr[j], u[j]);
                 xk[j] = tile128(sm + OFF_QK + 8192, QK_BLK, jj, row) * vNK[jj] * u[j];
             }
-            deposit_colsum(xk, red3, lg, chh);
+            deposit_colsum(xk, red3, lg, cq);
             __syncthreads();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int jj = 32 * chh + j;
+            for (int j = 0; j < 16; ++j) {
+                const int jj = 16 * cq + j;
                 float gk = u[j];
                 if (a.l2norm) gk = u[j] - tile128(sm + OFF_QK + 8192, QK_BLK, jj, row) * vNK[jj] * colsum(red3, jj);
                 if (jj < nv) {
@@ -932,7 +937,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         if (tid < 32) {  // last row: + sum_j kn.dKst_j + e^G_C <dS, S0>
             float s = vR4[tid] + vR4[tid + 32];
             s = warp_sum(s);
-            float d = (tid < 8) ? scal[1 + tid] : 0.f;
+            float d = (tid < 16) ? scal[1 + tid] : 0.f;
             d = warp_sum(d);
             if (tid == 0) vDG[63] += s + scal[0] * d;
         }
@@ -959,12 +964,12 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     if (ok && a.dh0) {
         float* dh0 = a.dh0 + ((int64_t)n * a.HV + hv) * 16384;
 #pragma unroll 1
-        for (int c0 = 0; c0 < 64; c0 += 16) {
+        for (int c0 = 0; c0 < 32; c0 += 16) {
             float v[16];
-            tmem_ld16(tS + lb + 64 * chh + c0, v);
+            tmem_ld16(tS + lb + 32 * cq + c0, v);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) dh0[(64 * chh + c0 + i) * 128 + row] = v[i];
+            for (int i = 0; i < 16; ++i) dh0[(32 * cq + c0 + i) * 128 + row] = v[i];
         }
     }
     sync_tc();
