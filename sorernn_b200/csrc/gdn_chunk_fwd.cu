@@ -1,7 +1,7 @@
 // Chunked gated-delta-rule forward on sm_100a: tcgen05 (UMMA) tile contractions, TMA-fed shared memory,
 // fp32 state resident in tensor memory (TMEM) for the whole sequence.
 //
-// One CTA (256 threads) per (sequence, value head) walks the sequence in chunks of C = 64 tokens.
+// One CTA (512 threads) per (sequence, value head) walks the sequence in chunks of C = 64 tokens.
 // With Gamma = in-chunk inclusive cumsum of g, E_ij = exp(Gamma_i - Gamma_j), S0 the state at the chunk
 // start, and nq_i, nk_j the L2 norms of the raw q/k rows (1 when the norm is off), the chunk computes
 // (algebra checked against the per-token recurrence in tests/test_chunk_algebra.py):
@@ -34,7 +34,7 @@ namespace gdn {
 using namespace sm100;
 
 namespace cf {
-constexpr int NTHR = 256;
+constexpr int NTHR = 512;  // 16 warps: 4 per TMEM lane quadrant, each owning 16 of 64 columns
 // shared memory carve (bytes from a 1024-aligned base)
 // Q/K: per d-block kb (24 KB apart): [K odd chunks 8 KB | Q 8 KB | K even chunks 8 KB], 64 rows x 128 B
 // each. K is double-buffered, Q single-buffered; either way [Q;K] (even) or [K;Q] (odd) is one
@@ -141,6 +141,10 @@ __device__ __forceinline__ void ld32(uint32_t taddr, float (&v)[32]) {
     tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(v + 16));
     tmem_wait_ld();
 }
+__device__ __forceinline__ void ld16(uint32_t taddr, float (&v)[16]) {
+    tmem_ld16(taddr, v);
+    tmem_wait_ld();
+}
 
 __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_constant__ ChunkFwdArgs a) {
     using namespace cf;
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     uint32_t* tmem_slot = (uint32_t*)(bar_k + 5);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int lg = warp & 3, chh = warp >> 2;  // TMEM lane group, column half
+    const int lg = warp & 3, cq = warp >> 2;  // TMEM lane group, column quarter
     const int row = 32 * lg + lane;            // accumulator row (TMEM lane) of this thread
     const int n = blockIdx.x / a.HV, hv = blockIdx.x % a.HV, hq = hv / (a.HV / a.H);
     int64_t bos, eos;
@@ -234,19 +238,19 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     uint32_t mma_phase = 0;
     bool ok = true;
 
-    // initial state -> TMEM: thread (row = dv, half chh) holds S^T[dv][dk] for dk in [64 chh, 64 chh + 64)
+    // initial state -> TMEM: thread (row = dv, quarter cq) holds S^T[dv][dk] for dk in [32 cq, 32 cq + 32)
     {
         const float* h0 = a.h0 ? a.h0 + ((int64_t)n * a.HV + hv) * 16384 : nullptr;
         if (recompute) h0 = a.ckpt + ((ck_base + blockIdx.y) * a.HV + hv) * 16384;
 #pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 16) {
+        for (int c0 = 0; c0 < 32; c0 += 16) {
             float v[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-                const int dk = 64 * chh + c0 + i;
+                const int dk = 32 * cq + c0 + i;
                 v[i] = (a.h0_identity && !recompute) ? (dk == row ? 1.f : 0.f) : (h0 ? h0[dk * 128 + row] : 0.f);
             }
-            tmem_st16(tS + lane_base + 64 * chh + c0, v);
+            tmem_st16(tS + lane_base + 32 * cq + c0, v);
         }
         tmem_wait_st();
     }
@@ -333,14 +337,14 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
         __syncthreads();
         if (tid >= 32 && tid < 64) vG[tid] += vG[31];
-        // (d) meanwhile: row norms of q and k (2 threads per row)
+        // (d) meanwhile: row norms of q and k (4 threads per row, 32 elements each)
         {
-            const int r = tid >> 1, half = tid & 1, i = r & 63;
-            const uint8_t* rowp = sm + OFF_QK + half * QK_BLK + (r < 64 ? 8192 : kofs) + i * 128;
+            const int r = tid >> 2, part = tid & 3, i = r & 63;
+            const uint8_t* rowp = sm + OFF_QK + (part >> 1) * QK_BLK + (r < 64 ? 8192 : kofs) + i * 128;
             float ss = 0.f;
 #pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                const uint4 u = *reinterpret_cast<const uint4*>(rowp + cc * 16);
+            for (int cc = 0; cc < 4; ++cc) {
+                const uint4 u = *reinterpret_cast<const uint4*>(rowp + (4 * (part & 1) + cc) * 16);
                 const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -349,9 +353,10 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 }
             }
             ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+            ss += __shfl_xor_sync(0xffffffffu, ss, 2);
             float inv = a.l2norm ? 1.f / fmaxf(sqrtf(ss), kL2Eps) : 1.f;
             if (i >= nv) inv = 0.f;
-            if (half == 0) (r < 64 ? vNQ : vNK)[i] = inv;
+            if (part == 0) (r < 64 ? vNQ : vNK)[i] = inv;
         }
         __syncthreads();
         if (tid < 64) {
@@ -368,11 +373,12 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             float* ckp = ck ? a.ckpt + ((ck_base + c / a.ckpt_every) * a.HV + hv) * 16384 : nullptr;
             uint8_t* s0g = recompute ? a.s0_out + ((cbase + c) * a.HV + hv) * 32768 : nullptr;
 #pragma unroll
-            for (int c0 = 0; c0 < 64; c0 += 16) {
+            for (int c0 = 0; c0 < 32; c0 += 16) {
                 float v[16];
-                tmem_ld16(tS + lane_base + 64 * chh + c0, v);
+                tmem_ld16(tS + lane_base + 32 * cq + c0, v);
                 tmem_wait_ld();
-                const uint32_t o0 = chh * 16384 + sw128_off(row, c0), o1 = chh * 16384 + sw128_off(row, c0 + 8);
+                const uint32_t blk = (cq >> 1) * 16384, cb_ = 32 * (cq & 1) + c0;
+                const uint32_t o0 = blk + sw128_off(row, cb_), o1 = blk + sw128_off(row, cb_ + 8);
                 st_chunk8_split(sm + OFF_S + o0, sm + OFF_SL + o0, v);
                 st_chunk8_split(sm + OFF_S + o1, sm + OFF_SL + o1, v + 8);
                 if (recompute) {  // the backward's S0^T operand tile: the same bytes, in the workspace
@@ -381,11 +387,11 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 }
                 if (ck) {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) ckp[(64 * chh + c0 + i) * 128 + row] = v[i];
+                    for (int i = 0; i < 16; ++i) ckp[(32 * cq + c0 + i) * 128 + row] = v[i];
                 }
 #pragma unroll
                 for (int i = 0; i < 16; ++i) v[i] *= eGC;
-                tmem_st16(tS + lane_base + 64 * chh + c0, v);
+                tmem_st16(tS + lane_base + 32 * cq + c0, v);
             }
             tmem_wait_st();
         }
@@ -393,31 +399,31 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (f) D1 -> P' (hi/lo bf16) for rows 0-63 and A (fp32) for rows 64-127
         {
-            float v[32];
-            ld32(tD1 + lane_base + 32 * chh, v);
+            float v[16];
+            ld16(tD1 + lane_base + 16 * cq, v);
             if ((lg < 2) == (s == 0)) {  // Q K^T row i (rows 0-63 on even chunks, 64-127 on odd)
                 const int i = row & 63;
                 const float gi = vG[i];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int jj = 32 * chh + j;
+                for (int j = 0; j < 16; ++j) {
+                    const int jj = 16 * cq + j;
                     v[j] = (jj <= i) ? a.scale * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    st_chunk8_split(sm + OFF_P + sw128_off(i, 32 * chh + 8 * q),
-                                    sm + OFF_PL + sw128_off(i, 32 * chh + 8 * q), v + 8 * q);
+                for (int q = 0; q < 2; ++q)
+                    st_chunk8_split(sm + OFF_P + sw128_off(i, 16 * cq + 8 * q),
+                                    sm + OFF_PL + sw128_off(i, 16 * cq + 8 * q), v + 8 * q);
             } else {  // K K^T row i
                 const int i = row & 63;
                 const float gi = vG[i], bi = vB[i] * vNK[i];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int jj = 32 * chh + j;
+                for (int j = 0; j < 16; ++j) {
+                    const int jj = 16 * cq + j;
                     v[j] = (jj < i) ? bi * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
                 }
-                float4* dst = reinterpret_cast<float4*>(Am + i * AST + 32 * chh);
+                float4* dst = reinterpret_cast<float4*>(Am + i * AST + 16 * cq);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             }
         }
         __syncthreads();
@@ -426,19 +432,19 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (h) TB = T diag(beta e^G / nk), TV = T diag(beta)  (bf16, K-major [i][j])
         {
-            const int i = tid >> 2, q = tid & 3;
-            float tb[16], tv[16];
+            const int i = tid >> 3, c8 = 8 * (tid & 7);
+            float tb[8], tv[8];
+            const float4 t0 = *reinterpret_cast<const float4*>(Am + i * AST + c8);
+            const float4 t1 = *reinterpret_cast<const float4*>(Am + i * AST + c8 + 4);
+            const float t[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int jj = 16 * q + j;
-                const float t = Am[i * AST + jj];
-                tv[j] = t * vB[jj];
+            for (int j = 0; j < 8; ++j) {
+                const int jj = c8 + j;
+                tv[j] = t[j] * vB[jj];
                 tb[j] = tv[j] * vEG[jj] * vNK[jj];
             }
-            st_chunk8(sm + OFF_TB + sw128_off(i, 16 * q), tb);
-            st_chunk8(sm + OFF_TB + sw128_off(i, 16 * q + 8), tb + 8);
-            st_chunk8(sm + OFF_TV + sw128_off(i, 16 * q), tv);
-            st_chunk8(sm + OFF_TV + sw128_off(i, 16 * q + 8), tv + 8);
+            st_chunk8(sm + OFF_TB + sw128_off(i, c8), tb);
+            st_chunk8(sm + OFF_TV + sw128_off(i, c8), tv);
         }
         fence_async_smem();
         block_sync_tc();
@@ -460,18 +466,15 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         if (tid == 0 && !a.zero_v && c + 1 < nchunks) issue_v(c + 1);
 
         // (j) W (TMEM rows i = lanes 0-63, columns d) -> -W bf16 [i][d] (K-major B operand of MMA4);
-        //     warp column half chh writes d-block chh with 16-byte stores
+        //     warp column quarter cq writes d = 32 cq .. 32 cq + 31 with 16-byte stores
         if (lg < 2) {
             float v[32];
-            uint8_t* dst = sm + OFF_W + chh * 8192;
+            uint8_t* dst = sm + OFF_W + (cq >> 1) * 8192;
+            ld32(tW + lane_base + 32 * cq, v);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                ld32(tW + lane_base + 64 * chh + 32 * h, v);
+            for (int e = 0; e < 32; ++e) v[e] = -v[e];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) v[e] = -v[e];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) st_chunk8(dst + sw128_off(row, 32 * h + 8 * q), v + 8 * q);
-            }
+            for (int q = 0; q < 4; ++q) st_chunk8(dst + sw128_off(row, 32 * (cq & 1) + 8 * q), v + 8 * q);
         }
         fence_async_smem();
         block_sync_tc();
@@ -502,13 +505,13 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (l) Delta^T (TMEM, lane = dv) -> hi/lo bf16 Delta^T and Dd^T (K-major A operands)
         {
-            float v[32], w2[32];
-            ld32(tU + lane_base + 32 * chh, v);
+            float v[16], w2[16];
+            ld16(tU + lane_base + 16 * cq, v);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) w2[j] = v[j] * vX[32 * chh + j];
+            for (int j = 0; j < 16; ++j) w2[j] = v[j] * vX[16 * cq + j];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const uint32_t off = sw128_off(row, 32 * chh + 8 * q);
+            for (int q = 0; q < 2; ++q) {
+                const uint32_t off = sw128_off(row, 16 * cq + 8 * q);
                 st_chunk8_split(sm + OFF_D + off, sm + OFF_DL + off, v + 8 * q);
                 st_chunk8_split(sm + OFF_DD + off, sm + OFF_DDL + off, w2 + 8 * q);
             }
@@ -542,23 +545,25 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         wait_mma(bar_mma, mma_phase, a.err, 5, ok);
 
         // (n) O = (scale e^G O1 + O2) / nq -> o[token][hv][dv]
-        //     rows i on lanes 64-127: each thread writes 64 contiguous dv of one token (16-byte stores)
+        //     rows i on lanes 64-127: each thread writes 32 contiguous dv of one token (16-byte stores)
         if (a.o_mode != 2 && lg >= 2) {
             const int i = row - 64;
             const float f1 = a.scale * vEG[i] * vNQ[i], f2 = vNQ[i];
-            __nv_bfloat16* orow = (__nv_bfloat16*)a.o + ((tok0 + i) * a.HV + hv) * 128 + 64 * chh;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            __nv_bfloat16* orow = (__nv_bfloat16*)a.o + ((tok0 + i) * a.HV + hv) * 128 + 32 * cq;
+            {
                 float v1[32], v2[32];
-                ld32(tO1 + lane_base + 64 * chh + 32 * h, v1);
-                ld32(tO2 + lane_base + 64 * chh + 32 * h, v2);
+                tmem_ld16(tO1 + lane_base + 32 * cq, *reinterpret_cast<float(*)[16]>(v1));
+                tmem_ld16(tO1 + lane_base + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v1 + 16));
+                tmem_ld16(tO2 + lane_base + 32 * cq, *reinterpret_cast<float(*)[16]>(v2));
+                tmem_ld16(tO2 + lane_base + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v2 + 16));
+                tmem_wait_ld();
                 if (i < nv) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         float y[8];
 #pragma unroll
                         for (int e = 0; e < 8; ++e) y[e] = fmaf(f1, v1[8 * q + e], f2 * v2[8 * q + e]);
-                        uint4* dst = reinterpret_cast<uint4*>(orow + 32 * h + 8 * q);
+                        uint4* dst = reinterpret_cast<uint4*>(orow + 8 * q);
                         if (a.o_mode == 1) {
                             const uint4 old = *dst;
                             const __nv_bfloat162* ob = reinterpret_cast<const __nv_bfloat162*>(&old);
@@ -586,13 +591,13 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     if (ok && a.ht) {
         float* ht = a.ht + ((int64_t)n * a.HV + hv) * 16384;
 #pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 16) {
+        for (int c0 = 0; c0 < 32; c0 += 16) {
             float v[16];
-            tmem_ld16(tS + lane_base + 64 * chh + c0, v);
+            tmem_ld16(tS + lane_base + 32 * cq + c0, v);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-                float* p = ht + (64 * chh + c0 + i) * 128 + row;
+                float* p = ht + (32 * cq + c0 + i) * 128 + row;
                 *p = a.ht_accumulate ? *p + v[i] : v[i];
             }
         }
