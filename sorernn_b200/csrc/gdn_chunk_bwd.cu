@@ -65,6 +65,7 @@ constexpr uint32_t OFF_DWT = OFF_S0 + 16384;  // dW^T bf16 [dk][i]
 constexpr uint32_t OFF_DKB = OFF_DS;          // dKb^T bf16 [dk][j]   (dS tile dead after step 8)
 constexpr uint32_t OFF_GS = OFF_DS + 16384;   // (dG + dG^T) / (nk nk) bf16 [j][m]
 constexpr uint32_t OFF_Y = OFF_DD;
+static_assert(OFF_Y + 32 * 32 * 4 <= OFF_PS, "solve scratch overlaps live tiles");
 constexpr uint32_t OFF_DDL = OFF_A;  // dDelta^T lo bf16 [dv][j] (16 KB; the fp32 solve area is dead after step 3)
 // TMEM columns (fp32, 128 lanes)
 constexpr uint32_t T_S = 0, T_D1 = 128, C192 = 192, C256 = 256, C320 = 320, C384 = 384, C448 = 448, T_COLS = 512;

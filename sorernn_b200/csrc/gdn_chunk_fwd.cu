@@ -62,7 +62,7 @@ static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 constexpr int AST = 68;  // padded fp32 row stride (conflict-free float4 rows)
 constexpr uint32_t OFF_A = OFF_D;
 constexpr uint32_t OFF_Y = OFF_A + 64 * AST * 4;
-static_assert(OFF_Y + 3 * 256 * 4 <= OFF_DD, "solve scratch overlaps live tiles");
+static_assert(OFF_Y + 32 * 32 * 4 <= OFF_DD, "solve scratch overlaps live tiles");
 // TMEM columns
 // O2 (128 columns) reuses D1 + U once both are read; O1 reuses W once it is read.
 constexpr uint32_t T_D1 = 0, T_U = 64, T_O2 = 0, T_S = 256, T_W = 384, T_O1 = 384, T_COLS = 512;

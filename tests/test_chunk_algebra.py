@@ -126,3 +126,33 @@ def test_chunked_forward_and_backward_equal_recurrence(T):
     for name, a, b in zip(names, got, grads_ref):
         b = b[0, 0] if name == "dh0" else sq(b)
         np.testing.assert_allclose(a, b, atol=1e-10, err_msg=name)
+
+
+def block_doubling_inverse(A):
+    """The kernels' (I + A)^-1 for a strictly lower 64 x 64 A (chunk_common.cuh, tri_inverse64): 16 x 16
+    diagonal blocks by forward substitution, then 16 -> 32 and 32 -> 64 merges via the lower-left block
+    -T1 (A10 T0) of [[I + A00, 0], [A10, I + A11]]^-1."""
+    T = np.array(A, dtype=np.float64)
+    for b in range(4):
+        s = slice(16 * b, 16 * b + 16)
+        L = np.eye(16) + np.tril(A[s, s], -1)
+        X = np.zeros((16, 16))
+        for c in range(16):  # column c: forward substitution
+            for i in range(16):
+                X[i, c] = (1.0 if i == c else 0.0) - L[i, :i] @ X[:i, c] if i >= c else 0.0
+        T[s, s] = X
+    for size in (16, 32):
+        for p in range(0, 64, 2 * size):
+            r0, c0 = p + size, p
+            Y = A[r0:r0 + size, c0:c0 + size] @ T[c0:c0 + size, c0:c0 + size]
+            T[r0:r0 + size, c0:c0 + size] = -T[r0:r0 + size, r0:r0 + size] @ Y
+    return T
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_block_doubling_inverse(seed):
+    rng = np.random.default_rng(seed)
+    A = np.tril(rng.standard_normal((64, 64)) * 0.3, -1)
+    T = block_doubling_inverse(A)
+    np.testing.assert_allclose(T, np.linalg.inv(np.eye(64) + A), rtol=1e-9, atol=1e-9)
+    assert np.all(np.triu(T, 1) == 0)
