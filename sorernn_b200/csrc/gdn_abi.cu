@@ -172,6 +172,9 @@ int gdn_decode_step(int64_t N, int64_t H, int64_t HV, int64_t DK, int64_t DV, fl
     if (!dtype_ok(act_dtype) || !dtype_ok(g_dtype) || !dtype_ok(beta_dtype)) return GDN_ERR_DTYPE;
     if (!q || !k || !v || !g || !beta || !state || !o) return GDN_ERR_ARGUMENT;
     if (DV == 128 && !aligned16(state)) return GDN_ERR_ALIGN;
+    if (decode_tma_supported(DK, DV, q, k, v, state))
+        return decode_tma(q, k, v, g, beta, state, o, N, H, HV, scale, act_dtype, g_dtype, beta_dtype,
+                          use_qk_l2norm, (cudaStream_t)stream);
     RecLaunch L{};
     L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.o = o;
     L.h0 = state;

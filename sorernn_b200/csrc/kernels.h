@@ -54,6 +54,12 @@ struct ChunkBwdLaunch {
     int g_dtype, beta_dtype, l2norm, ckpt_every;
 };
 
+// Single-token decode for DK = DV = 128 (persistent bulk-copy pipeline over the fp32 states).
+bool decode_tma_supported(int64_t DK, int64_t DV, const void* q, const void* k, const void* v, const float* state);
+int decode_tma(const void* q, const void* k, const void* v, const void* g, const void* beta, float* state, void* o,
+               int64_t N, int64_t H, int64_t HV, float scale, int act_dtype, int g_dtype, int beta_dtype, int l2norm,
+               cudaStream_t s);
+
 bool chunk_fwd_supported(int64_t DK, int64_t DV, int act_dtype);
 int chunk_fwd(const ChunkLaunch& L, cudaStream_t s);
 bool chunk_bwd_supported(int64_t DK, int64_t DV, int act_dtype);

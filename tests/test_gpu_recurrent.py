@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import assert_rms_close, to_np
+from helpers import assert_bf16_close, assert_rms_close, to_np
 from inputs import make_inputs, make_state_inputs
 from oracle import cgdn
 
@@ -102,6 +102,32 @@ def test_decode_steps_match_oracle(dtype, tol):
         xr = {n: to_np(t) for n, t in dev.items()}
         o_ref = cgdn.decode_step(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], st_ref, d ** -0.5)
         assert_rms_close(to_np(o), o_ref, tol, f"o step {step}")
+        assert_rms_close(to_np(st_dev), st_ref, 1e-4, f"state step {step}")
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2)])
+def test_decode_many_heads_per_cta(dtype, tol):
+    """600 heads: every CTA of the persistent d=128 decode kernel streams several heads through its
+    shared-memory stages (stage reuse, bulk-store / bulk-load ordering); L2 norm on, GVA 2."""
+    from sorernn_b200 import fused_recurrent_gated_delta_rule_step
+
+    N, H, HV, d = 75, 4, 8, 128
+    rng = np.random.default_rng(11)
+    state = (rng.standard_normal((N, HV, d, d)) * 0.05).astype(np.float32)
+    st_dev = torch.tensor(state, device="cuda")
+    st_ref = state.copy()
+    for step in range(2):
+        x = make_inputs(70 + step, N, 1, H, HV, d, d, normalized=False)
+        dev = {n: torch.tensor(x[n][:, 0], device="cuda").to(dtype) for n in ("q", "k", "v", "g", "beta")}
+        o = fused_recurrent_gated_delta_rule_step(dev["q"], dev["k"], dev["v"], dev["g"], dev["beta"], st_dev,
+                                                  scale=d ** -0.5, use_qk_l2norm_in_kernel=True)
+        xr = {n: to_np(t) for n, t in dev.items()}
+        o_ref = cgdn.decode_step(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], st_ref, d ** -0.5,
+                                 use_qk_l2norm=True)
+        if dtype == torch.bfloat16:  # o is rounded to bf16: judge the error beyond that rounding
+            assert_bf16_close(to_np(o), o_ref, tol, f"o step {step}")
+        else:
+            assert_rms_close(to_np(o), o_ref, tol, f"o step {step}")
         assert_rms_close(to_np(st_dev), st_ref, 1e-4, f"state step {step}")
 
 
