@@ -34,6 +34,11 @@ METRIC = "GDN fwd+bwd tokens/s (B8 T4096 H16 d128 bf16); decode-step HBM GB/s"
 C = 64
 FWD_FLOP_PER_TOKEN_HEAD = 10 * C * 128 + 6 * 128 * 128 + C * C / 3  # chunked fwd count, 181,589
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
+# DRAM bytes (read + write) per launch from ncu captures of this build, per profiles/*.md:
+# backward pass (recompute + sweep launches) at batch 2 scaled by 4 to batch 8 (chunk_kernels_batch2_full.md);
+# decode step at full config-3 size (decode_tma_config3.md).
+BWD_PASS_TRAFFIC_BYTES = (173.3e6 + 279.6e6) * 4
+DECODE_TRAFFIC_BYTES = 271.6e6 + 211.3e6
 
 
 def load_peaks():
@@ -158,14 +163,52 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
+def decode_bench(dev, rank, world, n_dec=200, timed=True):
+    """Decode (config 3): 256 sequences x 16 heads, fp32 state in HBM, bf16 token inputs; one step
+    updates every state in place. Returns (ms per step, HBM bytes per step)."""
+    import torch
+
+    from sorernn_b200 import fused_recurrent_gated_delta_rule_step
+
+    N, Hd, Dd = CFG3["N"], CFG3["H"], CFG3["D"]
+    gen = torch.Generator(device=dev).manual_seed(99 + rank)
+    state = torch.randn(N, Hd, Dd, Dd, device=dev, generator=gen) * 0.02
+    dq = torch.nn.functional.normalize(torch.randn(N, Hd, Dd, device=dev, generator=gen), dim=-1).bfloat16()
+    dk = torch.nn.functional.normalize(torch.randn(N, Hd, Dd, device=dev, generator=gen), dim=-1).bfloat16()
+    dv = torch.randn(N, Hd, Dd, device=dev, generator=gen).bfloat16()
+    dg = (torch.nn.functional.logsigmoid(torch.randn(N, Hd, device=dev, generator=gen)) / 16).bfloat16()
+    db = torch.sigmoid(torch.randn(N, Hd, device=dev, generator=gen)).bfloat16()
+    do_buf = torch.empty_like(dv)
+    for _ in range(5):
+        fused_recurrent_gated_delta_rule_step(dq, dk, dv, dg, db, state, out=do_buf)
+    dec_bytes = 2 * state.numel() * 4 + 3 * dv.numel() * 2 + do_buf.numel() * 2 + 2 * dg.numel() * 2
+    if not timed:
+        for _ in range(n_dec):
+            fused_recurrent_gated_delta_rule_step(dq, dk, dv, dg, db, state, out=do_buf)
+        torch.cuda.synchronize(dev)
+        return None, dec_bytes
+    barrier(world)
+    s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s3.record()
+    for _ in range(n_dec):
+        fused_recurrent_gated_delta_rule_step(dq, dk, dv, dg, db, state, out=do_buf)
+    e3.record()
+    barrier(world)
+    return max_over_ranks(s3.elapsed_time(e3) / n_dec, world), dec_bytes
+
+
 def run_ours(args):
     import torch
 
     from sorernn_b200 import _lib
-    from sorernn_b200 import chunk_gated_delta_rule, fused_recurrent_gated_delta_rule_step
+    from sorernn_b200 import chunk_gated_delta_rule
 
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
+    if args.profile_decode:  # profiling mode: decode steps only (no JSON line)
+        decode_bench(dev, rank, world, n_dec=args.profile_decode, timed=False)
+        print(json.dumps({"profile_decode": args.profile_decode, "ok": True}))
+        return
     B, T, H, D = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["D"]
     if args.profile_batch:
         B = args.profile_batch  # profiling mode: a small case, fwd+bwd steps only (no JSON line)
@@ -273,28 +316,7 @@ def run_ours(args):
     barrier(world)
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e2e_steps, world)
 
-    # decode (config 3): 256 sequences x 16 heads, fp32 state in HBM, bf16 token inputs
-    N, Hd, Dd = CFG3["N"], CFG3["H"], CFG3["D"]
-    gen = torch.Generator(device=dev).manual_seed(99 + rank)
-    state = torch.randn(N, Hd, Dd, Dd, device=dev, generator=gen) * 0.02
-    dq = torch.nn.functional.normalize(torch.randn(N, Hd, Dd, device=dev, generator=gen), dim=-1).bfloat16()
-    dk = torch.nn.functional.normalize(torch.randn(N, Hd, Dd, device=dev, generator=gen), dim=-1).bfloat16()
-    dv = torch.randn(N, Hd, Dd, device=dev, generator=gen).bfloat16()
-    dg = (torch.nn.functional.logsigmoid(torch.randn(N, Hd, device=dev, generator=gen)) / 16).bfloat16()
-    db = torch.sigmoid(torch.randn(N, Hd, device=dev, generator=gen)).bfloat16()
-    do_buf = torch.empty_like(dv)
-    for _ in range(5):
-        fused_recurrent_gated_delta_rule_step(dq, dk, dv, dg, db, state, out=do_buf)
-    n_dec = 200
-    barrier(world)
-    s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s3.record()
-    for _ in range(n_dec):
-        fused_recurrent_gated_delta_rule_step(dq, dk, dv, dg, db, state, out=do_buf)
-    e3.record()
-    barrier(world)
-    dec_ms = max_over_ranks(s3.elapsed_time(e3) / n_dec, world)
-    dec_bytes = 2 * state.numel() * 4 + 3 * dv.numel() * 2 + do_buf.numel() * 2 + 2 * dg.numel() * 2
+    dec_ms, dec_bytes = decode_bench(dev, rank, world)
     peaks, peak_kind = load_peaks()
     dec_gbs = dec_bytes / (dec_ms / 1e3) / 1e9
 
@@ -318,14 +340,18 @@ def run_ours(args):
         "gpu_launches": int(launches),
         "kernels": {"fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
                     "fwd_tflops": round(fwd_flop / (fwd_ms / 1e3) / 1e12, 2)},
-        "roofline": {"bound": "tensor", "kernel": "backward", "achieved": round(achieved_bwd, 2),
-                     "peak": peak_tf, "unit": "TFLOP/s", "frac": round(achieved_bwd / peak_tf, 4),
-                     "peak_source": f"{peak_kind} bf16_tflops_sustained", "traffic": None},
+        "roofline": {"bound": "tensor", "kernel": "backward pass (recompute + reverse-sweep launches)",
+                     "achieved": round(achieved_bwd, 2), "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": round(achieved_bwd / peak_tf, 4),
+                     "peak_source": f"{peak_kind} bf16_tflops_sustained (of {peak_kind})",
+                     "traffic": BWD_PASS_TRAFFIC_BYTES * B / 8,
+                     "traffic_note": "ncu DRAM read+write bytes per call, batch-2 capture scaled"},
         "decode": {"metric": "decode-step HBM GB/s (config 3: 256 seq x H16 x 128x128 fp32 state)",
                    "value": round(dec_gbs, 1), "unit": "GB/s", "us_per_step": round(dec_ms * 1e3, 2),
                    "roofline": {"bound": "hbm", "achieved": round(dec_gbs, 1), "peak": peaks["hbm_gbs"],
                                 "unit": "GB/s", "frac": round(dec_gbs / peaks["hbm_gbs"], 4),
-                                "peak_source": f"{peak_kind} hbm_gbs", "traffic": None}},
+                                "peak_source": f"{peak_kind} hbm_gbs (of {peak_kind})",
+                                "traffic": DECODE_TRAFFIC_BYTES, "algorithmic_bytes": dec_bytes}},
         "clocks": clk.summary(),
     }
     if rank == 0:
@@ -404,6 +430,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--profile-batch", type=int, default=0,
                     help="profiling mode: run only fwd+bwd steps of config 1 with this batch (for ncu captures)")
+    ap.add_argument("--profile-decode", type=int, default=0,
+                    help="profiling mode: run only this many decode steps of config 3 (for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
