@@ -355,7 +355,8 @@ def run_ours(args):
         "clocks": clk.summary(),
     }
     if rank == 0:
-        rec["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+        if world == 1:  # the host-core baseline is timed at N=1 only
+            rec["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
         print(json.dumps(rec), flush=True)
     if world > 1:
         import torch.distributed as dist
