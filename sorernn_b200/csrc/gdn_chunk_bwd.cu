@@ -54,7 +54,7 @@ constexpr uint32_t OFF_PS = 188416;   // P'' bf16 [i][j] -> dPs / nk_j
 constexpr uint32_t OFF_PS2 = 196608;  // dPs / (nq_i nk_j) -> Z bf16 [j][m]
 constexpr uint32_t OFF_A = 204800;    // A -> T fp32 [64][AST]
 constexpr int AST = 68;
-constexpr int NVEC = 10;
+constexpr int NVEC = 14;
 constexpr uint32_t OFF_VEC = OFF_A + 64 * AST * 4;     // NVEC x 64 fp32
 constexpr uint32_t OFF_RED = OFF_VEC + NVEC * 64 * 4;  // 4 reduction buffers of 4 x 64 fp32
 constexpr uint32_t OFF_BAR = OFF_RED + 4 * 256 * 4;    // 2 mbarriers, TMEM slot, scalars
@@ -175,6 +175,30 @@ __device__ __forceinline__ void deposit_colsum(float (&v)[16], float* red, int l
 __device__ __forceinline__ float colsum(const float* red, int col) {
     return red[col] + red[64 + col] + red[128 + col] + red[192 + col];
 }
+// o[j] = v[base + j], j < 16, as four float4 loads (base % 4 == 0): a warp-uniform float4 load costs
+// about 2.4 shared-memory cycles against 1.1 for each of four scalar loads.
+__device__ __forceinline__ void vec16(const float* v, int base, float (&o)[16]) {
+    const float4* p = reinterpret_cast<const float4*>(v + base);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float4 x = p[q];
+        o[4 * q] = x.x;
+        o[4 * q + 1] = x.y;
+        o[4 * q + 2] = x.z;
+        o[4 * q + 3] = x.w;
+    }
+}
+__device__ __forceinline__ void vec8(const float* v, int base, float (&o)[8]) {
+    const float4* p = reinterpret_cast<const float4*>(v + base);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const float4 x = p[q];
+        o[4 * q] = x.x;
+        o[4 * q + 1] = x.y;
+        o[4 * q + 2] = x.z;
+        o[4 * q + 3] = x.w;
+    }
+}
 
 __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_constant__ ChunkBwdArgs a) {
     using namespace cb;
@@ -192,6 +216,11 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     float* vDG = vG + 384;  // dGamma
     float* vDB = vG + 448;  // dbeta
     float* vR4 = vG + 512;  // kn_j . dKst_j
+    float* vEN = vG + 576;   // e^G / nk
+    float* vBEN = vG + 640;  // beta e^G / nk
+    float* vQ1 = vG + 704;   // scale e^G_i
+    float* vQ2 = vG + 768;   // dq norm term: (1/nq)^2 (scale e^G colsum(qn.S0dO) + colsum(qn.QB))
+    float* vK3 = vG + 832;   // dk norm term: (1/nk)^2 colsum(k.u)
     float* red0 = (float*)(sm + OFF_RED);
     float* red1 = red0 + 256;
     float* red2 = red0 + 512;
@@ -340,8 +369,12 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         __syncthreads();
         if (tid < 64) {
-            vEG[tid] = __expf(vG[tid]);
+            const float eg = __expf(vG[tid]);
+            vEG[tid] = eg;
             vX[tid] = __expf(vG[63] - vG[tid]) * vNK[tid];
+            vEN[tid] = eg * vNK[tid];
+            vBEN[tid] = vB[tid] * eg * vNK[tid];
+            vQ1[tid] = a.scale * eg;
         }
         if (tid == 64) scal[0] = __expf(vG[63]);
         __syncthreads();
@@ -389,11 +422,13 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             const float4 t1 = *reinterpret_cast<const float4*>(Tm + i * AST + c8 + 4);
             tt[0] = t0.x; tt[1] = t0.y; tt[2] = t0.z; tt[3] = t0.w;
             tt[4] = t1.x; tt[5] = t1.y; tt[6] = t1.z; tt[7] = t1.w;
+            float b8[8], en8[8];
+            vec8(vB, c8, b8);
+            vec8(vEN, c8, en8);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const int jj = c8 + j;
-                tv[j] = tt[j] * vB[jj];
-                tb[j] = tv[j] * vEG[jj] * vNK[jj];
+                tv[j] = tt[j] * b8[j];
+                tb[j] = tv[j] * en8[j];
             }
             st8(sm + OFF_TB + sw128_off(i, c8), tb);
             st8(sm + OFF_TV + sw128_off(i, c8), tv);
@@ -461,8 +496,9 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         mwait(bar_mma, mph, a.err, 14, ok);
         {
-            float v[16];
+            float v[16], x16[16];
             ld16c(tm + C256 + lb + 16 * cq, v);
+            vec16(vX, 16 * cq, x16);
             // Delta^T hi tile; and the lo part of Dd = Delta diag(vX) relative to the hi part that step 7
             // derives in place (bf16(bf16(Delta) vX)), stored where V was (V is reloaded for step 10)
 #pragma unroll
@@ -470,7 +506,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 float lo[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const float x = vX[16 * cq + 8 * q + e];
+                    const float x = x16[8 * q + e];
                     const float dh = __bfloat162float(__float2bfloat16_rn(v[8 * q + e]));
                     lo[e] = v[8 * q + e] * x - __bfloat162float(__float2bfloat16_rn(dh * x));
                 }
@@ -538,14 +574,15 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
         // ---- 7. dDelta^T = (320) + (384) diag(vX) -> tile; r4; dP -> dPs tiles, X_P sums -------------------
         {
-            float d1[16], d2[16], de[16];
+            float d1[16], d2[16], de[16], x16[16];
             tmem_ld16(tm + C320 + lb + 16 * cq, d1);
             tmem_ld16(tm + C384 + lb + 16 * cq, d2);
             tmem_ld16(tm + C256 + lb + 16 * cq, de);
+            vec16(vX, 16 * cq, x16);
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                const float x = vX[16 * cq + j];
+                const float x = x16[j];
                 de[j] = de[j] * d2[j] * x;  // kn_j . dKst_j partial over this lane (dv)
                 d1[j] = fmaf(d2[j], x, d1[j]);
             }
@@ -614,6 +651,8 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             *reinterpret_cast<uint4*>(pp) = u;
         }
         {  // Delta^T -> Dd^T = Delta^T diag(vX) in place (thread owns row dv, 16 columns)
+            float x16[16];
+            vec16(vX, 16 * cq, x16);
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 const uint32_t off = sw128_off(row, 16 * cq + 8 * q);
@@ -622,8 +661,8 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 #pragma unroll
                 for (int k2 = 0; k2 < 4; ++k2) {
                     const float2 z = __bfloat1622float2(h[k2]);
-                    const int j = 16 * cq + 8 * q + 2 * k2;
-                    h[k2] = __floats2bfloat162_rn(z.x * vX[j], z.y * vX[j + 1]);
+                    const int j = 8 * q + 2 * k2;
+                    h[k2] = __floats2bfloat162_rn(z.x * x16[j], z.y * x16[j + 1]);
                 }
                 *reinterpret_cast<uint4*>(sm + OFF_DEL + off) = u;
             }
@@ -722,14 +761,15 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         bwait(bar_v, v_phase, a.err, 21, ok);  // V is back (reloaded after step 8)
         v_phase ^= 1u;
         {
-            float v[16], r2[16], w[16];
+            float v[16], r2[16], w[16], b16[16];
             ld16x2(tm + C256 + lb + 16 * cq, v, tm + C320 + lb + 16 * cq, w);  // dVb^T[dv][j], -dW^T[dk][i]
+            vec16(vB, 16 * cq, b16);
             __nv_bfloat16* dvp = (__nv_bfloat16*)a.dv;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int jj = 16 * cq + j;
                 r2[j] = v[j] * tile128(sm + OFF_V, 8192, jj, row);
-                if (jj < nv) dvp[((tok0 + jj) * a.HV + hv) * 128 + row] = __float2bfloat16_rn(v[j] * vB[jj]);
+                if (jj < nv) dvp[((tok0 + jj) * a.HV + hv) * 128 + row] = __float2bfloat16_rn(v[j] * b16[j]);
                 w[j] = -w[j];
             }
 #pragma unroll
@@ -742,11 +782,12 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         float qa[16], qb[16];  // dqn^T pieces [dk][i] for this thread's 16 tokens
         {
             ld16x2(tm + C192 + lb + 16 * cq, qa, tm + C384 + lb + 16 * cq, qb);
-            float xa[16], xb[16];
+            float xa[16], xb[16], nq16[16];
+            vec16(vNQ, 16 * cq, nq16);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int i = 16 * cq + j;
-                const float qn = tile128(sm + OFF_QK, QK_BLK, i, row) * vNQ[i];
+                const float qn = tile128(sm + OFF_QK, QK_BLK, i, row) * nq16[j];
                 xa[j] = qn * qa[j];
                 xb[j] = qn * qb[j];
             }
@@ -771,19 +812,23 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
             umma_commit(bar_mma);
         }
-        {  // dq epilogue
-            float xs[16];
+        if (tid < 64) {  // per-column terms of the dq epilogue; dGamma and dbeta contributions
+            const float c1 = colsum(red1, tid);
+            vQ2[tid] = vNQ[tid] * vNQ[tid] * fmaf(vQ1[tid], c1, colsum(red2, tid));
+            vDG[tid] += vQ1[tid] * c1;      // rowsum(dO . O_inter)
+            vDB[tid] += colsum(red0, tid);  // dVb . v
+        }
+        __syncthreads();
+        {  // dq epilogue: dqn = scale e^G (dO S0^T) + dPs kn;  dq = dqn / nq - q_raw (qn . dqn) / nq^2
+            float xs[16], s16[16], nq16[16], c16[16];
+            vec16(vQ1, 16 * cq, s16);
+            vec16(vNQ, 16 * cq, nq16);
+            vec16(vQ2, 16 * cq, c16);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int i = 16 * cq + j;
-                const float sci = a.scale * vEG[i];
-                const float dqn = fmaf(sci, qa[j], qb[j]);
-                float gq = dqn;
-                if (a.l2norm) {
-                    const float qn = tile128(sm + OFF_QK, QK_BLK, i, row) * vNQ[i];
-                    gq = (dqn - qn * fmaf(sci, colsum(red1, i), colsum(red2, i))) * vNQ[i];
-                }
-                xs[j] = gq;
+                const float dqn = fmaf(s16[j], qa[j], qb[j]);
+                xs[j] = a.l2norm ? fmaf(-tile128(sm + OFF_QK, QK_BLK, i, row), c16[j], dqn * nq16[j]) : dqn;
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -795,22 +840,18 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 }
             }
         }
-        if (tid < 64) {
-            vDG[tid] += a.scale * vEG[tid] * colsum(red1, tid);  // rowsum(dO . O_inter)
-            vDB[tid] += colsum(red0, tid);                       // dVb . v
-        }
         mwait(bar_mma, mph, a.err, 17, ok);
-        __syncthreads();  // every reader of red0..red2 above is done before they are reused
 
         // ---- 11. dKb (kept in registers), dKb.kn, dKb tile ; Z2 = [-; dKb] K^T (320) -------------------
         float kbr[16];
         {
             ld16c(tm + C192 + lb + 16 * cq, kbr);  // dKb^T[dk][j]
-            float r3[16];
+            float r3[16], nk16[16];
+            vec16(vNK, 16 * cq, nk16);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int jj = 16 * cq + j;
-                r3[j] = kbr[j] * tile128(sm + OFF_QK + 8192, QK_BLK, jj, row) * vNK[jj];
+                r3[j] = kbr[j] * tile128(sm + OFF_QK + 8192, QK_BLK, jj, row) * nk16[j];
             }
 #pragma unroll
             for (int q = 0; q < 2; ++q) st8(sm + OFF_DKB + sw128_off(row, 16 * cq + 8 * q), kbr + 8 * q);
@@ -837,14 +878,13 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
         // ---- 12. Z = beta_m (Z1 + e^G_m / nk_m Z2) -> bf16 [j][m] ; dA' = [-; Z] T^T (256) ---------------
         if (lg >= 2) {
-            float z1[16], z2[16];
+            float z1[16], z2[16], b16[16], en16[16];
             ld16x2(tm + C256 + lb + 16 * cq, z1, tm + C320 + lb + 16 * cq, z2);
+            vec16(vB, 16 * cq, b16);
+            vec16(vEN, 16 * cq, en16);
             const int j = row - 64;
 #pragma unroll
-            for (int m = 0; m < 16; ++m) {
-                const int mm = 16 * cq + m;
-                z1[m] = vB[mm] * fmaf(vEG[mm] * vNK[mm], z2[m], z1[m]);
-            }
+            for (int m = 0; m < 16; ++m) z1[m] = b16[m] * fmaf(en16[m], z2[m], z1[m]);
 #pragma unroll
             for (int q = 0; q < 2; ++q) st8(sm + OFF_PS2 + sw128_off(j, 16 * cq + 8 * q), z1 + 8 * q);
         }
@@ -861,8 +901,10 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         {  // rows j on lanes 64-127: dA = -dA' (l < j); G E from the K K^T rows of D1
             float xa[16];
             if (lg >= 2) {
-                float dap[16], kk[16];
+                float dap[16], kk[16], g16[16], nk16[16];
                 ld16x2(tm + C256 + lb + 16 * cq, dap, tD1 + lb + 16 * cq, kk);
+                vec16(vG, 16 * cq, g16);
+                vec16(vNK, 16 * cq, nk16);
                 const int j = row - 64;
                 const float gj = vG[j], bj = vB[j], nkj = vNK[j];
                 float sb_ = 0.f, sx = 0.f;
@@ -870,8 +912,8 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 for (int t = 0; t < 16; ++t) {
                     const int l = 16 * cq + t;
                     const bool m = l < j;
-                    const float e = m ? __expf(gj - vG[l]) : 0.f;
-                    const float ge = kk[t] * nkj * vNK[l] * e;
+                    const float e = m ? __expf(gj - g16[t]) : 0.f;
+                    const float ge = kk[t] * nkj * nk16[t] * e;
                     const float dA = m ? -dap[t] : 0.f;
                     sb_ = fmaf(dA, ge, sb_);
                     xa[t] = dA * bj * ge;
@@ -890,11 +932,13 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         if (tid < 64) vDG[tid] -= colsum(red1, tid);
         {  // Gs = (dG + dG^T) / (nk nk)  bf16 [j][m]
             const int j = tid >> 3, c8 = 8 * (tid & 7);
-            float gs[8];
+            float gs[8], nk8[8];
+            vec8(vNK, c8, nk8);
+            const float nkj = vNK[j];
 #pragma unroll
             for (int t = 0; t < 8; ++t) {
                 const int m = c8 + t;
-                gs[t] = (dGm[j * 64 + (m ^ (j & 31))] + dGm[m * 64 + (j ^ (m & 31))]) * vNK[j] * vNK[m];
+                gs[t] = (dGm[j * 64 + (m ^ (j & 31))] + dGm[m * 64 + (j ^ (m & 31))]) * nkj * nk8[t];
             }
             st8(sm + OFF_GS + sw128_off(j, c8), gs);
         }
@@ -913,21 +957,26 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
         // ---- 14. dk = u - kn (kn.u), u = dK' + beta e^G / nk dKb ; dg, dbeta ---------------------------------
         {
-            float u[16], xk[16];
+            float u[16], xk[16], kr[16], w16[16];
             ld16c(tm + C448 + lb + 16 * cq, u);
+            vec16(vBEN, 16 * cq, w16);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                const int jj = 16 * cq + j;
-                u[j] = fmaf(vB[jj] * vEG[jj] * vNK[jj], kbr[j], u[j]);
-                xk[j] = tile128(sm + OFF_QK + 8192, QK_BLK, jj, row) * vNK[jj] * u[j];
+                kr[j] = tile128(sm + OFF_QK + 8192, QK_BLK, 16 * cq + j, row);
+                u[j] = fmaf(w16[j], kbr[j], u[j]);
             }
+            vec16(vNK, 16 * cq, w16);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xk[j] = kr[j] * w16[j] * u[j];
             deposit_colsum(xk, red3, lg, cq);
             __syncthreads();
+            if (tid < 64) vK3[tid] = vNK[tid] * colsum(red3, tid);  // (1/nk) (kn . u)
+            __syncthreads();
+            vec16(vK3, 16 * cq, w16);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int jj = 16 * cq + j;
-                float gk = u[j];
-                if (a.l2norm) gk = u[j] - tile128(sm + OFF_QK + 8192, QK_BLK, jj, row) * vNK[jj] * colsum(red3, jj);
+                const float gk = a.l2norm ? fmaf(-kr[j], w16[j], u[j]) : u[j];
                 if (jj < nv) {
                     const int64_t idx = ((tok0 + jj) * a.H + hq) * 128 + row;
                     if (a.accumulate_qk) atomicAdd((float*)a.dk + idx, gk);
