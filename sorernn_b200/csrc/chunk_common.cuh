@@ -6,14 +6,21 @@ namespace gdn {
 
 // T = (I + A)^-1 for a strictly lower-triangular 64 x 64 fp32 matrix A stored in shared memory with row
 // stride `ST` floats (ST % 4 == 0; the upper triangle holds zeros), in place; `Y` is 32 x 32 fp32
-// scratch. Called by all 512 threads of the CTA (contains barriers). Block doubling:
+// scratch. Only threads 0-63 compute; with GROUP64 the caller is those 64 threads alone (warps 0-1,
+// synchronised by named barrier 1, so the other warps can work meanwhile), otherwise every thread of the
+// CTA calls it (CTA barriers). Block doubling:
 //  1. the four 16 x 16 diagonal blocks by column-wise forward substitution (one thread per column);
 //  2. merge 16-blocks into 32-blocks, both pairs at once: for L = [[T0, 0], [A10, T1]]^-1 the lower-left
 //     block is -T1 (A10 T0): two 16 x 16 x 16 products;
 //  3. merge the two 32-blocks the same way: two 32 x 32 x 32 products.
 // Every product runs over the full block width (the zeros above the diagonals make that exact), so the
 // dependent chains are 16 + 16 + 32 + 32 multiply-adds after the substitution.
-template <int ST>
+template <bool GROUP64>
+__device__ __forceinline__ void solve_sync() {
+    if constexpr (GROUP64) asm volatile("bar.sync 1, 64;" ::: "memory");
+    else __syncthreads();
+}
+template <int ST, bool GROUP64 = false>
 __device__ __forceinline__ void tri_inverse64(float* Am, float* Y) {
     const int tid = threadIdx.x;
     {
@@ -28,12 +35,12 @@ __device__ __forceinline__ void tri_inverse64(float* Am, float* Y) {
                 x[i] = (i == cidx) ? 1.f : (i < cidx ? 0.f : -sacc);
             }
         }
-        __syncthreads();
+        solve_sync<GROUP64>();
         if (tid < 64) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) Am[(16 * b + i) * ST + 16 * b + cidx] = x[i];
         }
-        __syncthreads();
+        solve_sync<GROUP64>();
     }
     // The merge products are bound by shared-memory bandwidth (bytes delivered to threads), not by their
     // dependent chains, so each thread computes a register block (2 x 4 or 4 x 4 outputs) from float4 loads
@@ -69,7 +76,7 @@ __device__ __forceinline__ void tri_inverse64(float* Am, float* Y) {
                 *reinterpret_cast<float4*>(&Y[p * 256 + (i + 8 * r) * 16 + c4]) =
                     make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
         }
-        __syncthreads();
+        solve_sync<GROUP64>();
         if (tid < 64) {
             float acc[2][4] = {};
 #pragma unroll
@@ -97,7 +104,7 @@ __device__ __forceinline__ void tri_inverse64(float* Am, float* Y) {
                 *reinterpret_cast<float4*>(&Am[(r0 + i + 8 * r) * ST + c0 + c4]) =
                     make_float4(-acc[r][0], -acc[r][1], -acc[r][2], -acc[r][3]);
         }
-        __syncthreads();
+        solve_sync<GROUP64>();
     }
     {  // 32-blocks -> 64: rows 32-63, columns 0-31; 64 threads, rows {i, i + 8, i + 16, i + 24} x 4 columns
         const int i = (tid >> 3) & 7, c4 = 4 * (tid & 7);
@@ -128,7 +135,7 @@ __device__ __forceinline__ void tri_inverse64(float* Am, float* Y) {
                 *reinterpret_cast<float4*>(&Y[(i + 8 * r) * 32 + c4]) =
                     make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
         }
-        __syncthreads();
+        solve_sync<GROUP64>();
         if (tid < 64) {
             float acc[4][4] = {};
 #pragma unroll 2
@@ -156,7 +163,7 @@ __device__ __forceinline__ void tri_inverse64(float* Am, float* Y) {
                 *reinterpret_cast<float4*>(&Am[(32 + i + 8 * r) * ST + c4]) =
                     make_float4(-acc[r][0], -acc[r][1], -acc[r][2], -acc[r][3]);
         }
-        __syncthreads();
+        solve_sync<GROUP64>();
     }
 }
 

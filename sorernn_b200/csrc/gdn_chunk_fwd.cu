@@ -380,35 +380,6 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         if (tid == 64) vMisc[0] = __expf(vG[63]);
         __syncthreads();
 
-        // (e) S0 -> bf16 S0^T operand, TMEM state <- e^G_C S0, checkpoint
-        {
-            const float eGC = vMisc[0];
-            const bool ck = a.ckpt && !recompute && (c % a.ckpt_every == 0);
-            float* ckp = ck ? a.ckpt + ((ck_base + c / a.ckpt_every) * a.HV + hv) * 16384 : nullptr;
-            uint8_t* s0g = recompute ? a.s0_out + ((cbase + c) * a.HV + hv) * 32768 : nullptr;
-#pragma unroll
-            for (int c0 = 0; c0 < 32; c0 += 16) {
-                float v[16];
-                tmem_ld16(tS + lane_base + 32 * cq + c0, v);
-                tmem_wait_ld();
-                const uint32_t blk = (cq >> 1) * 16384, cb_ = 32 * (cq & 1) + c0;
-                const uint32_t o0 = blk + sw128_off(row, cb_), o1 = blk + sw128_off(row, cb_ + 8);
-                st_chunk8_split(sm + OFF_S + o0, sm + OFF_SL + o0, v);
-                st_chunk8_split(sm + OFF_S + o1, sm + OFF_SL + o1, v + 8);
-                if (recompute) {  // the backward's S0^T operand tile: the same bytes, in the workspace
-                    *reinterpret_cast<uint4*>(s0g + o0) = *reinterpret_cast<const uint4*>(sm + OFF_S + o0);
-                    *reinterpret_cast<uint4*>(s0g + o1) = *reinterpret_cast<const uint4*>(sm + OFF_S + o1);
-                }
-                if (ck) {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) ckp[(32 * cq + c0 + i) * 128 + row] = v[i];
-                }
-#pragma unroll
-                for (int i = 0; i < 16; ++i) v[i] *= eGC;
-                tmem_st16(tS + lane_base + 32 * cq + c0, v);
-            }
-            tmem_wait_st();
-        }
         wait_mma(bar_mma, mma_phase, a.err, 2, ok);
 
         // (f) D1 -> P' (hi/lo bf16) for rows 0-63 and A (fp32) for rows 64-127
@@ -442,7 +413,40 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
         __syncthreads();
 
-        tri_inverse64<AST>(Am, Yb);  // T = (I + A)^-1 in place
+        // (g) T = (I + A)^-1 in place on warps 0-1 (its steps use at most 64 threads), while warps 8-15 do
+        // (e): S0 -> bf16 S0^T operand (hi/lo), TMEM state <- e^G_C S0, checkpoint or recompute tile
+        if (warp < 2) {
+            tri_inverse64<AST, true>(Am, Yb);
+        } else if (warp >= 8) {
+            const int half = (warp - 8) >> 2;  // dk columns 64 half .. 64 half + 63 = S0^T block `half`
+            const float eGC = vMisc[0];
+            const bool ck = a.ckpt && !recompute && (c % a.ckpt_every == 0);
+            float* ckp = ck ? a.ckpt + ((ck_base + c / a.ckpt_every) * a.HV + hv) * 16384 : nullptr;
+            uint8_t* s0g = recompute ? a.s0_out + ((cbase + c) * a.HV + hv) * 32768 : nullptr;
+#pragma unroll 1
+            for (int c0 = 0; c0 < 64; c0 += 16) {
+                float v[16];
+                tmem_ld16(tS + lane_base + 64 * half + c0, v);
+                tmem_wait_ld();
+                const uint32_t blk = half * 16384;
+                const uint32_t o0 = blk + sw128_off(row, c0), o1 = blk + sw128_off(row, c0 + 8);
+                st_chunk8_split(sm + OFF_S + o0, sm + OFF_SL + o0, v);
+                st_chunk8_split(sm + OFF_S + o1, sm + OFF_SL + o1, v + 8);
+                if (recompute) {  // the backward's S0^T operand tile: the same bytes, in the workspace
+                    *reinterpret_cast<uint4*>(s0g + o0) = *reinterpret_cast<const uint4*>(sm + OFF_S + o0);
+                    *reinterpret_cast<uint4*>(s0g + o1) = *reinterpret_cast<const uint4*>(sm + OFF_S + o1);
+                }
+                if (ck) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) ckp[(64 * half + c0 + i) * 128 + row] = v[i];
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] *= eGC;
+                tmem_st16(tS + lane_base + 64 * half + c0, v);
+            }
+            tmem_wait_st();
+        }
+        __syncthreads();
 
         // (h) TB = T diag(beta e^G / nk), TV = T diag(beta)  (bf16, K-major [i][j])
         {
