@@ -136,6 +136,25 @@ int gdn_decode_step(int64_t N, int64_t H, int64_t HV, int64_t DK, int64_t DV, fl
                     float* state, void* o, gdn_stream_t stream);
 
 /*
+ * The gate and beta activations the layer can hand to the mixer (sore/model/gdn.py:157-162:
+ * use_gate_in_kernel=True, A_log, dt_bias, use_beta_sigmoid_in_kernel=True, with the raw a_proj / b_proj
+ * outputs passed as g and beta). Math of the layer's own path, gdn.py:191-194:
+ *   g = -exp(A_log[h]) * softplus(a + dt_bias[h]) (fp32; softplus(x) = x above 20),  beta = sigmoid(b).
+ * a, b [n_tokens, HV] (any act dtype), A_log, dt_bias [HV] (param_dtype; dt_bias may be NULL), HV <= 1024.
+ * Replaces: fla gdn_gate_chunk_cumsum / gdn_gate_bwd (fla/ops/gated_delta_rule/gate.py) and the in-kernel
+ * beta sigmoid of FLA 0.5.2. gdn_gate_bwd writes da (dtype of a) and dA_log, ddt_bias (fp32 [HV], zeroed
+ * by the call itself; ddt_bias is required iff dt_bias is given).
+ */
+int gdn_gate_fwd(int64_t n_tokens, int64_t HV, const void* a, int32_t a_dtype, const void* A_log,
+                 const void* dt_bias, int32_t param_dtype, float* g_out, gdn_stream_t stream);
+int gdn_gate_bwd(int64_t n_tokens, int64_t HV, const void* a, int32_t a_dtype, const void* A_log,
+                 const void* dt_bias, int32_t param_dtype, const float* dg, void* da, float* dA_log,
+                 float* ddt_bias, gdn_stream_t stream);
+int gdn_beta_sigmoid_fwd(int64_t n, const void* b, int32_t b_dtype, float* beta_out, gdn_stream_t stream);
+int gdn_beta_sigmoid_bwd(int64_t n, const void* b, int32_t b_dtype, const float* dbeta, void* db,
+                         gdn_stream_t stream);
+
+/*
  * Sequence split (no counterpart in the reference, which has no context parallelism: soreRNN only
  * grows the context by curriculum, configs/b0_8_pretrain.yaml:18-20). A segment of tokens maps the
  * state entering it to S_out = M S_in + C, where C is gdn_chunk_fwd's final_state from a zero state

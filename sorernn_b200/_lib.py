@@ -42,6 +42,10 @@ SIGNATURES = {
     "gdn_workspace_error": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_i32)]),
     "gdn_kernel_launches": (ctypes.c_uint64, []),
     "gdn_chunk_bwd_noalloc": (ctypes.c_int, [_P] + [_vp] * 16),
+    "gdn_gate_fwd": (ctypes.c_int, [_i64, _i64, _vp, _i32, _vp, _vp, _i32, _vp, _vp]),
+    "gdn_gate_bwd": (ctypes.c_int, [_i64, _i64, _vp, _i32, _vp, _vp, _i32] + [_vp] * 5),
+    "gdn_beta_sigmoid_fwd": (ctypes.c_int, [_i64, _vp, _i32, _vp, _vp]),
+    "gdn_beta_sigmoid_bwd": (ctypes.c_int, [_i64, _vp, _i32, _vp, _vp, _vp]),
 }
 
 _lib = None

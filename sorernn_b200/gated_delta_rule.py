@@ -152,6 +152,100 @@ torch.library.register_autograd("sorernn_b200::gdn_fwd", _backward, setup_contex
 
 
 # ------------------------------------------------------------------------------------------------
+# gate and beta activations (the layer's use_gate_in_kernel / use_beta_sigmoid_in_kernel, gdn.py:157-162)
+# ------------------------------------------------------------------------------------------------
+@torch.library.custom_op("sorernn_b200::gdn_gate", mutates_args=())
+def gdn_gate(a: Tensor, A_log: Tensor, dt_bias: Optional[Tensor]) -> Tensor:
+    """``g = -exp(A_log) * softplus(a + dt_bias)`` in fp32 for raw ``a [..., HV]`` (gdn.py:191-194)."""
+    HV = a.shape[-1]
+    g = torch.empty(a.shape, dtype=torch.float32, device=a.device)
+    A, dtb = A_log.float().contiguous(), None if dt_bias is None else dt_bias.float().contiguous()
+    _lib.check(_lib.lib().gdn_gate_fwd(a.numel() // HV, HV, _ptr(a), _DT[a.dtype], _ptr(A), _ptr(dtb), _lib.FP32,
+                                       _ptr(g), _stream(a)), "gdn_gate_fwd")
+    return g
+
+
+@gdn_gate.register_fake
+def _(a, A_log, dt_bias):
+    return torch.empty(a.shape, dtype=torch.float32, device=a.device)
+
+
+@torch.library.custom_op("sorernn_b200::gdn_gate_bwd", mutates_args=())
+def gdn_gate_bwd(a: Tensor, A_log: Tensor, dt_bias: Optional[Tensor], dg: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """Returns ``(da, dA_log, ddt_bias)``; ``ddt_bias`` is empty when ``dt_bias`` is None."""
+    HV = a.shape[-1]
+    da = torch.empty_like(a)
+    dA = torch.empty(HV, dtype=torch.float32, device=a.device)
+    ddt = torch.empty(HV if dt_bias is not None else 0, dtype=torch.float32, device=a.device)
+    A, dtb = A_log.float().contiguous(), None if dt_bias is None else dt_bias.float().contiguous()
+    _lib.check(_lib.lib().gdn_gate_bwd(a.numel() // HV, HV, _ptr(a), _DT[a.dtype], _ptr(A), _ptr(dtb), _lib.FP32,
+                                       _ptr(dg.float().contiguous()), _ptr(da), _ptr(dA),
+                                       _ptr(ddt) if dt_bias is not None else None, _stream(a)), "gdn_gate_bwd")
+    return da, dA, ddt
+
+
+@gdn_gate_bwd.register_fake
+def _(a, A_log, dt_bias, dg):
+    HV = a.shape[-1]
+    return (torch.empty_like(a), a.new_empty(HV, dtype=torch.float32),
+            a.new_empty(HV if dt_bias is not None else 0, dtype=torch.float32))
+
+
+def _gate_setup(ctx, inputs, output):
+    a, A_log, dt_bias = inputs
+    ctx.save_for_backward(a, A_log, dt_bias)
+    ctx.has_bias = dt_bias is not None
+
+
+def _gate_backward(ctx, dg):
+    a, A_log, dt_bias = ctx.saved_tensors
+    da, dA, ddt = gdn_gate_bwd(a, A_log, dt_bias, dg)
+    return da, dA.to(A_log.dtype), (ddt.to(dt_bias.dtype) if ctx.has_bias else None)
+
+
+torch.library.register_autograd("sorernn_b200::gdn_gate", _gate_backward, setup_context=_gate_setup)
+
+
+@torch.library.custom_op("sorernn_b200::gdn_beta_sigmoid", mutates_args=())
+def gdn_beta_sigmoid(b: Tensor) -> Tensor:
+    """``beta = sigmoid(b)`` in fp32."""
+    beta = torch.empty(b.shape, dtype=torch.float32, device=b.device)
+    _lib.check(_lib.lib().gdn_beta_sigmoid_fwd(b.numel(), _ptr(b), _DT[b.dtype], _ptr(beta), _stream(b)),
+               "gdn_beta_sigmoid_fwd")
+    return beta
+
+
+@gdn_beta_sigmoid.register_fake
+def _(b):
+    return torch.empty(b.shape, dtype=torch.float32, device=b.device)
+
+
+@torch.library.custom_op("sorernn_b200::gdn_beta_sigmoid_bwd", mutates_args=())
+def gdn_beta_sigmoid_bwd(b: Tensor, dbeta: Tensor) -> Tensor:
+    db = torch.empty_like(b)
+    _lib.check(_lib.lib().gdn_beta_sigmoid_bwd(b.numel(), _ptr(b), _DT[b.dtype], _ptr(dbeta.float().contiguous()),
+                                               _ptr(db), _stream(b)), "gdn_beta_sigmoid_bwd")
+    return db
+
+
+@gdn_beta_sigmoid_bwd.register_fake
+def _(b, dbeta):
+    return torch.empty_like(b)
+
+
+def _beta_setup(ctx, inputs, output):
+    ctx.save_for_backward(inputs[0])
+
+
+def _beta_backward(ctx, dbeta):
+    (b,) = ctx.saved_tensors
+    return gdn_beta_sigmoid_bwd(b, dbeta)
+
+
+torch.library.register_autograd("sorernn_b200::gdn_beta_sigmoid", _beta_backward, setup_context=_beta_setup)
+
+
+# ------------------------------------------------------------------------------------------------
 # public API
 # ------------------------------------------------------------------------------------------------
 def chunk_gated_delta_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: Optional[float] = None,
@@ -165,9 +259,32 @@ def chunk_gated_delta_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Ten
     beta ``[B,T,HV]``; initial_state ``[N,HV,K,V]``. Returns ``(o [B,T,HV,V], final_state [N,HV,K,V] fp32 or
     None)``. ``cu_seqlens`` (int64 ``[N+1]``, B == 1) resets the state at each document start;
     ``cu_seqlens_cpu`` (same values on the host) is read only to size buffers, never to synchronise.
+
+    FLA's gate keywords are accepted as the layer passes them (gdn.py:157-162): with
+    ``use_gate_in_kernel=True`` (and ``A_log [HV]``, optional ``dt_bias [HV]``), ``g`` is the raw a_proj
+    output and the log decay is ``-exp(A_log) * softplus(g + dt_bias)``; with
+    ``use_beta_sigmoid_in_kernel=True``, ``beta`` is the raw b_proj output and ``sigmoid(beta)`` is used.
+    Both activations run as fused CUDA kernels with their own backward (gradients reach a, b, A_log,
+    dt_bias).
     """
-    if kwargs.get("use_gate_in_kernel") or kwargs.get("cp_context") is not None:
-        raise NotImplementedError("use_gate_in_kernel / cp_context are not supported by this op")
+    use_gate = bool(kwargs.pop("use_gate_in_kernel", False))
+    A_log, dt_bias = kwargs.pop("A_log", None), kwargs.pop("dt_bias", None)
+    use_beta_sigmoid = bool(kwargs.pop("use_beta_sigmoid_in_kernel", False))
+    if kwargs.pop("cp_context", None) is not None:
+        raise NotImplementedError("cp_context is not supported by this op (see sorernn_b200.seqsplit)")
+    if kwargs:
+        raise TypeError(f"unexpected keyword arguments: {sorted(kwargs)}")
+    if use_gate:
+        if A_log is None:
+            raise ValueError("A_log must be provided when use_gate_in_kernel=True")
+        if not g.is_cuda:
+            raise RuntimeError("sorernn_b200 runs on CUDA tensors only (no CPU fallback)")
+        HV = g.shape[-1]
+        if A_log.numel() != HV or (dt_bias is not None and dt_bias.numel() != HV):
+            raise ValueError(f"A_log and dt_bias must have HV = {HV} elements")
+        g = gdn_gate(g.contiguous(), A_log.reshape(HV), None if dt_bias is None else dt_bias.reshape(HV))
+    if use_beta_sigmoid:
+        beta = gdn_beta_sigmoid(beta.contiguous())
     _check_inputs(q, k, v, g, beta, cu_seqlens)
     scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
     if cu_seqlens is not None:
