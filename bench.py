@@ -197,6 +197,39 @@ def decode_bench(dev, rank, world, n_dec=200, timed=True):
     return max_over_ranks(s3.elapsed_time(e3) / n_dec, world), dec_bytes
 
 
+def long_prefill_bench(dev, rank, world, reps=3):
+    """Config 4: one sequence of T = 262,144 tokens (H=16, d=128, bf16, forward only, in-kernel L2 norm),
+    cut into `world` contiguous segments, one per rank (strong scaling: the sequence is fixed), each run as
+    8 local pieces side by side (16 heads alone would fill 16 of 148 SMs): local chunk forward, piece
+    transitions, scan of the affine maps, NCCL send/recv of the boundary state between ranks, and one
+    incoming-state correction pass. Returns ms per call, max over ranks."""
+    import torch
+
+    from sorernn_b200.seqsplit import segmented_prefill
+
+    T, H, D, P = 262144, 16, 128, 8
+    Tr = T // world
+    x = make_inputs(1, Tr, H, D, dev, seed=4000 + rank)
+
+    def call():
+        with torch.no_grad():
+            segmented_prefill(x["q"], x["k"], x["v"], x["g"], x["beta"], use_qk_l2norm_in_kernel=True,
+                              local_segments=P)
+
+    call()
+    barrier(world)
+    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(reps):
+        call()
+    e0.record()
+    barrier(world)
+    ms = max_over_ranks(s0.elapsed_time(e0) / reps, world)
+    return {"config": f"config4: B1 T{T} H{H} d{D} bf16 forward, {world} rank segment(s) x {P} local pieces",
+            "ms_per_call": round(ms, 3), "tokens_per_s": round(T / (ms / 1e3), 1), "reps": reps,
+            "useful_tflops": round(T * H * FWD_FLOP_PER_TOKEN_HEAD / (ms / 1e3) / 1e12, 2)}
+
+
 def run_ours(args):
     import torch
 
@@ -317,6 +350,7 @@ def run_ours(args):
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e2e_steps, world)
 
     dec_ms, dec_bytes = decode_bench(dev, rank, world)
+    long_prefill = long_prefill_bench(dev, rank, world)
     peaks, peak_kind = load_peaks()
     dec_gbs = dec_bytes / (dec_ms / 1e3) / 1e9
 
@@ -353,6 +387,7 @@ def run_ours(args):
                                 "peak_source": f"{peak_kind} hbm_gbs (of {peak_kind})",
                                 "traffic": DECODE_TRAFFIC_BYTES, "algorithmic_bytes": dec_bytes}},
         "clocks": clk.summary(),
+        "long_prefill": long_prefill,
     }
     if rank == 0:
         if world == 1:  # the host-core baseline is timed at N=1 only

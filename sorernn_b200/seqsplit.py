@@ -98,6 +98,69 @@ def exchange_boundary_states(C: Tensor, M: Optional[Tensor], group=None) -> tupl
     return S_in, S_out
 
 
+def _local_split(q, k, v, g, beta, scale, l2, P, h0):
+    """Forward of one rank's sequence cut into P sub-segments run side by side as a batch of P (the
+    tensors are [1, T, ...] and contiguous, so the cut is a view). Sub-segment 0 starts from h0, the
+    others from zero. Returns the per-piece views, ``o``, the incoming state of every sub-segment that its
+    outputs still lack (zero for sub-segment 0), the prefix maps ``Mpre[s] = M_{s-1} ... M_0`` (identity
+    for s = 0) and the rank's map ``(M, C)`` (C = the outgoing state for a zero rank input)."""
+    T = q.shape[1]
+    Ts = T // P
+    seg = lambda x: x.view(P, Ts, *x.shape[2:])  # noqa: E731
+    qs, ks, vs, gs, bs = (seg(x) for x in (q, k, v, g, beta))
+    HV, dk, dv = v.shape[2], q.shape[3], v.shape[3]
+    init = None
+    if h0 is not None:
+        init = torch.zeros(P, HV, dk, dv, dtype=torch.float32, device=q.device)
+        init[0] = h0[0].float()
+    o, C = chunk_gated_delta_rule(qs, ks, vs, gs, bs, scale=scale, initial_state=init, output_final_state=True,
+                                  use_qk_l2norm_in_kernel=l2)
+    M = segment_transition(ks, gs, bs, l2, HV)  # [P, HV, dk, dk]
+    S_loc = torch.zeros(P, HV, dk, dv, dtype=torch.float32, device=q.device)
+    Mpre = torch.empty(P, HV, dk, dk, dtype=torch.float32, device=q.device)
+    Mpre[0] = torch.eye(dk, device=q.device)
+    for s_ in range(1, P):  # the exclusive scan over sub-segments (P - 1 batched 128 x 128 products)
+        S_loc[s_] = C[0] if s_ == 1 else combine(M[s_ - 1], C[s_ - 1], S_loc[s_ - 1])
+        Mpre[s_] = torch.matmul(M[s_ - 1], Mpre[s_ - 1])
+    M_rank = torch.matmul(M[P - 1], Mpre[P - 1])
+    C_rank = C[0] if P == 1 else combine(M[P - 1], C[P - 1], S_loc[P - 1])
+    return qs, ks, gs, bs, o, S_loc, Mpre, M_rank.unsqueeze(0), C_rank.unsqueeze(0)
+
+
+def segmented_prefill(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: Optional[float] = None,
+                      use_qk_l2norm_in_kernel: bool = False, initial_state: Optional[Tensor] = None,
+                      local_segments: int = 8, group=None) -> tuple[Tensor, Optional[Tensor]]:
+    """Forward of a long sequence ``[1, T, ...]`` cut into ``local_segments`` pieces per rank that run side by
+    side (a batch of pieces fills the SMs when there are few heads), joined by the same affine maps as the
+    cross-rank split. With a process group of P ranks, every rank passes its contiguous slice (rank order =
+    token order) and the boundary states cross ranks over NCCL; without one, the whole sequence is local.
+    Returns ``(o, final_state)``; ``final_state`` on the last rank only. ``initial_state`` is read on rank
+    0 only. Each rank's slice length must be a multiple of ``local_segments``."""
+    if q.shape[0] != 1:
+        raise ValueError("segmented_prefill takes one sequence ([1, T, ...])")
+    dist_on = group is not None or (dist.is_available() and dist.is_initialized())
+    rank = dist.get_rank(group) if dist_on else 0
+    world = dist.get_world_size(group) if dist_on else 1
+    scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
+    P = int(local_segments)
+    if P < 1 or q.shape[1] % P:
+        raise ValueError(f"slice length {q.shape[1]} is not a multiple of local_segments = {P}")
+    q, k, v, g, beta = (x.contiguous() for x in (q, k, v, g, beta))
+    h0 = initial_state if rank == 0 else None
+    qs, ks, gs, bs, o, S_loc, Mpre, M_r, C_r = _local_split(q, k, v, g, beta, scale, use_qk_l2norm_in_kernel,
+                                                           P, h0)
+    if world > 1:
+        S_in, S_out = exchange_boundary_states(C_r, M_r if rank > 0 else None, group)
+    else:
+        S_in, S_out = None, C_r
+    # every sub-segment's incoming state that its outputs still lack: the local part and the rank's input
+    S_tot = S_loc if S_in is None else S_loc + torch.matmul(Mpre, S_in.expand(P, -1, -1, -1))
+    if P > 1 or S_in is not None:
+        apply_incoming_state(qs, ks, gs, bs, S_tot, o, scale, use_qk_l2norm_in_kernel)
+    o = o.view(1, q.shape[1], *o.shape[2:])
+    return o, (S_out if rank == world - 1 else None)
+
+
 def sequence_split_prefill(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: Optional[float] = None,
                            use_qk_l2norm_in_kernel: bool = False, group=None,
                            initial_state: Optional[Tensor] = None) -> tuple[Tensor, Optional[Tensor]]:

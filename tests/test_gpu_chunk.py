@@ -199,3 +199,21 @@ def test_chunk_backward_varlen_short_documents():
 def test_chunk_backward_large_row_config1_shape():
     x = _inputs(22, 1, 4096, 16, 16, normalized=False)
     _grads_vs_oracle(x, None, None, True)
+
+
+@pytest.mark.parametrize("P,with_h0", [(4, True), (8, False), (1, True)])
+def test_segmented_prefill_matches_one_forward(P, with_h0):
+    """The sequence cut into P local pieces joined by affine maps == one chunk forward (bf16 bar)."""
+    from sorernn_b200 import chunk_gated_delta_rule
+    from sorernn_b200.seqsplit import segmented_prefill
+
+    T, H, HV = 2048, 2, 4
+    x = _inputs(15, 1, T, H, HV, normalized=False)
+    h0 = (torch.randn(1, HV, D, D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(4)) * 0.1
+          if with_h0 else None)
+    o_ref, s_ref = chunk_gated_delta_rule(x["q"], x["k"], x["v"], x["g"], x["beta"], initial_state=h0,
+                                          output_final_state=True, use_qk_l2norm_in_kernel=True)
+    o, s = segmented_prefill(x["q"], x["k"], x["v"], x["g"], x["beta"], use_qk_l2norm_in_kernel=True,
+                             initial_state=h0, local_segments=P)
+    assert_bf16_close(to_np(o), to_np(o_ref), 2e-2, "o")
+    assert_rms_close(to_np(s), to_np(s_ref), 2e-2, "final state")

@@ -24,7 +24,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, splits, result):
+def _worker(rank, world, port, splits, result, local_segments):
     import torch.distributed as dist
 
     from helpers import assert_bf16_close, assert_rms_close, to_np
@@ -37,7 +37,7 @@ def _worker(rank, world, port, splits, result):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        B, H, HV = 2, 2, 4
+        B, H, HV = (1 if local_segments else 2), 2, 4  # segmented_prefill takes one sequence
         T = sum(splits)
         x = make_inputs(321, B, T, H, HV, D, D, normalized=False)
         h0 = np.random.default_rng(8).standard_normal((B, HV, D, D)) * 0.05
@@ -47,8 +47,13 @@ def _worker(rank, world, port, splits, result):
                                                                 torch.float32).contiguous()
                for n in ("q", "k", "v", "g", "beta")}
         h0_dev = torch.tensor(h0, dtype=torch.float32, device="cuda")
-        o, fin = seqsplit.sequence_split_prefill(dev["q"], dev["k"], dev["v"], dev["g"], dev["beta"],
-                                                 use_qk_l2norm_in_kernel=True, initial_state=h0_dev)
+        if local_segments:
+            o, fin = seqsplit.segmented_prefill(dev["q"], dev["k"], dev["v"], dev["g"], dev["beta"],
+                                                use_qk_l2norm_in_kernel=True, initial_state=h0_dev,
+                                                local_segments=local_segments)
+        else:
+            o, fin = seqsplit.sequence_split_prefill(dev["q"], dev["k"], dev["v"], dev["g"], dev["beta"],
+                                                     use_qk_l2norm_in_kernel=True, initial_state=h0_dev)
         torch.cuda.synchronize()
         # oracle on the whole sequence, from the same rounded inputs
         full = {n: x[n] for n in ("q", "k", "v", "g", "beta")}
@@ -68,11 +73,12 @@ def _worker(rank, world, port, splits, result):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sequence_split_prefill_two_ranks_nccl():
+@pytest.mark.parametrize("local_segments", [0, 4])
+def test_sequence_split_prefill_two_ranks_nccl(local_segments):
     ctx = torch.multiprocessing.get_context("spawn")
     result = ctx.Array("i", [0, 0])
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, [640, 448], result)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, [640, 448], result, local_segments)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
