@@ -380,8 +380,9 @@ def run_ours(args):
                      "peak_source": f"{peak_kind} bf16_tflops_sustained (of {peak_kind})",
                      "traffic": BWD_PASS_TRAFFIC_BYTES * B / 8,
                      "traffic_note": "ncu DRAM read+write bytes per call, batch-2 capture scaled"},
-        "decode": {"metric": "decode-step HBM GB/s (config 3: 256 seq x H16 x 128x128 fp32 state)",
-                   "value": round(dec_gbs, 1), "unit": "GB/s", "us_per_step": round(dec_ms * 1e3, 2),
+        "decode": {"metric": "decode-step HBM GB/s (config 3: 256 seq x H16 x 128x128 fp32 state per GPU)",
+                   "value": round(dec_gbs * world, 1), "unit": "GB/s (all GPUs)", "per_gpu_gbs": round(dec_gbs, 1),
+                   "us_per_step": round(dec_ms * 1e3, 2),
                    "roofline": {"bound": "hbm", "achieved": round(dec_gbs, 1), "peak": peaks["hbm_gbs"],
                                 "unit": "GB/s", "frac": round(dec_gbs / peaks["hbm_gbs"], 4),
                                 "peak_source": f"{peak_kind} hbm_gbs (of {peak_kind})",
