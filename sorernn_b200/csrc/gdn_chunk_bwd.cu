@@ -3,7 +3,9 @@
 // One CTA (512 threads) per (sequence, value head) walks the chunks in reverse, carrying dS (the gradient
 // of the state at the chunk end, fp32 in TMEM). The chunk-start states S0 are not saved by the forward:
 // a segment-parallel pass of the forward kernel (chunk_fwd in recompute mode) rebuilds them from the
-// forward's checkpoints into the workspace as bf16 operand tiles; this kernel bulk-copies one per chunk.
+// forward's checkpoints into the workspace as bf16 operand tiles, together with the chunk's T = (I + A)^-1
+// and its TB, TV scalings (so the triangular solve runs once per chunk, in that pass); this kernel
+// bulk-copies one record per chunk.
 //
 // With qn = q/nq, kn = k/nk (the raw bf16 tiles feed the tensor cores; norms are applied in fp32),
 // Gamma = in-chunk cumsum(g), E_ij = exp(Gamma_i - Gamma_j), and the forward's A, T, W, U, Delta, P
@@ -28,7 +30,6 @@
 // within the bf16 tolerance.
 #include <cstring>
 
-#include "chunk_common.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
@@ -49,10 +50,10 @@ constexpr uint32_t OFF_W = 131072;               // -W bf16 [j][dk], 2 d-blocks 
 constexpr uint32_t OFF_TB = 131072, OFF_TV = 139264;
 constexpr uint32_t OFF_T = 147456;    // T bf16 [i][j]
 constexpr uint32_t OFF_DEL = 155648;  // Delta^T bf16 [dv][j] -> Dd^T; later dG fp32 [64][64]
-constexpr uint32_t OFF_DD = 172032;   // dDelta^T bf16 [dv][j]; solve scratch before
+constexpr uint32_t OFF_DD = 172032;   // dDelta^T bf16 [dv][j]
 constexpr uint32_t OFF_PS = 188416;   // P'' bf16 [i][j] -> dPs / nk_j
 constexpr uint32_t OFF_PS2 = 196608;  // dPs / (nq_i nk_j) -> Z bf16 [j][m]
-constexpr uint32_t OFF_A = 204800;    // A -> T fp32 [64][AST]
+constexpr uint32_t OFF_A = 204800;    // 17 KB: the dDelta^T lo tile (OFF_DDL) in steps 7-8
 constexpr int AST = 68;
 constexpr int NVEC = 14;
 constexpr uint32_t OFF_VEC = OFF_A + 64 * AST * 4;     // NVEC x 64 fp32
@@ -64,9 +65,7 @@ constexpr uint32_t OFF_DVB = OFF_S0;          // dVb^T bf16 [dv][j]   (S0 dead a
 constexpr uint32_t OFF_DWT = OFF_S0 + 16384;  // dW^T bf16 [dk][i]
 constexpr uint32_t OFF_DKB = OFF_DS;          // dKb^T bf16 [dk][j]   (dS tile dead after step 8)
 constexpr uint32_t OFF_GS = OFF_DS + 16384;   // (dG + dG^T) / (nk nk) bf16 [j][m]
-constexpr uint32_t OFF_Y = OFF_DD;
-static_assert(OFF_Y + 32 * 32 * 4 <= OFF_PS, "solve scratch overlaps live tiles");
-constexpr uint32_t OFF_DDL = OFF_A;  // dDelta^T lo bf16 [dv][j] (16 KB; the fp32 solve area is dead after step 3)
+constexpr uint32_t OFF_DDL = OFF_A;  // dDelta^T lo bf16 [dv][j] (16 KB)
 // TMEM columns (fp32, 128 lanes)
 constexpr uint32_t T_S = 0, T_D1 = 128, C192 = 192, C256 = 256, C320 = 320, C384 = 384, C448 = 448, T_COLS = 512;
 }  // namespace cb
@@ -75,7 +74,7 @@ struct ChunkBwdArgs {
     CUtensorMap tq, tk, tv, tdo;
     const void* g;
     const void* beta;
-    const uint8_t* s0_tiles;  // per (chunk, head) 32 KB bf16 S0^T images
+    const uint8_t* s0_tiles;  // per (chunk, head) kBwdRecordBytes records: S0^T, TB, TV, T tile images
     const float* dht;
     void* dq;  // bf16 [tok][H][128], or fp32 accumulators when accumulate_qk
     void* dk;
@@ -204,8 +203,6 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     using namespace cb;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    float* Tm = (float*)(sm + OFF_A);
-    float* Yb = (float*)(sm + OFF_Y);
     float* dGm = (float*)(sm + OFF_DEL);
     float* vG = (float*)(sm + OFF_VEC);
     float* vEG = vG + 64;
@@ -288,7 +285,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
     auto issue_inputs = [&](int c) {
         const int tok0 = (int)(bos + 64 * c);
-        mbar_arrive_expect_tx(bar_in, 8 * 8192 + 32768);
+        mbar_arrive_expect_tx(bar_in, 8 * 8192 + 32768 + 24576);
 #pragma unroll 1
         for (int kb = 0; kb < 2; ++kb) {
             tma_load_3d(sm + OFF_QK + kb * QK_BLK, &a.tq, bar_in, kb * 64, hq, tok0);
@@ -296,7 +293,9 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             tma_load_3d(sm + OFF_V + kb * 8192, &a.tv, bar_in, kb * 64, hv, tok0);
             tma_load_3d(sm + OFF_DO + kb * 8192, &a.tdo, bar_in, kb * 64, hv, tok0);
         }
-        bulk_load(sm + OFF_S0, a.s0_tiles + ((cbase + c) * a.HV + hv) * 32768, 32768, bar_in);
+        const uint8_t* rec = a.s0_tiles + ((cbase + c) * a.HV + hv) * kBwdRecordBytes;
+        bulk_load(sm + OFF_S0, rec, 32768, bar_in);
+        bulk_load(sm + OFF_TB, rec + kBwdRecordT, 24576, bar_in);  // TB | TV | T, contiguous in both
     };
     if (tid == 0 && nchunks > 0) issue_inputs(nchunks - 1);
     uint32_t in_phase = 0, v_phase = 0;
@@ -380,59 +379,26 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         __syncthreads();
         mwait(bar_mma, mph, a.err, 12, ok);
 
-        // ---- 3. D1 -> P'' (bf16) and A (fp32); T = (I + A)^-1; TB, TV, T tiles --------------------------
-        {
+        // ---- 3. D1 rows 0-63 -> P'' (bf16 hi and lo). T and its TB, TV scalings arrived with the inputs
+        //         (the recompute pass built them for its own W and U)
+        if (lg < 2) {  // P''_ij = scale qn_i.kn_j E_ij (j <= i)
             float v[16];
             ld16c(tD1 + lb + 16 * cq, v);
-            const int i = row & 63;
-            const float gi = vG[i];
-            if (lg < 2) {  // P''_ij = scale qn_i.kn_j E_ij (j <= i)
-                const float f = a.scale * vNQ[i];
+            const int i = row;
+            const float gi = vG[i], f = a.scale * vNQ[i];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int jj = 16 * cq + j;
-                    v[j] = (jj <= i) ? f * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
-                }
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {  // hi tile, and its lo part where dPs2 goes later (idle until step 7)
-                    float lo[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) lo[e] = v[8 * q + e] - __bfloat162float(__float2bfloat16_rn(v[8 * q + e]));
-                    st8(sm + OFF_PS + sw128_off(i, 16 * cq + 8 * q), v + 8 * q);
-                    st8(sm + OFF_PS2 + sw128_off(i, 16 * cq + 8 * q), lo);
-                }
-            } else {  // A_ij = beta_i kn_i.kn_j E_ij (j < i)
-                const float bi = vB[i] * vNK[i];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int jj = 16 * cq + j;
-                    v[j] = (jj < i) ? bi * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
-                }
-                float4* dst = reinterpret_cast<float4*>(Tm + i * AST + 16 * cq);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            for (int j = 0; j < 16; ++j) {
+                const int jj = 16 * cq + j;
+                v[j] = (jj <= i) ? f * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
             }
-        }
-        __syncthreads();
-        tri_inverse64<AST>(Tm, Yb);  // T = (I + A)^-1 in place
-        {
-            const int i = tid >> 3, c8 = 8 * (tid & 7);
-            float tb[8], tv[8], tt[8];
-            const float4 t0 = *reinterpret_cast<const float4*>(Tm + i * AST + c8);
-            const float4 t1 = *reinterpret_cast<const float4*>(Tm + i * AST + c8 + 4);
-            tt[0] = t0.x; tt[1] = t0.y; tt[2] = t0.z; tt[3] = t0.w;
-            tt[4] = t1.x; tt[5] = t1.y; tt[6] = t1.z; tt[7] = t1.w;
-            float b8[8], en8[8];
-            vec8(vB, c8, b8);
-            vec8(vEN, c8, en8);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                tv[j] = tt[j] * b8[j];
-                tb[j] = tv[j] * en8[j];
+            for (int q = 0; q < 2; ++q) {  // hi tile, and its lo part where dPs2 goes later (idle until step 7)
+                float lo[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) lo[e] = v[8 * q + e] - __bfloat162float(__float2bfloat16_rn(v[8 * q + e]));
+                st8(sm + OFF_PS + sw128_off(i, 16 * cq + 8 * q), v + 8 * q);
+                st8(sm + OFF_PS2 + sw128_off(i, 16 * cq + 8 * q), lo);
             }
-            st8(sm + OFF_TB + sw128_off(i, c8), tb);
-            st8(sm + OFF_TV + sw128_off(i, c8), tv);
-            st8(sm + OFF_T + sw128_off(i, c8), tt);
         }
         fence_async_smem();
         sync_tc();
@@ -1038,7 +1004,7 @@ bool chunk_bwd_supported(int64_t DK, int64_t DV, int act_dtype) {
 
 size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t HV, bool varlen) {
     const int64_t chunks = varlen ? (B * T + 63 * N) / 64 + N : N * ((T + 63) / 64);
-    size_t bytes = (size_t)chunks * HV * 32768;  // S0 tiles
+    size_t bytes = (size_t)chunks * HV * kBwdRecordBytes;  // S0^T, TB, TV, T tiles from the recompute pass
     if (HV > H) bytes += (size_t)B * T * H * 128 * 4 * 2;  // fp32 dq/dk accumulators (grouped value heads)
     return bytes;
 }
@@ -1074,7 +1040,7 @@ int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s) {
     if (!make_tmap_3d_sw128(&a.tdo, L.dout, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
     const bool acc = L.HV > L.H;
     const int64_t chunks = L.cu ? (L.B * L.T + 63 * L.N) / 64 + L.N : L.N * ((L.T + 63) / 64);
-    float* acc_q = acc ? (float*)((uint8_t*)L.ws + (size_t)chunks * L.HV * 32768) : nullptr;
+    float* acc_q = acc ? (float*)((uint8_t*)L.ws + (size_t)chunks * L.HV * kBwdRecordBytes) : nullptr;
     float* acc_k = acc ? acc_q + Ttot * L.H * 128 : nullptr;
     if (acc && cudaMemsetAsync(acc_q, 0, (size_t)Ttot * L.H * 128 * 4 * 2, s) != cudaSuccess) return GDN_ERR_LAUNCH;
     a.g = L.g;

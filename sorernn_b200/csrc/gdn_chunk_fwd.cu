@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             const float eGC = vMisc[0];
             const bool ck = a.ckpt && !recompute && (c % a.ckpt_every == 0);
             float* ckp = ck ? a.ckpt + ((ck_base + c / a.ckpt_every) * a.HV + hv) * 16384 : nullptr;
-            uint8_t* s0g = recompute ? a.s0_out + ((cbase + c) * a.HV + hv) * 32768 : nullptr;
+            uint8_t* s0g = recompute ? a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes : nullptr;
 #pragma unroll 1
             for (int c0 = 0; c0 < 64; c0 += 16) {
                 float v[16];
@@ -466,6 +466,13 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             }
             st_chunk8(sm + OFF_TB + sw128_off(i, c8), tb);
             st_chunk8(sm + OFF_TV + sw128_off(i, c8), tv);
+            if (recompute) {  // the backward's TB, TV, T operand tiles, as shared-memory images
+                uint8_t* tg = a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes + kBwdRecordT;
+                const uint32_t off = sw128_off(i, c8);
+                *reinterpret_cast<uint4*>(tg + off) = *reinterpret_cast<const uint4*>(sm + OFF_TB + off);
+                *reinterpret_cast<uint4*>(tg + 8192 + off) = *reinterpret_cast<const uint4*>(sm + OFF_TV + off);
+                st_chunk8(tg + 16384 + off, t);
+            }
         }
         fence_async_smem();
         block_sync_tc();

@@ -34,11 +34,17 @@ struct ChunkLaunch {
     float scale;
     int g_dtype, beta_dtype, l2norm, zero_v, o_mode, h0_identity, ht_accumulate, ckpt_every;
     // recompute mode (used by the backward): when s0_out is set, ckpt is READ (the forward's checkpoints),
-    // one CTA per (sequence, head, segment of ckpt_every chunks) restarts from its checkpoint and writes every
-    // chunk's bf16 S0^T operand tile (32 KB) to s0_out; no outputs, no final state.
+    // one CTA per (sequence, head, segment of ckpt_every chunks) restarts from its checkpoint and writes one
+    // kBwdRecordBytes record per (chunk, head) to s0_out: the bf16 S0^T operand tile (32 KB) and the bf16
+    // TB, TV, T operand tiles of the chunk's WY transform (8 KB each); no outputs, no final state.
     void* s0_out;
     int64_t max_seqlen;
 };
+
+// Per-(chunk, head) record the recompute pass writes for the backward sweep: shared-memory images of
+// [S0^T bf16 (2 x 16 KB) | TB | TV | T (8 KB each)], each in the 128-byte-swizzled operand layout.
+constexpr size_t kBwdRecordBytes = 57344;
+constexpr size_t kBwdRecordT = 32768;  // offset of the TB, TV, T tiles (24 KB, contiguous)
 
 // Arguments of the chunked backward.
 struct ChunkBwdLaunch {
