@@ -46,8 +46,7 @@ constexpr uint32_t OFF_V = 32768;                // [kb][8 KB]
 constexpr uint32_t OFF_DO = 49152;               // [kb][8 KB]
 constexpr uint32_t OFF_S0 = 65536;               // S0^T bf16 [dv][dk], 2 dk-blocks x 16 KB (workspace image)
 constexpr uint32_t OFF_DS = 98304;               // dS^T bf16 [dv][dk]
-constexpr uint32_t OFF_W = 131072;               // -W bf16 [j][dk], 2 d-blocks x 8 KB (TB, TV before)
-constexpr uint32_t OFF_TB = 131072, OFF_TV = 139264;
+constexpr uint32_t OFF_W = 131072;               // -W bf16 [j][dk], 2 d-blocks x 8 KB
 constexpr uint32_t OFF_T = 147456;    // T bf16 [i][j]
 constexpr uint32_t OFF_DEL = 155648;  // Delta^T bf16 [dv][j] -> Dd^T; later dG fp32 [64][64]
 constexpr uint32_t OFF_DD = 172032;   // dDelta^T bf16 [dv][j]
@@ -285,17 +284,20 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
     auto issue_inputs = [&](int c) {
         const int tok0 = (int)(bos + 64 * c);
-        mbar_arrive_expect_tx(bar_in, 8 * 8192 + 32768 + 24576);
+        mbar_arrive_expect_tx(bar_in, 6 * 8192 + 32768 + 24576 + 2 * 16384);
 #pragma unroll 1
         for (int kb = 0; kb < 2; ++kb) {
             tma_load_3d(sm + OFF_QK + kb * QK_BLK, &a.tq, bar_in, kb * 64, hq, tok0);
             tma_load_3d(sm + OFF_QK + kb * QK_BLK + 8192, &a.tk, bar_in, kb * 64, hq, tok0);
-            tma_load_3d(sm + OFF_V + kb * 8192, &a.tv, bar_in, kb * 64, hv, tok0);
             tma_load_3d(sm + OFF_DO + kb * 8192, &a.tdo, bar_in, kb * 64, hv, tok0);
         }
+        // the recompute pass's record: S0^T, -W | T (contiguous here and there), Delta^T, and the Dd^T low
+        // part where V goes later (V arrives after step 8 on bar_v)
         const uint8_t* rec = a.s0_tiles + ((cbase + c) * a.HV + hv) * kBwdRecordBytes;
         bulk_load(sm + OFF_S0, rec, 32768, bar_in);
-        bulk_load(sm + OFF_TB, rec + kBwdRecordT, 24576, bar_in);  // TB | TV | T, contiguous in both
+        bulk_load(sm + OFF_W, rec + kBwdRecW, 24576, bar_in);
+        bulk_load(sm + OFF_DEL, rec + kBwdRecDel, 16384, bar_in);
+        bulk_load(sm + OFF_V, rec + kBwdRecDdl, 16384, bar_in);
     };
     if (tid == 0 && nchunks > 0) issue_inputs(nchunks - 1);
     uint32_t in_phase = 0, v_phase = 0;
@@ -379,8 +381,9 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         __syncthreads();
         mwait(bar_mma, mph, a.err, 12, ok);
 
-        // ---- 3. D1 rows 0-63 -> P'' (bf16 hi and lo). T and its TB, TV scalings arrived with the inputs
-        //         (the recompute pass built them for its own W and U)
+        // ---- 3. D1 rows 0-63 -> P'' (bf16 hi and lo); dS^T -> hi tile and <dS, S0>. T, -W, Delta^T and
+        //         the Dd^T low part arrived with the inputs (the recompute pass built them for its own state
+        //         update)
         if (lg < 2) {  // P''_ij = scale qn_i.kn_j E_ij (j <= i)
             float v[16];
             ld16c(tD1 + lb + 16 * cq, v);
@@ -399,22 +402,6 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 st8(sm + OFF_PS + sw128_off(i, 16 * cq + 8 * q), v + 8 * q);
                 st8(sm + OFF_PS2 + sw128_off(i, 16 * cq + 8 * q), lo);
             }
-        }
-        fence_async_smem();
-        sync_tc();
-
-        // ---- 4. R2 [W; -] = [TB; TV] K (384-511, W rows on lanes 0-63), R3 U^T = V^T TV^T (256);
-        //         meanwhile dS^T -> hi tile
-        if (tid == 0) {
-            const uint32_t id = idesc_bf16(128, 64, 1, 0);
-#pragma unroll 1
-            for (int ks = 0; ks < 4; ++ks) {
-                umma_bf16(tm + C384, desc_kmajor(sb + OFF_TB + ks * 32), desc_mnmajor(aK + ks * 2048, QK_BLK),
-                          idesc_bf16(128, 128, 0, 1), ks > 0);
-                umma_bf16(tm + C256, desc_mnmajor(aV + ks * 2048, 8192), desc_kmajor(sb + OFF_TV + ks * 32), id,
-                          ks > 0);
-            }
-            umma_commit(bar_mma);
         }
         {  // dS^T -> bf16 hi tile (the lo part follows in step 8b), <dS, S0>
             float dss = 0.f;
@@ -435,50 +422,6 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
             dss = warp_sum(dss);
             if (lane == 0) scal[1 + warp] = dss;
-        }
-        mwait(bar_mma, mph, a.err, 13, ok);
-        if (lg < 2) {  // W rows j (lanes 0-63) -> -W bf16 [j][d], d = 32 cq .. 32 cq + 31, 16-byte stores
-            float v[32];
-            uint8_t* dst = sm + OFF_W + (cq >> 1) * 8192;
-            ld32c(tm + C384 + lb + 32 * cq, v);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = -v[e];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) st8(dst + sw128_off(row, 32 * (cq & 1) + 8 * q), v + 8 * q);
-        }
-        fence_async_smem();
-        sync_tc();
-
-        // ---- 5. R4: Delta^T = U^T + S0^T (-W)^T (256) -------------------------------------------------
-        if (tid == 0) {
-            const uint32_t id = idesc_bf16(128, 64, 0, 0);
-#pragma unroll 1
-            for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tm + C256, desc_kmajor(sb + OFF_S0 + kb * 16384 + ko),
-                          desc_kmajor(sb + OFF_W + kb * 8192 + ko), id, 1);
-            }
-            umma_commit(bar_mma);
-        }
-        mwait(bar_mma, mph, a.err, 14, ok);
-        {
-            float v[16], x16[16];
-            ld16c(tm + C256 + lb + 16 * cq, v);
-            vec16(vX, 16 * cq, x16);
-            // Delta^T hi tile; and the lo part of Dd = Delta diag(vX) relative to the hi part that step 7
-            // derives in place (bf16(bf16(Delta) vX)), stored where V was (V is reloaded for step 10)
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                float lo[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float x = x16[8 * q + e];
-                    const float dh = __bfloat162float(__float2bfloat16_rn(v[8 * q + e]));
-                    lo[e] = v[8 * q + e] * x - __bfloat162float(__float2bfloat16_rn(dh * x));
-                }
-                st8(sm + OFF_DEL + sw128_off(row, 16 * cq + 8 * q), v + 8 * q);
-                st8(sm + OFF_V + sw128_off(row, 16 * cq + 8 * q), lo);
-            }
         }
         fence_async_smem();
         sync_tc();
@@ -543,14 +486,28 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             float d1[16], d2[16], de[16], x16[16];
             tmem_ld16(tm + C320 + lb + 16 * cq, d1);
             tmem_ld16(tm + C384 + lb + 16 * cq, d2);
-            tmem_ld16(tm + C256 + lb + 16 * cq, de);
             vec16(vX, 16 * cq, x16);
+            // Delta x (= Dd) to ~16 bits: bf16(bf16(Delta) x) from the Delta^T tile plus the Dd^T low part
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t off = sw128_off(row, 16 * cq + 8 * h);
+                const uint4 dh = *reinterpret_cast<const uint4*>(sm + OFF_DEL + off);
+                const uint4 dl = *reinterpret_cast<const uint4*>(sm + OFF_V + off);
+                const __nv_bfloat162* ph = reinterpret_cast<const __nv_bfloat162*>(&dh);
+                const __nv_bfloat162* pl = reinterpret_cast<const __nv_bfloat162*>(&dl);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 fh = __bfloat1622float2(ph[e]), fl = __bfloat1622float2(pl[e]);
+                    const int j = 8 * h + 2 * e;
+                    de[j] = __bfloat162float(__float2bfloat16_rn(fh.x * x16[j])) + fl.x;
+                    de[j + 1] = __bfloat162float(__float2bfloat16_rn(fh.y * x16[j + 1])) + fl.y;
+                }
+            }
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                const float x = x16[j];
-                de[j] = de[j] * d2[j] * x;  // kn_j . dKst_j partial over this lane (dv)
-                d1[j] = fmaf(d2[j], x, d1[j]);
+                de[j] = de[j] * d2[j];  // kn_j . dKst_j partial over this lane (dv)
+                d1[j] = fmaf(d2[j], x16[j], d1[j]);
             }
 #pragma unroll
             for (int q = 0; q < 2; ++q) {

@@ -466,13 +466,8 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             }
             st_chunk8(sm + OFF_TB + sw128_off(i, c8), tb);
             st_chunk8(sm + OFF_TV + sw128_off(i, c8), tv);
-            if (recompute) {  // the backward's TB, TV, T operand tiles, as shared-memory images
-                uint8_t* tg = a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes + kBwdRecordT;
-                const uint32_t off = sw128_off(i, c8);
-                *reinterpret_cast<uint4*>(tg + off) = *reinterpret_cast<const uint4*>(sm + OFF_TB + off);
-                *reinterpret_cast<uint4*>(tg + 8192 + off) = *reinterpret_cast<const uint4*>(sm + OFF_TV + off);
-                st_chunk8(tg + 16384 + off, t);
-            }
+            if (recompute)  // the backward's T operand tile
+                st_chunk8(a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes + kBwdRecT + sw128_off(i, c8), t);
         }
         fence_async_smem();
         block_sync_tc();
@@ -503,6 +498,11 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             for (int e = 0; e < 32; ++e) v[e] = -v[e];
 #pragma unroll
             for (int q = 0; q < 4; ++q) st_chunk8(dst + sw128_off(row, 32 * (cq & 1) + 8 * q), v + 8 * q);
+            if (recompute) {  // the backward's -W operand tile
+                uint8_t* wg = a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes + kBwdRecW + (cq >> 1) * 8192;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) st_chunk8(wg + sw128_off(row, 32 * (cq & 1) + 8 * q), v + 8 * q);
+            }
         }
         fence_async_smem();
         block_sync_tc();
@@ -533,16 +533,31 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (l) Delta^T (TMEM, lane = dv) -> hi/lo bf16 Delta^T and Dd^T (K-major A operands)
         {
-            float v[16], w2[16];
+            float v[16], x16[16], w2[16];
             ld16(tU + lane_base + 16 * cq, v);
-            vecN(vX, 16 * cq, w2);
+            vecN(vX, 16 * cq, x16);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) w2[j] *= v[j];
+            for (int j = 0; j < 16; ++j) w2[j] = v[j] * x16[j];
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 const uint32_t off = sw128_off(row, 16 * cq + 8 * q);
                 st_chunk8_split(sm + OFF_D + off, sm + OFF_DL + off, v + 8 * q);
                 st_chunk8_split(sm + OFF_DD + off, sm + OFF_DDL + off, w2 + 8 * q);
+            }
+            if (recompute) {  // the backward's Delta^T tile and Dd^T low part (relative to bf16(bf16(Delta) x))
+                uint8_t* rg = a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes;
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const uint32_t off = sw128_off(row, 16 * cq + 8 * q);
+                    float lo[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float dh = __bfloat162float(__float2bfloat16_rn(v[8 * q + e]));
+                        lo[e] = w2[8 * q + e] - __bfloat162float(__float2bfloat16_rn(dh * x16[8 * q + e]));
+                    }
+                    st_chunk8(rg + kBwdRecDel + off, v + 8 * q);
+                    st_chunk8(rg + kBwdRecDdl + off, lo);
+                }
             }
         }
         fence_async_smem();

@@ -35,16 +35,21 @@ struct ChunkLaunch {
     int g_dtype, beta_dtype, l2norm, zero_v, o_mode, h0_identity, ht_accumulate, ckpt_every;
     // recompute mode (used by the backward): when s0_out is set, ckpt is READ (the forward's checkpoints),
     // one CTA per (sequence, head, segment of ckpt_every chunks) restarts from its checkpoint and writes one
-    // kBwdRecordBytes record per (chunk, head) to s0_out: the bf16 S0^T operand tile (32 KB) and the bf16
-    // TB, TV, T operand tiles of the chunk's WY transform (8 KB each); no outputs, no final state.
+    // kBwdRecordBytes record per (chunk, head) to s0_out (the operand tiles listed below); no outputs, no
+    // final state.
     void* s0_out;
     int64_t max_seqlen;
 };
 
-// Per-(chunk, head) record the recompute pass writes for the backward sweep: shared-memory images of
-// [S0^T bf16 (2 x 16 KB) | TB | TV | T (8 KB each)], each in the 128-byte-swizzled operand layout.
-constexpr size_t kBwdRecordBytes = 57344;
-constexpr size_t kBwdRecordT = 32768;  // offset of the TB, TV, T tiles (24 KB, contiguous)
+// Per-(chunk, head) record the recompute pass writes for the backward sweep: shared-memory images, in the
+// 128-byte-swizzled operand layouts, of the chunk's S0^T (bf16 [dv][dk], 32 KB), -W (bf16 [j][dk], 16 KB),
+// T = (I + A)^-1 (bf16 [i][j], 8 KB), Delta^T (bf16 [dv][j], 16 KB) and the low part of
+// Dd^T = Delta^T diag(e^(G_C - G) / nk) relative to bf16(bf16(Delta^T) diag(...)) (16 KB).
+constexpr size_t kBwdRecordBytes = 90112;
+constexpr size_t kBwdRecW = 32768;    // -W then T: 24 KB contiguous
+constexpr size_t kBwdRecT = 49152;
+constexpr size_t kBwdRecDel = 57344;  // Delta^T
+constexpr size_t kBwdRecDdl = 73728;  // Dd^T low part
 
 // Arguments of the chunked backward.
 struct ChunkBwdLaunch {
