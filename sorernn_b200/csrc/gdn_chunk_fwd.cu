@@ -118,6 +118,16 @@ __device__ __forceinline__ void st_chunk8_split(uint8_t* hi, uint8_t* lo, const 
     st_chunk8(lo, l);
 }
 
+// bulk (TMA) copy shared -> global, tracked by the issuing thread's bulk groups
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"((uint64_t)dst),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void block_sync_tc() {
     tc_fence_before();
     __syncthreads();
@@ -313,6 +323,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         const uint32_t aBlk = sbase + OFF_QK, aV = sbase + OFF_V;
         const uint32_t aK = aBlk + kofs, aQ = aBlk + 8192;  // d-block 0 of K and Q
         const uint32_t aA1 = s ? aK : aQ;                   // MMA1's 128-row A: [Q;K] even, [K;Q] odd
+        uint8_t* rec_g = recompute ? a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes : nullptr;
 
         // (a) gates: Gamma = cumsum(g) inside the chunk, beta; padded rows carry g = 0, beta = 0
         if (tid < 64) {
@@ -378,6 +389,9 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             vX[tid] = __expf(vG[63] - vG[tid]) * vNK[tid];  // includes 1/nk: Dd = diag(e^(G_C-G)/nk) Delta
         }
         if (tid == 64) vMisc[0] = __expf(vG[63]);
+        // recompute mode: the previous chunk's bulk stores must have read their tiles before (f) and (g)
+        // overwrite them
+        if (recompute && tid == 0) bulk_wait_read_all();
         __syncthreads();
 
         wait_mma(bar_mma, mma_phase, a.err, 2, ok);
@@ -387,6 +401,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             float v[16];
             ld16(tD1 + lane_base + 16 * cq, v);
             if ((lg < 2) == (s == 0)) {  // Q K^T row i (rows 0-63 on even chunks, 64-127 on odd)
+              if (!recompute) {  // no outputs in recompute mode: OFF_P carries the backward's T tile instead
                 const int i = row & 63;
                 const float gi = vG[i];
 #pragma unroll
@@ -398,6 +413,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 for (int q = 0; q < 2; ++q)
                     st_chunk8_split(sm + OFF_P + sw128_off(i, 16 * cq + 8 * q),
                                     sm + OFF_PL + sw128_off(i, 16 * cq + 8 * q), v + 8 * q);
+              }
             } else {  // K K^T row i
                 const int i = row & 63;
                 const float gi = vG[i], bi = vB[i] * vNK[i];
@@ -422,7 +438,6 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             const float eGC = vMisc[0];
             const bool ck = a.ckpt && !recompute && (c % a.ckpt_every == 0);
             float* ckp = ck ? a.ckpt + ((ck_base + c / a.ckpt_every) * a.HV + hv) * 16384 : nullptr;
-            uint8_t* s0g = recompute ? a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes : nullptr;
 #pragma unroll 1
             for (int c0 = 0; c0 < 64; c0 += 16) {
                 float v[16];
@@ -432,10 +447,6 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 const uint32_t o0 = blk + sw128_off(row, c0), o1 = blk + sw128_off(row, c0 + 8);
                 st_chunk8_split(sm + OFF_S + o0, sm + OFF_SL + o0, v);
                 st_chunk8_split(sm + OFF_S + o1, sm + OFF_SL + o1, v + 8);
-                if (recompute) {  // the backward's S0^T operand tile: the same bytes, in the workspace
-                    *reinterpret_cast<uint4*>(s0g + o0) = *reinterpret_cast<const uint4*>(sm + OFF_S + o0);
-                    *reinterpret_cast<uint4*>(s0g + o1) = *reinterpret_cast<const uint4*>(sm + OFF_S + o1);
-                }
                 if (ck) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) ckp[(64 * half + c0 + i) * 128 + row] = v[i];
@@ -445,8 +456,10 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 tmem_st16(tS + lane_base + 64 * half + c0, v);
             }
             tmem_wait_st();
+            fence_async_smem();
         }
         __syncthreads();
+        if (recompute && tid == 0) bulk_s2g(rec_g, sm + OFF_S, 32768);  // S0^T hi tile
 
         // (h) TB = T diag(beta e^G / nk), TV = T diag(beta)  (bf16, K-major [i][j])
         {
@@ -466,8 +479,8 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             }
             st_chunk8(sm + OFF_TB + sw128_off(i, c8), tb);
             st_chunk8(sm + OFF_TV + sw128_off(i, c8), tv);
-            if (recompute)  // the backward's T operand tile
-                st_chunk8(a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes + kBwdRecT + sw128_off(i, c8), t);
+            if (recompute)  // the backward's T operand tile, right after -W (P' is not formed in this mode)
+                st_chunk8(sm + OFF_P + sw128_off(i, c8), t);
         }
         fence_async_smem();
         block_sync_tc();
@@ -498,14 +511,10 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             for (int e = 0; e < 32; ++e) v[e] = -v[e];
 #pragma unroll
             for (int q = 0; q < 4; ++q) st_chunk8(dst + sw128_off(row, 32 * (cq & 1) + 8 * q), v + 8 * q);
-            if (recompute) {  // the backward's -W operand tile
-                uint8_t* wg = a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes + kBwdRecW + (cq >> 1) * 8192;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) st_chunk8(wg + sw128_off(row, 32 * (cq & 1) + 8 * q), v + 8 * q);
-            }
         }
         fence_async_smem();
         block_sync_tc();
+        if (recompute && tid == 0) bulk_s2g(rec_g + kBwdRecW, sm + OFF_W, 24576);  // -W | T (at OFF_P)
 
         // (k) MMA4: U^T += (S0hi + S0lo)^T (-W)^T -> Delta^T ; MMA5: [-; O1] = [-; Q] S0hi (O1 rows on
         //     lanes 64-127, N = dv = 128)   (K = dk = 128)
@@ -541,27 +550,25 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 const uint32_t off = sw128_off(row, 16 * cq + 8 * q);
-                st_chunk8_split(sm + OFF_D + off, sm + OFF_DL + off, v + 8 * q);
                 st_chunk8_split(sm + OFF_DD + off, sm + OFF_DDL + off, w2 + 8 * q);
-            }
-            if (recompute) {  // the backward's Delta^T tile and Dd^T low part (relative to bf16(bf16(Delta) x))
-                uint8_t* rg = a.s0_out + ((cbase + c) * a.HV + hv) * kBwdRecordBytes;
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const uint32_t off = sw128_off(row, 16 * cq + 8 * q);
+                if (!recompute) {
+                    st_chunk8_split(sm + OFF_D + off, sm + OFF_DL + off, v + 8 * q);
+                } else {  // the backward's Delta^T tile and Dd^T low part (relative to bf16(bf16(Delta) x)),
+                          // staged where MMA6's operands would go (no outputs in this mode)
                     float lo[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         const float dh = __bfloat162float(__float2bfloat16_rn(v[8 * q + e]));
                         lo[e] = w2[8 * q + e] - __bfloat162float(__float2bfloat16_rn(dh * x16[8 * q + e]));
                     }
-                    st_chunk8(rg + kBwdRecDel + off, v + 8 * q);
-                    st_chunk8(rg + kBwdRecDdl + off, lo);
+                    st_chunk8(sm + OFF_D + off, v + 8 * q);
+                    st_chunk8(sm + OFF_DL + off, lo);
                 }
             }
         }
         fence_async_smem();
         block_sync_tc();
+        if (recompute && tid == 0) bulk_s2g(rec_g + kBwdRecDel, sm + OFF_D, 32768);  // Delta^T | Dd^T lo
 
         // (m) MMA6: O2^T = Delta^T P'^T (hi.hi + lo.hi + hi.lo) ; MMA7: S^T += Dd^T K (hi + lo), N = 128
         // [-; O2] = [-; P'] Delta: the 64 rows below each P' tile (TV for P' hi, P' hi for P' lo, both
@@ -630,6 +637,8 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
         block_sync_tc();
     }
+
+    if (recompute && tid == 0) bulk_wait_all();  // the last chunk's record is in global memory
 
     // final state
     if (ok && a.ht) {
