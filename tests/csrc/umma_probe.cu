@@ -2,7 +2,10 @@
 // tests/_build/libumma_probe.so by tests/csrc/build_probe.py; never part of the product library):
 //   * umma_probe: one CTA computes D[128 x N] = A[128 x K] * B[N x K]^T with tcgen05.mma from shared-memory
 //     operands in every major-ness combination (K-major / MN-major), accumulator read back with tcgen05.ld;
-//   * tma_probe: one 128-byte-swizzled TMA tile load, de-swizzled by the layout formula the kernels use.
+//   * tma_probe: one 128-byte-swizzled TMA tile load, de-swizzled by the layout formula the kernels use;
+//   * wait_timeout_probe: the kernels' bounded mbarrier wait on a barrier nothing arrives on: it must give
+//     up after its poll limit, record the error code and return (no trap, no hang), leaving the context
+//     usable.
 #include <cuda_bf16.h>
 
 #include "../../sorernn_b200/csrc/sm100.cuh"
@@ -104,5 +107,27 @@ extern "C" int tma_probe(const void* src, long T, long H, int t0, int h, int hal
     CUtensorMap m;
     if (!gdn::make_tmap_3d_sw128(&m, src, 128, H, T, 128, H * 128, 64)) return -1;
     tma_probe_kernel<<<1, 128, 0, s>>>(m, half * 64, h, t0, (__nv_bfloat16*)out, err);
+    return (int)cudaGetLastError();
+}
+
+// One CTA: thread 0 inits an mbarrier expecting one arrival that never comes and waits on it with the
+// kernels' bounded wait (mbar_wait) and `limit` polls; every thread then waits on the same barrier
+// once more with limit 1 (the kernels' "already failed" mode). out[0] = 1 if the first wait reported
+// success, out[1] = number of threads whose second wait reported success; *err receives the code.
+__global__ void wait_timeout_probe_kernel(int* err, int* out, unsigned limit) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) out[0] = mbar_wait(&bar, 0, err, 77, limit) ? 1 : 0;
+    __syncthreads();
+    const bool ok2 = mbar_wait(&bar, 0, err, 78, 1u);
+    if (ok2) atomicAdd(&out[1], 1);
+}
+
+extern "C" int wait_timeout_probe(int* err, int* out, unsigned limit, cudaStream_t s) {
+    wait_timeout_probe_kernel<<<1, 64, 0, s>>>(err, out, limit);
     return (int)cudaGetLastError();
 }

@@ -22,6 +22,7 @@ def probe():
     vp = ctypes.c_void_p
     lib.umma_probe.argtypes = [vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp]
     lib.tma_probe.argtypes = [vp, ctypes.c_long, ctypes.c_long, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp, vp]
+    lib.wait_timeout_probe.argtypes = [vp, vp, ctypes.c_uint, vp]
     return lib
 
 
@@ -55,3 +56,18 @@ def test_tma_sw128_tile(probe, t0, h, half):
     n = min(64, T - t0)
     want[:n] = src[t0:t0 + n, h, half * 64:(half + 1) * 64]
     assert torch.equal(out, want)
+
+
+def test_bounded_wait_gives_up_and_reports(probe):
+    """A wait that nothing satisfies ends after its poll limit with the error code recorded; the context
+    stays usable (a later launch and copy succeed)."""
+    lib = probe
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.zeros(2, dtype=torch.int32, device="cuda")
+    assert lib.wait_timeout_probe(ctypes.c_void_p(err.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                  ctypes.c_uint(2000), None) == 0
+    torch.cuda.synchronize()
+    assert err.item() == 77, "the first timed-out wait records its code (first error wins)"
+    assert out.tolist() == [0, 0], "neither wait may report success"
+    x = torch.arange(1024, device="cuda", dtype=torch.float32)
+    assert float((x * 2).sum().item()) == 2.0 * 1023 * 1024 / 2
