@@ -403,17 +403,24 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 st8(sm + OFF_PS2 + sw128_off(i, 16 * cq + 8 * q), lo);
             }
         }
-        {  // dS^T -> bf16 hi tile (the lo part follows in step 8b), <dS, S0>
+        {  // dS^T -> bf16 hi tile and its lo part (dk block 0 at OFF_DD, 1 at OFF_A: both idle until step 7),
+           // <dS, S0>
             float dss = 0.f;
+            uint8_t* lo_blk = sm + ((cq >> 1) ? OFF_A : OFF_DD);
 #pragma unroll 1
             for (int c0 = 0; c0 < 32; c0 += 16) {
-                float v[16];
+                float v[16], lo[16];
                 tmem_ld16(tS + lb + 32 * cq + c0, v);
                 tmem_wait_ld();
                 const uint32_t cb_ = 32 * (cq & 1) + c0;
-                const uint32_t o0 = (cq >> 1) * 16384 + sw128_off(row, cb_), o1 = (cq >> 1) * 16384 + sw128_off(row, cb_ + 8);
+                const uint32_t s0 = sw128_off(row, cb_), s1 = sw128_off(row, cb_ + 8);
+                const uint32_t o0 = (cq >> 1) * 16384 + s0, o1 = (cq >> 1) * 16384 + s1;
                 st8(sm + OFF_DS + o0, v);
                 st8(sm + OFF_DS + o1, v + 8);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) lo[e] = v[e] - __bfloat162float(__float2bfloat16_rn(v[e]));
+                st8(lo_blk + s0, lo);
+                st8(lo_blk + s1, lo + 8);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     dss = fmaf(v[e], bfv(sm + OFF_S0, o0 + 2 * e), dss);
@@ -426,7 +433,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         fence_async_smem();
         sync_tc();
 
-        // ---- 6. dO^T P''^T (320); dS^T K^T (384); dP = [dO;-] Delta^T (448); QA = S0 dO^T (192) ---------
+        // ---- 6. dO^T P''^T (320); dS^T K^T, hi and lo (384); dP = [dO;-] Delta^T (448); QA = S0 dO^T (192)
         if (tid == 0) {
             const uint32_t id_mm = idesc_bf16(128, 64, 1, 1), id_kk = idesc_bf16(128, 64, 0, 0);
             const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
@@ -443,6 +450,8 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 umma_bf16(tm + C384, desc_kmajor(sb + OFF_DS + kb * 16384 + ko), desc_kmajor(aK + kb * QK_BLK + ko),
                           id_kk, ks > 0);
+                umma_bf16(tm + C384, desc_kmajor(sb + (kb ? OFF_A : OFF_DD) + ko), desc_kmajor(aK + kb * QK_BLK + ko),
+                          id_kk, 1);  // dS lo . K
                 umma_bf16(tm + C448, desc_kmajor(aDO + kb * 8192 + ko), desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192),
                           id_km, ks > 0);
                 umma_bf16(tm + C192, desc_mnmajor(sb + OFF_S0 + ks * 2048, 16384), desc_kmajor(aDO + kb * 8192 + ko),
@@ -451,35 +460,6 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             umma_commit(bar_mma);
         }
         mwait(bar_mma, mph, a.err, 15, ok);
-
-        // ---- 6b. lo part of dS^T K^T: overwrite the dS tile with dS - bf16(dS) and accumulate into (384);
-        //          step 7 restores the hi tile for the dS Dd^T products of step 8.
-        {
-#pragma unroll 1
-            for (int c0 = 0; c0 < 32; c0 += 16) {
-                float v[16];
-                tmem_ld16(tS + lb + 32 * cq + c0, v);
-                tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) v[e] -= __bfloat162float(__float2bfloat16_rn(v[e]));
-                const uint32_t blk = (cq >> 1) * 16384, cb_ = 32 * (cq & 1) + c0;
-                st8(sm + OFF_DS + blk + sw128_off(row, cb_), v);
-                st8(sm + OFF_DS + blk + sw128_off(row, cb_ + 8), v + 8);
-            }
-        }
-        fence_async_smem();
-        sync_tc();
-        if (tid == 0) {
-            const uint32_t id_kk = idesc_bf16(128, 64, 0, 0);
-#pragma unroll 1
-            for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tm + C384, desc_kmajor(sb + OFF_DS + kb * 16384 + ko), desc_kmajor(aK + kb * QK_BLK + ko),
-                          id_kk, 1);
-            }
-            umma_commit(bar_mma);
-        }
-        mwait(bar_mma, mph, a.err, 22, ok);
 
         // ---- 7. dDelta^T = (320) + (384) diag(vX) -> tile; r4; dP -> dPs tiles, X_P sums -------------------
         {
@@ -588,17 +568,6 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                     h[k2] = __floats2bfloat162_rn(z.x * x16[j], z.y * x16[j + 1]);
                 }
                 *reinterpret_cast<uint4*>(sm + OFF_DEL + off) = u;
-            }
-        }
-        {  // restore the dS hi tile (the lo part is in it since step 6b)
-#pragma unroll 1
-            for (int c0 = 0; c0 < 32; c0 += 16) {
-                float v[16];
-                tmem_ld16(tS + lb + 32 * cq + c0, v);
-                tmem_wait_ld();
-                const uint32_t blk = (cq >> 1) * 16384, cb_ = 32 * (cq & 1) + c0;
-                st8(sm + OFF_DS + blk + sw128_off(row, cb_), v);
-                st8(sm + OFF_DS + blk + sw128_off(row, cb_ + 8), v + 8);
             }
         }
         fence_async_smem();
