@@ -155,6 +155,36 @@ int gdn_beta_sigmoid_bwd(int64_t n, const void* b, int32_t b_dtype, const float*
                          gdn_stream_t stream);
 
 /*
+ * The layer's output step in one pass: y = RMSNorm(x) * weight * silu(gate) per row of D features
+ * (sore/model/gdn.py:180-188 with FLA's rms_norm_gated, activation "swish", no bias; RMSNorm of
+ * sore/model/layers.py:15-18: x * rsqrt(mean(x^2) + eps), fp32 math, one rounding to the act dtype).
+ * x, gate, y, dy, dx, dgate [rows, D] (act dtype), weight [D] (w_dtype), D a multiple of 32, <= 1024.
+ * Replaces: fla.modules.fused_norm_gate.rms_norm_gated. The backward writes dx, dgate (act dtype) and
+ * dweight (fp32 [D], zeroed by the call itself).
+ */
+int gdn_rms_norm_gated_fwd(int64_t rows, int64_t D, const void* x, const void* gate, int32_t act_dtype,
+                           const void* weight, int32_t w_dtype, float eps, void* y, gdn_stream_t stream);
+int gdn_rms_norm_gated_bwd(int64_t rows, int64_t D, const void* x, const void* gate, int32_t act_dtype,
+                           const void* weight, int32_t w_dtype, float eps, const void* dy, void* dx,
+                           void* dgate, float* dweight, gdn_stream_t stream);
+
+/*
+ * The layer's q/k/v prologue: short causal depthwise convolution, optionally followed by SiLU
+ * (sore/model/conv.py:6-23, FLA causal_conv1d at sore/model/gdn.py:199-207):
+ *   z[t, c] = sum_{j < K} w[c, K-1-j] x[t-j, c] over taps inside t's document,  y = silu(z) if silu.
+ * x, y, dy, dx [B, T, C] (act dtype, 16-byte aligned, C a multiple of 8), weight [C, K] (w_dtype),
+ * 1 <= K <= 4, C * K <= 16384. Documents are the batch rows, or with cu_seqlens (int64 [N+1], B == 1)
+ * the packed spans. Replaces: fla.modules.conv.causal_conv1d (activation "silu", no bias, no cache).
+ * The backward writes dx and dweight (fp32 [C, K], zeroed by the call itself).
+ */
+int gdn_causal_conv1d_fwd(int64_t B, int64_t T, int64_t C, int64_t K, const void* x, int32_t act_dtype,
+                          const void* weight, int32_t w_dtype, const int64_t* cu_seqlens, int64_t N,
+                          int32_t silu, void* y, gdn_stream_t stream);
+int gdn_causal_conv1d_bwd(int64_t B, int64_t T, int64_t C, int64_t K, const void* x, int32_t act_dtype,
+                          const void* weight, int32_t w_dtype, const int64_t* cu_seqlens, int64_t N,
+                          int32_t silu, const void* dy, void* dx, float* dweight, gdn_stream_t stream);
+
+/*
  * Sequence split (no counterpart in the reference, which has no context parallelism: soreRNN only
  * grows the context by curriculum, configs/b0_8_pretrain.yaml:18-20). A segment of tokens maps the
  * state entering it to S_out = M S_in + C, where C is gdn_chunk_fwd's final_state from a zero state

@@ -190,3 +190,27 @@ def gate_and_beta(a, b, A_log, dt_bias):
     g = -np.exp(np.asarray(A_log, np.float64)) * sp
     beta = 1.0 / (1.0 + np.exp(-np.asarray(b, np.float64)))
     return g, beta
+
+
+def rms_norm_gated(x, g, weight, eps):
+    """The layer's output step (gdn.py:180-188; RMSNorm of layers.py:15-18):
+    ``x * rsqrt(mean(x^2, -1) + eps) * weight * silu(g)``, in fp64."""
+    x, g, w = (np.asarray(t, np.float64) for t in (x, g, weight))
+    r = 1.0 / np.sqrt((x * x).mean(-1, keepdims=True) + eps)
+    return x * r * w * (g / (1.0 + np.exp(-g)))
+
+
+def causal_conv1d(x, weight, doc_ids=None, silu=True):
+    """The layer's q/k/v prologue (sore/model/conv.py:6-23, then F.silu at gdn.py:210):
+    ``z_t = sum_j weight[:, K-1-j] x_{t-j}`` over taps of t's document; ``x [B,T,C]``, ``weight [C,K]``,
+    ``doc_ids [T]`` (None = one document per batch row). fp64."""
+    x, w = np.asarray(x, np.float64), np.asarray(weight, np.float64)
+    T, K = x.shape[1], w.shape[1]
+    z = x * w[:, K - 1]
+    for j in range(1, min(K, T)):
+        term = x[:, : T - j] * w[:, K - 1 - j]
+        if doc_ids is not None:
+            same = np.asarray(doc_ids)[j:] == np.asarray(doc_ids)[: T - j]
+            term = np.where(same[None, :, None], term, 0.0)
+        z[:, j:] += term
+    return z / (1.0 + np.exp(-z)) if silu else z

@@ -46,6 +46,10 @@ SIGNATURES = {
     "gdn_gate_bwd": (ctypes.c_int, [_i64, _i64, _vp, _i32, _vp, _vp, _i32] + [_vp] * 5),
     "gdn_beta_sigmoid_fwd": (ctypes.c_int, [_i64, _vp, _i32, _vp, _vp]),
     "gdn_beta_sigmoid_bwd": (ctypes.c_int, [_i64, _vp, _i32, _vp, _vp, _vp]),
+    "gdn_rms_norm_gated_fwd": (ctypes.c_int, [_i64, _i64, _vp, _vp, _i32, _vp, _i32, _f32, _vp, _vp]),
+    "gdn_rms_norm_gated_bwd": (ctypes.c_int, [_i64, _i64, _vp, _vp, _i32, _vp, _i32, _f32] + [_vp] * 5),
+    "gdn_causal_conv1d_fwd": (ctypes.c_int, [_i64] * 4 + [_vp, _i32, _vp, _i32, _vp, _i64, _i32, _vp, _vp]),
+    "gdn_causal_conv1d_bwd": (ctypes.c_int, [_i64] * 4 + [_vp, _i32, _vp, _i32, _vp, _i64, _i32] + [_vp] * 4),
 }
 
 _lib = None
