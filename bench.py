@@ -230,6 +230,51 @@ def long_prefill_bench(dev, rank, world, reps=3):
             "useful_tflops": round(T * H * FWD_FLOP_PER_TOKEN_HEAD / (ms / 1e3) / 1e12, 2)}
 
 
+def layer_ops_bench(dev, world, reps=10):
+    """The layer's neighbouring steps at config-1 sizes (B=8, T=4096, H=16, d=128, bf16): the output step
+    RMSNorm(o)*silu(gate) over o [8, 4096, 16, 128] and the q-projection's causal conv + SiLU over
+    [8, 4096, 2048] (K = 4), forward and backward. HBM-bound: reports GB/s of the algorithmic bytes (each
+    tensor read or written once) per call, max over ranks."""
+    import torch
+
+    from sorernn_b200.layer_ops import causal_conv1d, rms_norm_gated
+
+    gen = torch.Generator(device=dev).manual_seed(7)
+    B, T, H, D = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["D"]
+    o = torch.randn(B, T, H, D, device=dev, generator=gen).bfloat16().requires_grad_(True)
+    gate = torch.randn(B, T, H, D, device=dev, generator=gen).bfloat16().requires_grad_(True)
+    w = torch.ones(D, device=dev, requires_grad=True)
+    dy = torch.randn(B, T, H, D, device=dev, generator=gen).bfloat16()
+    xc = torch.randn(B, T, H * D, device=dev, generator=gen).bfloat16().requires_grad_(True)
+    wc = (torch.randn(H * D, 4, device=dev, generator=gen) * 0.5).requires_grad_(True)
+    dyc = torch.randn(B, T, H * D, device=dev, generator=gen).bfloat16()
+    nb = o.numel() * 2  # bytes of one bf16 tensor of this size
+
+    def timed(fn):
+        fn()
+        barrier(world)
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(reps):
+            fn()
+        e0.record()
+        barrier(world)
+        return max_over_ranks(s0.elapsed_time(e0) / reps, world)
+
+    def ng():
+        rms_norm_gated(o, gate, w, None, activation="swish", eps=1e-6).backward(dy)
+
+    def cv():
+        causal_conv1d(xc, wc, activation="silu")[0].backward(dyc)
+
+    ms_ng, ms_cv = timed(ng), timed(cv)
+    # fwd reads x, gate and writes y; bwd reads x, gate, dy and writes dx, dgate: 8 tensor passes
+    # conv: fwd reads x, writes y; bwd reads x, dy, writes dx: 5 tensor passes
+    return {"config": "config1 sizes, bf16: rms_norm_gated over [8,4096,16,128]; causal_conv1d K=4 over [8,4096,2048]",
+            "rms_norm_gated_fwd_bwd_ms": round(ms_ng, 4), "rms_norm_gated_gbs": round(8 * nb / (ms_ng / 1e3) / 1e9, 1),
+            "causal_conv1d_fwd_bwd_ms": round(ms_cv, 4), "causal_conv1d_gbs": round(5 * nb / (ms_cv / 1e3) / 1e9, 1)}
+
+
 def run_ours(args):
     import torch
 
@@ -351,6 +396,7 @@ def run_ours(args):
 
     dec_ms, dec_bytes = decode_bench(dev, rank, world)
     long_prefill = long_prefill_bench(dev, rank, world)
+    layer_ops = layer_ops_bench(dev, world)
     peaks, peak_kind = load_peaks()
     dec_gbs = dec_bytes / (dec_ms / 1e3) / 1e9
 
@@ -389,6 +435,7 @@ def run_ours(args):
                                 "traffic": DECODE_TRAFFIC_BYTES, "algorithmic_bytes": dec_bytes}},
         "clocks": clk.summary(),
         "long_prefill": long_prefill,
+        "layer_ops": layer_ops,
     }
     if rank == 0:
         if world == 1:  # the host-core baseline is timed at N=1 only

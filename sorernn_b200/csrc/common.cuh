@@ -42,6 +42,51 @@ __device__ __forceinline__ void seq_bounds(const int64_t* cu, int64_t T, int64_t
 
 constexpr float kL2Eps = 1e-12f;  // F.normalize's eps (gdn.py:177)
 
+// PER consecutive elements of type TA at p + i (as floats), in the widest vector loads that PER elements
+// allow; the address must be aligned to that width.
+template <typename TA, int PER>
+__device__ __forceinline__ void ldv(const void* p, int64_t i, float (&o)[PER]) {
+    const TA* q = (const TA*)p + i;
+    constexpr int BYTES = PER * (int)sizeof(TA);
+    constexpr int CH = BYTES % 16 == 0 ? 16 : (BYTES % 8 == 0 ? 8 : (BYTES % 4 == 0 ? 4 : 0));
+    if constexpr (CH == 0) {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) o[e] = ld(q, e);
+    } else {
+        constexpr int EPC = CH / (int)sizeof(TA);  // elements per chunk
+#pragma unroll
+        for (int c = 0; c < PER / EPC; ++c) {
+            alignas(16) TA h[EPC];
+            if constexpr (CH == 16) *reinterpret_cast<uint4*>(h) = *reinterpret_cast<const uint4*>(q + c * EPC);
+            else if constexpr (CH == 8) *reinterpret_cast<uint2*>(h) = *reinterpret_cast<const uint2*>(q + c * EPC);
+            else *reinterpret_cast<uint32_t*>(h) = *reinterpret_cast<const uint32_t*>(q + c * EPC);
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) o[c * EPC + e] = ld(h, e);
+        }
+    }
+}
+template <typename TA, int PER>
+__device__ __forceinline__ void stv(void* p, int64_t i, const float (&v)[PER]) {
+    TA* q = (TA*)p + i;
+    constexpr int BYTES = PER * (int)sizeof(TA);
+    constexpr int CH = BYTES % 16 == 0 ? 16 : (BYTES % 8 == 0 ? 8 : (BYTES % 4 == 0 ? 4 : 0));
+    if constexpr (CH == 0) {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) st(q, e, v[e]);
+    } else {
+        constexpr int EPC = CH / (int)sizeof(TA);
+#pragma unroll
+        for (int c = 0; c < PER / EPC; ++c) {
+            alignas(16) TA h[EPC];
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) st(h, e, v[c * EPC + e]);
+            if constexpr (CH == 16) *reinterpret_cast<uint4*>(q + c * EPC) = *reinterpret_cast<const uint4*>(h);
+            else if constexpr (CH == 8) *reinterpret_cast<uint2*>(q + c * EPC) = *reinterpret_cast<const uint2*>(h);
+            else *reinterpret_cast<uint32_t*>(q + c * EPC) = *reinterpret_cast<const uint32_t*>(h);
+        }
+    }
+}
+
 }  // namespace gdn
 
 // Dispatch a dtype code to a C++ type.

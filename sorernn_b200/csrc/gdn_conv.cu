@@ -6,63 +6,14 @@
 // Backward, with dz = dy silu'(z) recomputed from x:
 //   dx[t, c] = sum_{j < K} w[c, K-1-j] dz[t+j, c]   over t+j inside t's document,
 //   dw[c, K-1-j] = sum_t x[t-j, c] dz[t, c]          (fp32, reduced per block, then one atomic add each).
-// One thread per (token, 8 consecutive channels): 16-byte rows for bf16/fp16, fp32 accumulation.
+// One thread per (tile of 32 consecutive tokens, 8 channels forward / 4 backward): a sliding window over
+// the taps, vector row loads, fp32 accumulation, weights and weight gradients in registers.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace gdn {
 
 constexpr int kConvThreads = 256;
-
-template <typename T> struct Vec8;
-template <> struct Vec8<__nv_bfloat16> {
-    static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&o)[8]) {
-        const uint4 u = *reinterpret_cast<const uint4*>(p);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(h[e]);
-            o[2 * e] = f.x;
-            o[2 * e + 1] = f.y;
-        }
-    }
-    static __device__ __forceinline__ void store(__nv_bfloat16* p, const float (&v)[8]) {
-        uint4 u;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
-        *reinterpret_cast<uint4*>(p) = u;
-    }
-};
-template <> struct Vec8<__half> {
-    static __device__ __forceinline__ void load(const __half* p, float (&o)[8]) {
-        const uint4 u = *reinterpret_cast<const uint4*>(p);
-        const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(h[e]);
-            o[2 * e] = f.x;
-            o[2 * e + 1] = f.y;
-        }
-    }
-    static __device__ __forceinline__ void store(__half* p, const float (&v)[8]) {
-        uint4 u;
-        __half2* h = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
-        *reinterpret_cast<uint4*>(p) = u;
-    }
-};
-template <> struct Vec8<float> {
-    static __device__ __forceinline__ void load(const float* p, float (&o)[8]) {
-        const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
-    }
-    static __device__ __forceinline__ void store(float* p, const float (&v)[8]) {
-        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
-        *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
-    }
-};
 
 struct ConvArgs {
     const void *x, *w, *dy;
@@ -97,90 +48,168 @@ __device__ __forceinline__ void doc_span(const ConvArgs& a, int64_t t, int64_t& 
     e = a.cu[lo + 1];
 }
 
-template <typename TA, int K>
+constexpr int kConvTile = 32;  // consecutive tokens per thread (a sliding window over the taps)
+
+// Thread (token tile, group of CW channels): the C / CW threads of a tile are consecutive, so a warp's row
+// loads are contiguous. Window rows before the document start read as zero. The next row is prefetched
+// one token ahead.
+template <typename TA, int K, int CW>
 __global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const ConvArgs a) {
-    const int64_t groups = a.C / 8, total = a.B * a.T * groups;
-    for (int64_t i = blockIdx.x * (int64_t)kConvThreads + threadIdx.x; i < total; i += (int64_t)gridDim.x * kConvThreads) {
-        const int64_t t = i / groups, c0 = (i % groups) * 8;
+    const int64_t groups = a.C / CW, BT = a.B * a.T, tiles = (BT + kConvTile - 1) / kConvTile;
+    for (int64_t i = blockIdx.x * (int64_t)kConvThreads + threadIdx.x; i < tiles * groups;
+         i += (int64_t)gridDim.x * kConvThreads) {
+        const int64_t c0 = (i % groups) * CW, t0 = (i / groups) * kConvTile;
+        const int64_t t1 = t0 + kConvTile < BT ? t0 + kConvTile : BT;
+        float w[CW][K];
+#pragma unroll
+        for (int q = 0; q < CW; ++q)
+#pragma unroll
+            for (int j = 0; j < K; ++j) w[q][j] = ld_w(a.w, a.w_dtype, (c0 + q) * K + j);
         int64_t s, e;
-        doc_span(a, t, s, e);
-        float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        doc_span(a, t0, s, e);
+        float win[K][CW];  // win[j] = x[t - j]
 #pragma unroll
-        for (int j = 0; j < K; ++j) {
-            if (t - j < s) break;
-            float xv[8];
-            Vec8<TA>::load((const TA*)a.x + (t - j) * a.C + c0, xv);
+        for (int j = 1; j < K; ++j) {
+            if (t0 - j >= s) ldv<TA, CW>(a.x, (t0 - j) * a.C + c0, win[j]);
+            else {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) z[q] = fmaf(ld_w(a.w, a.w_dtype, (c0 + q) * K + (K - 1 - j)), xv[q], z[q]);
+                for (int q = 0; q < CW; ++q) win[j][q] = 0.f;
+            }
         }
-        if (a.silu) {
+        float nxt[CW];
+        ldv<TA, CW>(a.x, t0 * a.C + c0, nxt);
+        for (int64_t t = t0; t < t1; ++t) {
+            if (t >= e) {  // the next document starts here: no taps before it
+                doc_span(a, t, s, e);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) z[q] *= sig(z[q]);
+                for (int j = 1; j < K; ++j)
+#pragma unroll
+                    for (int q = 0; q < CW; ++q) win[j][q] = 0.f;
+            }
+#pragma unroll
+            for (int q = 0; q < CW; ++q) win[0][q] = nxt[q];
+            if (t + 1 < t1) ldv<TA, CW>(a.x, (t + 1) * a.C + c0, nxt);
+            float z[CW];
+#pragma unroll
+            for (int q = 0; q < CW; ++q) {
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < K; ++j) acc = fmaf(w[q][K - 1 - j], win[j][q], acc);
+                z[q] = a.silu ? acc * sig(acc) : acc;
+            }
+            stv<TA, CW>(a.y, t * a.C + c0, z);
+#pragma unroll
+            for (int j = K - 1; j >= 1; --j)
+#pragma unroll
+                for (int q = 0; q < CW; ++q) win[j][q] = win[j - 1][q];
         }
-        Vec8<TA>::store((TA*)a.y + t * a.C + c0, z);
     }
 }
 
-template <typename TA, int K>
-__global__ void __launch_bounds__(kConvThreads) conv_bwd_kernel(const ConvArgs a) {
+// Backward over the same tiles: a window of x rows [t-K+1, t+K-1] and of dz rows [t, t+K-1] slides
+// forward (the rows entering at t+K-1 are prefetched a token ahead); dw stays in registers for the tile.
+template <typename TA, int K, int CW>
+__global__ void __launch_bounds__(kConvThreads, 2) conv_bwd_kernel(const ConvArgs a) {
     extern __shared__ float s_dw[];  // [C][K] block partials
     for (int64_t i = threadIdx.x; i < a.C * K; i += kConvThreads) s_dw[i] = 0.f;
     __syncthreads();
-    const int64_t groups = a.C / 8, total = a.B * a.T * groups;
-    for (int64_t i = blockIdx.x * (int64_t)kConvThreads + threadIdx.x; i < total; i += (int64_t)gridDim.x * kConvThreads) {
-        const int64_t t = i / groups, c0 = (i % groups) * 8;
-        int64_t s, e;
-        doc_span(a, t, s, e);
-        float w[8][K];
+    const int64_t groups = a.C / CW, BT = a.B * a.T, tiles = (BT + kConvTile - 1) / kConvTile;
+    for (int64_t i = blockIdx.x * (int64_t)kConvThreads + threadIdx.x; i < tiles * groups;
+         i += (int64_t)gridDim.x * kConvThreads) {
+        const int64_t c0 = (i % groups) * CW, t0 = (i / groups) * kConvTile;
+        const int64_t t1 = t0 + kConvTile < BT ? t0 + kConvTile : BT;
+        float w[CW][K], dw[CW][K];
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
+        for (int q = 0; q < CW; ++q)
 #pragma unroll
-            for (int j = 0; j < K; ++j) w[q][j] = ld_w(a.w, a.w_dtype, (c0 + q) * K + j);
-        // x rows t-K+1 .. t+K-1 (inside the document), zero outside
-        float xr[2 * K - 1][8];
-#pragma unroll
-        for (int r = 0; r < 2 * K - 1; ++r) {
-            const int64_t tt = t - (K - 1) + r;
-            if (tt >= s && tt < e) {
-                Vec8<TA>::load((const TA*)a.x + tt * a.C + c0, xr[r]);
-            } else {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) xr[r][q] = 0.f;
+            for (int j = 0; j < K; ++j) {
+                w[q][j] = ld_w(a.w, a.w_dtype, (c0 + q) * K + j);
+                dw[q][j] = 0.f;
             }
-        }
-        float dx[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        int64_t s = 0, e = 0;
+        float xw[2 * K - 1][CW];  // xw[r] = x[t - (K-1) + r]
+        float dzw[K][CW];         // dzw[j] = dz[t + j]
+        float px[CW], pdy[CW];    // raw rows t + K (prefetch for the next slide)
+        // dz at token u (inside [s, e)) from dy[u] and the x window rows ending at u (xw index base..base+K-1)
+        auto make_dz = [&](int64_t u, int base, const float (&dyv)[CW], float (&out)[CW]) {
 #pragma unroll
-        for (int j = 0; j < K; ++j) {  // dz at t + j
-            const int64_t tj = t + j;
-            if (tj >= e) break;
-            float dyv[8], dz[8];
-            Vec8<TA>::load((const TA*)a.dy + tj * a.C + c0, dyv);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
+            for (int q = 0; q < CW; ++q) {
                 float z = 0.f;
 #pragma unroll
-                for (int i2 = 0; i2 < K; ++i2) z = fmaf(w[q][K - 1 - i2], xr[K - 1 + j - i2][q], z);
+                for (int i2 = 0; i2 < K; ++i2) z = fmaf(w[q][K - 1 - i2], xw[base + K - 1 - i2][q], z);
+                float d = dyv[q];
                 if (a.silu) {
                     const float sg = sig(z);
-                    dz[q] = dyv[q] * sg * (1.f + z * (1.f - sg));
-                } else {
-                    dz[q] = dyv[q];
+                    d *= sg * (1.f + z * (1.f - sg));
                 }
-                dx[q] = fmaf(w[q][K - 1 - j], dz[q], dx[q]);
+                out[q] = u < e ? d : 0.f;
             }
-            if (j == 0) {  // this thread owns dz[t]: its weight-gradient terms
+        };
+        bool fresh = true;
+        for (int64_t t = t0; t < t1; ++t) {
+            if (fresh || t >= e) {  // (re)build both windows at t: first token of the tile or of a document
+                doc_span(a, t, s, e);
 #pragma unroll
-                for (int q = 0; q < 8; ++q)
+                for (int r = 0; r < 2 * K - 1; ++r) {
+                    const int64_t u = t - (K - 1) + r;
+                    if (u >= s && u < e) ldv<TA, CW>(a.x, u * a.C + c0, xw[r]);
+                    else {
 #pragma unroll
-                    for (int i2 = 0; i2 < K; ++i2) atomicAdd(&s_dw[(c0 + q) * K + (K - 1 - i2)], xr[K - 1 - i2][q] * dz[q]);
+                        for (int q = 0; q < CW; ++q) xw[r][q] = 0.f;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < K; ++j) {
+                    float dyv[CW];
+                    if (t + j < e) ldv<TA, CW>(a.dy, (t + j) * a.C + c0, dyv);
+                    else {
+#pragma unroll
+                        for (int q = 0; q < CW; ++q) dyv[q] = 0.f;
+                    }
+                    make_dz(t + j, j, dyv, dzw[j]);
+                }
+                fresh = false;
+            } else {  // slide by one token: x row and dz at t+K-1 enter from the prefetch
+                const int64_t u = t + K - 1;
+#pragma unroll
+                for (int r = 0; r < 2 * K - 2; ++r)
+#pragma unroll
+                    for (int q = 0; q < CW; ++q) xw[r][q] = xw[r + 1][q];
+#pragma unroll
+                for (int q = 0; q < CW; ++q) xw[2 * K - 2][q] = u < e ? px[q] : 0.f;
+#pragma unroll
+                for (int j = 0; j < K - 1; ++j)
+#pragma unroll
+                    for (int q = 0; q < CW; ++q) dzw[j][q] = dzw[j + 1][q];
+                make_dz(u, K - 1, pdy, dzw[K - 1]);
             }
+            if (t + K < BT && t + 1 < t1) {  // rows entering at the next step
+                ldv<TA, CW>(a.x, (t + K) * a.C + c0, px);
+                ldv<TA, CW>(a.dy, (t + K) * a.C + c0, pdy);
+            }
+            float dx[CW];
+#pragma unroll
+            for (int q = 0; q < CW; ++q) {
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < K; ++j) acc = fmaf(w[q][K - 1 - j], dzw[j][q], acc);
+                dx[q] = acc;
+#pragma unroll
+                for (int i2 = 0; i2 < K; ++i2) dw[q][K - 1 - i2] = fmaf(xw[K - 1 - i2][q], dzw[0][q], dw[q][K - 1 - i2]);
+            }
+            stv<TA, CW>(a.dx, t * a.C + c0, dx);
         }
-        Vec8<TA>::store((TA*)a.dx + t * a.C + c0, dx);
+#pragma unroll
+        for (int q = 0; q < CW; ++q)
+#pragma unroll
+            for (int j = 0; j < K; ++j) atomicAdd(&s_dw[(c0 + q) * K + j], dw[q][j]);
     }
     __syncthreads();
     for (int64_t i = threadIdx.x; i < a.C * K; i += kConvThreads)
         if (s_dw[i] != 0.f) atomicAdd(&a.dw[i], s_dw[i]);
 }
+
+constexpr int kConvFwdCW = 8, kConvBwdCW = 4;
 
 static unsigned conv_grid(int64_t work) {
     const int64_t blocks = (work + kConvThreads - 1) / kConvThreads;
@@ -189,20 +218,21 @@ static unsigned conv_grid(int64_t work) {
 
 template <typename TA>
 static int conv_launch(const ConvArgs& a, int K, bool bwd, cudaStream_t s) {
-    const unsigned grid = conv_grid(a.B * a.T * (a.C / 8));
+    const int cw = bwd ? kConvBwdCW : kConvFwdCW;
+    const unsigned grid = conv_grid((a.B * a.T + kConvTile - 1) / kConvTile * (a.C / cw));
     const size_t smem = bwd ? (size_t)a.C * K * sizeof(float) : 0;
     if (bwd && smem > 48 * 1024) {
         auto set = [&](const void* f) { return cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); };
-        if ((K == 1 && set((const void*)conv_bwd_kernel<TA, 1>) != cudaSuccess) ||
-            (K == 2 && set((const void*)conv_bwd_kernel<TA, 2>) != cudaSuccess) ||
-            (K == 3 && set((const void*)conv_bwd_kernel<TA, 3>) != cudaSuccess) ||
-            (K == 4 && set((const void*)conv_bwd_kernel<TA, 4>) != cudaSuccess))
+        if ((K == 1 && set((const void*)conv_bwd_kernel<TA, 1, kConvBwdCW>) != cudaSuccess) ||
+            (K == 2 && set((const void*)conv_bwd_kernel<TA, 2, kConvBwdCW>) != cudaSuccess) ||
+            (K == 3 && set((const void*)conv_bwd_kernel<TA, 3, kConvBwdCW>) != cudaSuccess) ||
+            (K == 4 && set((const void*)conv_bwd_kernel<TA, 4, kConvBwdCW>) != cudaSuccess))
             return GDN_ERR_LAUNCH;
     }
-#define CONV_CASE(KK)                                                                  \
-    case KK:                                                                           \
-        if (bwd) conv_bwd_kernel<TA, KK><<<grid, kConvThreads, smem, s>>>(a);          \
-        else conv_fwd_kernel<TA, KK><<<grid, kConvThreads, 0, s>>>(a);                 \
+#define CONV_CASE(KK)                                                                       \
+    case KK:                                                                                \
+        if (bwd) conv_bwd_kernel<TA, KK, kConvBwdCW><<<grid, kConvThreads, smem, s>>>(a);   \
+        else conv_fwd_kernel<TA, KK, kConvFwdCW><<<grid, kConvThreads, 0, s>>>(a);          \
         break;
     switch (K) {
         CONV_CASE(1)

@@ -37,28 +37,28 @@ struct NormGateArgs {
     float eps;
 };
 
-template <int PER>
+template <typename TA, int PER>
 __global__ void __launch_bounds__(32 * kNgWarps) norm_gate_fwd_kernel(const NormGateArgs a) {
     const int lane = threadIdx.x & 31;
+    float w[PER];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) w[e] = ld_c(a.w, a.w_dtype, lane * PER + e);
     const int64_t warp0 = blockIdx.x * (int64_t)kNgWarps + (threadIdx.x >> 5);
     for (int64_t r = warp0; r < a.rows; r += (int64_t)gridDim.x * kNgWarps) {
         const int64_t base = r * a.D + lane * PER;
-        float x[PER], ss = 0.f;
+        float x[PER], g[PER], y[PER], ss = 0.f;
+        ldv<TA, PER>(a.x, base, x);
+        ldv<TA, PER>(a.g, base, g);
 #pragma unroll
-        for (int e = 0; e < PER; ++e) {
-            x[e] = ld_c(a.x, a.act_dtype, base + e);
-            ss = fmaf(x[e], x[e], ss);
-        }
+        for (int e = 0; e < PER; ++e) ss = fmaf(x[e], x[e], ss);
         const float rs = rsqrtf(warp_sum(ss) / a.D + a.eps);
 #pragma unroll
-        for (int e = 0; e < PER; ++e) {
-            const float g = ld_c(a.g, a.act_dtype, base + e);
-            st_c(a.y, a.act_dtype, base + e, x[e] * rs * ld_c(a.w, a.w_dtype, lane * PER + e) * g * sigm(g));
-        }
+        for (int e = 0; e < PER; ++e) y[e] = x[e] * rs * w[e] * g[e] * sigm(g[e]);
+        stv<TA, PER>(a.y, base, y);
     }
 }
 
-template <int PER>
+template <typename TA, int PER>
 __global__ void __launch_bounds__(32 * kNgWarps) norm_gate_bwd_kernel(const NormGateArgs a) {
     __shared__ float s_dw[1024];
     for (int i = threadIdx.x; i < a.D; i += 32 * kNgWarps) s_dw[i] = 0.f;
@@ -73,26 +73,27 @@ __global__ void __launch_bounds__(32 * kNgWarps) norm_gate_bwd_kernel(const Norm
     const int64_t warp0 = blockIdx.x * (int64_t)kNgWarps + (threadIdx.x >> 5);
     for (int64_t r = warp0; r < a.rows; r += (int64_t)gridDim.x * kNgWarps) {
         const int64_t base = r * a.D + lane * PER;
-        float x[PER], dn[PER], ss = 0.f;
+        float x[PER], g[PER], dy[PER], dn[PER], dg[PER], dx[PER], ss = 0.f;
+        ldv<TA, PER>(a.x, base, x);
+        ldv<TA, PER>(a.g, base, g);
+        ldv<TA, PER>(a.dy, base, dy);
 #pragma unroll
-        for (int e = 0; e < PER; ++e) {
-            x[e] = ld_c(a.x, a.act_dtype, base + e);
-            ss = fmaf(x[e], x[e], ss);
-        }
+        for (int e = 0; e < PER; ++e) ss = fmaf(x[e], x[e], ss);
         const float rs = rsqrtf(warp_sum(ss) / a.D + a.eps);
         float c = 0.f;
 #pragma unroll
         for (int e = 0; e < PER; ++e) {
-            const float g = ld_c(a.g, a.act_dtype, base + e), dy = ld_c(a.dy, a.act_dtype, base + e);
-            const float sg = sigm(g), s = g * sg, n = x[e] * rs;
-            st_c(a.dg, a.act_dtype, base + e, dy * n * w[e] * sg * (1.f + g * (1.f - sg)));
-            dn[e] = dy * s * w[e];
-            dwp[e] = fmaf(dy * s, n, dwp[e]);
+            const float sg = sigm(g[e]), sv = g[e] * sg, n = x[e] * rs;
+            dg[e] = dy[e] * n * w[e] * sg * (1.f + g[e] * (1.f - sg));
+            dn[e] = dy[e] * sv * w[e];
+            dwp[e] = fmaf(dy[e] * sv, n, dwp[e]);
             c = fmaf(dn[e], n, c);
         }
         c = warp_sum(c) / a.D;
 #pragma unroll
-        for (int e = 0; e < PER; ++e) st_c(a.dx, a.act_dtype, base + e, rs * (dn[e] - x[e] * rs * c));
+        for (int e = 0; e < PER; ++e) dx[e] = rs * (dn[e] - x[e] * rs * c);
+        stv<TA, PER>(a.dg, base, dg);
+        stv<TA, PER>(a.dx, base, dx);
     }
 #pragma unroll
     for (int e = 0; e < PER; ++e) atomicAdd(&s_dw[lane * PER + e], dwp[e]);
@@ -105,14 +106,14 @@ static unsigned ng_grid(int64_t rows) {
     return (unsigned)(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
 }
 
-#define NG_DISPATCH_PER(D, KERNEL, ...)                                         \
+#define NG_DISPATCH_PER(TA, D, KERNEL, ...)                                     \
     switch ((D) / 32) {                                                         \
-        case 1: KERNEL<1><<<__VA_ARGS__>>>(a); break;                           \
-        case 2: KERNEL<2><<<__VA_ARGS__>>>(a); break;                           \
-        case 4: KERNEL<4><<<__VA_ARGS__>>>(a); break;                           \
-        case 8: KERNEL<8><<<__VA_ARGS__>>>(a); break;                           \
-        case 16: KERNEL<16><<<__VA_ARGS__>>>(a); break;                         \
-        case 32: KERNEL<32><<<__VA_ARGS__>>>(a); break;                         \
+        case 1: KERNEL<TA, 1><<<__VA_ARGS__>>>(a); break;                       \
+        case 2: KERNEL<TA, 2><<<__VA_ARGS__>>>(a); break;                       \
+        case 4: KERNEL<TA, 4><<<__VA_ARGS__>>>(a); break;                       \
+        case 8: KERNEL<TA, 8><<<__VA_ARGS__>>>(a); break;                       \
+        case 16: KERNEL<TA, 16><<<__VA_ARGS__>>>(a); break;                     \
+        case 32: KERNEL<TA, 32><<<__VA_ARGS__>>>(a); break;                     \
         default: return GDN_ERR_SHAPE;                                          \
     }
 
@@ -131,7 +132,7 @@ extern "C" int gdn_rms_norm_gated_fwd(int64_t rows, int64_t D, const void* x, co
     NormGateArgs a{};
     a.x = x; a.g = gate; a.w = weight; a.y = y;
     a.rows = rows; a.D = (int)D; a.act_dtype = act_dtype; a.w_dtype = w_dtype; a.eps = eps;
-    NG_DISPATCH_PER(D, norm_gate_fwd_kernel, ng_grid(rows), 32 * kNgWarps, 0, (cudaStream_t)stream)
+    GDN_DISPATCH_DTYPE(act_dtype, TA, NG_DISPATCH_PER(TA, D, norm_gate_fwd_kernel, ng_grid(rows), 32 * kNgWarps, 0, (cudaStream_t)stream))
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
@@ -148,7 +149,7 @@ extern "C" int gdn_rms_norm_gated_bwd(int64_t rows, int64_t D, const void* x, co
     NormGateArgs a{};
     a.x = x; a.g = gate; a.w = weight; a.dy = dy; a.dx = dx; a.dg = dgate; a.dw = dweight;
     a.rows = rows; a.D = (int)D; a.act_dtype = act_dtype; a.w_dtype = w_dtype; a.eps = eps;
-    NG_DISPATCH_PER(D, norm_gate_bwd_kernel, ng_grid(rows), 32 * kNgWarps, 0, s)
+    GDN_DISPATCH_DTYPE(act_dtype, TA, NG_DISPATCH_PER(TA, D, norm_gate_bwd_kernel, ng_grid(rows), 32 * kNgWarps, 0, s))
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
