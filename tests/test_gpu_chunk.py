@@ -217,3 +217,34 @@ def test_segmented_prefill_matches_one_forward(P, with_h0):
                              initial_state=h0, local_segments=P)
     assert_bf16_close(to_np(o), to_np(o_ref), 2e-2, "o")
     assert_rms_close(to_np(s), to_np(s_ref), 2e-2, "final state")
+
+
+def test_chunk_varlen_empty_documents_fwd_bwd():
+    """Zero-length documents at the start, middle and end: their final state is their initial state, their
+    dh0 is their dht, and the neighbours are unaffected (forward and backward against the oracle)."""
+    cu = [0, 0, 5, 5, 70, 70, 200, 200]
+    N = len(cu) - 1
+    x = _inputs(23, 1, 200, 2, 2, normalized=False)
+    gen = torch.Generator(device="cuda").manual_seed(24)
+    h0 = torch.randn(N, 2, D, D, device="cuda", generator=gen) * 0.05
+    dht = torch.randn(N, 2, D, D, device="cuda", generator=gen) * 0.1
+    _grads_vs_oracle(x, h0, dht, True, cu=cu)
+
+
+def test_zero_length_sequences():
+    """T = 0: empty outputs, the final state is the initial state and dh0 is dht."""
+    from sorernn_b200 import chunk_gated_delta_rule
+
+    B, H = 2, 2
+    x = _inputs(25, B, 64, H, H)
+    x0 = {n: t[:, :0].contiguous() for n, t in x.items()}
+    gen = torch.Generator(device="cuda").manual_seed(26)
+    h0 = (torch.randn(B, H, D, D, device="cuda", generator=gen) * 0.05).requires_grad_(True)
+    leaves = {n: x0[n].clone().requires_grad_(True) for n in ("q", "k", "v", "g", "beta")}
+    o, ht = chunk_gated_delta_rule(leaves["q"], leaves["k"], leaves["v"], leaves["g"], leaves["beta"],
+                                   initial_state=h0, output_final_state=True, use_qk_l2norm_in_kernel=True)
+    assert o.shape == (B, 0, H, D)
+    assert torch.equal(ht, h0.detach())
+    dht = torch.randn(B, H, D, D, device="cuda", generator=gen)
+    (ht * dht).sum().backward()
+    assert torch.equal(h0.grad, dht)

@@ -124,3 +124,29 @@ def test_c_oracle_decode_step():
     o_c = cgdn.decode_step(x["q"][:, 0], x["k"][:, 0], x["v"][:, 0], x["g"][:, 0], x["beta"][:, 0], st_c, 0.25)
     np.testing.assert_allclose(o_c, o, atol=1e-5)
     np.testing.assert_allclose(st_c, st, atol=1e-5)
+
+
+def test_oracles_agree_on_empty_documents():
+    """Zero-length documents: both restatements (numpy, C) keep h0 as the final state, pass dht through
+    as dh0, and agree elsewhere."""
+    from inputs import make_inputs, make_state_inputs
+    from oracle import cgdn
+    from oracle import gdn_oracle as orc
+
+    cu = [0, 0, 5, 5, 17, 17]
+    x = make_inputs(3, 1, 17, 1, 2, 8, 8)
+    h0, dht = make_state_inputs(3, len(cu) - 1, 2, 8, 8)
+    o_n, s_n = orc.gdn_forward(x["q"], x["k"], x["v"], x["g"], x["beta"], initial_state=h0, cu_seqlens=cu)
+    o_c, s_c = cgdn.forward(x["q"], x["k"], x["v"], x["g"], x["beta"], 8 ** -0.5, initial_state=h0, cu_seqlens=cu)
+    np.testing.assert_allclose(o_c, o_n, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(s_c, s_n, rtol=1e-5, atol=1e-6)
+    for n in (0, 2, 4):
+        np.testing.assert_allclose(s_n[n], h0[n])
+    g_n = orc.gdn_backward(x["q"], x["k"], x["v"], x["g"], x["beta"], x["do"], initial_state=h0, dht=dht,
+                           cu_seqlens=cu)
+    g_c = cgdn.backward(x["q"], x["k"], x["v"], x["g"], x["beta"], x["do"], 8 ** -0.5, initial_state=h0, dht=dht,
+                        cu_seqlens=cu)
+    for a, b in zip(g_c, g_n):
+        np.testing.assert_allclose(a, b, rtol=1e-4, atol=1e-5)
+    for n in (0, 2, 4):
+        np.testing.assert_allclose(g_n[5][n], dht[n])
