@@ -124,9 +124,18 @@ int gdn_chunk_fwd(const gdn_problem* p, const void* q, const void* k, const void
                   void* workspace, size_t workspace_bytes, gdn_stream_t stream) {
     int st = check_problem(p);
     if (st != GDN_OK) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (p->B * p->T == 0) {  // no tokens: the final state is the initial state (token pointers may be null)
+        if (!final_state) return GDN_OK;
+        const size_t bytes = (size_t)p->N * p->HV * p->DK * p->DV * sizeof(float);
+        if (bytes == 0) return GDN_OK;
+        const cudaError_t e = initial_state ? cudaMemcpyAsync(final_state, initial_state, bytes,
+                                                              cudaMemcpyDeviceToDevice, s)
+                                            : cudaMemsetAsync(final_state, 0, bytes, s);
+        return e == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+    }
     if (!q || !k || !v || !g || !beta || !o) return GDN_ERR_ARGUMENT;
     if (!workspace || workspace_bytes < gdn_chunk_fwd_workspace_size(p)) return GDN_ERR_WORKSPACE;
-    cudaStream_t s = (cudaStream_t)stream;
     if (cudaMemsetAsync(workspace, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
     RecLaunch L = rec_launch(p);
     L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.o = o;
@@ -141,10 +150,18 @@ int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void
                   void* workspace, size_t workspace_bytes, gdn_stream_t stream) {
     int st = check_problem(p);
     if (st != GDN_OK) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (p->B * p->T == 0) {  // no tokens: dh0 is dht (token pointers may be null)
+        if (!dh0) return GDN_OK;
+        const size_t bytes = (size_t)p->N * p->HV * p->DK * p->DV * sizeof(float);
+        if (bytes == 0) return GDN_OK;
+        const cudaError_t e = dht ? cudaMemcpyAsync(dh0, dht, bytes, cudaMemcpyDeviceToDevice, s)
+                                  : cudaMemsetAsync(dh0, 0, bytes, s);
+        return e == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+    }
     if (!q || !k || !v || !g || !beta || !dout || !dq || !dk || !dv || !dg || !dbeta) return GDN_ERR_ARGUMENT;
     if (!workspace || workspace_bytes < gdn_chunk_bwd_workspace_size(p)) return GDN_ERR_WORKSPACE;
     if (!aligned16(workspace)) return GDN_ERR_ALIGN;
-    cudaStream_t s = (cudaStream_t)stream;
     if (cudaMemsetAsync(workspace, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
     if (gdn_uses_chunk_kernels(p)) {
         if (!checkpoints) return GDN_ERR_ARGUMENT;  // the chunked backward restarts from the forward's checkpoints
