@@ -16,7 +16,8 @@
 //   MMA1  D1[128x64] = [Q;K] K^T                 (rows 0-63: Q K^T, rows 64-127: K K^T)
 //   MMA2  [W; -] = [TB; TV] K  (W rows on lanes 0-63)       MMA3  U^T = V^T TV^T,  TV = T diag(beta)
 //         TB = T diag(beta e^G / nk)
-//   MMA4  U^T += S0^T (-W)^T  -> Delta^T                   MMA5  [-; O1] = [-; Q] S0  (O rows on lanes 64-127)
+//   MMA4  U^T += S0^T (-W)^T  -> Delta^T                   MMA5  [-; O1] = [-; Q] S0  (O rows on lanes 64-127,
+//         issued right after S0's read-out, into TMEM columns 128-255)
 //   MMA6  [-; O2] = [-; P'] Delta  (hi.hi + lo.hi + hi.lo) MMA7  S^T += Dd^T K,  Dd = diag(e^(G_C-G)/nk) Delta
 // A 128-row A operand whose half is ignored always takes that half from an allocated tile below or above
 // the real one (never past the end of shared memory).
@@ -64,8 +65,8 @@ constexpr uint32_t OFF_A = OFF_D;
 constexpr uint32_t OFF_Y = OFF_A + 64 * AST * 4;
 static_assert(OFF_Y + 32 * 32 * 4 <= OFF_DD, "solve scratch overlaps live tiles");
 // TMEM columns
-// O2 (128 columns) reuses D1 + U once both are read; O1 reuses W once it is read.
-constexpr uint32_t T_D1 = 0, T_U = 64, T_O2 = 0, T_S = 256, T_W = 384, T_O1 = 384, T_COLS = 512;
+// O2 (128 columns) reuses D1 + U once both are read; O1 has its own columns (it is computed early).
+constexpr uint32_t T_D1 = 0, T_U = 64, T_O2 = 0, T_O1 = 128, T_S = 256, T_W = 384, T_COLS = 512;
 constexpr uint32_t TX_QK = 4 * 8192, TX_V = 2 * 8192;
 }  // namespace cf
 
@@ -460,6 +461,18 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
         __syncthreads();
         if (recompute && tid == 0) bulk_s2g(rec_g, sm + OFF_S, 32768);  // S0^T hi tile
+        if (tid == 0 && a.o_mode != 2) {  // MMA5 as soon as S0^T is in place: [-; O1] = [-; Q] S0hi
+            tc_fence_after();             // (O1 in the otherwise idle columns 128-255; waited on with MMA4)
+            const uint32_t id5 = idesc_bf16(128, 128, 0, 0);
+            const uint64_t dS_h = desc_kmajor(sbase + OFF_S);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                // A = [K odd slot (ignored); Q]: rows 64-127 are Q, so O1 lands on lanes 64-127
+                umma_bf16(tO1, desc_kmajor(aQ - 8192 + kb * QK_BLK + ko), dS_h + ((kb * 16384 + ko) >> 4), id5,
+                          ks > 0);
+            }
+        }
 
         // (h) TB = T diag(beta e^G / nk), TV = T diag(beta)  (bf16, K-major [i][j])
         {
@@ -516,10 +529,9 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         block_sync_tc();
         if (recompute && tid == 0) bulk_s2g(rec_g + kBwdRecW, sm + OFF_W, 24576);  // -W | T (at OFF_P)
 
-        // (k) MMA4: U^T += (S0hi + S0lo)^T (-W)^T -> Delta^T ; MMA5: [-; O1] = [-; Q] S0hi (O1 rows on
-        //     lanes 64-127, N = dv = 128)   (K = dk = 128)
+        // (k) MMA4: U^T += (S0hi + S0lo)^T (-W)^T -> Delta^T   (K = dk = 128); the commit also covers MMA5
         if (tid == 0) {
-            const uint32_t id = idesc_bf16(128, 64, 0, 0), id5 = idesc_bf16(128, 128, 0, 0);
+            const uint32_t id = idesc_bf16(128, 64, 0, 0);
             // base descriptors; the 14-bit start-address field (bytes >> 4) never carries for smem addresses
             const uint64_t dS_h = desc_kmajor(sbase + OFF_S), dS_l = desc_kmajor(sbase + OFF_SL);
             const uint64_t dW_ = desc_kmajor(sbase + OFF_W);
@@ -531,8 +543,6 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
                 const uint64_t bw = dW_ + ((kb * 8192 + ko) >> 4);
                 umma_bf16(tU, ah, bw, id, 1);
                 umma_bf16(tU, al, bw, id, 1);
-                // A = [K odd slot (ignored); Q]: rows 64-127 are Q, so O1 lands on lanes 64-127
-                if (a.o_mode != 2) umma_bf16(tO1, desc_kmajor(aQ - 8192 + kb * QK_BLK + ko), ah, id5, ks > 0);
             }
             umma_commit(bar_mma);
         }
