@@ -3,13 +3,14 @@
 // One CTA (512 threads) per (sequence, value head) walks the chunks in reverse, carrying dS (the gradient
 // of the state at the chunk end, fp32 in TMEM). The chunk-start states S0 are not saved by the forward:
 // a segment-parallel pass of the forward kernel (chunk_fwd in recompute mode) rebuilds them from the
-// forward's checkpoints into the workspace as bf16 operand tiles, together with the chunk's T = (I + A)^-1
-// and its TB, TV scalings (so the triangular solve runs once per chunk, in that pass); this kernel
-// bulk-copies one record per chunk.
+// forward's checkpoints and writes one record per (chunk, head) to the workspace: the bf16 operand tiles of
+// S0^T, -W, T = (I + A)^-1, Delta^T and the low part of Dd^T (kBwdRecordBytes, kernels.h), so the
+// triangular solve and the W, U, Delta products run once per chunk, in that pass; this kernel bulk-copies
+// the record with the chunk's Q, K, dO tiles and recomputes only the Gram matrix D1 = [Q;K] K^T.
 //
 // With qn = q/nq, kn = k/nk (the raw bf16 tiles feed the tensor cores; norms are applied in fp32),
-// Gamma = in-chunk cumsum(g), E_ij = exp(Gamma_i - Gamma_j), and the forward's A, T, W, U, Delta, P
-// recomputed per chunk (the algebra of tests/test_chunk_algebra.py::chunked_backward):
+// Gamma = in-chunk cumsum(g), E_ij = exp(Gamma_i - Gamma_j), P, A from D1, and T, W, Delta from the
+// record (the algebra of tests/test_chunk_algebra.py::chunked_backward):
 //   dDelta = P^T dO + Kd dS                      Kd = kn e^(Gamma_C - Gamma)
 //   dS0    = scale (qn e^Gamma)^T dO + e^Gamma_C dS - W^T dDelta
 //   dP     = dO Delta^T,  dPs = lower_incl(dP . scale E)
