@@ -26,7 +26,7 @@ from torch import Tensor
 from . import _lib
 
 _DT = {torch.bfloat16: _lib.BF16, torch.float16: _lib.FP16, torch.float32: _lib.FP32}
-DEFAULT_CKPT_EVERY = 4  # chunks of 64 tokens between forward state checkpoints kept for the backward
+DEFAULT_CKPT_EVERY = 8  # chunks of 64 tokens between forward state checkpoints kept for the backward
 
 
 def _ptr(t: Optional[Tensor]):
