@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     };
     if (tid == 0 && nchunks > 0) {
         issue_k(c_begin, 0);
-        issue_q(c_begin);
+        if (!recompute) issue_q(c_begin);  // recompute mode forms no outputs: Q is never read
         if (!a.zero_v) issue_v(c_begin);
     }
 
@@ -347,10 +347,11 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (b) this chunk's Q, K tiles; prefetch the next chunk's into the other stage
         wait_bar(&bar_k[s], (uint32_t)(cl >> 1) & 1u, a.err, 1, ok);
-        wait_bar(bar_q, (uint32_t)cl & 1u, a.err, 7, ok);
+        if (!recompute) wait_bar(bar_q, (uint32_t)cl & 1u, a.err, 7, ok);
         if (tid == 0 && c + 1 < nchunks) issue_k(c + 1, s ^ 1);  // the other K slot: MMA7 of chunk c-1 is done
 
-        // (c) MMA1: D1 = [Q;K] K^T (even chunks) or [K;Q] K^T (odd) on the raw tiles (M=128, N=64, K=128)
+        // (c) MMA1: D1 = [Q;K] K^T (even chunks) or [K;Q] K^T (odd) on the raw tiles (M=128, N=64, K=128);
+        //     in recompute mode the Q half of A is whatever the Q slot holds and its rows of D1 go unread
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id = idesc_bf16(128, 64, 0, 0);
@@ -363,8 +364,9 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
         __syncthreads();
         if (tid >= 32 && tid < 64) vG[tid] += vG[31];
-        // (d) meanwhile: row norms of q and k (4 threads per row, 32 elements each)
-        {
+        // (d) meanwhile: row norms of q and k (4 threads per row, 32 elements each; rows 0-63 are q, on warps
+        //     0-7, skipped in recompute mode)
+        if (!recompute || tid >= 256) {
             const int r = tid >> 2, part = tid & 3, i = r & 63;
             const uint8_t* rowp = sm + OFF_QK + (part >> 1) * QK_BLK + (r < 64 ? 8192 : kofs) + i * 128;
             float ss = 0.f;
@@ -548,7 +550,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
         wait_mma(bar_mma, mma_phase, a.err, 4, ok);
         // Q is consumed: load the next chunk's Q
-        if (tid == 0 && c + 1 < nchunks) issue_q(c + 1);
+        if (tid == 0 && !recompute && c + 1 < nchunks) issue_q(c + 1);
 
         // (l) Delta^T (TMEM, lane = dv) -> hi/lo bf16 Delta^T and Dd^T (K-major A operands)
         {
