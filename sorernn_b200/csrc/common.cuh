@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "../../include/gdn_b200.h"
 
 namespace gdn {
@@ -86,6 +88,31 @@ __device__ __forceinline__ void stv(void* p, int64_t i, const float (&v)[PER]) {
         }
     }
 }
+
+// N elements of type TA kept as loaded (not widened to fp32), so that many rows can be in flight in few
+// registers; load() uses the widest vector N elements allow (the address must be aligned to it).
+template <typename TA, int N>
+struct RawVec {
+    static constexpr int BYTES = N * (int)sizeof(TA);
+    static constexpr int CH = BYTES % 16 == 0 ? 16 : (BYTES % 8 == 0 ? 8 : (BYTES % 4 == 0 ? 4 : 2));
+    using Chunk = typename std::conditional<CH == 16, uint4,
+                  typename std::conditional<CH == 8, uint2,
+                  typename std::conditional<CH == 4, uint32_t, uint16_t>::type>::type>::type;
+    union {
+        Chunk c[BYTES / CH];
+        TA h[N];
+    };
+    __device__ __forceinline__ void load(const void* p, int64_t i) {
+        const Chunk* q = reinterpret_cast<const Chunk*>((const TA*)p + i);
+#pragma unroll
+        for (int k = 0; k < BYTES / CH; ++k) c[k] = q[k];
+    }
+    __device__ __forceinline__ void zero() {
+#pragma unroll
+        for (int k = 0; k < BYTES / CH; ++k) c[k] = Chunk{};
+    }
+    __device__ __forceinline__ float get(int e) const { return ld(h, e); }
+};
 
 }  // namespace gdn
 

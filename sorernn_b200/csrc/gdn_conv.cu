@@ -5,15 +5,15 @@
 // the document start contributes nothing, as the reference's masked_fill does).
 // Backward, with dz = dy silu'(z) recomputed from x:
 //   dx[t, c] = sum_{j < K} w[c, K-1-j] dz[t+j, c]   over t+j inside t's document,
-//   dw[c, K-1-j] = sum_t x[t-j, c] dz[t, c]          (fp32, reduced per block, then one atomic add each).
-// One thread per (tile of 32 consecutive tokens, 8 channels forward / 4 backward): a sliding window over
-// the taps, vector row loads, fp32 accumulation, weights and weight gradients in registers.
+//   dw[c, K-1-j] = sum_t x[t-j, c] dz[t, c]          (fp32 per thread over its range, one atomic add per block).
+// HBM-bound streaming: rows are bulk-copied into a shared-memory ring and each thread slides a window over
+// the taps for its 16-byte channel group (conv_kernel below); fp32 accumulation, weights and weight
+// gradients in registers.
+#include "bulk.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
 namespace gdn {
-
-constexpr int kConvThreads = 256;
 
 struct ConvArgs {
     const void *x, *w, *dy;
@@ -29,7 +29,7 @@ __device__ __forceinline__ float ld_w(const void* p, int dtype, int64_t i) {
     if (dtype == GDN_BF16) return __bfloat162float(((const __nv_bfloat16*)p)[i]);
     return __half2float(((const __half*)p)[i]);
 }
-__device__ __forceinline__ float sig(float x) { return 1.f / (1.f + expf(-x)); }
+__device__ __forceinline__ float sig(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 // [start, end) of the document holding flattened token t
 __device__ __forceinline__ void doc_span(const ConvArgs& a, int64_t t, int64_t& s, int64_t& e) {
@@ -48,202 +48,250 @@ __device__ __forceinline__ void doc_span(const ConvArgs& a, int64_t t, int64_t& 
     e = a.cu[lo + 1];
 }
 
-constexpr int kConvTile = 32;  // consecutive tokens per thread (a sliding window over the taps)
+namespace cvs {
+constexpr int STAGES = 3;
+// one stage: TT rows of the slab of every staged input (backward: one block per SM, so larger stages)
+template <bool BWD> __host__ __device__ constexpr uint32_t stage_bytes() { return BWD ? 65536 : 32768; }
+constexpr uint32_t SLAB_BYTES = 4096;    // bytes of a row one block covers
+// bytes of a row one thread covers: 16 forward; 8 backward, whose windows hold twice the state per channel
+template <bool BWD> __host__ __device__ constexpr int group_bytes() { return BWD ? 8 : 16; }
+}  // namespace cvs
 
-// Thread (token tile, group of CW channels): the C / CW threads of a tile are consecutive, so a warp's row
-// loads are contiguous. Window rows before the document start read as zero. The next row is prefetched
-// one token ahead.
-template <typename TA, int K, int CW>
-__global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const ConvArgs a) {
-    const int64_t groups = a.C / CW, BT = a.B * a.T, tiles = (BT + kConvTile - 1) / kConvTile;
-    for (int64_t i = blockIdx.x * (int64_t)kConvThreads + threadIdx.x; i < tiles * groups;
-         i += (int64_t)gridDim.x * kConvThreads) {
-        const int64_t c0 = (i % groups) * CW, t0 = (i / groups) * kConvTile;
-        const int64_t t1 = t0 + kConvTile < BT ? t0 + kConvTile : BT;
-        float w[CW][K];
+// Block = (slab of channels, contiguous range [tb, te) of the flattened token axis). The block streams the
+// rows u of its range, plus the K-1 rows before it (and, backward, the K-1 after it), through a STAGES-deep
+// ring: tile i of TT rows lands in stage i % STAGES by bulk copies (one per input when the slab is the whole
+// row, else one per row, issued by warp 0). Each thread owns one channel group of the slab (16 bytes
+// forward, 8 backward) and slides a window over the rows in order:
+//   forward:  x window [u-K+1, u] -> y[u] for u in [tb, te)
+//   backward: x window -> z[u], dz[u] for u in [tb, te+K-1); dz window [t, t+K-1] -> dx[t], t = u-K+1 in
+//             [tb, te); dw += x[u-j] dz[u] for u in [tb, te), kept in registers and added once per block.
+// Window rows from before the current document are zero, and dz rows past the document end of t are masked.
+template <typename TA, int K, bool BWD>
+__global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t range_len, int nslabs) {
+    using namespace cvs;
+    constexpr int VEC = group_bytes<BWD>() / (int)sizeof(TA);  // channels per thread
+    constexpr int MAX_GROUPS = SLAB_BYTES / group_bytes<BWD>();
+    constexpr int NTN = BWD ? 2 : 1;                              // staged inputs: x (and dy)
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr uint32_t STAGE_BYTES = stage_bytes<BWD>();
+    uint64_t* bar = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+    const int tid = threadIdx.x;
+    const int64_t BT = a.B * a.T;
+    const int slab = blockIdx.x % nslabs;
+    const int64_t c_begin = (int64_t)slab * MAX_GROUPS * VEC;
+    const int64_t cs = (a.C - c_begin < MAX_GROUPS * VEC) ? a.C - c_begin : MAX_GROUPS * VEC;  // slab width
+    const uint32_t rbs = (uint32_t)(cs * sizeof(TA));                                       // slab row bytes
+    const int64_t rstride = a.C * (int64_t)sizeof(TA);                                      // global row bytes
+    const uint32_t per_t = STAGE_BYTES / NTN;
+    const int TT = (int)(per_t / rbs) < 64 ? (int)(per_t / rbs) : 64;  // rows per tile
+    const int64_t tb = (blockIdx.x / nslabs) * range_len;
+    const int64_t te = tb + range_len < BT ? tb + range_len : BT;
+    if (tb >= te) return;
+    const int64_t u_lo = tb - (K - 1) > 0 ? tb - (K - 1) : 0;
+    const int64_t u_end = BWD ? te + (K - 1) : te;  // rows the window passes (past BT: zero)
+    const int64_t u_hi = u_end < BT ? u_end : BT;   // rows that exist
+    const int64_t ntiles = (u_hi - u_lo + TT - 1) / TT;
+    const void* src[2] = {a.x, a.dy};
+
+    auto issue = [&](int64_t tile, int s) {  // warp 0: rows [u0, u0 + n) of every staged input into stage s
+        const int64_t u0 = u_lo + tile * TT;
+        const int n = (int)(u_hi - u0 < TT ? u_hi - u0 : TT);
+        if ((tid & 31) == 0) sm100::mbar_arrive_expect_tx(&bar[s], NTN * n * rbs);
+        __syncwarp();
 #pragma unroll
-        for (int q = 0; q < CW; ++q)
-#pragma unroll
-            for (int j = 0; j < K; ++j) w[q][j] = ld_w(a.w, a.w_dtype, (c0 + q) * K + j);
-        int64_t s, e;
-        doc_span(a, t0, s, e);
-        float win[K][CW];  // win[j] = x[t - j]
-#pragma unroll
-        for (int j = 1; j < K; ++j) {
-            if (t0 - j >= s) ldv<TA, CW>(a.x, (t0 - j) * a.C + c0, win[j]);
-            else {
-#pragma unroll
-                for (int q = 0; q < CW; ++q) win[j][q] = 0.f;
+        for (int t = 0; t < NTN; ++t) {
+            uint8_t* dst = smem + s * STAGE_BYTES + t * per_t;
+            const uint8_t* g = (const uint8_t*)src[t] + u0 * rstride + c_begin * (int64_t)sizeof(TA);
+            if (cs == a.C) {  // whole rows: one contiguous copy
+                if ((tid & 31) == 0) bulk::load(dst, g, n * rbs, &bar[s]);
+            } else {
+                for (int r = tid & 31; r < n; r += 32) bulk::load(dst + r * rbs, g + r * rstride, rbs, &bar[s]);
             }
         }
-        float nxt[CW];
-        ldv<TA, CW>(a.x, t0 * a.C + c0, nxt);
-        for (int64_t t = t0; t < t1; ++t) {
-            if (t >= e) {  // the next document starts here: no taps before it
-                doc_span(a, t, s, e);
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) sm100::mbar_init(&bar[s], 1);
+        sm100::fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid < 32)
+        for (int s = 0; s < STAGES && s < ntiles; ++s) issue(s, s);
+
+    const bool active = (int64_t)tid * VEC < cs;
+    const int64_t c0 = c_begin + (int64_t)tid * VEC;
+    float w[VEC][K], dw[VEC][K];
 #pragma unroll
-                for (int j = 1; j < K; ++j)
+    for (int q = 0; q < VEC; ++q)
 #pragma unroll
-                    for (int q = 0; q < CW; ++q) win[j][q] = 0.f;
-            }
+        for (int j = 0; j < K; ++j) {
+            w[q][j] = active ? ld_w(a.w, a.w_dtype, (c0 + q) * K + j) : 0.f;
+            dw[q][j] = 0.f;
+        }
+    float xw[K][VEC];   // xw[j] = x[u - j] (zero before the document start)
+    float dzw[K][VEC];  // dzw[j] = dz[u - K + 1 + j] (backward)
+    int64_t ew[K];      // document end of the token of dzw[j]
 #pragma unroll
-            for (int q = 0; q < CW; ++q) win[0][q] = nxt[q];
-            if (t + 1 < t1) ldv<TA, CW>(a.x, (t + 1) * a.C + c0, nxt);
-            float z[CW];
+    for (int j = 0; j < K; ++j) {
+        ew[j] = 0;
 #pragma unroll
-            for (int q = 0; q < CW; ++q) {
+        for (int q = 0; q < VEC; ++q) xw[j][q] = dzw[j][q] = 0.f;
+    }
+    int64_t s_doc, e_doc;
+    doc_span(a, u_lo, s_doc, e_doc);
+
+    // one row u of the current document through the window; `have`: the row exists (u < BT), else zero.
+    // No branches besides the predicated stores, so the unrolled rows of a document segment interleave.
+    auto row = [&](int64_t u, const TA* xrow, const TA* dyrow, bool have) {
+#pragma unroll
+        for (int j = K - 1; j >= 1; --j)
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) xw[j][q] = xw[j - 1][q];
+        if (have) ldv<TA, VEC>(xrow, 0, xw[0]);
+        else {
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) xw[0][q] = 0.f;
+        }
+        if constexpr (!BWD) {
+            float y[VEC];
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) {
                 float acc = 0.f;
 #pragma unroll
-                for (int j = 0; j < K; ++j) acc = fmaf(w[q][K - 1 - j], win[j][q], acc);
-                z[q] = a.silu ? acc * sig(acc) : acc;
+                for (int j = 0; j < K; ++j) acc = fmaf(w[q][K - 1 - j], xw[j][q], acc);
+                y[q] = a.silu ? acc * sig(acc) : acc;
             }
-            stv<TA, CW>(a.y, t * a.C + c0, z);
+            if (active && u >= tb) stv<TA, VEC>(a.y, u * a.C + c0, y);
+        } else {
+            float dyv[VEC];
+            if (have) ldv<TA, VEC>(dyrow, 0, dyv);
+            else {
 #pragma unroll
-            for (int j = K - 1; j >= 1; --j)
-#pragma unroll
-                for (int q = 0; q < CW; ++q) win[j][q] = win[j - 1][q];
-        }
-    }
-}
-
-// Backward over the same tiles: a window of x rows [t-K+1, t+K-1] and of dz rows [t, t+K-1] slides
-// forward (the rows entering at t+K-1 are prefetched a token ahead); dw stays in registers for the tile.
-template <typename TA, int K, int CW>
-__global__ void __launch_bounds__(kConvThreads, 2) conv_bwd_kernel(const ConvArgs a) {
-    extern __shared__ float s_dw[];  // [C][K] block partials
-    for (int64_t i = threadIdx.x; i < a.C * K; i += kConvThreads) s_dw[i] = 0.f;
-    __syncthreads();
-    const int64_t groups = a.C / CW, BT = a.B * a.T, tiles = (BT + kConvTile - 1) / kConvTile;
-    for (int64_t i = blockIdx.x * (int64_t)kConvThreads + threadIdx.x; i < tiles * groups;
-         i += (int64_t)gridDim.x * kConvThreads) {
-        const int64_t c0 = (i % groups) * CW, t0 = (i / groups) * kConvTile;
-        const int64_t t1 = t0 + kConvTile < BT ? t0 + kConvTile : BT;
-        float w[CW][K], dw[CW][K];
-#pragma unroll
-        for (int q = 0; q < CW; ++q)
-#pragma unroll
-            for (int j = 0; j < K; ++j) {
-                w[q][j] = ld_w(a.w, a.w_dtype, (c0 + q) * K + j);
-                dw[q][j] = 0.f;
+                for (int q = 0; q < VEC; ++q) dyv[q] = 0.f;
             }
-        int64_t s = 0, e = 0;
-        float xw[2 * K - 1][CW];  // xw[r] = x[t - (K-1) + r]
-        float dzw[K][CW];         // dzw[j] = dz[t + j]
-        float px[CW], pdy[CW];    // raw rows t + K (prefetch for the next slide)
-        // dz at token u (inside [s, e)) from dy[u] and the x window rows ending at u (xw index base..base+K-1)
-        auto make_dz = [&](int64_t u, int base, const float (&dyv)[CW], float (&out)[CW]) {
 #pragma unroll
-            for (int q = 0; q < CW; ++q) {
+            for (int j = 0; j < K - 1; ++j) {
+                ew[j] = ew[j + 1];
+#pragma unroll
+                for (int q = 0; q < VEC; ++q) dzw[j][q] = dzw[j + 1][q];
+            }
+            const bool acc_dw = u < te;  // rows past the range feed dx only
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) {
                 float z = 0.f;
 #pragma unroll
-                for (int i2 = 0; i2 < K; ++i2) z = fmaf(w[q][K - 1 - i2], xw[base + K - 1 - i2][q], z);
+                for (int j = 0; j < K; ++j) z = fmaf(w[q][K - 1 - j], xw[j][q], z);
                 float d = dyv[q];
                 if (a.silu) {
                     const float sg = sig(z);
                     d *= sg * (1.f + z * (1.f - sg));
                 }
-                out[q] = u < e ? d : 0.f;
+                const float dd = acc_dw ? d : 0.f;
+#pragma unroll
+                for (int j = 0; j < K; ++j) dw[q][K - 1 - j] = fmaf(xw[j][q], dd, dw[q][K - 1 - j]);
+                dzw[K - 1][q] = d;
             }
-        };
-        bool fresh = true;
-        for (int64_t t = t0; t < t1; ++t) {
-            if (fresh || t >= e) {  // (re)build both windows at t: first token of the tile or of a document
-                doc_span(a, t, s, e);
+            ew[K - 1] = have ? e_doc : 0;
+            const int64_t t = u - (K - 1);  // < te, as u < te + K - 1
+            float dx[VEC];
 #pragma unroll
-                for (int r = 0; r < 2 * K - 1; ++r) {
-                    const int64_t u = t - (K - 1) + r;
-                    if (u >= s && u < e) ldv<TA, CW>(a.x, u * a.C + c0, xw[r]);
-                    else {
-#pragma unroll
-                        for (int q = 0; q < CW; ++q) xw[r][q] = 0.f;
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < K; ++j) {
-                    float dyv[CW];
-                    if (t + j < e) ldv<TA, CW>(a.dy, (t + j) * a.C + c0, dyv);
-                    else {
-#pragma unroll
-                        for (int q = 0; q < CW; ++q) dyv[q] = 0.f;
-                    }
-                    make_dz(t + j, j, dyv, dzw[j]);
-                }
-                fresh = false;
-            } else {  // slide by one token: x row and dz at t+K-1 enter from the prefetch
-                const int64_t u = t + K - 1;
-#pragma unroll
-                for (int r = 0; r < 2 * K - 2; ++r)
-#pragma unroll
-                    for (int q = 0; q < CW; ++q) xw[r][q] = xw[r + 1][q];
-#pragma unroll
-                for (int q = 0; q < CW; ++q) xw[2 * K - 2][q] = u < e ? px[q] : 0.f;
-#pragma unroll
-                for (int j = 0; j < K - 1; ++j)
-#pragma unroll
-                    for (int q = 0; q < CW; ++q) dzw[j][q] = dzw[j + 1][q];
-                make_dz(u, K - 1, pdy, dzw[K - 1]);
-            }
-            if (t + K < BT && t + 1 < t1) {  // rows entering at the next step
-                ldv<TA, CW>(a.x, (t + K) * a.C + c0, px);
-                ldv<TA, CW>(a.dy, (t + K) * a.C + c0, pdy);
-            }
-            float dx[CW];
-#pragma unroll
-            for (int q = 0; q < CW; ++q) {
+            for (int q = 0; q < VEC; ++q) {
                 float acc = 0.f;
 #pragma unroll
-                for (int j = 0; j < K; ++j) acc = fmaf(w[q][K - 1 - j], dzw[j][q], acc);
+                for (int j = 0; j < K; ++j) acc = fmaf(t + j < ew[0] ? w[q][K - 1 - j] : 0.f, dzw[j][q], acc);
                 dx[q] = acc;
-#pragma unroll
-                for (int i2 = 0; i2 < K; ++i2) dw[q][K - 1 - i2] = fmaf(xw[K - 1 - i2][q], dzw[0][q], dw[q][K - 1 - i2]);
             }
-            stv<TA, CW>(a.dx, t * a.C + c0, dx);
+            if (active && t >= tb) stv<TA, VEC>(a.dx, t * a.C + c0, dx);
         }
+    };
+
+    bool ok = true;
+    for (int64_t tile = 0; tile < ntiles; ++tile) {
+        const int s = (int)(tile % STAGES);
+        ok = sm100::mbar_wait(&bar[s], (uint32_t)(tile / STAGES) & 1u, nullptr, 0, ok ? (1u << 22) : 1u) && ok;
+        const int64_t u0 = u_lo + tile * TT;
+        const int n = (int)(u_hi - u0 < TT ? u_hi - u0 : TT);
+        // inactive threads (past a narrow slab's last group) read the group-0 column and store nothing
+        const uint8_t* st = smem + s * STAGE_BYTES + (active ? (uint32_t)tid * group_bytes<BWD>() : 0u);
+        int r = 0;
+        while (r < n) {
+            if (u0 + r >= e_doc) {  // a new document starts here: no taps before it
+                doc_span(a, u0 + r, s_doc, e_doc);
 #pragma unroll
-        for (int q = 0; q < CW; ++q)
+                for (int j = 0; j < K; ++j)
 #pragma unroll
-            for (int j = 0; j < K; ++j) atomicAdd(&s_dw[(c0 + q) * K + j], dw[q][j]);
+                    for (int q = 0; q < VEC; ++q) xw[j][q] = 0.f;
+            }
+            const int r_end = (int)(e_doc - u0 < n ? e_doc - u0 : n);  // rows of this document in the tile
+            if constexpr (BWD) {
+                for (; r < r_end && u0 + r < tb; ++r) {  // rows before the range only fill the x window
+#pragma unroll
+                    for (int j = K - 1; j >= 1; --j)
+#pragma unroll
+                        for (int q = 0; q < VEC; ++q) xw[j][q] = xw[j - 1][q];
+                    ldv<TA, VEC>((const TA*)(st + r * rbs), 0, xw[0]);
+                }
+            }
+#pragma unroll 4
+            for (; r < r_end; ++r) row(u0 + r, (const TA*)(st + r * rbs), (const TA*)(st + per_t + r * rbs), true);
+        }
+        __syncthreads();  // every read of stage s is done: refill it
+        if (tid < 32 && tile + STAGES < ntiles) issue(tile + STAGES, s);
     }
-    __syncthreads();
-    for (int64_t i = threadIdx.x; i < a.C * K; i += kConvThreads)
-        if (s_dw[i] != 0.f) atomicAdd(&a.dw[i], s_dw[i]);
-}
-
-constexpr int kConvFwdCW = 8, kConvBwdCW = 4;
-
-static unsigned conv_grid(int64_t work) {
-    const int64_t blocks = (work + kConvThreads - 1) / kConvThreads;
-    return (unsigned)(blocks < 148 * 8 ? (blocks > 0 ? blocks : 1) : 148 * 8);
+    for (int64_t u = u_hi; u < u_end; ++u) row(u, nullptr, nullptr, false);  // backward: rows past BT
+    if constexpr (BWD) {
+        if (active) {
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) {
+                if constexpr (K == 4) {
+                    atomicAdd(reinterpret_cast<float4*>(a.dw + (c0 + q) * K),
+                              make_float4(dw[q][0], dw[q][1], dw[q][2], dw[q][3]));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < K; ++j) atomicAdd(&a.dw[(c0 + q) * K + j], dw[q][j]);
+                }
+            }
+        }
+    }
 }
 
 template <typename TA>
 static int conv_launch(const ConvArgs& a, int K, bool bwd, cudaStream_t s) {
-    const int cw = bwd ? kConvBwdCW : kConvFwdCW;
-    const unsigned grid = conv_grid((a.B * a.T + kConvTile - 1) / kConvTile * (a.C / cw));
-    const size_t smem = bwd ? (size_t)a.C * K * sizeof(float) : 0;
-    if (bwd && smem > 48 * 1024) {
-        auto set = [&](const void* f) { return cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); };
-        if ((K == 1 && set((const void*)conv_bwd_kernel<TA, 1, kConvBwdCW>) != cudaSuccess) ||
-            (K == 2 && set((const void*)conv_bwd_kernel<TA, 2, kConvBwdCW>) != cudaSuccess) ||
-            (K == 3 && set((const void*)conv_bwd_kernel<TA, 3, kConvBwdCW>) != cudaSuccess) ||
-            (K == 4 && set((const void*)conv_bwd_kernel<TA, 4, kConvBwdCW>) != cudaSuccess))
-            return GDN_ERR_LAUNCH;
-    }
-#define CONV_CASE(KK)                                                                       \
-    case KK:                                                                                \
-        if (bwd) conv_bwd_kernel<TA, KK, kConvBwdCW><<<grid, kConvThreads, smem, s>>>(a);   \
-        else conv_fwd_kernel<TA, KK, kConvFwdCW><<<grid, kConvThreads, 0, s>>>(a);          \
-        break;
-    switch (K) {
-        CONV_CASE(1)
-        CONV_CASE(2)
-        CONV_CASE(3)
-        CONV_CASE(4)
+    using namespace cvs;
+    const int VEC = (bwd ? group_bytes<true>() : group_bytes<false>()) / (int)sizeof(TA);
+    const int MAX_GROUPS = (int)SLAB_BYTES / (bwd ? group_bytes<true>() : group_bytes<false>());
+    const int64_t BT = a.B * a.T;
+    const int nslabs = (int)((a.C + MAX_GROUPS * VEC - 1) / (MAX_GROUPS * VEC));
+    const int64_t g0 = (a.C < MAX_GROUPS * VEC ? a.C : MAX_GROUPS * VEC) / VEC;  // groups of the widest slab
+    const int nthr = (int)((g0 + 31) / 32 * 32);
+    const size_t smem = (size_t)STAGES * (bwd ? stage_bytes<true>() : stage_bytes<false>()) + bulk::kBarBytes;
+    const void* k = nullptr;
+    switch (K * 2 + (bwd ? 1 : 0)) {
+        case 2: k = (const void*)conv_kernel<TA, 1, false>; break;
+        case 3: k = (const void*)conv_kernel<TA, 1, true>; break;
+        case 4: k = (const void*)conv_kernel<TA, 2, false>; break;
+        case 5: k = (const void*)conv_kernel<TA, 2, true>; break;
+        case 6: k = (const void*)conv_kernel<TA, 3, false>; break;
+        case 7: k = (const void*)conv_kernel<TA, 3, true>; break;
+        case 8: k = (const void*)conv_kernel<TA, 4, false>; break;
+        case 9: k = (const void*)conv_kernel<TA, 4, true>; break;
         default: return GDN_ERR_SHAPE;
     }
-#undef CONV_CASE
+    int per_sm = 0;
+    if (bulk::allow_smem(k, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, nthr, smem) != cudaSuccess || per_sm < 1)
+        return GDN_ERR_LAUNCH;
+    // ranges per slab: fill every SM's resident blocks, no range shorter than 16 tokens
+    int64_t nranges = ((int64_t)bulk::sm_count() * per_sm + nslabs - 1) / nslabs;
+    if (nranges > (BT + 15) / 16) nranges = (BT + 15) / 16;
+    if (nranges < 1) nranges = 1;
+    const int64_t range_len = (BT + nranges - 1) / nranges;
+    nranges = (BT + range_len - 1) / range_len;
+    void* args[] = {(void*)&a, (void*)&range_len, (void*)&nslabs};
+    if (cudaLaunchKernel(k, dim3((unsigned)(nranges * nslabs)), dim3(nthr), args, smem, s) != cudaSuccess)
+        return GDN_ERR_LAUNCH;
     count_launch();
-    return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+    return GDN_OK;
 }
 
 }  // namespace gdn
@@ -282,7 +330,7 @@ extern "C" int gdn_causal_conv1d_bwd(int64_t B, int64_t T, int64_t C, int64_t K,
     int st = conv_check(B, T, C, K, act_dtype, w_dtype, cu_seqlens, N);
     if (st != GDN_OK) return st;
     if (!x || !weight || !dy || !dx || !dweight) return GDN_ERR_ARGUMENT;
-    if (((uintptr_t)x | (uintptr_t)dy | (uintptr_t)dx) % 16) return GDN_ERR_ALIGN;
+    if (((uintptr_t)x | (uintptr_t)dy | (uintptr_t)dx | (uintptr_t)dweight) % 16) return GDN_ERR_ALIGN;
     cudaStream_t s = (cudaStream_t)stream;
     if (cudaMemsetAsync(dweight, 0, C * K * sizeof(float), s) != cudaSuccess) return GDN_ERR_LAUNCH;
     if (B * T == 0) return GDN_OK;

@@ -6,27 +6,30 @@
 // Backward, with s = silu(g), a = n w:
 //   dg = dy a s'(g),  s'(g) = sigmoid(g) (1 + g (1 - sigmoid(g)))
 //   dn = dy s w,  dx = r (dn - n mean(dn n)),  dw = sum over rows of dy s n
-// One warp per row; each lane holds D/32 consecutive features (D % 32 == 0, D <= 1024). dw is reduced
-// per block in shared memory and added to global memory with one atomic add per feature per block.
+// HBM-bound streaming: each block walks tiles of whole rows (8 KB of each input per tile), bulk-copied into
+// a 3-stage shared-memory ring by one thread, so two tiles per block are in flight while the block computes
+// the third. A row of D features is held by LPR = min(32, D / VEC) consecutive lanes, PER = D / LPR features
+// each (VEC = the elements of 16 bytes: at D = 128 bf16, 16 lanes of 8 features). Outputs go straight from
+// registers to global memory in 16-byte stores. dw is reduced across the lanes that share features, then
+// per block in shared memory, then added to global memory with one atomic add per feature per block.
+#include "bulk.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
 namespace gdn {
 
-constexpr int kNgWarps = 8;
-constexpr int kNgMaxPer = 32;  // features per lane: D <= 1024
+namespace ngs {
+constexpr int NTHR = 256;
+constexpr int STAGES = 3;
+constexpr uint32_t TILE = 8192;  // bytes of one input per tile (whole rows)
+}  // namespace ngs
 
 __device__ __forceinline__ float ld_c(const void* p, int dtype, int64_t i) {
     if (dtype == GDN_FP32) return ((const float*)p)[i];
     if (dtype == GDN_BF16) return __bfloat162float(((const __nv_bfloat16*)p)[i]);
     return __half2float(((const __half*)p)[i]);
 }
-__device__ __forceinline__ void st_c(void* p, int dtype, int64_t i, float x) {
-    if (dtype == GDN_FP32) ((float*)p)[i] = x;
-    else if (dtype == GDN_BF16) ((__nv_bfloat16*)p)[i] = __float2bfloat16_rn(x);
-    else ((__half*)p)[i] = __float2half_rn(x);
-}
-__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + expf(-x)); }
+__device__ __forceinline__ float sigm(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 struct NormGateArgs {
     const void *x, *g, *w, *dy;
@@ -37,85 +40,148 @@ struct NormGateArgs {
     float eps;
 };
 
-template <typename TA, int PER>
-__global__ void __launch_bounds__(32 * kNgWarps) norm_gate_fwd_kernel(const NormGateArgs a) {
-    const int lane = threadIdx.x & 31;
-    float w[PER];
+template <int LPR>
+__device__ __forceinline__ float group_sum(float x) {  // sum over the LPR lanes of this row
 #pragma unroll
-    for (int e = 0; e < PER; ++e) w[e] = ld_c(a.w, a.w_dtype, lane * PER + e);
-    const int64_t warp0 = blockIdx.x * (int64_t)kNgWarps + (threadIdx.x >> 5);
-    for (int64_t r = warp0; r < a.rows; r += (int64_t)gridDim.x * kNgWarps) {
-        const int64_t base = r * a.D + lane * PER;
-        float x[PER], g[PER], y[PER], ss = 0.f;
-        ldv<TA, PER>(a.x, base, x);
-        ldv<TA, PER>(a.g, base, g);
-#pragma unroll
-        for (int e = 0; e < PER; ++e) ss = fmaf(x[e], x[e], ss);
-        const float rs = rsqrtf(warp_sum(ss) / a.D + a.eps);
-#pragma unroll
-        for (int e = 0; e < PER; ++e) y[e] = x[e] * rs * w[e] * g[e] * sigm(g[e]);
-        stv<TA, PER>(a.y, base, y);
-    }
+    for (int o = LPR / 2; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
 }
 
-template <typename TA, int PER>
-__global__ void __launch_bounds__(32 * kNgWarps) norm_gate_bwd_kernel(const NormGateArgs a) {
-    __shared__ float s_dw[1024];
-    for (int i = threadIdx.x; i < a.D; i += 32 * kNgWarps) s_dw[i] = 0.f;
+// NT inputs staged per tile: x, g (forward) and dy (backward)
+template <typename TA, int PER, int LPR, bool BWD>
+__global__ void __launch_bounds__(ngs::NTHR) norm_gate_kernel(const NormGateArgs a) {
+    using namespace ngs;
+    constexpr int NT = BWD ? 3 : 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* bar = (uint64_t*)(smem + STAGES * NT * TILE);
+    float* s_dw = (float*)(smem + STAGES * NT * TILE + bulk::kBarBytes);  // [D], backward only
+    const int tid = threadIdx.x, lane = tid & 31, f0 = (lane % LPR) * PER;
+    const int rpass = NTHR / LPR;                    // rows one pass of the block covers
+    const int row_in_pass = (tid >> 5) * (32 / LPR) + lane / LPR;
+    const uint32_t rb = (uint32_t)a.D * sizeof(TA);  // bytes per row
+    const int tr = (int)(TILE / rb);                 // rows per tile
+    const int64_t tiles = (a.rows + tr - 1) / tr;
+    const void* src[3] = {a.x, a.g, a.dy};
+
+    auto issue = [&](int64_t tile, int s) {  // thread 0: the tile's rows of every input into stage s
+        const int64_t r0 = tile * tr;
+        const uint32_t bytes = (uint32_t)((a.rows - r0 < tr ? a.rows - r0 : tr) * rb);
+        sm100::mbar_arrive_expect_tx(&bar[s], NT * bytes);
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+            bulk::load(smem + (s * NT + t) * TILE, (const uint8_t*)src[t] + r0 * rb, bytes, &bar[s]);
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) sm100::mbar_init(&bar[s], 1);
+        sm100::fence_barrier_init();
+    }
+    if (BWD)
+        for (int i = tid; i < a.D; i += NTHR) s_dw[i] = 0.f;
     __syncthreads();
-    const int lane = threadIdx.x & 31;
+    if (tid == 0)
+        for (int s = 0; s < STAGES; ++s)
+            if (blockIdx.x + (int64_t)s * gridDim.x < tiles) issue(blockIdx.x + (int64_t)s * gridDim.x, s);
+
     float w[PER], dwp[PER];
 #pragma unroll
     for (int e = 0; e < PER; ++e) {
-        w[e] = ld_c(a.w, a.w_dtype, lane * PER + e);
+        w[e] = ld_c(a.w, a.w_dtype, f0 + e);
         dwp[e] = 0.f;
     }
-    const int64_t warp0 = blockIdx.x * (int64_t)kNgWarps + (threadIdx.x >> 5);
-    for (int64_t r = warp0; r < a.rows; r += (int64_t)gridDim.x * kNgWarps) {
-        const int64_t base = r * a.D + lane * PER;
-        float x[PER], g[PER], dy[PER], dn[PER], dg[PER], dx[PER], ss = 0.f;
-        ldv<TA, PER>(a.x, base, x);
-        ldv<TA, PER>(a.g, base, g);
-        ldv<TA, PER>(a.dy, base, dy);
+    bool ok = true;
+    int it = 0;
+    for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+        const int s = it % STAGES;
+        ok = sm100::mbar_wait(&bar[s], (uint32_t)(it / STAGES) & 1u, nullptr, 0, ok ? (1u << 22) : 1u) && ok;
+        const int64_t r0 = tile * tr;
+        const int nr = (int)(a.rows - r0 < tr ? a.rows - r0 : tr);
+        const uint8_t* st = smem + s * NT * TILE;
+        for (int p = 0; p < tr; p += rpass) {  // every lane takes part in the row reductions
+            const int rr = p + row_in_pass;
+            const bool valid = rr < nr;
+            const int rs_ = valid ? rr : 0;  // rows past the tile's end read row 0 and store nothing
+            float x[PER], g[PER];
+            ldv<TA, PER>(st, (int64_t)rs_ * a.D + f0, x);
+            ldv<TA, PER>(st + TILE, (int64_t)rs_ * a.D + f0, g);
+            float ss = 0.f;
 #pragma unroll
-        for (int e = 0; e < PER; ++e) ss = fmaf(x[e], x[e], ss);
-        const float rs = rsqrtf(warp_sum(ss) / a.D + a.eps);
-        float c = 0.f;
+            for (int e = 0; e < PER; ++e) ss = fmaf(x[e], x[e], ss);
+            const float rs = rsqrtf(group_sum<LPR>(ss) / a.D + a.eps);
+            const int64_t go = (r0 + rr) * a.D + f0;
+            if constexpr (!BWD) {
+                float y[PER];
 #pragma unroll
-        for (int e = 0; e < PER; ++e) {
-            const float sg = sigm(g[e]), sv = g[e] * sg, n = x[e] * rs;
-            dg[e] = dy[e] * n * w[e] * sg * (1.f + g[e] * (1.f - sg));
-            dn[e] = dy[e] * sv * w[e];
-            dwp[e] = fmaf(dy[e] * sv, n, dwp[e]);
-            c = fmaf(dn[e], n, c);
+                for (int e = 0; e < PER; ++e) y[e] = x[e] * rs * w[e] * g[e] * sigm(g[e]);
+                if (valid) stv<TA, PER>(a.y, go, y);
+            } else {
+                float dy[PER], dn[PER], dg[PER], dx[PER], c = 0.f;
+                ldv<TA, PER>(st + 2 * TILE, (int64_t)rs_ * a.D + f0, dy);
+#pragma unroll
+                for (int e = 0; e < PER; ++e) {
+                    const float sg = sigm(g[e]), sv = g[e] * sg, n = x[e] * rs;
+                    dg[e] = dy[e] * n * w[e] * sg * (1.f + g[e] * (1.f - sg));
+                    dn[e] = dy[e] * sv * w[e];
+                    if (valid) dwp[e] = fmaf(dy[e] * sv, n, dwp[e]);
+                    c = fmaf(dn[e], n, c);
+                }
+                c = group_sum<LPR>(c) / a.D;
+#pragma unroll
+                for (int e = 0; e < PER; ++e) dx[e] = rs * (dn[e] - x[e] * rs * c);
+                if (valid) {
+                    stv<TA, PER>(a.dg, go, dg);
+                    stv<TA, PER>(a.dx, go, dx);
+                }
+            }
         }
-        c = warp_sum(c) / a.D;
-#pragma unroll
-        for (int e = 0; e < PER; ++e) dx[e] = rs * (dn[e] - x[e] * rs * c);
-        stv<TA, PER>(a.dg, base, dg);
-        stv<TA, PER>(a.dx, base, dx);
+        __syncthreads();  // every read of stage s is done: refill it
+        if (tid == 0 && tile + (int64_t)STAGES * gridDim.x < tiles) issue(tile + (int64_t)STAGES * gridDim.x, s);
     }
+    if constexpr (BWD) {
 #pragma unroll
-    for (int e = 0; e < PER; ++e) atomicAdd(&s_dw[lane * PER + e], dwp[e]);
-    __syncthreads();
-    for (int i = threadIdx.x; i < a.D; i += 32 * kNgWarps) atomicAdd(&a.dw[i], s_dw[i]);
+        for (int e = 0; e < PER; ++e) {  // lanes with equal lane % LPR hold the same features
+#pragma unroll
+            for (int o = LPR; o < 32; o <<= 1) dwp[e] += __shfl_xor_sync(0xffffffffu, dwp[e], o);
+        }
+        if (lane < LPR) {
+#pragma unroll
+            for (int e = 0; e < PER; ++e) atomicAdd(&s_dw[f0 + e], dwp[e]);
+        }
+        __syncthreads();
+        for (int i = tid; i < a.D; i += NTHR) atomicAdd(&a.dw[i], s_dw[i]);
+    }
 }
 
-static unsigned ng_grid(int64_t rows) {
-    const int64_t blocks = (rows + kNgWarps - 1) / kNgWarps;
-    return (unsigned)(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
-}
-
-#define NG_DISPATCH_PER(TA, D, KERNEL, ...)                                     \
-    switch ((D) / 32) {                                                         \
-        case 1: KERNEL<TA, 1><<<__VA_ARGS__>>>(a); break;                       \
-        case 2: KERNEL<TA, 2><<<__VA_ARGS__>>>(a); break;                       \
-        case 4: KERNEL<TA, 4><<<__VA_ARGS__>>>(a); break;                       \
-        case 8: KERNEL<TA, 8><<<__VA_ARGS__>>>(a); break;                       \
-        case 16: KERNEL<TA, 16><<<__VA_ARGS__>>>(a); break;                     \
-        case 32: KERNEL<TA, 32><<<__VA_ARGS__>>>(a); break;                     \
-        default: return GDN_ERR_SHAPE;                                          \
+// LPR = min(32, D / VEC) lanes per row, PER = D / LPR features per lane (D a power of two in [32, 1024])
+template <typename TA, bool BWD>
+static int ng_launch(const NormGateArgs& a, cudaStream_t s) {
+    using namespace ngs;
+    constexpr int VEC = 16 / (int)sizeof(TA);
+    const int lpr = a.D / VEC < 32 ? a.D / VEC : 32;
+    const size_t smem = (size_t)STAGES * (BWD ? 3 : 2) * TILE + bulk::kBarBytes + (BWD ? a.D * sizeof(float) : 0);
+    const int64_t tr = TILE / (a.D * sizeof(TA));
+    const int64_t tiles = (a.rows + tr - 1) / tr;
+#define NG_CASE(LPR_, PER_)                                                                               \
+    if (lpr == LPR_ && a.D / lpr == PER_) {                                                              \
+        const void* k_ = (const void*)norm_gate_kernel<TA, PER_, LPR_, BWD>;                             \
+        int per_sm = 0;                                                                                  \
+        if (bulk::allow_smem(k_, smem) != cudaSuccess ||                                                 \
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, norm_gate_kernel<TA, PER_, LPR_, BWD>, \
+                                                          NTHR, smem) != cudaSuccess || per_sm < 1)       \
+            return GDN_ERR_LAUNCH;                                                                       \
+        const int64_t cap = (int64_t)bulk::sm_count() * per_sm;                                          \
+        const unsigned grid_ = (unsigned)(tiles < cap ? tiles : cap);                                    \
+        norm_gate_kernel<TA, PER_, LPR_, BWD><<<grid_, NTHR, smem, s>>>(a);                              \
+        return GDN_OK;                                                                                   \
     }
+    if constexpr (VEC == 8) {
+        NG_CASE(4, 8) NG_CASE(8, 8) NG_CASE(16, 8) NG_CASE(32, 8) NG_CASE(32, 16) NG_CASE(32, 32)
+    } else {
+        NG_CASE(8, 4) NG_CASE(16, 4) NG_CASE(32, 4) NG_CASE(32, 8) NG_CASE(32, 16) NG_CASE(32, 32)
+    }
+#undef NG_CASE
+    return GDN_ERR_SHAPE;
+}
 
 }  // namespace gdn
 
@@ -128,11 +194,14 @@ extern "C" int gdn_rms_norm_gated_fwd(int64_t rows, int64_t D, const void* x, co
     if (rows < 0 || D <= 0 || D > 1024 || D % 32) return GDN_ERR_SHAPE;
     if (!ng_dtype_ok(act_dtype) || !ng_dtype_ok(w_dtype)) return GDN_ERR_DTYPE;
     if (!x || !gate || !weight || !y) return GDN_ERR_ARGUMENT;
+    if (((uintptr_t)x | (uintptr_t)gate | (uintptr_t)y) % 16) return GDN_ERR_ALIGN;
     if (rows == 0) return GDN_OK;
     NormGateArgs a{};
     a.x = x; a.g = gate; a.w = weight; a.y = y;
     a.rows = rows; a.D = (int)D; a.act_dtype = act_dtype; a.w_dtype = w_dtype; a.eps = eps;
-    GDN_DISPATCH_DTYPE(act_dtype, TA, NG_DISPATCH_PER(TA, D, norm_gate_fwd_kernel, ng_grid(rows), 32 * kNgWarps, 0, (cudaStream_t)stream))
+    int st = GDN_ERR_DTYPE;
+    GDN_DISPATCH_DTYPE(act_dtype, TA, st = (ng_launch<TA, false>(a, (cudaStream_t)stream)))
+    if (st != GDN_OK) return st;
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
@@ -143,13 +212,16 @@ extern "C" int gdn_rms_norm_gated_bwd(int64_t rows, int64_t D, const void* x, co
     if (rows < 0 || D <= 0 || D > 1024 || D % 32) return GDN_ERR_SHAPE;
     if (!ng_dtype_ok(act_dtype) || !ng_dtype_ok(w_dtype)) return GDN_ERR_DTYPE;
     if (!x || !gate || !weight || !dy || !dx || !dgate || !dweight) return GDN_ERR_ARGUMENT;
+    if (((uintptr_t)x | (uintptr_t)gate | (uintptr_t)dy | (uintptr_t)dx | (uintptr_t)dgate) % 16) return GDN_ERR_ALIGN;
     cudaStream_t s = (cudaStream_t)stream;
     if (cudaMemsetAsync(dweight, 0, D * sizeof(float), s) != cudaSuccess) return GDN_ERR_LAUNCH;
     if (rows == 0) return GDN_OK;
     NormGateArgs a{};
     a.x = x; a.g = gate; a.w = weight; a.dy = dy; a.dx = dx; a.dg = dgate; a.dw = dweight;
     a.rows = rows; a.D = (int)D; a.act_dtype = act_dtype; a.w_dtype = w_dtype; a.eps = eps;
-    GDN_DISPATCH_DTYPE(act_dtype, TA, NG_DISPATCH_PER(TA, D, norm_gate_bwd_kernel, ng_grid(rows), 32 * kNgWarps, 0, s))
+    int st = GDN_ERR_DTYPE;
+    GDN_DISPATCH_DTYPE(act_dtype, TA, st = (ng_launch<TA, true>(a, s)))
+    if (st != GDN_OK) return st;
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }

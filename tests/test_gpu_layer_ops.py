@@ -12,7 +12,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("D", [128, 64, 32, 1024])
 def test_rms_norm_gated_forward_backward(dtype, D):
     from sorernn_b200.layer_ops import rms_norm_gated
 
@@ -46,13 +46,15 @@ def _doc_ids(cu, T):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("K,varlen", [(4, False), (4, True), (3, True), (2, False)])
-def test_causal_conv1d_silu_forward_backward(dtype, K, varlen):
+# C = 2144: several channel slabs per row (one block covers 4 KB of a row), the last one narrow
+@pytest.mark.parametrize("K,varlen,C", [(4, False, 64), (4, True, 96), (3, True, 96), (2, False, 64), (1, False, 64),
+                                        (4, True, 2144), (3, False, 2144)])
+def test_causal_conv1d_silu_forward_backward(dtype, K, varlen, C):
     from oracle.gdn_oracle import causal_conv1d as conv_ref
     from sorernn_b200.layer_ops import causal_conv1d
 
-    gen = torch.Generator(device="cuda").manual_seed(K * 10 + int(varlen))
-    B, T, C = (1, 301, 96) if varlen else (2, 150, 64)
+    gen = torch.Generator(device="cuda").manual_seed(K * 10 + int(varlen) + C)
+    B, T = (1, 301) if varlen else (2, 150)
     cu = [0, 1, 3, 90, 91, 200, 301] if varlen else None
     x = torch.randn(B, T, C, device="cuda", generator=gen).to(dtype).requires_grad_(True)
     w = (torch.randn(C, K, device="cuda", generator=gen) * K ** -0.5).requires_grad_(True)
