@@ -63,7 +63,7 @@ static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 constexpr int AST = 68;  // padded fp32 row stride (conflict-free float4 rows)
 constexpr uint32_t OFF_A = OFF_D;
 constexpr uint32_t OFF_Y = OFF_A + 64 * AST * 4;
-static_assert(OFF_Y + 32 * 32 * 4 <= OFF_DD, "solve scratch overlaps live tiles");
+static_assert(OFF_Y + 32 * kSolveYStride * 4 <= OFF_DD, "solve scratch overlaps live tiles");
 // TMEM columns
 // O2 (128 columns) reuses D1 + U once both are read; O1 has its own columns (it is computed early).
 constexpr uint32_t T_D1 = 0, T_U = 64, T_O2 = 0, T_O1 = 128, T_S = 256, T_W = 384, T_COLS = 512;
@@ -432,10 +432,10 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
         __syncthreads();
 
-        // (g) T = (I + A)^-1 in place on warps 0-1 (its steps use at most 64 threads), while warps 8-15 do
+        // (g) T = (I + A)^-1 in place on warps 0-7, while warps 8-15 do
         // (e): S0 -> bf16 S0^T operand (hi/lo), TMEM state <- e^G_C S0, checkpoint or recompute tile
-        if (warp < 2) {
-            tri_inverse64<AST, true>(Am, Yb);
+        if (warp < 8) {
+            tri_inverse64<AST>(Am, Yb);
         } else if (warp >= 8) {
             const int half = (warp - 8) >> 2;  // dk columns 64 half .. 64 half + 63 = S0^T block `half`
             const float eGC = vMisc[0];
