@@ -73,7 +73,7 @@ typedef struct gdn_problem {
 /* Human-readable text for a status code (static storage). */
 const char* gdn_status_string(int status);
 
-/* Which kernel family a problem runs on: 1 = chunked tcgen05 (bf16/fp16, DK = DV = 128),
+/* Which kernel family a problem runs on: 1 = chunked tcgen05 (bf16, DK = DV = 128),
  * 0 = recurrent fp32-accumulating kernels (fp32 inputs, other head sizes). */
 int gdn_uses_chunk_kernels(const gdn_problem* p);
 
