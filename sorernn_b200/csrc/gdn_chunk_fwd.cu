@@ -171,7 +171,13 @@ __device__ __forceinline__ void vecN(const float* v, int base, float (&o)[N]) {
     }
 }
 
+// MODE 0: plain forward (o written, no transition-map flags); 1: recompute pass (records, no outputs);
+// 2: the sequence-split passes (zero_v / h0_identity / o_mode 1 / ht_accumulate read at run time)
+template <int MODE>
 __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_constant__ ChunkFwdArgs a) {
+    const int o_mode = MODE == 0 ? 0 : (MODE == 1 ? 2 : a.o_mode);
+    const bool zero_v = MODE == 2 && a.zero_v, h0_identity = MODE == 2 && a.h0_identity;
+    const bool ht_accumulate = MODE == 2 && a.ht_accumulate;
     using namespace cf;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -199,7 +205,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     const int64_t len = eos - bos;
     const int nchunks_seq = (int)((len + 63) / 64);
     // recompute mode: this CTA covers chunks [c_begin, c_end) of its sequence, starting from a checkpoint
-    const bool recompute = a.s0_out != nullptr;
+    constexpr bool recompute = MODE == 1;
     const int c_begin = recompute ? (int)blockIdx.y * a.ckpt_every : 0;
     if (c_begin >= nchunks_seq && c_begin > 0) return;
     const int nchunks = recompute ? min(nchunks_seq, c_begin + a.ckpt_every) : nchunks_seq;
@@ -249,10 +255,10 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         fence_barrier_init();
         prefetch_tmap(&a.tq);
         prefetch_tmap(&a.tk);
-        if (!a.zero_v) prefetch_tmap(&a.tv);
+        if (!zero_v) prefetch_tmap(&a.tv);
     }
     if (warp == 0) tmem_alloc(tmem_slot, T_COLS);
-    if (a.zero_v) {
+    if (zero_v) {
         for (int e = tid; e < 16384 / 16; e += NTHR) ((uint4*)(sm + OFF_V))[e] = make_uint4(0, 0, 0, 0);
         fence_async_smem();
     }
@@ -273,7 +279,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 const int dk = 32 * cq + c0 + i;
-                v[i] = (a.h0_identity && !recompute) ? (dk == row ? 1.f : 0.f) : (h0 ? h0[dk * 128 + row] : 0.f);
+                v[i] = (h0_identity && !recompute) ? (dk == row ? 1.f : 0.f) : (h0 ? h0[dk * 128 + row] : 0.f);
             }
             tmem_st16(tS + lane_base + 32 * cq + c0, v);
         }
@@ -304,7 +310,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     if (tid == 0 && nchunks > 0) {
         issue_k(c_begin, 0);
         if (!recompute) issue_q(c_begin);  // recompute mode forms no outputs: Q is never read
-        if (!a.zero_v) issue_v(c_begin);
+        if (!zero_v) issue_v(c_begin);
     }
 
     const uint32_t sbase = smem_u32(sm);
@@ -463,7 +469,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
         __syncthreads();
         if (recompute && tid == 0) bulk_s2g(rec_g, sm + OFF_S, 32768);  // S0^T hi tile
-        if (tid == 0 && a.o_mode != 2) {  // MMA5 as soon as S0^T is in place: [-; O1] = [-; Q] S0hi
+        if (tid == 0 && o_mode != 2) {  // MMA5 as soon as S0^T is in place: [-; O1] = [-; Q] S0hi
             tc_fence_after();             // (O1 in the otherwise idle columns 128-255; waited on with MMA4)
             const uint32_t id5 = idesc_bf16(128, 128, 0, 0);
             const uint64_t dS_h = desc_kmajor(sbase + OFF_S);
@@ -502,7 +508,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (i) MMA2: W^T = K^T TB^T ; MMA3: U^T = V^T TV^T   (M=128, N=64, K=64 tokens)
         if (tid == 0) {
-            if (!a.zero_v) wait_bar(bar_v, (uint32_t)cl & 1u, a.err, 6, ok);
+            if (!zero_v) wait_bar(bar_v, (uint32_t)cl & 1u, a.err, 6, ok);
             const uint32_t id = idesc_bf16(128, 64, 1, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
@@ -514,7 +520,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
         wait_mma(bar_mma, mma_phase, a.err, 3, ok);
         // V is consumed: load the next chunk's V
-        if (tid == 0 && !a.zero_v && c + 1 < nchunks) issue_v(c + 1);
+        if (tid == 0 && !zero_v && c + 1 < nchunks) issue_v(c + 1);
 
         // (j) W (TMEM rows i = lanes 0-63, columns d) -> -W bf16 [i][d] (K-major B operand of MMA4);
         //     warp column quarter cq writes d = 32 cq .. 32 cq + 31 with 16-byte stores
@@ -594,7 +600,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             for (int ks = 0; ks < 4; ++ks) {
                 const uint64_t dh = dD_ + ks * 2, dl = dDL_ + ks * 2;  // +32 bytes per K step
                 const uint64_t ph = dP_ + ks * 2, pl = dPL_ + ks * 2;
-                if (a.o_mode != 2) {
+                if (o_mode != 2) {
                     umma_bf16(tO2, ph, dh, id6, ks > 0);
                     umma_bf16(tO2, pl, dh, id6, 1);
                     umma_bf16(tO2, ph, dl, id6, 1);
@@ -609,7 +615,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (n) O = (scale e^G O1 + O2) / nq -> o[token][hv][dv]
         //     rows i on lanes 64-127: each thread writes 32 contiguous dv of one token (16-byte stores)
-        if (a.o_mode != 2 && lg >= 2) {
+        if (o_mode != 2 && lg >= 2) {
             const int i = row - 64;
             const float f1 = a.scale * vEG[i] * vNQ[i], f2 = vNQ[i];
             __nv_bfloat16* orow = (__nv_bfloat16*)a.o + ((tok0 + i) * a.HV + hv) * 128 + 32 * cq;
@@ -627,7 +633,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 #pragma unroll
                         for (int e = 0; e < 8; ++e) y[e] = fmaf(f1, v1[8 * q + e], f2 * v2[8 * q + e]);
                         uint4* dst = reinterpret_cast<uint4*>(orow + 8 * q);
-                        if (a.o_mode == 1) {
+                        if (o_mode == 1) {
                             const uint4 old = *dst;
                             const __nv_bfloat162* ob = reinterpret_cast<const __nv_bfloat162*>(&old);
 #pragma unroll
@@ -663,7 +669,7 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 float* p = ht + (32 * cq + c0 + i) * 128 + row;
-                *p = a.ht_accumulate ? *p + v[i] : v[i];
+                *p = ht_accumulate ? *p + v[i] : v[i];
             }
         }
     }
@@ -679,8 +685,12 @@ int chunk_fwd(const ChunkLaunch& L, cudaStream_t s) {
     using namespace cf;
     static bool attr_set = false;
     if (!attr_set) {
-        if (cudaFuncSetAttribute(chunk_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(chunk_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(chunk_fwd_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(chunk_fwd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+                cudaSuccess)
             return GDN_ERR_LAUNCH;
         attr_set = true;
     }
@@ -722,7 +732,10 @@ int chunk_fwd(const ChunkLaunch& L, cudaStream_t s) {
         a.o_mode = 2;
     }
     if (grid.x == 0) return GDN_OK;
-    chunk_fwd_kernel<<<grid, NTHR, SMEM_BYTES, s>>>(a);
+    if (a.s0_out) chunk_fwd_kernel<1><<<grid, NTHR, SMEM_BYTES, s>>>(a);
+    else if (a.o_mode == 0 && !a.zero_v && !a.h0_identity && !a.ht_accumulate)
+        chunk_fwd_kernel<0><<<grid, NTHR, SMEM_BYTES, s>>>(a);
+    else chunk_fwd_kernel<2><<<grid, NTHR, SMEM_BYTES, s>>>(a);
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
