@@ -289,6 +289,10 @@ def run_ours(args):
 
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
+    if args.profile_layer:  # profiling mode: the layer-neighbour ops only, two fwd+bwd calls each (no JSON line)
+        layer_ops_bench(dev, world, 1.0, reps=1)
+        print(json.dumps({"profile_layer": True, "ok": True}))
+        return
     if args.profile_decode:  # profiling mode: decode steps only (no JSON line)
         decode_bench(dev, rank, world, n_dec=args.profile_decode, timed=False)
         print(json.dumps({"profile_decode": args.profile_decode, "ok": True}))
@@ -523,6 +527,8 @@ def main():
                     help="profiling mode: run only fwd+bwd steps of config 1 with this batch (for ncu captures)")
     ap.add_argument("--profile-decode", type=int, default=0,
                     help="profiling mode: run only this many decode steps of config 3 (for ncu captures)")
+    ap.add_argument("--profile-layer", action="store_true",
+                    help="profiling mode: run only the layer-neighbour ops at config-1 sizes (for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -24,7 +24,9 @@ __device__ __forceinline__ void mma_m16n8k16_bf16(float (&d)[4], const uint32_t 
 // b[k * ldb + n], both fp32 in shared memory (lda even). Fragment layout of m16n8k16 (lane = 4 g + t):
 // A registers (g, 2t..2t+1), (g+8, 2t..), (g, 2t+8..), (g+8, 2t+8..); B registers (2t..2t+1, g),
 // (2t+8.., g); accumulator (g, 2t..2t+1), (g+8, 2t..2t+1).
-__device__ __forceinline__ void mma_split_k16(float (&d)[4], const float* a, int lda, const float* b, int ldb) {
+// the hi*hi term accumulates in d, the two cross terms in e (independent chains); the result is d + e
+__device__ __forceinline__ void mma_split_k16(float (&d)[4], float (&e)[4], const float* a, int lda, const float* b,
+                                              int ldb) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     uint32_t ah[4], al[4], bh[2], bl[2];
     float2 x;
@@ -39,14 +41,15 @@ __device__ __forceinline__ void mma_split_k16(float (&d)[4], const float* a, int
     split_bf16x2(b[(2 * t) * ldb + g], b[(2 * t + 1) * ldb + g], bh[0], bl[0]);
     split_bf16x2(b[(2 * t + 8) * ldb + g], b[(2 * t + 9) * ldb + g], bh[1], bl[1]);
     mma_m16n8k16_bf16(d, ah, bh);
-    mma_m16n8k16_bf16(d, ah, bl);
-    mma_m16n8k16_bf16(d, al, bh);
+    mma_m16n8k16_bf16(e, ah, bl);
+    mma_m16n8k16_bf16(e, al, bh);
 }
 // store a warp's 16 x 8 accumulator tile (times `sign`) at c[r * ldc + n] (ldc even)
-__device__ __forceinline__ void store_tile16x8(float* c, int ldc, const float (&d)[4], float sign) {
+__device__ __forceinline__ void store_tile16x8(float* c, int ldc, const float (&d)[4], const float (&e)[4],
+                                               float sign) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    *reinterpret_cast<float2*>(c + g * ldc + 2 * t) = make_float2(sign * d[0], sign * d[1]);
-    *reinterpret_cast<float2*>(c + (g + 8) * ldc + 2 * t) = make_float2(sign * d[2], sign * d[3]);
+    *reinterpret_cast<float2*>(c + g * ldc + 2 * t) = make_float2(sign * (d[0] + e[0]), sign * (d[1] + e[1]));
+    *reinterpret_cast<float2*>(c + (g + 8) * ldc + 2 * t) = make_float2(sign * (d[2] + e[2]), sign * (d[3] + e[3]));
 }
 
 // T = (I + A)^-1 for a strictly lower-triangular 64 x 64 fp32 matrix A stored in shared memory with row
@@ -103,32 +106,32 @@ __device__ __forceinline__ void tri_inverse64(float* Am, float* Y) {
     {  // 3. 16 -> 32: warp w < 4 takes pair p = w / 2 (rows/columns 32p .. 32p + 31), output columns 8 (w & 1) ..
         const int p = warp >> 1, n0 = 8 * (warp & 1), B0 = 32 * p;
         float* Yp = Y + p * 16 * LY;
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};
         if (warp < 4) {
-            mma_split_k16(d, Am + (B0 + 16) * ST + B0, ST, Am + B0 * ST + B0 + n0, ST);  // A10 T0
-            store_tile16x8(Yp + n0, LY, d, 1.f);
+            mma_split_k16(d, e, Am + (B0 + 16) * ST + B0, ST, Am + B0 * ST + B0 + n0, ST);  // A10 T0
+            store_tile16x8(Yp + n0, LY, d, e, 1.f);
         }
         solve_sync256();
         if (warp < 4) {
-            d[0] = d[1] = d[2] = d[3] = 0.f;
-            mma_split_k16(d, Am + (B0 + 16) * ST + B0 + 16, ST, Yp + n0, LY);  // T1 (A10 T0)
-            store_tile16x8(Am + (B0 + 16) * ST + B0 + n0, ST, d, -1.f);
+            d[0] = d[1] = d[2] = d[3] = e[0] = e[1] = e[2] = e[3] = 0.f;
+            mma_split_k16(d, e, Am + (B0 + 16) * ST + B0 + 16, ST, Yp + n0, LY);  // T1 (A10 T0)
+            store_tile16x8(Am + (B0 + 16) * ST + B0 + n0, ST, d, e, -1.f);
         }
         solve_sync256();
     }
     {  // 4. 32 -> 64: warp w takes rows 32 + 16 (w >> 2) .., output columns 8 (w & 3) .. of the lower-left block
         const int m0 = 16 * (warp >> 2), n0 = 8 * (warp & 3);
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int ks = 0; ks < 32; ks += 16)
-            mma_split_k16(d, Am + (32 + m0) * ST + ks, ST, Am + ks * ST + n0, ST);  // A10 T0
-        store_tile16x8(Y + m0 * LY + n0, LY, d, 1.f);
+            mma_split_k16(d, e, Am + (32 + m0) * ST + ks, ST, Am + ks * ST + n0, ST);  // A10 T0
+        store_tile16x8(Y + m0 * LY + n0, LY, d, e, 1.f);
         solve_sync256();
-        d[0] = d[1] = d[2] = d[3] = 0.f;
+        d[0] = d[1] = d[2] = d[3] = e[0] = e[1] = e[2] = e[3] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < 32; ks += 16)
-            mma_split_k16(d, Am + (32 + m0) * ST + 32 + ks, ST, Y + ks * LY + n0, LY);  // T1 (A10 T0)
-        store_tile16x8(Am + (32 + m0) * ST + n0, ST, d, -1.f);
+            mma_split_k16(d, e, Am + (32 + m0) * ST + 32 + ks, ST, Y + ks * LY + n0, LY);  // T1 (A10 T0)
+        store_tile16x8(Am + (32 + m0) * ST + n0, ST, d, e, -1.f);
         solve_sync256();
     }
 }
