@@ -378,7 +378,10 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
             float ss = 0.f;
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
-                const uint4 u = *reinterpret_cast<const uint4*>(rowp + (4 * (part & 1) + cc) * 16);
+                // chunk order rotated by (2 d-block + row parity): the 8 lanes of a quarter-warp read 8
+                // distinct 16-byte bank groups (the sum is order-free)
+                const int ch = (cc + 4 * (part & 1) + 2 * (part >> 1) + (r & 1)) & 7;
+                const uint4 u = *reinterpret_cast<const uint4*>(rowp + ch * 16);
                 const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
