@@ -225,6 +225,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     uint64_t* bar_in = (uint64_t*)(sm + OFF_BAR);
     uint64_t* bar_mma = bar_in + 1;
     uint64_t* bar_v = bar_in + 2;  // V tile reloaded for Z1 (its region holds the Dd lo tile in steps 5-8)
+    uint64_t* bar_mma2 = bar_in + 13;  // second MMA group of a step (after the scalars below)
     uint32_t* tmem_slot = (uint32_t*)(bar_in + 3);
     float* scal = (float*)(bar_in + 4);  // [0] e^G_C, [1..16] <dS, S0> per warp
 
@@ -255,6 +256,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         mbar_init(bar_in, 1);
         mbar_init(bar_mma, 1);
         mbar_init(bar_v, 1);
+        mbar_init(bar_mma2, 1);
         fence_barrier_init();
         prefetch_tmap(&a.tq);
         prefetch_tmap(&a.tk);
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     const uint32_t tm = *tmem_slot;
     const uint32_t lb = (uint32_t)(32 * lg) << 16;
     const uint32_t tS = tm + T_S, tD1 = tm + T_D1;
-    uint32_t mph = 0;
+    uint32_t mph = 0, mph2 = 0;
     bool ok = true;
     const uint32_t sb = smem_u32(sm);
 
@@ -456,12 +458,17 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                           id_kk, ks > 0);
                 umma_bf16(tm + C384, desc_kmajor(sb + (kb ? OFF_A : OFF_DD) + ko), desc_kmajor(aK + kb * QK_BLK + ko),
                           id_kk, 1);  // dS lo . K
+            }
+            umma_commit(bar_mma);  // dDelta's two products: step 7 starts on them
+#pragma unroll 1
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 umma_bf16(tm + C448, desc_kmajor(aDO + kb * 8192 + ko), desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192),
                           id_km, ks > 0);
                 umma_bf16(tm + C192, desc_mnmajor(sb + OFF_S0 + ks * 2048, 16384), desc_kmajor(aDO + kb * 8192 + ko),
                           id_mk, ks > 0);
             }
-            umma_commit(bar_mma);
+            umma_commit(bar_mma2);  // dP and QA: run while step 7 forms dDelta
         }
         mwait(bar_mma, mph, a.err, 15, ok);
 
@@ -503,6 +510,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
             deposit_colsum(de, red0, lg, cq);
         }
+        mwait(bar_mma2, mph2, a.err, 24, ok);
         {
             float v[16], p[16];
             ld16x2(tm + C448 + lb + 16 * cq, v, tD1 + lb + 16 * cq, p);

@@ -486,8 +486,10 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
         }
 
         // (h) TB = T diag(beta e^G / nk), TV = T diag(beta)  (bf16, K-major [i][j])
-        {
-            const int i = tid >> 3, c8 = 8 * (tid & 7);
+        {  // a quarter-warp covers rows i, i + 1 and four chunks of one 32-column half: its row loads and
+           // vector loads hit distinct banks
+            const int wl = tid & 31, qq = wl >> 3, sub = wl & 7;
+            const int i = 4 * (tid >> 5) + 2 * (qq & 1) + (sub >> 2), c8 = 8 * ((sub & 3) + 4 * (qq >> 1));
             float tb[8], tv[8];
             const float4 t0 = *reinterpret_cast<const float4*>(Am + i * AST + c8);
             const float4 t1 = *reinterpret_cast<const float4*>(Am + i * AST + c8 + 4);
