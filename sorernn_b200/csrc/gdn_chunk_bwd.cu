@@ -460,6 +460,8 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                           id_kk, 1);  // dS lo . K
             }
             umma_commit(bar_mma);  // dDelta's two products: step 7 starts on them
+        } else if (tid == 32) {  // a second issuing thread: its MMAs and commit are tracked apart from thread 0's
+            const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
 #pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
@@ -586,16 +588,11 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         sync_tc();
 
         // ---- 8. dVb^T = dDelta^T T (256); S0 dDelta^T = -dW^T (320); QB = K^T dPs1^T (384);
-        //         dK' = Q^T dPs2 + dS Dd^T (448)
+        //         dK' = Q^T dPs2 + dS Dd^T (448). Thread 0 issues QB and dK', thread 32 dVb and -dW^T.
         if (tid == 0) {
-            const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mm = idesc_bf16(128, 64, 1, 1);
-            const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
+            const uint32_t id_mm = idesc_bf16(128, 64, 1, 1), id_mk = idesc_bf16(128, 64, 1, 0);
 #pragma unroll 1
             for (int ks = 0; ks < 4; ++ks) {  // K = tokens
-                umma_bf16(tm + C256, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
-                          id_km, ks > 0);
-                umma_bf16(tm + C256, desc_kmajor(sb + OFF_DDL + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
-                          id_km, 1);
                 umma_bf16(tm + C384, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_PS + ks * 32), id_mk,
                           ks > 0);
                 umma_bf16(tm + C448, desc_mnmajor(aQ + ks * 2048, QK_BLK), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
@@ -603,16 +600,29 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
 #pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {  // K = dv
-                umma_bf16(tm + C320, desc_mnmajor(sb + OFF_S0 + ks * 2048, 16384),
-                          desc_mnmajor(sb + OFF_DD + ks * 2048, 8192), id_mm, ks > 0);
                 umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
                           desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192), id_mm, 1);
                 umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
                           desc_mnmajor(sb + OFF_V + ks * 2048, 8192), id_mm, 1);  // dS hi . Dd lo
             }
             umma_commit(bar_mma);
+        } else if (tid == 32) {
+            const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mm = idesc_bf16(128, 64, 1, 1);
+#pragma unroll 1
+            for (int ks = 0; ks < 4; ++ks) {  // K = tokens
+                umma_bf16(tm + C256, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
+                          id_km, ks > 0);
+                umma_bf16(tm + C256, desc_kmajor(sb + OFF_DDL + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
+                          id_km, 1);
+            }
+#pragma unroll 1
+            for (int ks = 0; ks < 8; ++ks)  // K = dv
+                umma_bf16(tm + C320, desc_mnmajor(sb + OFF_S0 + ks * 2048, 16384),
+                          desc_mnmajor(sb + OFF_DD + ks * 2048, 8192), id_mm, ks > 0);
+            umma_commit(bar_mma2);
         }
         mwait(bar_mma, mph, a.err, 16, ok);
+        mwait(bar_mma2, mph2, a.err, 25, ok);
         if (tid == 0) {  // the Dd lo tile is consumed: bring V back for Z1 (step 10)
             const int tok0i = (int)tok0;
             mbar_arrive_expect_tx(bar_v, 2 * 8192);
@@ -644,13 +654,14 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         fence_async_smem();
         sync_tc();
-        if (tid == 0) {
-            const uint32_t id_mm = idesc_bf16(128, 64, 1, 1), id_mm128 = idesc_bf16(128, 128, 1, 1);
-            const uint32_t id_km128 = idesc_bf16(128, 128, 0, 1);
+        if (tid == 0) {  // dK' (thread 0, after its other dK' products) and the dS update (thread 32)
+            const uint32_t id_mm = idesc_bf16(128, 64, 1, 1);
 #pragma unroll 1
             for (int ks = 0; ks < 8; ++ks)  // K = dv
                 umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
                           desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192), id_mm, 1);
+        } else if (tid == 32) {
+            const uint32_t id_mm128 = idesc_bf16(128, 128, 1, 1), id_km128 = idesc_bf16(128, 128, 0, 1);
 #pragma unroll 1
             for (int ks = 0; ks < 4; ++ks) {  // K = tokens
                 umma_bf16(tS, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(aQ + ks * 2048, QK_BLK), id_mm128, 1);
@@ -702,19 +713,22 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         sync_tc();
 
         // ---- 10. dKb^T = dW^T T (192) ; Z1 = [-; dVb] V^T (256, rows j on lanes 64-127) ------------------
-        if (tid == 0) {
-            const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
+        if (tid == 0) {  // dKb (thread 0) and Z1 (thread 32); each commit also covers that thread's step-8b MMAs
+            const uint32_t id_km = idesc_bf16(128, 64, 0, 1);
 #pragma unroll 1
             for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tm + C192, desc_kmajor(sb + OFF_DWT + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
                           id_km, ks > 0);
+            umma_commit(bar_mma);
+        } else if (tid == 32) {
+            const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
 #pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 umma_bf16(tm + C256, desc_mnmajor(sb + OFF_DVB - 16384 + ks * 2048, 16384),
                           desc_kmajor(aV + kb * 8192 + ko), id_mk, ks > 0);
             }
-            umma_commit(bar_mma);
+            umma_commit(bar_mma2);
         }
         if (tid < 64) {  // per-column terms of the dq epilogue; dGamma and dbeta contributions
             const float c1 = colsum(red1, tid);
@@ -745,6 +759,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
         }
         mwait(bar_mma, mph, a.err, 17, ok);
+        mwait(bar_mma2, mph2, a.err, 26, ok);
 
         // ---- 11. dKb (kept in registers), dKb.kn, dKb tile ; Z2 = [-; dKb] K^T (320) -------------------
         float kbr[16];
