@@ -226,6 +226,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     uint64_t* bar_mma = bar_in + 1;
     uint64_t* bar_v = bar_in + 2;  // V tile reloaded for Z1 (its region holds the Dd lo tile in steps 5-8)
     uint64_t* bar_mma2 = bar_in + 13;  // second MMA group of a step (after the scalars below)
+    uint64_t* bar_mma3 = bar_in + 14;  // thread 32's share of step 6's first group
     uint32_t* tmem_slot = (uint32_t*)(bar_in + 3);
     float* scal = (float*)(bar_in + 4);  // [0] e^G_C, [1..16] <dS, S0> per warp
 
@@ -257,6 +258,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         mbar_init(bar_mma, 1);
         mbar_init(bar_v, 1);
         mbar_init(bar_mma2, 1);
+        mbar_init(bar_mma3, 1);
         fence_barrier_init();
         prefetch_tmap(&a.tq);
         prefetch_tmap(&a.tk);
@@ -268,7 +270,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     const uint32_t tm = *tmem_slot;
     const uint32_t lb = (uint32_t)(32 * lg) << 16;
     const uint32_t tS = tm + T_S, tD1 = tm + T_D1;
-    uint32_t mph = 0, mph2 = 0;
+    uint32_t mph = 0, mph2 = 0, mph3 = 0;
     bool ok = true;
     const uint32_t sb = smem_u32(sm);
 
@@ -441,16 +443,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
         // ---- 6. dO^T P''^T (320); dS^T K^T, hi and lo (384); dP = [dO;-] Delta^T (448); QA = S0 dO^T (192)
         if (tid == 0) {
-            const uint32_t id_mm = idesc_bf16(128, 64, 1, 1), id_kk = idesc_bf16(128, 64, 0, 0);
-            const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
-#pragma unroll 1
-            for (int ks = 0; ks < 4; ++ks)  // K = i
-            {
-                umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS + ks * 2048, 8192),
-                          id_mm, ks > 0);
-                umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
-                          id_mm, 1);
-            }
+            const uint32_t id_kk = idesc_bf16(128, 64, 0, 0);
 #pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
@@ -460,8 +453,17 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                           id_kk, 1);  // dS lo . K
             }
             umma_commit(bar_mma);  // dDelta's two products: step 7 starts on them
-        } else if (tid == 32) {  // a second issuing thread: its MMAs and commit are tracked apart from thread 0's
+        } else if (tid == 32) {  // a second issuing thread: its MMAs and commits are tracked apart from thread 0's
             const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
+            const uint32_t id_mm = idesc_bf16(128, 64, 1, 1);
+#pragma unroll 1
+            for (int ks = 0; ks < 4; ++ks) {  // K = i: dDelta's first product
+                umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS + ks * 2048, 8192),
+                          id_mm, ks > 0);
+                umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
+                          id_mm, 1);
+            }
+            umma_commit(bar_mma3);
 #pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
@@ -473,6 +475,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             umma_commit(bar_mma2);  // dP and QA: run while step 7 forms dDelta
         }
         mwait(bar_mma, mph, a.err, 15, ok);
+        mwait(bar_mma3, mph3, a.err, 27, ok);
 
         // ---- 7. dDelta^T = (320) + (384) diag(vX) -> tile; r4; dP -> dPs tiles, X_P sums -------------------
         {
@@ -590,14 +593,11 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         // ---- 8. dVb^T = dDelta^T T (256); S0 dDelta^T = -dW^T (320); QB = K^T dPs1^T (384);
         //         dK' = Q^T dPs2 + dS Dd^T (448). Thread 0 issues QB and dK', thread 32 dVb and -dW^T.
         if (tid == 0) {
-            const uint32_t id_mm = idesc_bf16(128, 64, 1, 1), id_mk = idesc_bf16(128, 64, 1, 0);
+            const uint32_t id_mm = idesc_bf16(128, 64, 1, 1);
 #pragma unroll 1
-            for (int ks = 0; ks < 4; ++ks) {  // K = tokens
-                umma_bf16(tm + C384, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_PS + ks * 32), id_mk,
-                          ks > 0);
+            for (int ks = 0; ks < 4; ++ks)  // K = tokens
                 umma_bf16(tm + C448, desc_mnmajor(aQ + ks * 2048, QK_BLK), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
                           id_mm, ks > 0);
-            }
 #pragma unroll 1
             for (int ks = 0; ks < 8; ++ks) {  // K = dv
                 umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
@@ -608,8 +608,11 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             umma_commit(bar_mma);
         } else if (tid == 32) {
             const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mm = idesc_bf16(128, 64, 1, 1);
+            const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
 #pragma unroll 1
             for (int ks = 0; ks < 4; ++ks) {  // K = tokens
+                umma_bf16(tm + C384, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_PS + ks * 32), id_mk,
+                          ks > 0);
                 umma_bf16(tm + C256, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
                           id_km, ks > 0);
                 umma_bf16(tm + C256, desc_kmajor(sb + OFF_DDL + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
