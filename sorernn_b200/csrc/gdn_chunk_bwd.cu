@@ -474,16 +474,12 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
             umma_commit(bar_mma2);  // dP and QA: run while step 7 forms dDelta
         }
-        mwait(bar_mma, mph, a.err, 15, ok);
-        mwait(bar_mma3, mph3, a.err, 27, ok);
-
         // ---- 7. dDelta^T = (320) + (384) diag(vX) -> tile; r4; dP -> dPs tiles, X_P sums -------------------
         {
             float d1[16], d2[16], de[16], x16[16];
-            tmem_ld16(tm + C320 + lb + 16 * cq, d1);
-            tmem_ld16(tm + C384 + lb + 16 * cq, d2);
             vec16(vX, 16 * cq, x16);
             // Delta x (= Dd) to ~16 bits: bf16(bf16(Delta) x) from the Delta^T tile plus the Dd^T low part
+            // (shared-memory operands only: formed while step 6's MMAs run)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const uint32_t off = sw128_off(row, 16 * cq + 8 * h);
@@ -499,6 +495,10 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                     de[j + 1] = __bfloat162float(__float2bfloat16_rn(fh.y * x16[j + 1])) + fl.y;
                 }
             }
+            mwait(bar_mma, mph, a.err, 15, ok);
+            mwait(bar_mma3, mph3, a.err, 27, ok);
+            tmem_ld16(tm + C320 + lb + 16 * cq, d1);
+            tmem_ld16(tm + C384 + lb + 16 * cq, d2);
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -875,18 +875,18 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 umma_bf16(tm + C448, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_GS + ks * 32), id_mk, 1);
             umma_commit(bar_mma);
         }
+        float kr[16], w16[16];  // step 14's shared-memory operands, loaded while the MMAs run
+#pragma unroll
+        for (int j = 0; j < 16; ++j) kr[j] = tile128(sm + OFF_QK + 8192, QK_BLK, 16 * cq + j, row);
+        vec16(vBEN, 16 * cq, w16);
         mwait(bar_mma, mph, a.err, 20, ok);
 
         // ---- 14. dk = u - kn (kn.u), u = dK' + beta e^G / nk dKb ; dg, dbeta ---------------------------------
         {
-            float u[16], xk[16], kr[16], w16[16];
+            float u[16], xk[16];
             ld16c(tm + C448 + lb + 16 * cq, u);
-            vec16(vBEN, 16 * cq, w16);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                kr[j] = tile128(sm + OFF_QK + 8192, QK_BLK, 16 * cq + j, row);
-                u[j] = fmaf(w16[j], kbr[j], u[j]);
-            }
+            for (int j = 0; j < 16; ++j) u[j] = fmaf(w16[j], kbr[j], u[j]);
             vec16(vNK, 16 * cq, w16);
 #pragma unroll
             for (int j = 0; j < 16; ++j) xk[j] = kr[j] * w16[j] * u[j];
