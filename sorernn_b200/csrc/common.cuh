@@ -89,6 +89,20 @@ __device__ __forceinline__ void stv(void* p, int64_t i, const float (&v)[PER]) {
     }
 }
 
+// A gate value (g or beta) kept as loaded: fp32 as 32 bits, bf16/fp16 as 16 bits (no conversion, so the
+// load does not stall the thread that issues it ahead of use); gate_f converts it when it is used.
+__device__ __forceinline__ uint32_t ld_gate_raw(const void* p, int dtype, int64_t i) {
+    uint32_t r;
+    if (dtype == GDN_FP32) r = ((const uint32_t*)p)[i];
+    else r = ((const uint16_t*)p)[i];
+    return r;
+}
+__device__ __forceinline__ float gate_f(uint32_t r, int dtype) {
+    if (dtype == GDN_FP32) return __uint_as_float(r);
+    if (dtype == GDN_BF16) return __uint_as_float(r << 16);
+    return __half2float(__ushort_as_half((unsigned short)r));
+}
+
 // N elements of type TA kept as loaded (not widened to fp32), so that many rows can be in flight in few
 // registers; load() uses the widest vector N elements allow (the address must be aligned to it).
 template <typename TA, int N>

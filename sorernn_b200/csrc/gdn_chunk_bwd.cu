@@ -90,11 +90,6 @@ struct ChunkBwdArgs {
     int l2norm, accumulate_qk;
 };
 
-__device__ __forceinline__ float ld_gb(const void* p, int dtype, int64_t i) {
-    if (dtype == GDN_FP32) return ((const float*)p)[i];
-    if (dtype == GDN_BF16) return __bfloat162float(((const __nv_bfloat16*)p)[i]);
-    return __half2float(((const __half*)p)[i]);
-}
 __device__ __forceinline__ uint32_t pk_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -308,12 +303,14 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     uint32_t in_phase = 0, v_phase = 0;
     const uint32_t aQ = sb + OFF_QK, aK = sb + OFF_QK + 8192, aV = sb + OFF_V, aDO = sb + OFF_DO;
 
-    float g_next = 0.f, b_next = 0.f;  // gates of the chunk processed next (threads 0-63)
+    uint32_t g_next = 0u, b_next = 0u;  // gates of the chunk processed next (threads 0-63), raw
     if (tid < 64 && nchunks > 0) {
         const int64_t t0 = bos + 64 * (int64_t)(nchunks - 1);
         const bool in = tid < len - 64 * (int64_t)(nchunks - 1);
-        g_next = in ? ld_gb(a.g, a.g_dtype, (t0 + tid) * a.HV + hv) : 0.f;
-        b_next = in ? ld_gb(a.beta, a.beta_dtype, (t0 + tid) * a.HV + hv) : 0.f;
+        if (in) {
+            g_next = ld_gate_raw(a.g, a.g_dtype, (t0 + tid) * a.HV + hv);
+            b_next = ld_gate_raw(a.beta, a.beta_dtype, (t0 + tid) * a.HV + hv);
+        }
     }
     for (int c = nchunks - 1; c >= 0; --c) {
         const int64_t tok0 = bos + 64 * (int64_t)c;
@@ -321,12 +318,12 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
 
         // ---- 1. gates; wait for this chunk's tiles ------------------------------------------------------
         if (tid < 64) {
-            float x = g_next;
-            vB[tid] = b_next;
+            float x = gate_f(g_next, a.g_dtype);
+            vB[tid] = gate_f(b_next, a.beta_dtype);
             if (c > 0) {  // gates of chunk c-1 (always 64 tokens): their latency hides behind this chunk
                 const int64_t gi = (tok0 - 64 + tid) * a.HV + hv;
-                g_next = ld_gb(a.g, a.g_dtype, gi);
-                b_next = ld_gb(a.beta, a.beta_dtype, gi);
+                g_next = ld_gate_raw(a.g, a.g_dtype, gi);
+                b_next = ld_gate_raw(a.beta, a.beta_dtype, gi);
             }
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {

@@ -87,12 +87,6 @@ struct ChunkFwdArgs {
     uint8_t* s0_out;  // recompute mode: checkpoints are read, S0^T tiles written here (see ChunkLaunch)
 };
 
-__device__ __forceinline__ float ld_any2(const void* p, int dtype, int64_t i) {
-    if (dtype == GDN_FP32) return ((const float*)p)[i];
-    if (dtype == GDN_BF16) return __bfloat162float(((const __nv_bfloat16*)p)[i]);
-    return __half2float(((const __half*)p)[i]);
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -314,12 +308,14 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
     }
 
     const uint32_t sbase = smem_u32(sm);
-    float g_next = 0.f, b_next = 0.f;  // gates of the next chunk (threads 0-63), loaded one chunk ahead
+    uint32_t g_next = 0u, b_next = 0u;  // gates of the next chunk (threads 0-63), loaded one chunk ahead, raw
     if (tid < 64 && c_begin < nchunks) {
         const bool in = tid < len - 64 * (int64_t)c_begin;
         const int64_t gi = (bos + 64 * (int64_t)c_begin + tid) * a.HV + hv;
-        g_next = in ? ld_any2(a.g, a.g_dtype, gi) : 0.f;
-        b_next = in ? ld_any2(a.beta, a.beta_dtype, gi) : 0.f;
+        if (in) {
+            g_next = ld_gate_raw(a.g, a.g_dtype, gi);
+            b_next = ld_gate_raw(a.beta, a.beta_dtype, gi);
+        }
     }
     for (int c = c_begin; c < nchunks; ++c) {
         const int cl = c - c_begin;
@@ -334,14 +330,16 @@ __global__ void __launch_bounds__(cf::NTHR, 1) chunk_fwd_kernel(const __grid_con
 
         // (a) gates: Gamma = cumsum(g) inside the chunk, beta; padded rows carry g = 0, beta = 0
         if (tid < 64) {
-            float x = g_next;
-            vB[tid] = b_next;
+            float x = gate_f(g_next, a.g_dtype);
+            vB[tid] = gate_f(b_next, a.beta_dtype);
+            g_next = b_next = 0u;
             if (c + 1 < nchunks) {  // next chunk's gates: their latency hides behind this chunk
                 const int64_t len1 = len - 64 * (int64_t)(c + 1);
-                const bool in = tid < len1;
                 const int64_t gi = (tok0 + 64 + tid) * a.HV + hv;
-                g_next = in ? ld_any2(a.g, a.g_dtype, gi) : 0.f;
-                b_next = in ? ld_any2(a.beta, a.beta_dtype, gi) : 0.f;
+                if (tid < len1) {
+                    g_next = ld_gate_raw(a.g, a.g_dtype, gi);
+                    b_next = ld_gate_raw(a.beta, a.beta_dtype, gi);
+                }
             }
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
