@@ -41,11 +41,6 @@ struct DecodeArgs {
     float scale;
 };
 
-__device__ __forceinline__ float ld_gate(const void* p, int dtype, int64_t i) {
-    if (dtype == GDN_FP32) return ((const float*)p)[i];
-    if (dtype == GDN_BF16) return __bfloat162float(((const __nv_bfloat16*)p)[i]);
-    return __half2float(((const __half*)p)[i]);
-}
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_u32(dst)),
@@ -94,19 +89,19 @@ __global__ void __launch_bounds__(dec::NTHR, 1) decode_tma_kernel(const __grid_c
         if (h0 + stride < a.heads) issue(h0 + stride, 1);
     }
     // gates of the current head, loaded one head ahead (their latency hides behind a whole head)
-    float g_nx = 0.f, b_nx = 0.f;
+    uint32_t g_nx = 0u, b_nx = 0u;  // kept as loaded bits (no stall at the load); converted at use
     if (h0 < a.heads) {
-        g_nx = ld_gate(a.g, a.g_dtype, h0);
-        b_nx = ld_gate(a.beta, a.beta_dtype, h0);
+        g_nx = ld_gate_raw(a.g, a.g_dtype, h0);
+        b_nx = ld_gate_raw(a.beta, a.beta_dtype, h0);
     }
     bool ok = true;
     int it = 0;
     for (int64_t h = h0; h < a.heads; h += stride, ++it) {
         const int s = it % STAGES;
-        const float gam = __expf(g_nx), bt = b_nx;
+        const float gam = __expf(gate_f(g_nx, a.g_dtype)), bt = gate_f(b_nx, a.beta_dtype);
         if (h + stride < a.heads) {
-            g_nx = ld_gate(a.g, a.g_dtype, h + stride);
-            b_nx = ld_gate(a.beta, a.beta_dtype, h + stride);
+            g_nx = ld_gate_raw(a.g, a.g_dtype, h + stride);
+            b_nx = ld_gate_raw(a.beta, a.beta_dtype, h + stride);
         }
         ok = mbar_wait(&bar[s], (uint32_t)(it / STAGES) & 1u, nullptr, 0, ok ? (1u << 22) : 1u) && ok;
         float* S = (float*)(sm + s * STAGE_BYTES);
