@@ -679,12 +679,14 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             float v[16], r2[16], w[16], b16[16];
             ld16x2(tm + C256 + lb + 16 * cq, v, tm + C320 + lb + 16 * cq, w);  // dVb^T[dv][j], -dW^T[dk][i]
             vec16(vB, 16 * cq, b16);
-            __nv_bfloat16* dvp = (__nv_bfloat16*)a.dv;
+            // dv[token][hv][dv]: this thread's column, tokens 16 cq .. 16 cq + 15 (stride HV x 128)
+            __nv_bfloat16* dvp = (__nv_bfloat16*)a.dv + ((tok0 + 16 * cq) * a.HV + hv) * 128 + row;
+            const int64_t vstride = (int64_t)a.HV * 128;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int jj = 16 * cq + j;
                 r2[j] = v[j] * tile128(sm + OFF_V, 8192, jj, row);
-                if (jj < nv) dvp[((tok0 + jj) * a.HV + hv) * 128 + row] = __float2bfloat16_rn(v[j] * b16[j]);
+                if (jj < nv) dvp[j * vstride] = __float2bfloat16_rn(v[j] * b16[j]);
                 w[j] = -w[j];
             }
 #pragma unroll
@@ -748,14 +750,17 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 const float dqn = fmaf(s16[j], qa[j], qb[j]);
                 xs[j] = a.l2norm ? fmaf(-tile128(sm + OFF_QK, QK_BLK, i, row), c16[j], dqn * nq16[j]) : dqn;
             }
+            // dq[token][hq][dk]: this thread's column, tokens 16 cq .. (stride H x 128)
+            const int64_t qidx = ((tok0 + 16 * cq) * a.H + hq) * 128 + row, qstride = (int64_t)a.H * 128;
+            if (a.accumulate_qk) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int i = 16 * cq + j;
-                if (i < nv) {
-                    const int64_t idx = ((tok0 + i) * a.H + hq) * 128 + row;
-                    if (a.accumulate_qk) atomicAdd((float*)a.dq + idx, xs[j]);
-                    else ((__nv_bfloat16*)a.dq)[idx] = __float2bfloat16_rn(xs[j]);
-                }
+                for (int j = 0; j < 16; ++j)
+                    if (16 * cq + j < nv) atomicAdd((float*)a.dq + qidx + j * qstride, xs[j]);
+            } else {
+                __nv_bfloat16* dqp = (__nv_bfloat16*)a.dq + qidx;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (16 * cq + j < nv) dqp[j * qstride] = __float2bfloat16_rn(xs[j]);
             }
         }
         mwait(bar_mma, mph, a.err, 17, ok);
@@ -892,15 +897,19 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             if (tid < 64) vK3[tid] = vNK[tid] * colsum(red3, tid);  // (1/nk) (kn . u)
             __syncthreads();
             vec16(vK3, 16 * cq, w16);
+            // dk[token][hq][dk]: this thread's column, tokens 16 cq .. (stride H x 128)
+            const int64_t kidx = ((tok0 + 16 * cq) * a.H + hq) * 128 + row, kstride = (int64_t)a.H * 128;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int jj = 16 * cq + j;
-                const float gk = a.l2norm ? fmaf(-kr[j], w16[j], u[j]) : u[j];
-                if (jj < nv) {
-                    const int64_t idx = ((tok0 + jj) * a.H + hq) * 128 + row;
-                    if (a.accumulate_qk) atomicAdd((float*)a.dk + idx, gk);
-                    else ((__nv_bfloat16*)a.dk)[idx] = __float2bfloat16_rn(gk);
-                }
+            for (int j = 0; j < 16; ++j) u[j] = a.l2norm ? fmaf(-kr[j], w16[j], u[j]) : u[j];
+            if (a.accumulate_qk) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (16 * cq + j < nv) atomicAdd((float*)a.dk + kidx + j * kstride, u[j]);
+            } else {
+                __nv_bfloat16* dkp = (__nv_bfloat16*)a.dk + kidx;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (16 * cq + j < nv) dkp[j * kstride] = __float2bfloat16_rn(u[j]);
             }
         }
         if (tid < 32) {  // last row: + sum_j kn.dKst_j + e^G_C <dS, S0>
