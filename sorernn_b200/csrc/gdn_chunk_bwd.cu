@@ -282,24 +282,34 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         tmem_wait_st();
     }
 
-    auto issue_inputs = [&](int c) {
+    // A chunk's inputs arrive on bar_in in two parts (one expect_tx for both): part A (Q, dO, and the record's
+    // S0^T and Dd^T low part, where V goes later) as soon as the previous chunk's step-11 MMAs completed, the
+    // last readers of those regions; part B (K, and the record's -W | T and Delta^T) at the chunk's end.
+    auto issue_inputs_a = [&](int c) {
         const int tok0 = (int)(bos + 64 * c);
         mbar_arrive_expect_tx(bar_in, 6 * 8192 + 32768 + 24576 + 2 * 16384);
 #pragma unroll 1
         for (int kb = 0; kb < 2; ++kb) {
             tma_load_3d(sm + OFF_QK + kb * QK_BLK, &a.tq, bar_in, kb * 64, hq, tok0);
-            tma_load_3d(sm + OFF_QK + kb * QK_BLK + 8192, &a.tk, bar_in, kb * 64, hq, tok0);
             tma_load_3d(sm + OFF_DO + kb * 8192, &a.tdo, bar_in, kb * 64, hv, tok0);
         }
-        // the recompute pass's record: S0^T, -W | T (contiguous here and there), Delta^T, and the Dd^T low
-        // part where V goes later (V arrives after step 8 on bar_v)
         const uint8_t* rec = a.s0_tiles + ((cbase + c) * a.HV + hv) * kBwdRecordBytes;
         bulk_load(sm + OFF_S0, rec, 32768, bar_in);
-        bulk_load(sm + OFF_W, rec + kBwdRecW, 24576, bar_in);
-        bulk_load(sm + OFF_DEL, rec + kBwdRecDel, 16384, bar_in);
         bulk_load(sm + OFF_V, rec + kBwdRecDdl, 16384, bar_in);
     };
-    if (tid == 0 && nchunks > 0) issue_inputs(nchunks - 1);
+    auto issue_inputs_b = [&](int c) {
+        const int tok0 = (int)(bos + 64 * c);
+#pragma unroll 1
+        for (int kb = 0; kb < 2; ++kb)
+            tma_load_3d(sm + OFF_QK + kb * QK_BLK + 8192, &a.tk, bar_in, kb * 64, hq, tok0);
+        const uint8_t* rec = a.s0_tiles + ((cbase + c) * a.HV + hv) * kBwdRecordBytes;
+        bulk_load(sm + OFF_W, rec + kBwdRecW, 24576, bar_in);  // -W | T, contiguous here and there
+        bulk_load(sm + OFF_DEL, rec + kBwdRecDel, 16384, bar_in);
+    };
+    if (tid == 0 && nchunks > 0) {
+        issue_inputs_a(nchunks - 1);
+        issue_inputs_b(nchunks - 1);
+    }
     uint32_t in_phase = 0, v_phase = 0;
     const uint32_t aQ = sb + OFF_QK, aK = sb + OFF_QK + 8192, aV = sb + OFF_V, aDO = sb + OFF_DO;
 
@@ -799,6 +809,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             vDG[tid] += vB[tid] * vEG[tid] * r3;
         }
         mwait(bar_mma, mph, a.err, 18, ok);
+        if (tid == 0 && c > 0) issue_inputs_a(c - 1);  // Z2 was the last reader of the part-A regions
 
         // ---- 12. Z = beta_m (Z1 + e^G_m / nk_m Z2) -> bf16 [j][m] ; dA' = [-; Z] T^T (256) ---------------
         if (lg >= 2) {
@@ -936,7 +947,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             a.dbeta[(tok0 + tid) * a.HV + hv] = vDB[tid];
         }
         sync_tc();
-        if (tid == 0 && c > 0) issue_inputs(c - 1);
+        if (tid == 0 && c > 0) issue_inputs_b(c - 1);
     }
 
     if (ok && a.dh0) {
