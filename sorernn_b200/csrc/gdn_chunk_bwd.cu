@@ -22,6 +22,10 @@
 //   dGamma = rowsum-colsum(dA . A) + rowsum-colsum(dP . P) + scale e^Gamma qn.(S0 dO) + beta e^Gamma dKb.kn
 //            - kn.dKst_j  (+ sum_j kn.dKst_j + e^Gamma_C <dS, S0> on the last row);  dg = reverse cumsum
 //   dq = (dqn - qn (qn.dqn)) / nq,  dk likewise (chain rule through the L2 norm)
+// MMAs are issued by two threads, 0 and 32, each committing its groups to its own mbarriers (thread 0:
+// bar_mma; thread 32: bar_mma2, and bar_mma3 for its share of step 6's first group): one thread issues a
+// tcgen05.mma about every 70 cycles, so two issuers halve the issue time of the larger steps, and a phase
+// waits only for the groups it reads. Products that accumulate into one TMEM region stay on one thread.
 // Every GEMM is an M = 128 UMMA with a 128-wide dimension on the TMEM lanes. The three 64 x 64 x K
 // products (dP, Z, dA) use a 128-row A operand of which one 64-row half is ignored; Z and dA put their
 // rows on lanes 64-127, where the same threads also hold the K K^T rows of the recomputed Gram matrix.
