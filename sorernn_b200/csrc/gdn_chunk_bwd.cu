@@ -552,7 +552,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                     st8(sm + OFF_PS + sw128_off(i, 16 * cq + 8 * q), d1v + 8 * q);
                     st8(sm + OFF_PS2 + sw128_off(i, 16 * cq + 8 * q), d2v + 8 * q);
                 }
-                atomicAdd(&vDG[i], rs);
+                red2[cq * 64 + i] = rs;  // row i's four column-quarter partials, summed in fixed order below
             } else {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) p[j] = 0.f;
@@ -563,7 +563,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         if (tid < 64) {
             const float r4 = colsum(red0, tid);
             vR4[tid] = r4;
-            vDG[tid] -= colsum(red1, tid) + r4;
+            vDG[tid] += colsum(red2, tid) - (colsum(red1, tid) + r4);
         }
         // dO <- dO scale e^G / nq in place (A operand of the dS update; the raw dO readers have finished)
 #pragma unroll 1
@@ -859,8 +859,8 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                     sx += xa[t];
                     dGm[j * 64 + (l ^ (j & 31))] = dA * bj * e;  // column swizzled by the row: conflict-free
                 }
-                atomicAdd(&vDB[j], sb_);
-                atomicAdd(&vDG[j], sx);
+                red2[cq * 64 + j] = sb_;  // partials per column quarter, summed in fixed order below
+                red3[cq * 64 + j] = sx;
             } else {
 #pragma unroll
                 for (int t = 0; t < 16; ++t) xa[t] = 0.f;
@@ -868,7 +868,10 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             deposit_colsum(xa, red1, lg, cq);
         }
         __syncthreads();
-        if (tid < 64) vDG[tid] -= colsum(red1, tid);
+        if (tid < 64) {
+            vDB[tid] += colsum(red2, tid);
+            vDG[tid] += colsum(red3, tid) - colsum(red1, tid);
+        }
         {  // Gs = (dG + dG^T) / (nk nk)  bf16 [j][m]
             const int j = tid >> 3, c8 = 8 * (tid & 7);
             float gs[8], nk8[8];
