@@ -37,7 +37,7 @@ PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=
 # DRAM bytes (read + write) per launch from ncu captures of this build, per profiles/*.md:
 # backward pass (recompute + sweep launches) at batch 2 scaled by 4 to batch 8 (chunk_kernels_batch2_full.md);
 # decode step at full config-3 size (decode_tma_config3.md).
-BWD_PASS_TRAFFIC_BYTES = (211.1e6 + 405.9e6) * 4
+BWD_PASS_TRAFFIC_BYTES = (211.7e6 + 405.3e6) * 4
 DECODE_TRAFFIC_BYTES = 271.6e6 + 210.9e6
 
 
