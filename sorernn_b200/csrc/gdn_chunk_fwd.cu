@@ -5,7 +5,8 @@
 // With Gamma = in-chunk inclusive cumsum of g, E_ij = exp(Gamma_i - Gamma_j), S0 the state at the chunk
 // start, and nq_i, nk_j the L2 norms of the raw q/k rows (1 when the norm is off), the chunk computes
 // (algebra checked against the per-token recurrence in tests/test_chunk_algebra.py):
-//   A   = strict_lower(diag(beta) (K K^T / nk nk^T) . E)    T = (I + A)^-1   (fp32, blocked 16x16 solve)
+//   A   = strict_lower(diag(beta) (K K^T / nk nk^T) . E)    T = (I + A)^-1   (fp32 block doubling from
+//         8x8 blocks on warps 0-7, beside the S0 read-out on warps 8-15; tri_inverse64 in chunk_common.cuh)
 //   W   = T diag(beta e^Gamma / nk) K     U = T diag(beta) V     Delta = U - W S0
 //   O_i = [ scale e^Gamma_i (S0^T q_i) + (P' Delta)_i ] / nq_i,   P' = scale lower_incl(Q K^T / nk^T . E)
 //   S1  = e^Gamma_C S0 + K^T diag(e^(Gamma_C - Gamma) / nk) Delta
