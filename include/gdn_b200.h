@@ -25,7 +25,9 @@
  *    With cu_seqlens (int64 [N+1], device) B must be 1 and the state restarts at every
  *    cu_seqlens[i] (gdn_ref.py:53-61); without it every batch row is one sequence (N = B).
  *  - the caller allocates every output and the workspace (size from the *_workspace_size query);
- *    the library never allocates device memory and keeps no device state between calls.
+ *    the library never allocates device memory. Its only device state: one 4-byte error word per
+ *    workspace-less streaming kernel family (decode, norm-gate, conv; see gdn_stream_kernels_error)
+ *    and the fixed scratch array of gdn_chunk_bwd_noalloc.
  *  - every call is stream-ordered on `stream`, does not synchronise the host, and returns a status
  *    code (GDN_OK = 0); nothing aborts or traps. Shapes, dtypes and alignment are checked on the host
  *    before any launch.
@@ -107,17 +109,24 @@ int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void
                   const float* dht, void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0,
                   void* workspace, size_t workspace_bytes, gdn_stream_t stream);
 
+/* Size of gdn_chunk_bwd_noalloc's fixed scratch array (36 MiB). */
+#define GDN_NOALLOC_SCRATCH_BYTES ((size_t)36 << 20)
+
 /*
  * gdn_chunk_bwd for callers that cannot allocate device memory. No counterpart in the reference.
  * Some callers have no device allocator at call time: a host runtime reaching this library over a plain
  * C FFI without an allocator of its own, or a plugin whose execute hook must not allocate. This variant
  * takes gdn_chunk_bwd's arguments minus the workspace and allocates nothing (no cudaMalloc/cudaFree);
- * its scratch is one fixed array of 36 MiB inside the library's device image, held on every GPU that
- * loads the library until the process exits. Problems whose gdn_chunk_bwd_workspace_size() exceeds
- * 36 MiB are rejected with GDN_ERR_SCRATCH_LIMIT (one 4,096-token sequence with 16 heads fits). All calls
- * on a device share the array: calls whose GPU work overlaps (other streams, other host threads) race,
- * so order them on one stream. The first call on each device looks the array's address up; make that
- * first call before any stream capture begins.
+ * its scratch is one fixed array of GDN_NOALLOC_SCRATCH_BYTES inside the library's device image, held on
+ * every GPU that loads the library until the process exits. Problems whose
+ * gdn_chunk_bwd_workspace_size() exceeds it are rejected with GDN_ERR_SCRATCH_LIMIT before any launch;
+ * invalid problems get gdn_chunk_bwd's status. With the chunked kernels the array holds 418 chunk-heads
+ * (64-token chunks x value heads): e.g. T = 1,024 with 16 heads, or T = 4,096 with 6 heads, per call.
+ * All calls on a device share the array: calls whose GPU work overlaps (other streams, other host
+ * threads) race, so order them on one stream. Device-side timeouts are not reported (the error word is
+ * in the array): use gdn_chunk_bwd + gdn_workspace_error for that. The first call on each device looks
+ * the array's address up and keeps it for the life of the device's primary context; make that first
+ * call before any stream capture begins.
  */
 int gdn_chunk_bwd_noalloc(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
                           const void* beta, const float* initial_state, const float* checkpoints,
@@ -212,6 +221,13 @@ size_t gdn_segment_workspace_size(const gdn_problem* p);
 /* Reads the error word that device-side bounded waits leave in `workspace` (0 = none; the word is
  * cleared at the start of every call that takes the workspace). Synchronises `stream`. */
 int gdn_workspace_error(const void* workspace, gdn_stream_t stream, int32_t* error_out);
+
+/* Reads and clears the device error words of the workspace-less streaming kernels (gdn_decode_step,
+ * the norm-gate and conv entry points) on the current device: 0 = none, else the code of the first
+ * kernel family whose bounded stage wait gave up (31 decode, 32 norm-gate, 33 conv). A kernel that gave
+ * up stores nothing from then on (the decode step leaves those states unchanged). Synchronises `stream`.
+ * No counterpart in the reference. */
+int gdn_stream_kernels_error(gdn_stream_t stream, int32_t* error_out);
 
 /* Number of kernels this library has launched in the process so far (host-side counter, for
  * benchmark accounting). No counterpart in the reference. */

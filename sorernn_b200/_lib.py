@@ -10,6 +10,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgdn_b200.so"
 
 BF16, FP16, FP32 = 0, 1, 2
+NOALLOC_SCRATCH_BYTES = 36 << 20  # GDN_NOALLOC_SCRATCH_BYTES
 
 
 class Problem(ctypes.Structure):
@@ -41,6 +42,7 @@ SIGNATURES = {
     "gdn_segment_workspace_size": (_sz, [_P]),
     "gdn_workspace_error": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_i32)]),
     "gdn_kernel_launches": (ctypes.c_uint64, []),
+    "gdn_stream_kernels_error": (ctypes.c_int, [_vp, ctypes.POINTER(_i32)]),
     "gdn_chunk_bwd_noalloc": (ctypes.c_int, [_P] + [_vp] * 16),
     "gdn_gate_fwd": (ctypes.c_int, [_i64, _i64, _vp, _i32, _vp, _vp, _i32, _vp, _vp]),
     "gdn_gate_bwd": (ctypes.c_int, [_i64, _i64, _vp, _i32, _vp, _vp, _i32] + [_vp] * 5),

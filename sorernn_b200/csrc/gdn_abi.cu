@@ -61,6 +61,10 @@ bool aligned16(const void* x) { return ((uintptr_t)x & 15) == 0; }
 
 }  // namespace
 
+namespace gdn {
+int problem_status(const gdn_problem* p) { return check_problem(p); }
+}  // namespace gdn
+
 extern "C" {
 
 const char* gdn_status_string(int status) {
@@ -247,6 +251,18 @@ int gdn_segment_apply_state(const gdn_problem* p, const void* q, const void* k, 
 }
 
 uint64_t gdn_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int gdn_stream_kernels_error(gdn_stream_t stream, int32_t* error_out) {
+    if (!error_out) return GDN_ERR_ARGUMENT;
+    cudaStream_t s = (cudaStream_t)stream;
+    int e[3] = {0, 0, 0};
+    if (read_clear_decode_error(s, &e[0]) != GDN_OK || read_clear_norm_gate_error(s, &e[1]) != GDN_OK ||
+        read_clear_conv_error(s, &e[2]) != GDN_OK)
+        return GDN_ERR_LAUNCH;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return GDN_ERR_LAUNCH;
+    *error_out = e[0] ? e[0] : (e[1] ? e[1] : e[2]);
+    return GDN_OK;
+}
 
 int gdn_workspace_error(const void* workspace, gdn_stream_t stream, int32_t* error_out) {
     if (!workspace || !error_out) return GDN_ERR_ARGUMENT;

@@ -37,6 +37,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.h"
 #include "sm100.cuh"
 #include "tmap.h"
 
@@ -991,13 +992,7 @@ size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t H
 
 int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s) {
     using namespace cb;
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(chunk_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-            cudaSuccess)
-            return GDN_ERR_LAUNCH;
-        attr_set = true;
-    }
+    if (smem_optin((const void*)chunk_bwd_kernel, SMEM_BYTES) != cudaSuccess) return GDN_ERR_LAUNCH;
     // 1. rebuild every chunk-start state from the checkpoints (segment-parallel forward, no outputs)
     ChunkLaunch R{};
     R.q = L.q; R.k = L.k; R.v = L.v; R.g = L.g; R.beta = L.beta; R.o = nullptr;

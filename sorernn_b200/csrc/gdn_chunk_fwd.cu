@@ -29,6 +29,7 @@
 #include "chunk_common.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.h"
 #include "sm100.cuh"
 #include "tmap.h"
 
@@ -687,17 +688,10 @@ bool chunk_fwd_supported(int64_t DK, int64_t DV, int act_dtype) {
 
 int chunk_fwd(const ChunkLaunch& L, cudaStream_t s) {
     using namespace cf;
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(chunk_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(chunk_fwd_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(chunk_fwd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-                cudaSuccess)
-            return GDN_ERR_LAUNCH;
-        attr_set = true;
-    }
+    if (smem_optin((const void*)chunk_fwd_kernel<0>, SMEM_BYTES) != cudaSuccess ||
+        smem_optin((const void*)chunk_fwd_kernel<1>, SMEM_BYTES) != cudaSuccess ||
+        smem_optin((const void*)chunk_fwd_kernel<2>, SMEM_BYTES) != cudaSuccess)
+        return GDN_ERR_LAUNCH;
     ChunkFwdArgs a;
     memset(&a, 0, sizeof(a));
     const int64_t Ttot = L.B * L.T;

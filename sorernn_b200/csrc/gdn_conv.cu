@@ -15,6 +15,10 @@
 
 namespace gdn {
 
+// Device error word of this file's kernels (a stage wait that gave up); read and cleared by
+// read_clear_conv_error().
+static __device__ int g_conv_err;
+
 struct ConvArgs {
     const void *x, *w, *dy;
     void *y, *dx;
@@ -140,6 +144,7 @@ __global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t ran
     int64_t s_doc, e_doc;
     doc_span(a, u_lo, s_doc, e_doc);
 
+    bool ok = true;  // false once a stage wait timed out: from then on this thread stores nothing
     // one row u of the current document through the window; `have`: the row exists (u < BT), else zero.
     // No branches besides the predicated stores, so the unrolled rows of a document segment interleave.
     auto row = [&](int64_t u, const TA* xrow, const TA* dyrow, bool have) {
@@ -161,7 +166,7 @@ __global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t ran
                 for (int j = 0; j < K; ++j) acc = fmaf(w[q][K - 1 - j], xw[j][q], acc);
                 y[q] = a.silu ? acc * sig(acc) : acc;
             }
-            if (active && u >= tb) stv<TA, VEC>(a.y, u * a.C + c0, y);
+            if (active && ok && u >= tb) stv<TA, VEC>(a.y, u * a.C + c0, y);
         } else {
             float dyv[VEC];
             if (have) ldv<TA, VEC>(dyrow, 0, dyv);
@@ -175,7 +180,7 @@ __global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t ran
 #pragma unroll
                 for (int q = 0; q < VEC; ++q) dzw[j][q] = dzw[j + 1][q];
             }
-            const bool acc_dw = u < te;  // rows past the range feed dx only
+            const bool acc_dw = u < te && ok;  // rows past the range feed dx only
 #pragma unroll
             for (int q = 0; q < VEC; ++q) {
                 float z = 0.f;
@@ -201,14 +206,14 @@ __global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t ran
                 for (int j = 0; j < K; ++j) acc = fmaf(t + j < ew[0] ? w[q][K - 1 - j] : 0.f, dzw[j][q], acc);
                 dx[q] = acc;
             }
-            if (active && t >= tb) stv<TA, VEC>(a.dx, t * a.C + c0, dx);
+            if (active && ok && t >= tb) stv<TA, VEC>(a.dx, t * a.C + c0, dx);
         }
     };
 
-    bool ok = true;
     for (int64_t tile = 0; tile < ntiles; ++tile) {
         const int s = (int)(tile % STAGES);
-        ok = sm100::mbar_wait(&bar[s], (uint32_t)(tile / STAGES) & 1u, nullptr, 0, ok ? (1u << 22) : 1u) && ok;
+        ok = sm100::mbar_wait(&bar[s], (uint32_t)(tile / STAGES) & 1u, &g_conv_err, GDN_DEV_ERR_CONV,
+                              ok ? (1u << 22) : 1u) && ok;
         const int64_t u0 = u_lo + tile * TT;
         const int n = (int)(u_hi - u0 < TT ? u_hi - u0 : TT);
         // inactive threads (past a narrow slab's last group) read the group-0 column and store nothing
@@ -291,6 +296,14 @@ static int conv_launch(const ConvArgs& a, int K, bool bwd, cudaStream_t s) {
     if (cudaLaunchKernel(k, dim3((unsigned)(nranges * nslabs)), dim3(nthr), args, smem, s) != cudaSuccess)
         return GDN_ERR_LAUNCH;
     count_launch();
+    return GDN_OK;
+}
+
+int read_clear_conv_error(cudaStream_t s, int* out) {
+    static const int zero = 0;
+    if (cudaMemcpyFromSymbolAsync(out, g_conv_err, sizeof(int), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemcpyToSymbolAsync(g_conv_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) != cudaSuccess)
+        return GDN_ERR_LAUNCH;
     return GDN_OK;
 }
 

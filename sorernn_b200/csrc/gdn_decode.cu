@@ -15,10 +15,15 @@
 // 512-byte shared-memory line; the column sums over rows go through shared memory across the 8 warps.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.h"
 #include "sm100.cuh"
 
 namespace gdn {
 using namespace sm100;
+
+// Device error word of the decode kernel (a stage wait that gave up); read and cleared by
+// read_clear_decode_error().
+static __device__ int g_decode_err;
 
 namespace dec {
 constexpr int NTHR = 256;
@@ -103,7 +108,8 @@ __global__ void __launch_bounds__(dec::NTHR, 1) decode_tma_kernel(const __grid_c
             g_nx = ld_gate_raw(a.g, a.g_dtype, h + stride);
             b_nx = ld_gate_raw(a.beta, a.beta_dtype, h + stride);
         }
-        ok = mbar_wait(&bar[s], (uint32_t)(it / STAGES) & 1u, nullptr, 0, ok ? (1u << 22) : 1u) && ok;
+        ok = mbar_wait(&bar[s], (uint32_t)(it / STAGES) & 1u, &g_decode_err, GDN_DEV_ERR_DECODE,
+                       ok ? (1u << 22) : 1u) && ok;
         float* S = (float*)(sm + s * STAGE_BYTES);
         const TA* qs = (const TA*)(sm + s * STAGE_BYTES + STATE_BYTES);
         const TA* ks = (const TA*)(sm + s * STAGE_BYTES + STATE_BYTES + ACT_BYTES);
@@ -142,7 +148,9 @@ __global__ void __launch_bounds__(dec::NTHR, 1) decode_tma_kernel(const __grid_c
         }
         *reinterpret_cast<float4*>(red + rg * 128 + 4 * c) = pk;
         *reinterpret_cast<float4*>(red + 1024 + rg * 128 + 4 * c) = pq;
-        __syncthreads();
+        // every thread learns whether all waits so far succeeded: after a timeout the stage holds no valid
+        // state, so neither o nor the state is written from then on (the resident state keeps its old value)
+        ok = __syncthreads_and(ok) != 0;
         float4 sk = make_float4(0.f, 0.f, 0.f, 0.f), sq = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
@@ -156,7 +164,7 @@ __global__ void __launch_bounds__(dec::NTHR, 1) decode_tma_kernel(const __grid_c
         dl[1] = bt * (ld(vs, 4 * c + 1) - sk.y);
         dl[2] = bt * (ld(vs, 4 * c + 2) - sk.z);
         dl[3] = bt * (ld(vs, 4 * c + 3) - sk.w);
-        if (rg == 0) {  // o = scale (S'^T qn + delta (qn . kn))
+        if (rg == 0 && ok) {  // o = scale (S'^T qn + delta (qn . kn))
             const float kq = qk * iq * ik;
             TA* o = (TA*)a.o + h * 128 + 4 * c;
             st(o, 0, a.scale * fmaf(dl[0], kq, sq.x));
@@ -165,19 +173,21 @@ __global__ void __launch_bounds__(dec::NTHR, 1) decode_tma_kernel(const __grid_c
             st(o, 3, a.scale * fmaf(dl[3], kq, sq.w));
         }
         // S_new = S' + kn delta^T, back into the stage for the bulk store
+        if (ok) {
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int i = rg + 8 * r;
-            const float ki = ld(ks, i) * ik;
-            float4 x = sv[r];
-            x.x = fmaf(ki, dl[0], x.x); x.y = fmaf(ki, dl[1], x.y); x.z = fmaf(ki, dl[2], x.z); x.w = fmaf(ki, dl[3], x.w);
-            *reinterpret_cast<float4*>(S + i * 128 + 4 * c) = x;
+            for (int r = 0; r < 16; ++r) {
+                const int i = rg + 8 * r;
+                const float ki = ld(ks, i) * ik;
+                float4 x = sv[r];
+                x.x = fmaf(ki, dl[0], x.x); x.y = fmaf(ki, dl[1], x.y); x.z = fmaf(ki, dl[2], x.z); x.w = fmaf(ki, dl[3], x.w);
+                *reinterpret_cast<float4*>(S + i * 128 + 4 * c) = x;
+            }
         }
         fence_async_smem();
         __syncthreads();  // also: every read of red is done before the next head writes it
         if (tid == 0) {
-            bulk_s2g(a.state + h * 16384, S, STATE_BYTES);
-            bulk_commit();
+            if (ok) bulk_s2g(a.state + h * 16384, S, STATE_BYTES);
+            bulk_commit();  // an empty group after a timeout keeps the group count of the refill schedule
             if (h + 2 * stride < a.heads) {
                 bulk_wait_read_1();  // stage (it + 2) % 3 held head h - stride, whose store has now read it
                 issue(h + 2 * stride, (it + 2) % STAGES);
@@ -207,16 +217,18 @@ int decode_tma(const void* q, const void* k, const void* v, const void* g, const
         return GDN_ERR_LAUNCH;
     const unsigned grid = (unsigned)(a.heads < sms ? a.heads : sms);
     GDN_DISPATCH_DTYPE(act_dtype, TA,
-        static bool attr_set = false;
-        if (!attr_set) {
-            if (cudaFuncSetAttribute(decode_tma_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-                cudaSuccess)
-                return GDN_ERR_LAUNCH;
-            attr_set = true;
-        }
+        if (smem_optin((const void*)decode_tma_kernel<TA>, SMEM_BYTES) != cudaSuccess) return GDN_ERR_LAUNCH;
         decode_tma_kernel<TA><<<grid, NTHR, SMEM_BYTES, s>>>(a);)
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+int read_clear_decode_error(cudaStream_t s, int* out) {
+    static const int zero = 0;
+    if (cudaMemcpyFromSymbolAsync(out, g_decode_err, sizeof(int), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemcpyToSymbolAsync(g_decode_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) != cudaSuccess)
+        return GDN_ERR_LAUNCH;
+    return GDN_OK;
 }
 
 }  // namespace gdn

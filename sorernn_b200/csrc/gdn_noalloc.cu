@@ -1,24 +1,29 @@
 // gdn_chunk_bwd_noalloc: the backward entry point for callers that cannot allocate device memory.
 //
-// gdn_chunk_bwd needs a caller-provided workspace (the chunk-start state tiles it rebuilds from the
-// forward's checkpoints, an error word, and fp32 dq/dk accumulators for grouped value heads). Some callers
-// have no way to allocate it at call time: a host runtime that reaches this library over a plain C FFI
-// with no device allocator of its own, or a plugin whose execute/enqueue hook is not allowed to allocate.
-// This entry point takes the same arguments minus the workspace and uses a fixed scratch array that lives
-// in this library's device image instead. It allocates nothing: no cudaMalloc, no cudaFree, no allocating
+// gdn_chunk_bwd needs a caller-provided workspace (the per-chunk records it rebuilds from the forward's
+// checkpoints, an error word, and fp32 dq/dk accumulators for grouped value heads). Some callers have no
+// way to allocate it at call time: a host runtime that reaches this library over a plain C FFI with no
+// device allocator of its own, or a plugin whose execute/enqueue hook is not allowed to allocate. This
+// entry point takes the same arguments minus the workspace and uses a fixed scratch array that lives in
+// this library's device image instead. It allocates nothing: no cudaMalloc, no cudaFree, no allocating
 // library routine.
 //
 // Limits and sharing:
-//  * the scratch holds kNoAllocScratchBytes (36 MiB) on every GPU that loads the library, until the process
-//    exits; a problem whose gdn_chunk_bwd_workspace_size() exceeds it is rejected with
-//    GDN_ERR_SCRATCH_LIMIT before anything is launched (for example: 1,024 chunk-heads of 64 tokens,
-//    i.e. one 4,096-token sequence with 16 heads, fits);
+//  * the scratch holds GDN_NOALLOC_SCRATCH_BYTES (36 MiB) on every GPU that loads the library, until the
+//    process exits; a problem whose gdn_chunk_bwd_workspace_size() exceeds it is rejected with
+//    GDN_ERR_SCRATCH_LIMIT before anything is launched. The workspace is 256 bytes plus one record per
+//    (64-token chunk, value head), so the array holds 418 chunk-heads of the chunked kernels: for example
+//    T = 1,024 tokens with 16 heads (256 chunk-heads) or T = 4,096 with 6 heads (384) in one call;
 //  * every call on a device uses the same array and leaves its contents behind; what must start at zero
 //    (the error word, the dq/dk accumulators) is cleared by each call, on its stream;
 //  * calls whose work overlaps on the GPU (different streams, or several host threads) race on the array:
 //    order them on one stream or serialize them;
+//  * the device-side error word of the bounded waits sits in the array, which the caller never sees: a
+//    noalloc call cannot report a device-side timeout (GDN_ERR_TIMEOUT); use gdn_chunk_bwd with a workspace
+//    and gdn_workspace_error where that report is needed;
 //  * the first call on each device looks up the array's device address (cudaGetSymbolAddress, with that
-//    device current); make that first call before any stream capture begins.
+//    device current) and keeps it for the life of the device's primary context; make that first call
+//    before any stream capture begins.
 #include <mutex>
 
 #include "common.cuh"
@@ -26,7 +31,7 @@
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = (size_t)36 << 20;
+constexpr size_t kNoAllocScratchBytes = GDN_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
 
 // In host code this name is only a host-side stand-in for the device array; the kernels are given the
@@ -43,8 +48,9 @@ extern "C" int gdn_chunk_bwd_noalloc(const gdn_problem* p, const void* q, const 
                                      const void* g, const void* beta, const float* initial_state,
                                      const float* checkpoints, const void* dout, const float* dht, void* dq,
                                      void* dk, void* dv, float* dg, float* dbeta, float* dh0, gdn_stream_t stream) {
+    const int st = gdn::problem_status(p);  // an invalid problem reports the same status as gdn_chunk_bwd
+    if (st != GDN_OK) return st;
     const size_t need = gdn_chunk_bwd_workspace_size(p);
-    if (need == 0) return GDN_ERR_SHAPE;  // the problem itself is invalid
     if (need > kNoAllocScratchBytes) return GDN_ERR_SCRATCH_LIMIT;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GDN_ERR_LAUNCH;

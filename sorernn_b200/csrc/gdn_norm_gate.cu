@@ -18,6 +18,10 @@
 
 namespace gdn {
 
+// Device error word of this file's kernels (a stage wait that gave up); read and cleared by
+// read_clear_norm_gate_error().
+static __device__ int g_norm_gate_err;
+
 namespace ngs {
 constexpr int NTHR = 256;
 constexpr int STAGES = 3;
@@ -93,13 +97,14 @@ __global__ void __launch_bounds__(ngs::NTHR) norm_gate_kernel(const NormGateArgs
     int it = 0;
     for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
         const int s = it % STAGES;
-        ok = sm100::mbar_wait(&bar[s], (uint32_t)(it / STAGES) & 1u, nullptr, 0, ok ? (1u << 22) : 1u) && ok;
+        ok = sm100::mbar_wait(&bar[s], (uint32_t)(it / STAGES) & 1u, &g_norm_gate_err, GDN_DEV_ERR_NORM_GATE,
+                              ok ? (1u << 22) : 1u) && ok;
         const int64_t r0 = tile * tr;
         const int nr = (int)(a.rows - r0 < tr ? a.rows - r0 : tr);
         const uint8_t* st = smem + s * NT * TILE;
         for (int p = 0; p < tr; p += rpass) {  // every lane takes part in the row reductions
             const int rr = p + row_in_pass;
-            const bool valid = rr < nr;
+            const bool valid = rr < nr && ok;  // after a timed-out wait the stage holds nothing usable
             const int rs_ = valid ? rr : 0;  // rows past the tile's end read row 0 and store nothing
             float x[PER], g[PER];
             ldv<TA, PER>(st, (int64_t)rs_ * a.D + f0, x);
@@ -181,6 +186,14 @@ static int ng_launch(const NormGateArgs& a, cudaStream_t s) {
     }
 #undef NG_CASE
     return GDN_ERR_SHAPE;
+}
+
+int read_clear_norm_gate_error(cudaStream_t s, int* out) {
+    static const int zero = 0;
+    if (cudaMemcpyFromSymbolAsync(out, g_norm_gate_err, sizeof(int), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemcpyToSymbolAsync(g_norm_gate_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) != cudaSuccess)
+        return GDN_ERR_LAUNCH;
+    return GDN_OK;
 }
 
 }  // namespace gdn

@@ -3,10 +3,15 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/gdn_b200.h"
+
 namespace gdn {
 
 // Host-side count of kernel launches made by the library (gdn_kernel_launches()).
 void count_launch(int n = 1);
+
+// Validation of a gdn_problem (status code; GDN_OK when the problem is well formed).
+int problem_status(const gdn_problem* p);
 
 // Arguments of the recurrent (token-by-token) kernels.
 struct RecLaunch {
@@ -64,6 +69,15 @@ struct ChunkBwdLaunch {
     float scale;
     int g_dtype, beta_dtype, l2norm, ckpt_every;
 };
+
+// Codes the workspace-less streaming kernels leave in their device error words when a stage wait gives up
+// (read through gdn_stream_kernels_error).
+constexpr int GDN_DEV_ERR_DECODE = 31;
+constexpr int GDN_DEV_ERR_NORM_GATE = 32;
+constexpr int GDN_DEV_ERR_CONV = 33;
+int read_clear_decode_error(cudaStream_t s, int* out);
+int read_clear_norm_gate_error(cudaStream_t s, int* out);
+int read_clear_conv_error(cudaStream_t s, int* out);
 
 // Single-token decode for DK = DV = 128 (persistent bulk-copy pipeline over the fp32 states).
 bool decode_tma_supported(int64_t DK, int64_t DV, const void* q, const void* k, const void* v, const float* state);

@@ -87,3 +87,33 @@ def test_decode_rejects_bad_shapes():
     assert lib.gdn_decode_step(4, 3, 4, 128, 128, 0.1, 0, 0, 0, 0, vp, vp, vp, vp, vp, vp, vp, None) == 1
     assert lib.gdn_decode_step(4, 4, 4, 128, 128, 0.1, 9, 0, 0, 0, vp, vp, vp, vp, vp, vp, vp, None) == 2
     assert lib.gdn_decode_step(4, 4, 4, 128, 128, 0.1, 0, 0, 0, 0, vp, vp, vp, vp, vp, None, vp, None) == 7
+
+
+def _chunk_problem(T, H, B=1):
+    return _problem(B=B, T=T, H=H, HV=H, N=B, DK=128, DV=128, act_dtype=_lib.BF16, g_dtype=_lib.FP32,
+                    beta_dtype=_lib.BF16, max_seqlen=T, ckpt_every=8)
+
+
+@pytest.mark.parametrize("T,H,fits", [(1024, 16, True), (4096, 6, True), (64, 418, True), (64, 419, False),
+                                      (4096, 16, False)])
+def test_noalloc_capacity_matches_its_documentation(T, H, fits):
+    """The header states the fixed array holds 418 chunk-heads (e.g. T = 1,024 x 16 heads, T = 4,096 x 6):
+    those problems' workspaces fit, one chunk-head more does not, and gdn_chunk_bwd_noalloc rejects a problem
+    that does not fit with GDN_ERR_SCRATCH_LIMIT before touching the device."""
+    lib = _lib.lib()
+    p = _chunk_problem(T, H)
+    need = lib.gdn_chunk_bwd_workspace_size(ctypes.byref(p))
+    assert need > 0
+    assert (need <= _lib.NOALLOC_SCRATCH_BYTES) == fits, need
+    if not fits:
+        vp = ctypes.c_void_p(256)
+        assert lib.gdn_chunk_bwd_noalloc(ctypes.byref(p), *([vp] * 15), None) == 8
+
+
+def test_noalloc_reports_the_same_status_as_the_workspace_backward_for_invalid_problems():
+    lib = _lib.lib()
+    vp = ctypes.c_void_p(256)
+    for bad, want in ((dict(act_dtype=7), 2), (dict(HV=6), 1), (dict(ckpt_every=0), 7)):
+        p = _problem(**bad)
+        assert lib.gdn_chunk_bwd_noalloc(ctypes.byref(p), *([vp] * 15), None) == want
+        assert lib.gdn_chunk_bwd(ctypes.byref(p), *([vp] * 15), vp, 1 << 30, None) == want
