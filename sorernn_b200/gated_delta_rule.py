@@ -47,6 +47,17 @@ def _problem(q, k, v, g, beta, scale, cu_seqlens, max_seqlen, use_qk_l2norm, ckp
                         beta_dtype=_DT[beta.dtype], use_qk_l2norm=int(use_qk_l2norm), ckpt_every=ckpt_every)
 
 
+def checkpoint_count(B: int, T: int, N: int, ckpt_every: int, varlen: bool) -> int:
+    """Number of forward state checkpoints, the same count as ``gdn_checkpoint_count`` (gdn_abi.cu) computes:
+    one per ``ckpt_every`` 64-token chunks of each sequence; with ``cu_seqlens`` an upper bound from the
+    packed length and the number of sequences alone (no device read)."""
+    if not varlen:
+        nc = (T + 63) // 64
+        return N * ((nc + ckpt_every - 1) // ckpt_every)
+    nc = (B * T + 63 * N) // 64
+    return nc // ckpt_every + N + 1
+
+
 def _check_inputs(q, k, v, g, beta, cu_seqlens):
     if not q.is_cuda:
         raise RuntimeError("sorernn_b200 runs on CUDA tensors only (no CPU fallback)")
@@ -92,11 +103,7 @@ def _(q, k, v, g, beta, initial_state, cu_seqlens, scale, use_qk_l2norm, max_seq
     B, T, H, DK = q.shape
     HV, DV = v.shape[2], v.shape[3]
     N = B if cu_seqlens is None else cu_seqlens.shape[0] - 1
-    p = _problem(q, k, v, g, beta, scale, None, max_seqlen, use_qk_l2norm, ckpt_every)
-    p.N = N
-    if cu_seqlens is not None:
-        p.cu_seqlens = 1  # only its presence matters for the count
-    n_ck = _lib.lib().gdn_checkpoint_count(ctypes.byref(p))
+    n_ck = checkpoint_count(B, T, N, ckpt_every, cu_seqlens is not None)  # no library call while tracing
     return (torch.empty_like(v), q.new_empty(N, HV, DK, DV, dtype=torch.float32),
             q.new_empty(max(n_ck, 0), HV, DK, DV, dtype=torch.float32))
 

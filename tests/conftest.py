@@ -23,3 +23,27 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """Worst parity figure per output over the run: the strict max-abs/RMS beside the error beyond the
+    bf16 output rounding (the figure the bf16 bars are applied to); fp32 outputs show the strict one only."""
+    from helpers import PARITY_LOG
+
+    if not PARITY_LOG:
+        return
+    worst = {}
+    for name, strict, excess, tol in PARITY_LOG:
+        w = worst.setdefault(name, [0.0, None, tol, 0])
+        w[0] = max(w[0], strict)
+        if excess is not None:
+            w[1] = excess if w[1] is None else max(w[1], excess)
+        w[2] = max(w[2], tol)
+        w[3] += 1
+    tr = terminalreporter
+    tr.write_sep("-", "parity: worst max-abs error / RMS(reference) per output")
+    tr.write_line(f"{'output':<16}{'checks':>8}{'strict':>12}{'beyond bf16 rounding':>24}{'bar':>8}")
+    for name in sorted(worst):
+        strict, excess, tol, n = worst[name]
+        ex = "-" if excess is None else f"{excess:.4f}"
+        tr.write_line(f"{name:<16}{n:>8}{strict:>12.4f}{ex:>24}{tol:>8}")

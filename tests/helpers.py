@@ -2,6 +2,13 @@
 import numpy as np
 
 
+# Every parity comparison made in this process: (output name, strict max-abs/RMS, error beyond the bf16
+# output rounding / RMS or None for fp32 outputs, bar). conftest.py prints the worst per output at the end
+# of the run, so the log shows how far each output is from the literal north-star bar and from the bar
+# applied beyond rounding.
+PARITY_LOG = []
+
+
 def rms(x) -> float:
     x = np.asarray(x, dtype=np.float64)
     return float(np.sqrt((x * x).mean())) if x.size else 0.0
@@ -15,6 +22,7 @@ def assert_rms_close(actual, ref, tol, name=""):
     err = float(np.abs(a - r).max()) if a.size else 0.0
     bound = tol * max(rms(r), 1e-30)
     assert np.isfinite(a).all(), f"{name}: non-finite values"
+    PARITY_LOG.append((name, err / max(rms(r), 1e-30), None, tol))
     assert err <= bound, f"{name}: max abs err {err:.3e} > {tol} * RMS(ref) = {bound:.3e}"
     return err / max(rms(r), 1e-30)
 
@@ -34,6 +42,7 @@ def assert_bf16_close(actual, ref, tol, name=""):
     rr = max(rms(r), 1e-30)
     err = np.abs(a - r)
     excess = float((err - 2.0 ** -8 * np.abs(r)).max()) if a.size else 0.0
+    PARITY_LOG.append((name, float(err.max() / rr) if a.size else 0.0, excess / rr, tol))
     assert excess <= tol * rr, (f"{name}: error beyond bf16 output rounding {excess:.3e} > {tol} * RMS(ref) = "
                                 f"{tol * rr:.3e} (strict max-abs/RMS {err.max() / rr:.4f})")
     return float(err.max() / rr), excess / rr

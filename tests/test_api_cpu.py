@@ -38,3 +38,43 @@ def test_cpu_tensors_are_refused():
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         fused_recurrent_gated_delta_rule_step(q[:, 0], k[:, 0], v[:, 0], g[:, 0], beta[:, 0], state)
 
+
+
+@pytest.mark.parametrize("B,T,N,K,varlen", [(8, 4096, 8, 8, False), (2, 300, 2, 4, False), (1, 1000, 5, 8, True),
+                                            (1, 64, 1, 1, False), (1, 0, 3, 8, True)])
+def test_python_checkpoint_count_matches_library(B, T, N, K, varlen):
+    import ctypes
+
+    from sorernn_b200 import _lib
+    from sorernn_b200.gated_delta_rule import checkpoint_count
+
+    p = _lib.Problem(B=B, T=T, H=2, HV=2, DK=128, DV=128, N=N, cu_seqlens=16 if varlen else None, max_seqlen=T,
+                     scale=1.0, act_dtype=_lib.BF16, g_dtype=_lib.FP32, beta_dtype=_lib.BF16, use_qk_l2norm=1,
+                     ckpt_every=K)
+    assert checkpoint_count(B, T, N, K, varlen) == _lib.lib().gdn_checkpoint_count(ctypes.byref(p))
+
+
+def test_fake_kernels_trace_without_the_library(monkeypatch):
+    """The custom ops' fake (meta) kernels compute output shapes in Python, so tracing (torch.compile,
+    activation-checkpoint policies) needs neither a GPU nor the CUDA library."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    from sorernn_b200 import _lib
+    import sorernn_b200.gated_delta_rule  # noqa: F401  (registers the ops)
+
+    def no_lib():
+        raise AssertionError("the CUDA library was called while tracing")
+
+    monkeypatch.setattr(_lib, "lib", no_lib)
+    with FakeTensorMode():
+        q = torch.empty(1, 300, 2, 128, dtype=torch.bfloat16, device="cuda")
+        v = torch.empty(1, 300, 4, 128, dtype=torch.bfloat16, device="cuda")
+        g = torch.empty(1, 300, 4, dtype=torch.float32, device="cuda")
+        b = torch.empty(1, 300, 4, dtype=torch.bfloat16, device="cuda")
+        cu = torch.empty(4, dtype=torch.int64, device="cuda")
+        o, ht, ck = torch.ops.sorernn_b200.gdn_fwd(q, q, v, g, b, None, cu, 0.1, True, 300, 8)
+        assert o.shape == v.shape and ht.shape == (3, 4, 128, 128)
+        assert ck.shape[0] == (300 + 63 * 3) // 64 // 8 + 3 + 1
+        dq, dk, dv, dg, db, dh0 = torch.ops.sorernn_b200.gdn_bwd(q, q, v, g, b, None, ck, v, None, cu, 0.1, True,
+                                                                 300, 8)
+        assert dq.shape == q.shape and dv.shape == v.shape and dh0.shape == (3, 4, 128, 128)

@@ -1,0 +1,144 @@
+"""GPU checks of the op's contract with its callers (the boundary, not the numbers):
+
+* fwd + bwd of a packed micro-batch never synchronises the host, the contract soreRNN enforces for its
+  FLA path with ``torch.cuda.set_sync_debug_mode("error")`` (tests/model/test_lm.py:292-320 of the
+  reference); ``cu_seqlens_cpu`` is read only to size buffers;
+* the custom ops pass ``torch.library.opcheck`` (schema, fake kernels, autograd registration), so
+  ``torch.compile`` and activation-checkpoint policies treat the mixer as one opaque op
+  (sore/model/checkpointing.py:10-17 relies on that for FLA's op);
+* a ``torch.compile``d call runs the same kernels as the eager call (bitwise equal results);
+* the streaming kernels' device error words read zero after normal runs;
+* one process can drive two GPUs (the large shared-memory opt-in is per device).
+"""
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.filterwarnings("ignore:Synchronization debug mode is a prototype:UserWarning")]
+D = 128
+
+
+def _packed(seed, cu, H=2, HV=4, requires_grad=True):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    T = cu[-1]
+    x = dict(q=torch.randn(1, T, H, D, device="cuda", generator=g).bfloat16(),
+             k=torch.randn(1, T, H, D, device="cuda", generator=g).bfloat16(),
+             v=torch.randn(1, T, HV, D, device="cuda", generator=g).bfloat16(),
+             g=torch.nn.functional.logsigmoid(torch.randn(1, T, HV, device="cuda", generator=g)) / 16,
+             beta=torch.sigmoid(torch.randn(1, T, HV, device="cuda", generator=g)).bfloat16())
+    if requires_grad:
+        x = {n: t.requires_grad_(True) for n, t in x.items()}
+    do = torch.randn(1, T, HV, D, device="cuda", generator=g).bfloat16()
+    return x, do
+
+
+@pytest.mark.parametrize("gate_in_kernel", [False, True], ids=["gates", "gate_in_kernel"])
+def test_packed_fwd_bwd_has_no_host_sync(gate_in_kernel):
+    from sorernn_b200 import chunk_gated_delta_rule
+
+    cu = [0, 1, 70, 200, 200, 451, 512]
+    cu_dev = torch.tensor(cu, device="cuda")
+    cu_cpu = torch.tensor(cu)
+    A_log = torch.zeros(4, device="cuda", requires_grad=True)
+    dt_bias = torch.zeros(4, device="cuda", requires_grad=True)
+
+    def step(x, do):
+        kw = {}
+        if gate_in_kernel:
+            kw = dict(use_gate_in_kernel=True, A_log=A_log, dt_bias=dt_bias, use_beta_sigmoid_in_kernel=True)
+        o, _ = chunk_gated_delta_rule(x["q"], x["k"], x["v"], x["g"], x["beta"], cu_seqlens=cu_dev,
+                                      cu_seqlens_cpu=cu_cpu, use_qk_l2norm_in_kernel=True, **kw)
+        o.backward(do)
+
+    step(*_packed(1, cu))  # warm-up: library load, tensor-map driver entry point, shared-memory opt-in
+    torch.cuda.synchronize()
+    x, do = _packed(2, cu)
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        step(x, do)
+    finally:
+        torch.cuda.set_sync_debug_mode("default")
+    torch.cuda.synchronize()
+    assert all(t.grad is not None and torch.isfinite(t.grad.float()).all() for t in x.values())
+
+
+def test_custom_ops_pass_opcheck():
+    import sorernn_b200.gated_delta_rule  # noqa: F401  (registers the ops)
+
+    x, do = _packed(3, [0, 130, 300], requires_grad=False)
+    cu = torch.tensor([0, 130, 300], device="cuda")
+    h0 = torch.randn(2, 4, D, D, device="cuda") * 0.05
+    fwd_args = (x["q"], x["k"], x["v"], x["g"], x["beta"], h0, cu, D ** -0.5, True, 170, 4)
+    torch.library.opcheck(torch.ops.sorernn_b200.gdn_fwd.default, fwd_args)
+    _, _, ck = torch.ops.sorernn_b200.gdn_fwd(*fwd_args)
+    dht = torch.randn(2, 4, D, D, device="cuda") * 0.1
+    bwd_args = (x["q"], x["k"], x["v"], x["g"], x["beta"], h0, ck, do, dht, cu, D ** -0.5, True, 170, 4)
+    torch.library.opcheck(torch.ops.sorernn_b200.gdn_bwd.default, bwd_args)
+
+
+def test_torch_compile_runs_the_same_kernels():
+    from sorernn_b200 import chunk_gated_delta_rule
+
+    def fwd_bwd(q, k, v, g, beta, do):
+        o, ht = chunk_gated_delta_rule(q, k, v, g, beta, output_final_state=True, use_qk_l2norm_in_kernel=True)
+        (o.float() * do.float()).sum().backward()
+        return o, ht
+
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    base = dict(q=torch.randn(2, 200, 2, D, device="cuda", generator=gen).bfloat16(),
+                k=torch.randn(2, 200, 2, D, device="cuda", generator=gen).bfloat16(),
+                v=torch.randn(2, 200, 2, D, device="cuda", generator=gen).bfloat16(),
+                g=torch.nn.functional.logsigmoid(torch.randn(2, 200, 2, device="cuda", generator=gen)) / 16,
+                beta=torch.sigmoid(torch.randn(2, 200, 2, device="cuda", generator=gen)).bfloat16())
+    do = torch.randn(2, 200, 2, D, device="cuda", generator=gen).bfloat16()
+    results = []
+    for fn in (fwd_bwd, torch.compile(fwd_bwd)):
+        x = {n: t.clone().requires_grad_(True) for n, t in base.items()}
+        o, ht = fn(x["q"], x["k"], x["v"], x["g"], x["beta"], do)
+        results.append([o, ht] + [x[n].grad for n in ("q", "k", "v", "g", "beta")])
+    for a, b in zip(*results):
+        assert torch.equal(a, b)
+
+
+def test_stream_kernel_error_words_are_clear_after_normal_runs():
+    import ctypes
+
+    from sorernn_b200 import _lib, fused_recurrent_gated_delta_rule_step
+    from sorernn_b200.layer_ops import causal_conv1d, rms_norm_gated
+
+    gen = torch.Generator(device="cuda").manual_seed(6)
+    state = torch.randn(8, 4, D, D, device="cuda", generator=gen) * 0.02
+    q = torch.randn(8, 4, D, device="cuda", generator=gen).bfloat16()
+    g = torch.zeros(8, 4, device="cuda")
+    fused_recurrent_gated_delta_rule_step(q, q, q, g, g + 0.5, state, use_qk_l2norm_in_kernel=True)
+    x = torch.randn(2, 64, 4, D, device="cuda", generator=gen).bfloat16()
+    rms_norm_gated(x, x, torch.ones(D, device="cuda"), None, activation="swish", eps=1e-6)
+    causal_conv1d(x.view(2, 64, 4 * D), torch.randn(4 * D, 4, device="cuda", generator=gen), activation="silu")
+    err = ctypes.c_int32(-1)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.check(_lib.lib().gdn_stream_kernels_error(stream, ctypes.byref(err)), "gdn_stream_kernels_error")
+    assert err.value == 0
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in one process")
+def test_one_process_drives_two_devices():
+    """The 230 KB shared-memory opt-in of the chunk kernels is made per device: the same forward and
+    backward run on device 0 and then on device 1 of one process and agree bitwise."""
+    from sorernn_b200 import chunk_gated_delta_rule
+
+    outs = []
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            gen = torch.Generator(device=f"cuda:{dev}").manual_seed(7)
+            x = {n: torch.randn(1, 300, 2, D, device=f"cuda:{dev}", generator=gen).bfloat16().requires_grad_(True)
+                 for n in ("q", "k", "v")}
+            gg = (torch.nn.functional.logsigmoid(torch.randn(1, 300, 2, device=f"cuda:{dev}", generator=gen))
+                  / 16).requires_grad_(True)
+            bb = torch.sigmoid(torch.randn(1, 300, 2, device=f"cuda:{dev}", generator=gen)).bfloat16()
+            bb.requires_grad_(True)
+            o, _ = chunk_gated_delta_rule(x["q"], x["k"], x["v"], gg, bb, use_qk_l2norm_in_kernel=True)
+            o.float().sum().backward()
+            torch.cuda.synchronize()
+            outs.append([t.cpu() for t in (o, x["q"].grad, x["k"].grad, x["v"].grad, gg.grad, bb.grad)])
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
