@@ -33,10 +33,12 @@ CFG3 = dict(N=256, H=16, D=128)
 METRIC = "GDN fwd+bwd tokens/s (B8 T4096 H16 d128 bf16); decode-step HBM GB/s"
 C = 64
 FWD_FLOP_PER_TOKEN_HEAD = 10 * C * 128 + 6 * 128 * 128 + C * C / 3  # chunked fwd count, 181,589
+# What bounds the strong-scaling side line (the serial part of the step at few units per GPU).
+STRONG_LIMITER = ("each (sequence, head) unit walks its 64 chunks serially in one CTA: with {units} units per "
+                  "rank, {units} SMs work and the step time stays the per-unit chain time")
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
-# DRAM bytes (read + write) per launch from ncu captures of this build, per profiles/*.md:
-# backward pass (recompute + sweep launches) at batch 2 scaled by 4 to batch 8 (chunk_kernels_batch2_full.md);
-# decode step at full config-3 size (decode_tma_config3.md).
+# DRAM bytes (read + write) per launch from ncu captures of this build: the backward pass (recompute +
+# sweep launches) captured at batch 2 and scaled by 4 to batch 8; the decode step at full config-3 size.
 BWD_PASS_TRAFFIC_BYTES = (211.7e6 + 405.3e6) * 4
 DECODE_TRAFFIC_BYTES = 271.6e6 + 210.9e6
 
@@ -163,9 +165,10 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
-def decode_bench(dev, rank, world, n_dec=200, timed=True):
+def decode_bench(dev, rank, world, n_dec=1024, timed=True):
     """Decode (config 3): 256 sequences x 16 heads, fp32 state in HBM, bf16 token inputs; one step
-    updates every state in place. Returns (ms per step, HBM bytes per step)."""
+    updates every state in place; 1,024 consecutive steps are timed, as config 3 specifies. Returns
+    (ms per step, HBM bytes per step)."""
     import torch
 
     from sorernn_b200 import fused_recurrent_gated_delta_rule_step
@@ -281,6 +284,79 @@ def layer_ops_bench(dev, world, hbm_peak, reps=10):
             "causal_conv1d_hbm_frac": round(gbs_cv / hbm_peak, 4)}
 
 
+def activation_memory(leaf, do, step, zero):
+    """Device memory of one config-1 fwd+bwd, from the caching allocator's counters: the bytes the forward
+    leaves allocated until the backward (its output o, the final state and the op's own saved tensors:
+    the fp32 state checkpoints every 8 chunks; q, k, v, g, beta are the caller's and not counted) and the
+    backward's peak above that (its transient workspace plus the gradients). Beside them, what storing
+    every chunk's fp32 state would take (FLA's chunk_fwd_h materialises [B, NT, H, 128, 128] in its
+    backward), so that the bytes the checkpoint recompute saves are a measured figure."""
+    import torch
+
+    from sorernn_b200.gated_delta_rule import DEFAULT_CKPT_EVERY, chunk_gated_delta_rule
+
+    zero()
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated()
+    o, _ = chunk_gated_delta_rule(leaf["q"], leaf["k"], leaf["v"], leaf["g"], leaf["beta"],
+                                  use_qk_l2norm_in_kernel=True)
+    torch.cuda.synchronize()
+    held = torch.cuda.memory_allocated() - base
+    o_bytes = o.numel() * o.element_size()
+    torch.cuda.reset_peak_memory_stats()
+    after_fwd = torch.cuda.memory_allocated()
+    o.backward(do)
+    torch.cuda.synchronize()
+    bwd_peak = torch.cuda.max_memory_allocated() - after_fwd
+    grads = sum(t.grad.numel() * t.grad.element_size() for t in leaf.values())
+    del o
+    zero()
+    B, T, H, D = leaf["q"].shape
+    per_chunk_states = B * H * ((T + 63) // 64) * D * D * 4
+    return {"held_fwd_to_bwd_bytes": held, "of_which_output_o": o_bytes, "op_saved_bytes": held - o_bytes,
+            "bwd_peak_above_fwd_bytes": bwd_peak, "of_which_gradients": grads,
+            "bwd_transient_bytes": bwd_peak - grads, "ckpt_every_chunks": DEFAULT_CKPT_EVERY,
+            "per_chunk_fp32_states_bytes": per_chunk_states,
+            "saved_vs_per_chunk_states_bytes": per_chunk_states - (held - o_bytes),
+            "note": "torch.cuda.memory_allocated / max_memory_allocated around one call"}
+
+
+def strong_scaling_bench(dev, rank, world, step, steps):
+    """Config 1 with its total work fixed: the B=8 rows (x 16 heads) are split across the ranks (B/N rows
+    per rank, i.e. 128/N (sequence, head) units) and every rank times fwd+bwd of its share; value = the
+    8 x 4096 tokens / the slowest rank's time per step (strong scaling). The main line is the weak one
+    (every rank a full B=8 problem)."""
+    import torch
+
+    B, T, H, D = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["D"]
+    if B % world:
+        return {"skipped": f"B={B} rows do not split over {world} ranks"}
+    Br = B // world
+    x = make_inputs(Br, T, H, D, dev, seed=77 + rank)
+    leaf = {n: x[n].clone().requires_grad_(n != "do") for n in ("q", "k", "v", "g", "beta")}
+
+    def zero_s():
+        for t in leaf.values():
+            t.grad = None
+
+    for _ in range(3):
+        zero_s()
+        step(leaf, x["do"])
+    barrier(world)
+    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(steps):
+        zero_s()
+        step(leaf, x["do"])
+    e0.record()
+    barrier(world)
+    ms = max_over_ranks(s0.elapsed_time(e0) / steps, world)
+    return {"workload": f"config1 B{B} T{T} H{H} d{D} fwd+bwd split by batch rows over {world} rank(s)",
+            "per_rank_batch": Br, "units_per_rank": Br * H, "ms_per_step": round(ms, 4),
+            "tokens_per_s": round(B * T / (ms / 1e3), 1), "scaling": "strong",
+            "limiter": STRONG_LIMITER.format(units=Br * H)}
+
+
 def run_ours(args):
     import torch
 
@@ -323,6 +399,7 @@ def run_ours(args):
         zero()
         step(leaf, x["do"])
     barrier(world)
+    mem = activation_memory(leaf, x["do"], step, zero) if not args.profile_batch else None
     if args.profile_batch:
         for _ in range(args.steps):
             zero()
@@ -404,6 +481,7 @@ def run_ours(args):
     barrier(world)
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e2e_steps, world)
 
+    strong = strong_scaling_bench(dev, rank, world, step, args.steps)
     dec_ms, dec_bytes = decode_bench(dev, rank, world)
     long_prefill = long_prefill_bench(dev, rank, world)
     peaks, peak_kind = load_peaks()
@@ -447,6 +525,8 @@ def run_ours(args):
         "clocks": clk.summary(),
         "long_prefill": long_prefill,
         "layer_ops": layer_ops,
+        "activation_memory": mem,
+        "config1_strong": strong,
     }
     if rank == 0:
         if world == 1:  # the host-core baseline is timed at N=1 only
@@ -509,8 +589,9 @@ def run_reference(args):
     rec = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-           "config": {"workload": "config1 sample on host cores: reference recurrence fwd+bwd (C port of "
-                                  "sore/model/gdn_ref.py), 1 batch row of B8 T4096 H16 d128"},
+           "config": {"workload": "config1 on host cores: reference recurrence fwd+bwd (C port of "
+                                  "sore/model/gdn_ref.py) of B8 T4096 H16 d128 rows, each step a bounded "
+                                  "sample of them (see cpu_baseline.sample)"},
            "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                        "d2h_bytes_per_step": 0}}
     print(json.dumps(rec), flush=True)

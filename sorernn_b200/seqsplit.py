@@ -9,13 +9,13 @@ A segment of tokens is an affine map on the state entering it (gdn_ref.py:18-21 
 
 1. runs the forward of its segment from a zero state (rank 0: from ``h0``): local outputs and ``C_r``;
    ranks r > 0 also compute ``M_r`` (``gdn_segment_transition``);
-2. exclusive scan over ranks: rank 0's outgoing state is ``C_0`` (or ``M_0 h0 + C_0``); rank r receives
-   ``S_in`` from rank r-1 over NCCL (NVLink), forms ``S_out = M_r S_in + C_r`` and sends it to rank r+1;
+2. exclusive scan over ranks: one NCCL all_gather (NVLink) of every rank's map ``(M_r, C_r)``; rank r
+   composes the maps of ranks 0 .. r-1 locally into ``S_in`` (rank 0's ``C_0`` already includes ``h0``);
 3. ranks r > 0 add the incoming state's contribution to their outputs (``gdn_segment_apply_state``:
    the recurrence with v = 0 from ``S_in``), and the last rank's ``S_out`` is the sequence's final state.
 
-Only step 2 crosses GPUs: one ``[N, HV, dk, dv]`` fp32 state per boundary (2 MiB at HV=16, d=128),
-received into this GPU's memory by NCCL before any kernel reads it.
+Only step 2 crosses GPUs: one ``[N, HV, dk, dk]`` map and one ``[N, HV, dk, dv]`` state per rank (2 MiB at
+HV=16, d=128), gathered into this GPU's memory by NCCL before any kernel reads them.
 """
 from __future__ import annotations
 
@@ -75,27 +75,45 @@ def apply_incoming_state(q: Tensor, k: Tensor, g: Tensor, beta: Tensor, S_in: Te
                "gdn_segment_apply_state")
 
 
-def exchange_boundary_states(C: Tensor, M: Optional[Tensor], group=None) -> tuple[Optional[Tensor], Tensor]:
-    """Step 2, the only cross-rank step: the exclusive scan of segment maps along the rank chain.
+def affine_inclusive_scan(M: Tensor, C: Tensor) -> tuple[Tensor, Tensor]:
+    """Inclusive scan of segment maps along dim 0: entry s becomes ``(M_s, C_s) o ... o (M_0, C_0)`` with
+    ``(M2, C2) o (M1, C1) = (M2 M1, M2 C1 + C2)`` (apply map 1, then map 2). Hillis-Steele: ceil(log2 P)
+    rounds, each two batched products over all entries at once, instead of P - 1 dependent steps.
+    The C part of an entry never reads M_0, so M_0 may be a placeholder when only states are wanted."""
+    P = M.shape[0]
+    d = 1
+    while d < P:
+        C = torch.cat([C[:d], torch.matmul(M[d:], C[:-d]) + C[d:]])
+        M = torch.cat([M[:d], torch.matmul(M[d:], M[:-d])])
+        d *= 2
+    return M, C
 
-    Rank r receives ``S_in`` (the state entering its segment) from rank r-1, forms ``S_out = M S_in + C``
-    and sends it to rank r+1; rank 0's ``S_out`` is ``C`` (its forward already started from ``h0``).
-    Returns ``(S_in, S_out)``; ``S_in`` is None on rank 0. ``M`` is read on ranks r > 0 only.
-    Every rank issues its receive before its send, so the chain completes in rank order.
+
+def exchange_boundary_states(C: Tensor, M: Optional[Tensor], group=None) -> tuple[Optional[Tensor], Tensor]:
+    """Step 2, the only cross-rank step: the exclusive scan of segment maps over the ranks.
+
+    One ``all_gather`` brings every rank's map ``(M_r, C_r)`` (2 MiB per rank at HV = 16, d = 128) into
+    this GPU's memory; each rank then composes the maps of the ranks before it locally
+    (``affine_inclusive_scan``, log-depth batched products). There is no dependent chain of transfers:
+    every rank takes the same single collective. Rank 0's ``M`` is not needed (it starts the sequence) and
+    goes as zeros. Returns ``(S_in, S_out)``: the state entering and leaving this rank's segment; ``S_in``
+    is None on rank 0, whose ``S_out`` is ``C``.
     """
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
-    glob = (lambda r: dist.get_global_rank(group, r)) if group is not None else (lambda r: r)
-    S_in = None
-    if rank > 0:
-        S_in = torch.empty_like(C)
-        dist.recv(S_in, src=glob(rank - 1), group=group)
-        S_out = combine(M, C, S_in)
-    else:
-        S_out = C
-    if rank < world - 1:
-        dist.send(S_out.contiguous(), dst=glob(rank + 1), group=group)
-    return S_in, S_out
+    dk = C.shape[-2]
+    if M is None:
+        M = torch.zeros(*C.shape[:-2], dk, dk, dtype=C.dtype, device=C.device)
+    flat = torch.cat([M.reshape(-1), C.to(M.dtype).reshape(-1)])
+    gathered = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
+    dist.all_gather_into_tensor(gathered, flat, group=group)
+    parts = gathered.view(world, -1)
+    Ms = parts[:, :M.numel()].reshape(world, *M.shape)
+    Cs = parts[:, M.numel():].reshape(world, *C.shape)
+    if rank == 0:
+        return None, C
+    _, Cin = affine_inclusive_scan(Ms[:rank + 1], Cs[:rank + 1])
+    return Cin[rank - 1].to(C.dtype), Cin[rank].to(C.dtype)
 
 
 def _local_split(q, k, v, g, beta, scale, l2, P, h0):
@@ -116,14 +134,13 @@ def _local_split(q, k, v, g, beta, scale, l2, P, h0):
     o, C = chunk_gated_delta_rule(qs, ks, vs, gs, bs, scale=scale, initial_state=init, output_final_state=True,
                                   use_qk_l2norm_in_kernel=l2)
     M = segment_transition(ks, gs, bs, l2, HV)  # [P, HV, dk, dk]
-    S_loc = torch.zeros(P, HV, dk, dv, dtype=torch.float32, device=q.device)
-    Mpre = torch.empty(P, HV, dk, dk, dtype=torch.float32, device=q.device)
-    Mpre[0] = torch.eye(dk, device=q.device)
-    for s_ in range(1, P):  # the exclusive scan over sub-segments (P - 1 batched 128 x 128 products)
-        S_loc[s_] = C[0] if s_ == 1 else combine(M[s_ - 1], C[s_ - 1], S_loc[s_ - 1])
-        Mpre[s_] = torch.matmul(M[s_ - 1], Mpre[s_ - 1])
-    M_rank = torch.matmul(M[P - 1], Mpre[P - 1])
-    C_rank = C[0] if P == 1 else combine(M[P - 1], C[P - 1], S_loc[P - 1])
+    # prefix of the piece maps (log-depth batched products): piece s's incoming state from a zero rank input,
+    # and the map from the rank's input to piece s's input
+    Mi, Ci = affine_inclusive_scan(M, C)
+    S_loc = torch.cat([torch.zeros_like(C[:1]), Ci[:-1]])
+    eye = torch.eye(dk, dtype=M.dtype, device=q.device).expand(1, HV, dk, dk)
+    Mpre = torch.cat([eye, Mi[:-1]])
+    M_rank, C_rank = Mi[P - 1], Ci[P - 1]
     return qs, ks, gs, bs, o, S_loc, Mpre, M_rank.unsqueeze(0), C_rank.unsqueeze(0)
 
 

@@ -1,5 +1,6 @@
-"""Sequence-split prefill across ranks, host side: the boundary-state chain of
-``sorernn_b200.seqsplit.exchange_boundary_states`` run over ``gloo`` ranks on CPU.
+"""Sequence-split prefill across ranks, host side: the boundary-state exchange of
+``sorernn_b200.seqsplit.exchange_boundary_states`` (one all_gather of the segment maps, composed locally)
+run over ``gloo`` ranks on CPU.
 
 Each rank computes its segment's pieces with the oracle (the reference recurrence, gdn_ref.py:18-21):
 outputs and final state ``C_r`` from a zero state (rank 0 from ``h0``), the transition ``M_r`` (the same
@@ -83,7 +84,8 @@ def test_boundary_state_chain_matches_unsplit_oracle(splits, l2):
 
 
 def _lost_sender_worker(rank: int, world: int, port: int, result):
-    """Rank 0 leaves without sending; rank 1's receive must end with an error inside the group timeout."""
+    """Rank 0 leaves without joining the exchange; rank 1's all_gather must end with an error inside the
+    group timeout."""
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
@@ -92,13 +94,13 @@ def _lost_sender_worker(rank: int, world: int, port: int, result):
     C = torch.zeros(1, 1, 4, 4, dtype=torch.float64)
     M = torch.eye(4, dtype=torch.float64).reshape(1, 1, 4, 4)
     if rank == 0:
-        result[0] = 1  # left without sending
+        result[0] = 1  # left without joining the collective
         return
     try:
         seqsplit.exchange_boundary_states(C, M)
-        result[1] = 2  # received (must not happen)
+        result[1] = 2  # completed (must not happen)
     except RuntimeError:
-        result[1] = 1  # the receive ended with an error
+        result[1] = 1  # the collective ended with an error
 
 
 def test_lost_sender_ends_the_receive_with_an_error():
@@ -115,3 +117,19 @@ def test_lost_sender_ends_the_receive_with_an_error():
         p.kill()
     assert not alive, "a rank did not finish within 60 s"
     assert list(result) == [1, 1]
+
+
+def test_affine_scan_matches_sequential_composition():
+    from sorernn_b200.seqsplit import affine_inclusive_scan
+
+    g = torch.Generator().manual_seed(3)
+    for P in (1, 2, 3, 5, 8):
+        M = torch.randn(P, 2, 6, 6, generator=g, dtype=torch.float64) * 0.4
+        C = torch.randn(P, 2, 6, 5, generator=g, dtype=torch.float64)
+        Mi, Ci = affine_inclusive_scan(M, C)
+        m, c = M[0], C[0]
+        for s in range(P):
+            if s:
+                m, c = M[s] @ m, M[s] @ c + C[s]
+            torch.testing.assert_close(Mi[s], m, rtol=1e-12, atol=1e-12)
+            torch.testing.assert_close(Ci[s], c, rtol=1e-12, atol=1e-12)
