@@ -89,7 +89,10 @@ def gdn_fwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, initial_st
     o = torch.empty_like(v)
     final = torch.empty(p.N, p.HV, p.DK, p.DV, dtype=torch.float32, device=q.device)
     n_ck = L.gdn_checkpoint_count(ctypes.byref(p))
-    ck = torch.empty(max(n_ck, 0), p.HV, p.DK, p.DV, dtype=torch.float32, device=q.device)
+    # with cu_seqlens the count is an upper bound: the slots no sequence fills are zeros, so the output is
+    # deterministic (the same in eager mode and under tracing)
+    alloc = torch.zeros if cu_seqlens is not None else torch.empty
+    ck = alloc(max(n_ck, 0), p.HV, p.DK, p.DV, dtype=torch.float32, device=q.device)
     ws_bytes = L.gdn_chunk_fwd_workspace_size(ctypes.byref(p))
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
     h0 = None if initial_state is None else initial_state.float().contiguous()
