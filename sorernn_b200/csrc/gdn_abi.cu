@@ -114,7 +114,8 @@ int64_t gdn_checkpoint_count(const gdn_problem* p) {
 
 size_t gdn_chunk_fwd_workspace_size(const gdn_problem* p) {
     if (check_problem(p) != GDN_OK) return 0;
-    return kErrBytes;
+    if (!gdn_uses_chunk_kernels(p)) return kErrBytes;
+    return kErrBytes + chunk_fwd_split_workspace(p->B, p->T, p->N, p->HV, p->cu_seqlens != nullptr);
 }
 
 size_t gdn_chunk_bwd_workspace_size(const gdn_problem* p) {
@@ -145,6 +146,16 @@ int gdn_chunk_fwd(const gdn_problem* p, const void* q, const void* k, const void
     L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.o = o;
     L.h0 = initial_state;
     L.ht = final_state;
+    if (gdn_uses_chunk_kernels(p)) {  // chunk-parallel prep + per-(sequence, head) state pass
+        ChunkLaunch C{};
+        C.q = q; C.k = k; C.v = v; C.g = g; C.beta = beta; C.o = o;
+        C.h0 = initial_state; C.ht = final_state; C.ckpt = checkpoints; C.cu = p->cu_seqlens;
+        C.err = (int*)workspace;
+        C.B = p->B; C.T = p->T; C.N = p->N; C.H = p->H; C.HV = p->HV; C.max_seqlen = max_len(p);
+        C.scale = p->scale; C.g_dtype = p->g_dtype; C.beta_dtype = p->beta_dtype; C.l2norm = p->use_qk_l2norm;
+        C.ckpt_every = p->ckpt_every;
+        return chunk_fwd_split(C, (char*)workspace + kErrBytes, s);
+    }
     return dispatch_forward(p, L, checkpoints, workspace, s);
 }
 

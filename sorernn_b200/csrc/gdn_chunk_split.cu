@@ -1,0 +1,737 @@
+// Chunked gated-delta-rule forward split in two launches on sm_100a: a chunk-parallel prep pass and a lean
+// per-(sequence, head) state pass.
+//
+// Notation (the algebra of tests/test_chunk_algebra.py, the same as gdn_chunk_fwd.cu): Gamma = in-chunk
+// cumsum of g, E_ij = exp(Gamma_i - Gamma_j), nq_i, nk_j the inverse L2 norms of the raw q/k rows (1 without
+// the norm, 0 on rows past the sequence end), S0 the state at the chunk start.
+//   A  = strict_lower(diag(beta) (K K^T . nk nk^T) . E)       T = (I + A)^-1
+//   W  = T diag(beta e^Gamma nk) K      U = T diag(beta) V      Delta = U - W S0
+//   O_i = f1_i (Q S0)_i + f2_i (P Delta)_i,   f1 = scale e^Gamma nq,  f2 = nq,
+//         P_ij = scale (q_i . k_j) nk_j E_ij  (j <= i)
+//   S1 = e^Gamma_C S0 + K^T diag(e^(Gamma_C - Gamma) nk) Delta
+// Everything except Delta, O and S1 is independent of the state, so it is computed for all (chunk, head)
+// pairs at once by chunk_prep_kernel (8,192 CTAs at B8 T4096 H16, three per SM) and handed to the state pass
+// as one record per (chunk, head) in the workspace: the bf16 operand tiles -W, TV = T diag(beta), P (hi and
+// lo parts) as shared-memory images in the 128-byte-swizzled layout, and the vectors the state pass needs.
+// chunk_state_kernel then runs one CTA per (sequence, value head) that keeps S^T (fp32) in tensor memory and
+// per chunk only forms the S0 operand, Delta and Dd = diag(e^(Gamma_C - Gamma) nk) Delta, and the outputs:
+//   G1:  D = [Z; TV] V + [Q; -W] (S0hi + S0lo)    (M = 128: rows 0-63 Q S0, rows 64-127 U - W S0 = Delta)
+//   G2:  S^T += Dd^T K (hi + lo)                   E = P Delta  (rows 0-63; P and Delta in hi + lo parts)
+// The output step of chunk c-1 (rows 0-63 of D and E, on warps 0-7 of lanes 0-63) runs while warps of lanes
+// 64-127 turn chunk c's Delta into operand tiles, and the E products of chunk c execute on the tensor core
+// while chunk c+1 reads the state out. The raw bf16 q, k, v tiles feed the tensor cores unmodified.
+#include <cstring>
+
+#include "chunk_common.cuh"
+#include "common.cuh"
+#include "kernels.h"
+#include "launch.h"
+#include "sm100.cuh"
+#include "tmap.h"
+
+namespace gdn {
+using namespace sm100;
+
+namespace split {
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint4 pack8(const float* v) {
+    return make_uint4(pack2(v[0], v[1]), pack2(v[2], v[3]), pack2(v[4], v[5]), pack2(v[6], v[7]));
+}
+// hi = bf16(v), lo = bf16(v - hi): the pair carries ~16 significant bits
+__device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
+    float h[8], l[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        h[e] = __bfloat162float(__float2bfloat16_rn(v[e]));
+        l[e] = v[e] - h[e];
+    }
+    hi = pack8(h);
+    lo = pack8(l);
+}
+__device__ __forceinline__ void sync_tc() {
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+}
+// bounded waits (see gdn_chunk_fwd.cu): after a timeout every later wait polls once and the CTA runs out
+__device__ __forceinline__ void wait_bar(uint64_t* bar, uint32_t parity, int* err, int code, bool& ok) {
+    ok = mbar_wait(bar, parity, err, code, ok ? (1u << 22) : 1u) && ok;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"((uint64_t)src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+template <int N>
+__device__ __forceinline__ void vload(const float* v, int base, float (&o)[N]) {
+    const float4* p = reinterpret_cast<const float4*>(v + base);
+#pragma unroll
+    for (int q = 0; q < N / 4; ++q) {
+        const float4 x = p[q];
+        o[4 * q] = x.x;
+        o[4 * q + 1] = x.y;
+        o[4 * q + 2] = x.z;
+        o[4 * q + 3] = x.w;
+    }
+}
+
+}  // namespace split
+
+// ================================================================================================
+// chunk_prep_kernel: one CTA (256 threads) per (chunk, sequence, value head)
+// ================================================================================================
+namespace cp {
+constexpr int NTHR = 256;
+constexpr uint32_t OFF_QK = 0;       // per d-block kb (16 KB apart): [Q 8 KB | K 8 KB], 64 rows x 128 B
+constexpr uint32_t OFF_A = 32768;    // fp32 A / T, 64 x AST
+constexpr int AST = 68;
+constexpr uint32_t OFF_Y = OFF_A + 64 * AST * 4;       // solve scratch
+constexpr uint32_t OFF_TB = 55296;                     // TB bf16 [i][j] 8 KB, then TV: [TB; TV] is MMA2's A
+constexpr uint32_t OFF_VEC = OFF_TB + 16384;           // G, EG, B, NQ, NK: 5 x 64 fp32
+constexpr uint32_t OFF_BAR = OFF_VEC + 5 * 256;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 64 + 1024;   // three CTAs per SM
+constexpr uint32_t T_COLS = 128;                       // D1 in columns 0-63, then W in 0-127
+static_assert(OFF_Y + 32 * kSolveYStride * 4 <= OFF_TB, "solve scratch overlaps TB");
+}  // namespace cp
+
+struct ChunkPrepArgs {
+    CUtensorMap tq, tk;
+    const void* g;
+    const void* beta;
+    const int64_t* cu;
+    const int64_t* cbase;  // varlen: first flattened chunk of each sequence (NULL: n * ceil(T / 64))
+    uint8_t* rec;          // kFwdRecordBytes per (flattened chunk, value head)
+    int* err;
+    int64_t T;
+    int H, HV, g_dtype, beta_dtype, l2norm;
+    float scale;
+};
+
+__global__ void __launch_bounds__(cp::NTHR, 3) chunk_prep_kernel(const __grid_constant__ ChunkPrepArgs a) {
+    using namespace cp;
+    using namespace split;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    float* Am = (float*)(sm + OFF_A);
+    float* Yb = (float*)(sm + OFF_Y);
+    float* vG = (float*)(sm + OFF_VEC);
+    float* vEG = vG + 64;
+    float* vB = vG + 128;
+    float* vNQ = vG + 192;
+    float* vNK = vG + 256;
+    uint64_t* bar_in = (uint64_t*)(sm + OFF_BAR);
+    uint64_t* bar_mma = bar_in + 1;
+    uint32_t* tmem_slot = (uint32_t*)(bar_in + 2);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int lg = warp & 3, hf = warp >> 2;  // TMEM lane quadrant, column half
+    const int row = 32 * lg + lane;
+    const int c = blockIdx.x;
+    const int n = blockIdx.y / a.HV, hv = blockIdx.y % a.HV, hq = hv / (a.HV / a.H);
+    int64_t bos, eos;
+    seq_bounds(a.cu, a.T, n, bos, eos);
+    const int64_t len = eos - bos;
+    if (64 * (int64_t)c >= len) return;
+    const int nv = (len - 64 * (int64_t)c) < 64 ? (int)(len - 64 * (int64_t)c) : 64;
+    const int64_t tok0 = bos + 64 * (int64_t)c;
+    const int64_t cb = a.cbase ? a.cbase[n] : (int64_t)n * ((a.T + 63) / 64);
+    uint8_t* rec = a.rec + ((cb + c) * a.HV + hv) * kFwdRecordBytes;
+
+    if (tid == 0) {
+        mbar_init(bar_in, 1);
+        mbar_init(bar_mma, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) tmem_alloc(tmem_slot, T_COLS);
+    sync_tc();
+    const uint32_t tm = *tmem_slot;
+    const uint32_t lb = (uint32_t)(32 * lg) << 16;
+    const uint32_t sb = smem_u32(sm);
+    bool ok = true;
+    if (tid == 0) {
+        mbar_arrive_expect_tx(bar_in, 4 * 8192);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+            tma_load_3d(sm + OFF_QK + kb * 16384, &a.tq, bar_in, kb * 64, hq, (int)tok0);
+            tma_load_3d(sm + OFF_QK + kb * 16384 + 8192, &a.tk, bar_in, kb * 64, hq, (int)tok0);
+        }
+    }
+    // gates: Gamma = inclusive cumsum of g in the chunk; rows past the sequence end carry g = 0, beta = 0
+    if (tid < 64) {
+        float x = 0.f, bt = 0.f;
+        if (tid < nv) {
+            const int64_t gi = (tok0 + tid) * a.HV + hv;
+            x = gate_f(ld_gate_raw(a.g, a.g_dtype, gi), a.g_dtype);
+            bt = gate_f(ld_gate_raw(a.beta, a.beta_dtype, gi), a.beta_dtype);
+        }
+        vB[tid] = bt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        vG[tid] = x;
+    }
+    wait_bar(bar_in, 0, a.err, 41, ok);
+    // MMA1: D1 = [Q; K] K^T on the raw tiles (M = 128, N = 64, K = 128)
+    if (tid == 0) {
+        tc_fence_after();
+        const uint32_t id = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+            umma_bf16(tm, desc_kmajor(sb + OFF_QK + kb * 16384 + ko), desc_kmajor(sb + OFF_QK + kb * 16384 + 8192 + ko),
+                      id, ks > 0);
+        }
+        umma_commit(bar_mma);
+    }
+    __syncthreads();
+    if (tid >= 32 && tid < 64) vG[tid] += vG[31];
+    {  // inverse row norms: 2 threads per row (one d-block each); rows 0-63 q, 64-127 k
+        const int r = tid >> 1, kb = tid & 1, i = r & 63;
+        const uint8_t* rowp = sm + OFF_QK + kb * 16384 + (r < 64 ? 0 : 8192) + i * 128;
+        float ss = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((cc + 4 * kb) & 7) * 16);
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __bfloat1622float2(h[e]);
+                ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+            }
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        float inv = a.l2norm ? 1.f / fmaxf(sqrtf(ss), kL2Eps) : 1.f;
+        if (i >= nv) inv = 0.f;
+        if (kb == 0) (r < 64 ? vNQ : vNK)[i] = inv;
+    }
+    __syncthreads();
+    if (tid < 64) {  // record vectors: vX = e^(G_C - G) nk, f1 = scale e^G nq, f2 = nq, e^G_C
+        const float eg = __expf(vG[tid]);
+        vEG[tid] = eg;
+        float* rv = (float*)(rec + kFwdRecVec);
+        rv[tid] = __expf(vG[63] - vG[tid]) * vNK[tid];
+        rv[64 + tid] = a.scale * eg * vNQ[tid];
+        rv[128 + tid] = vNQ[tid];
+        if (tid == 0) rv[192] = __expf(vG[63]);
+    }
+    __syncthreads();
+    wait_bar(bar_mma, 0, a.err, 42, ok);
+    tc_fence_after();
+    // D1 rows 0-63 -> P hi/lo (straight to the record), rows 64-127 -> A (fp32, shared memory)
+    {
+        float v[32];
+        tmem_ld16(tm + lb + 32 * hf, *reinterpret_cast<float(*)[16]>(v));
+        tmem_ld16(tm + lb + 32 * hf + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+        tmem_wait_ld();
+        const int i = row & 63;
+        const float gi = vG[i];
+        if (lg < 2) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int jj = 32 * hf + j;
+                v[j] = (jj <= i) ? a.scale * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint4 hi, lo;
+                split8(v + 8 * q, hi, lo);
+                const uint32_t off = sw128_off(i, 32 * hf + 8 * q);
+                *reinterpret_cast<uint4*>(rec + kFwdRecP + off) = hi;
+                *reinterpret_cast<uint4*>(rec + kFwdRecP + 8192 + off) = lo;
+            }
+        } else {
+            const float bi = vB[i] * vNK[i];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int jj = 32 * hf + j;
+                v[j] = (jj < i) ? bi * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
+            }
+            float4* dst = reinterpret_cast<float4*>(Am + i * AST + 32 * hf);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+    }
+    sync_tc();
+    // T = (I + A)^-1 in place (all 8 warps)
+    tri_inverse64<AST>(Am, Yb);
+    __syncthreads();
+    // TB = T diag(beta e^G nk), TV = T diag(beta): bf16 K-major [i][j] tiles in shared memory (MMA2's A);
+    // TV also to the record
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+        const int wl = tid & 31, qq = wl >> 3, sub = wl & 7;
+        const int i = 32 * it + 4 * warp + 2 * (qq & 1) + (sub >> 2), c8 = 8 * ((sub & 3) + 4 * (qq >> 1));
+        const float4 t0 = *reinterpret_cast<const float4*>(Am + i * AST + c8);
+        const float4 t1 = *reinterpret_cast<const float4*>(Am + i * AST + c8 + 4);
+        const float t[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+        float b8[8], e8[8], n8[8], tb[8], tv[8];
+        vload(vB, c8, b8);
+        vload(vEG, c8, e8);
+        vload(vNK, c8, n8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            tv[j] = t[j] * b8[j];
+            tb[j] = tv[j] * e8[j] * n8[j];
+        }
+        const uint32_t off = sw128_off(i, c8);
+        const uint4 uv = pack8(tv);
+        *reinterpret_cast<uint4*>(sm + OFF_TB + off) = pack8(tb);
+        *reinterpret_cast<uint4*>(sm + OFF_TB + 8192 + off) = uv;
+        *reinterpret_cast<uint4*>(rec + kFwdRecTV + off) = uv;
+    }
+    fence_async_smem();
+    sync_tc();
+    // MMA2: [W; TV K] = [TB; TV] K  (M = 128, N = 128 = dk, K = 64 tokens); W rows on lanes 0-63
+    if (tid == 0) {
+        const uint32_t id = idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+            umma_bf16(tm, desc_kmajor(sb + OFF_TB + ks * 32), desc_mnmajor(sb + OFF_QK + 8192 + ks * 2048, 16384), id,
+                      ks > 0);
+        umma_commit(bar_mma);
+    }
+    wait_bar(bar_mma, 1, a.err, 43, ok);
+    tc_fence_after();
+    // -W (bf16, K-major [i][dk]) to the record: warps of lanes 0-63, 64 columns each
+    if (lg < 2) {
+        uint8_t* dst = rec + kFwdRecW + hf * 8192;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // two halves of 32 columns (the register cap of three CTAs per SM)
+            float v[32];
+            tmem_ld16(tm + lb + 64 * hf + 32 * h, *reinterpret_cast<float(*)[16]>(v));
+            tmem_ld16(tm + lb + 64 * hf + 32 * h + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = -v[e];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                *reinterpret_cast<uint4*>(dst + sw128_off(row, 32 * h + 8 * q)) = pack8(v + 8 * q);
+        }
+    }
+    sync_tc();
+    if (warp == 0) tmem_dealloc(tm, T_COLS);
+}
+
+// ================================================================================================
+// chunk_state_kernel: one CTA (512 threads) per (sequence, value head), chunks in order
+// ================================================================================================
+namespace cs {
+constexpr int NTHR = 512;
+constexpr uint32_t OFF_QW = 0;         // per d-block kb (16 KB apart): [Q 8 KB | -W 8 KB] = MMA G1's A
+constexpr uint32_t OFF_PH = 32768;     // P hi [i][j]; [P hi; P lo] and [P lo; Z] are G2's 128-row A operands
+constexpr uint32_t OFF_PL = 40960;
+constexpr uint32_t OFF_Z = 49152;      // zeros: [Z; TV] puts U on rows 64-127 and zeros on 0-63
+constexpr uint32_t OFF_TV = 57344;
+constexpr uint32_t OFF_V = 65536;      // V [token][dv], 2 x 8 KB
+constexpr uint32_t OFF_K = 81920;      // K [token][dk], 2 x 8 KB
+constexpr uint32_t OFF_S0 = 98304;     // S0^T hi bf16 [dv][dk], 2 dk-blocks x 16 KB
+constexpr uint32_t OFF_S0L = 131072;   // S0^T lo
+constexpr uint32_t OFF_DH = 163840;    // Delta hi [token][dv], 2 x 8 KB
+constexpr uint32_t OFF_DL = 180224;    // Delta lo
+constexpr uint32_t OFF_DDH = 196608;   // Dd hi
+constexpr uint32_t OFF_DDL = 212992;   // Dd lo
+constexpr uint32_t OFF_VEC = 229376;   // record vectors, two buffers of kFwdRecVecBytes
+constexpr uint32_t OFF_BAR = OFF_VEC + 2 * kFwdRecVecBytes;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 128 + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+// TMEM columns: S^T, the two D buffers (G1 output, M = 128), E (P Delta, rows 0-63)
+constexpr uint32_t T_S = 0, T_D = 128, T_E = 384, T_COLS = 512;
+constexpr uint32_t TX_L1 = 2 * 8192 + 2 * 8192 + 8192 + 2 * 8192 + kFwdRecVecBytes;  // Q, -W, TV, V, vectors
+}  // namespace cs
+
+struct ChunkStateArgs {
+    CUtensorMap tq, tk, tv;
+    const uint8_t* rec;
+    const int64_t* cbase;
+    void* o;
+    const float* h0;
+    float* ht;
+    float* ckpt;
+    const int64_t* cu;
+    int* err;
+    int64_t T;
+    int HV, H, ckpt_every;
+};
+
+__global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_constant__ ChunkStateArgs a) {
+    using namespace cs;
+    using namespace split;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bar = (uint64_t*)(sm + OFF_BAR);
+    uint64_t* bar_l1 = bar;      // Q, -W, TV, V, vectors of a chunk
+    uint64_t* bar_l2 = bar + 1;  // K
+    uint64_t* bar_l3 = bar + 2;  // P hi/lo
+    uint64_t* bar_g = bar + 3;   // G1 done
+    uint64_t* bar_s = bar + 4;   // state update done
+    uint64_t* bar_o = bar + 5;   // E products done
+    uint32_t* tmem_slot = (uint32_t*)(bar + 6);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int lg = warp & 3, cq = warp >> 2;
+    const int row = 32 * lg + lane;
+    const int n = blockIdx.x / a.HV, hv = blockIdx.x % a.HV, hq = hv / (a.HV / a.H);
+    int64_t bos, eos;
+    seq_bounds(a.cu, a.T, n, bos, eos);
+    const int64_t len = eos - bos;
+    const int nchunks = (int)((len + 63) / 64);
+    const int64_t cb = a.cbase ? a.cbase[n] : (int64_t)n * ((a.T + 63) / 64);
+
+    // checkpoint slot of this sequence's first checkpoint
+    int64_t ck_base = 0;
+    if (a.ckpt) {
+        const int K = a.ckpt_every;
+        if (!a.cu) {
+            ck_base = (int64_t)n * (((a.T + 63) / 64 + K - 1) / K);
+        } else {
+            int64_t part = 0;
+            for (int m = tid; m < n; m += NTHR) part += (((a.cu[m + 1] - a.cu[m] + 63) / 64) + K - 1) / K;
+            for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+            int64_t* red = (int64_t*)(sm + OFF_DH);
+            if (lane == 0) red[warp] = part;
+            __syncthreads();
+            for (int w = 0; w < NTHR / 32; ++w) ck_base += red[w];
+            __syncthreads();
+        }
+    }
+
+    if (tid == 0) {
+        for (int i = 0; i < 6; ++i) mbar_init(&bar[i], 1);
+        fence_barrier_init();
+        prefetch_tmap(&a.tq);
+        prefetch_tmap(&a.tk);
+        prefetch_tmap(&a.tv);
+    }
+    if (warp == 0) tmem_alloc(tmem_slot, T_COLS);
+    for (int e = tid; e < 8192 / 16; e += NTHR) ((uint4*)(sm + OFF_Z))[e] = make_uint4(0, 0, 0, 0);
+    fence_async_smem();
+    sync_tc();
+    const uint32_t tm = *tmem_slot;
+    const uint32_t tS = tm + T_S, tE = tm + T_E;
+    const uint32_t lb = (uint32_t)(32 * lg) << 16;
+    const uint32_t sb = smem_u32(sm);
+    bool ok = true;
+
+    // initial state -> TMEM: thread (row = dv, quarter cq) holds S^T[dv][dk] for dk in [32 cq, 32 cq + 32)
+    {
+        const float* h0 = a.h0 ? a.h0 + ((int64_t)n * a.HV + hv) * 16384 : nullptr;
+#pragma unroll
+        for (int c0 = 0; c0 < 32; c0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = h0 ? h0[(32 * cq + c0 + i) * 128 + row] : 0.f;
+            tmem_st16(tS + lb + 32 * cq + c0, v);
+        }
+        tmem_wait_st();
+    }
+
+    auto recp = [&](int c) { return a.rec + ((cb + c) * a.HV + hv) * kFwdRecordBytes; };
+    auto issue_l1 = [&](int c) {  // Q, -W, TV, V, vectors of chunk c
+        const int tok0 = (int)(bos + 64 * c);
+        const uint8_t* r = recp(c);
+        mbar_arrive_expect_tx(bar_l1, TX_L1);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+            tma_load_3d(sm + OFF_QW + kb * 16384, &a.tq, bar_l1, kb * 64, hq, tok0);
+            bulk_g2s(sm + OFF_QW + kb * 16384 + 8192, r + kFwdRecW + kb * 8192, 8192, bar_l1);
+            tma_load_3d(sm + OFF_V + kb * 8192, &a.tv, bar_l1, kb * 64, hv, tok0);
+        }
+        bulk_g2s(sm + OFF_TV, r + kFwdRecTV, 8192, bar_l1);
+        bulk_g2s(sm + OFF_VEC + (c & 1) * kFwdRecVecBytes, r + kFwdRecVec, kFwdRecVecBytes, bar_l1);
+    };
+    auto issue_l2 = [&](int c) {  // K of chunk c
+        const int tok0 = (int)(bos + 64 * c);
+        mbar_arrive_expect_tx(bar_l2, 2 * 8192);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) tma_load_3d(sm + OFF_K + kb * 8192, &a.tk, bar_l2, kb * 64, hq, tok0);
+    };
+    auto issue_l3 = [&](int c) {  // P hi | lo of chunk c (contiguous in the record and here)
+        mbar_arrive_expect_tx(bar_l3, 16384);
+        bulk_g2s(sm + OFF_PH, recp(c) + kFwdRecP, 16384, bar_l3);
+    };
+    // output step of chunk c (warps of lanes 0-63): O = f1 (Q S0) + f2 (P Delta) -> o[token][hv][dv]
+    auto output_step = [&](int c) {
+        const int i = row;
+        const float* vec = (const float*)(sm + OFF_VEC + (c & 1) * kFwdRecVecBytes);
+        const float f1 = vec[64 + i], f2 = vec[128 + i];
+        const int nv = (len - 64 * (int64_t)c) < 64 ? (int)(len - 64 * (int64_t)c) : 64;
+        float v1[32], v2[32];
+        const uint32_t tD = tm + T_D + (uint32_t)(c & 1) * 128;
+        tmem_ld16(tD + lb + 32 * cq, *reinterpret_cast<float(*)[16]>(v1));
+        tmem_ld16(tD + lb + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v1 + 16));
+        tmem_ld16(tE + lb + 32 * cq, *reinterpret_cast<float(*)[16]>(v2));
+        tmem_ld16(tE + lb + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v2 + 16));
+        tmem_wait_ld();
+        if (i < nv) {
+            uint4* dst = reinterpret_cast<uint4*>((__nv_bfloat16*)a.o + ((bos + 64 * (int64_t)c + i) * a.HV + hv) * 128 +
+                                                  32 * cq);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float y[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[e] = fmaf(f1, v1[8 * q + e], f2 * v2[8 * q + e]);
+                dst[q] = pack8(y);
+            }
+        }
+    };
+
+    if (tid == 0 && nchunks > 0) {
+        issue_l1(0);
+        issue_l2(0);
+        issue_l3(0);
+    }
+
+    for (int c = 0; c < nchunks; ++c) {
+        const uint32_t par = (uint32_t)c & 1u;
+        const uint32_t tD = tm + T_D + par * 128;
+        const float* vec = (const float*)(sm + OFF_VEC + par * kFwdRecVecBytes);
+        // A. this chunk's Q, -W, TV, V and vectors; U = TV V into D (rows 64-127), zeros into rows 0-63
+        wait_bar(bar_l1, par, a.err, 51, ok);
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t id = idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+                umma_bf16(tD, desc_kmajor(sb + OFF_Z + ks * 32), desc_mnmajor(sb + OFF_V + ks * 2048, 8192), id, ks > 0);
+        }
+        // B. the previous chunk's state update has landed: K of this chunk may overwrite the K tile; read S out
+        if (c > 0) {
+            wait_bar(bar_s, par ^ 1u, a.err, 52, ok);
+            tc_fence_after();
+        }
+        if (tid == 0 && c > 0) issue_l2(c);
+        {
+            const float eGC = vec[192];
+            const bool ck = a.ckpt && (c % a.ckpt_every == 0);
+            float* ckp = ck ? a.ckpt + ((ck_base + c / a.ckpt_every) * a.HV + hv) * 16384 : nullptr;
+            float v[32];
+            tmem_ld16(tS + lb + 32 * cq, *reinterpret_cast<float(*)[16]>(v));
+            tmem_ld16(tS + lb + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+            tmem_wait_ld();
+            if (ck) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) ckp[(32 * cq + i) * 128 + row] = v[i];
+            }
+            const uint32_t blk = (uint32_t)(cq >> 1) * 16384;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint4 hi, lo;
+                split8(v + 8 * q, hi, lo);
+                const uint32_t off = blk + sw128_off(row, 32 * (cq & 1) + 8 * q);
+                *reinterpret_cast<uint4*>(sm + OFF_S0 + off) = hi;
+                *reinterpret_cast<uint4*>(sm + OFF_S0L + off) = lo;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= eGC;
+            tmem_st16(tS + lb + 32 * cq, *reinterpret_cast<float(*)[16]>(v));
+            tmem_st16(tS + lb + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+            tmem_wait_st();
+        }
+        fence_async_smem();
+        sync_tc();
+        // C. G1: D += [Q; -W] (S0hi + S0lo)  (K = dk = 128); then P of this chunk may replace the previous one
+        if (tid == 0) {
+            const uint32_t id = idesc_bf16(128, 128, 0, 0);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t s0 = sb + (h ? OFF_S0L : OFF_S0);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                    umma_bf16(tD, desc_kmajor(sb + OFF_QW + kb * 16384 + ko), desc_kmajor(s0 + kb * 16384 + ko), id, 1);
+                }
+            }
+            umma_commit(bar_g);
+            if (c > 0) {
+                wait_bar(bar_o, par ^ 1u, a.err, 53, ok);
+                issue_l3(c);
+            }
+        }
+        // D. Delta (lanes 64-127) -> Delta and Dd tiles; meanwhile lanes 0-63 emit the previous chunk's outputs
+        wait_bar(bar_g, par, a.err, 54, ok);
+        tc_fence_after();
+        if (lg >= 2) {
+            const int j = row - 64;
+            const float x = vec[j];  // e^(G_C - G_j) nk_j
+            float v[32];
+            tmem_ld16(tD + lb + 32 * cq, *reinterpret_cast<float(*)[16]>(v));
+            tmem_ld16(tD + lb + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+            tmem_wait_ld();
+            const uint32_t blk = (uint32_t)(cq >> 1) * 8192;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float d[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) d[e] = v[8 * q + e] * x;
+                uint4 hi, lo, dhi, dlo;
+                split8(v + 8 * q, hi, lo);
+                split8(d, dhi, dlo);
+                const uint32_t off = blk + sw128_off(j, 32 * (cq & 1) + 8 * q);
+                *reinterpret_cast<uint4*>(sm + OFF_DH + off) = hi;
+                *reinterpret_cast<uint4*>(sm + OFF_DL + off) = lo;
+                *reinterpret_cast<uint4*>(sm + OFF_DDH + off) = dhi;
+                *reinterpret_cast<uint4*>(sm + OFF_DDL + off) = dlo;
+            }
+        } else if (c > 0) {
+            output_step(c - 1);
+        }
+        fence_async_smem();
+        sync_tc();
+        // E. G2: S^T += Dd^T K (hi + lo) -> bar_s; E = P Delta (hi.hi + lo.hi + hi.lo) -> bar_o; next loads
+        if (tid == 0) {
+            wait_bar(bar_l2, par, a.err, 55, ok);
+            wait_bar(bar_l3, par, a.err, 56, ok);
+            tc_fence_after();
+            const uint32_t idS = idesc_bf16(128, 128, 1, 1), idE = idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t dd = sb + (h ? OFF_DDL : OFF_DDH);
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks)
+                    umma_bf16(tS, desc_mnmajor(dd + ks * 2048, 8192), desc_mnmajor(sb + OFF_K + ks * 2048, 8192), idS, 1);
+            }
+            umma_commit(bar_s);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                const uint64_t dh = desc_mnmajor(sb + OFF_DH + ks * 2048, 8192);
+                const uint64_t dl = desc_mnmajor(sb + OFF_DL + ks * 2048, 8192);
+                umma_bf16(tE, desc_kmajor(sb + OFF_PH + ks * 32), dh, idE, ks > 0);
+                umma_bf16(tE, desc_kmajor(sb + OFF_PL + ks * 32), dh, idE, 1);
+                umma_bf16(tE, desc_kmajor(sb + OFF_PH + ks * 32), dl, idE, 1);
+            }
+            umma_commit(bar_o);
+            if (c + 1 < nchunks) issue_l1(c + 1);  // G1 has read Q, -W, TV, V; the other vector buffer is free
+        }
+    }
+    // the last chunk's outputs and the final state
+    if (nchunks > 0) {
+        const uint32_t par = (uint32_t)(nchunks - 1) & 1u;
+        wait_bar(bar_o, par, a.err, 57, ok);
+        wait_bar(bar_s, par, a.err, 58, ok);
+        tc_fence_after();
+        if (lg < 2) output_step(nchunks - 1);
+    }
+    if (ok && a.ht) {
+        float* ht = a.ht + ((int64_t)n * a.HV + hv) * 16384;
+        float v[32];
+        tmem_ld16(tS + lb + 32 * cq, *reinterpret_cast<float(*)[16]>(v));
+        tmem_ld16(tS + lb + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ht[(32 * cq + i) * 128 + row] = v[i];
+    }
+    sync_tc();
+    if (warp == 0) tmem_dealloc(tm, T_COLS);
+}
+
+// First flattened chunk of every sequence: exclusive scan of ceil(len_n / 64) over cu_seqlens (one CTA).
+__global__ void __launch_bounds__(1024) chunk_base_kernel(const int64_t* __restrict__ cu, int64_t N,
+                                                          int64_t* __restrict__ cbase) {
+    __shared__ int64_t wsum[32];
+    __shared__ int64_t carry;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) carry = 0;
+    __syncthreads();
+    for (int64_t base = 0; base < N; base += 1024) {
+        const int64_t n = base + tid;
+        const int64_t x = n < N ? (cu[n + 1] - cu[n] + 63) / 64 : 0;
+        int64_t s = x;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int64_t y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        if (lane == 31) wsum[warp] = s;
+        __syncthreads();
+        if (warp == 0) {
+            int64_t w = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += y;
+            }
+            wsum[lane] = w;
+        }
+        __syncthreads();
+        const int64_t incl = s + (warp > 0 ? wsum[warp - 1] : 0) + carry;
+        if (n < N) cbase[n] = incl - x;
+        __syncthreads();
+        if (tid == 1023) carry = incl;
+        __syncthreads();
+    }
+}
+
+size_t chunk_fwd_split_workspace(int64_t B, int64_t T, int64_t N, int64_t HV, bool varlen) {
+    const int64_t chunks = varlen ? (B * T + 63 * N) / 64 + N : N * ((T + 63) / 64);
+    size_t bytes = (size_t)chunks * HV * kFwdRecordBytes;
+    if (varlen) bytes += ((size_t)(N + 1) * 8 + 255) / 256 * 256;
+    return bytes;
+}
+
+int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s) {
+    if (L.N * L.HV == 0) return GDN_OK;
+    if (smem_optin((const void*)chunk_prep_kernel, (int)cp::SMEM_BYTES) != cudaSuccess ||
+        smem_optin((const void*)chunk_state_kernel, (int)cs::SMEM_BYTES) != cudaSuccess)
+        return GDN_ERR_LAUNCH;
+    const int64_t Ttot = L.B * L.T;
+    uint8_t* rec = (uint8_t*)ws;
+    int64_t* cbase = nullptr;
+    if (L.cu) {
+        cbase = (int64_t*)ws;
+        rec = (uint8_t*)ws + ((size_t)(L.N + 1) * 8 + 255) / 256 * 256;
+        chunk_base_kernel<<<1, 1024, 0, s>>>(L.cu, L.N, cbase);
+        count_launch();
+    }
+    ChunkPrepArgs p;
+    memset(&p, 0, sizeof(p));
+    if (!make_tmap_3d_sw128(&p.tq, L.q, 128, L.H, Ttot, 128, L.H * 128, 64)) return GDN_ERR_ALIGN;
+    if (!make_tmap_3d_sw128(&p.tk, L.k, 128, L.H, Ttot, 128, L.H * 128, 64)) return GDN_ERR_ALIGN;
+    p.g = L.g;
+    p.beta = L.beta;
+    p.cu = L.cu;
+    p.cbase = cbase;
+    p.rec = rec;
+    p.err = L.err;
+    p.T = L.T;
+    p.H = (int)L.H;
+    p.HV = (int)L.HV;
+    p.g_dtype = L.g_dtype;
+    p.beta_dtype = L.beta_dtype;
+    p.l2norm = L.l2norm;
+    p.scale = L.scale;
+    const int64_t maxlen = L.max_seqlen > 0 ? L.max_seqlen : (L.cu ? Ttot : L.T);
+    const int64_t maxchunks = (maxlen + 63) / 64;
+    if (maxchunks > 0) {
+        chunk_prep_kernel<<<dim3((unsigned)maxchunks, (unsigned)(L.N * L.HV)), cp::NTHR, cp::SMEM_BYTES, s>>>(p);
+        count_launch();
+    }
+    ChunkStateArgs a;
+    memset(&a, 0, sizeof(a));
+    a.tq = p.tq;
+    a.tk = p.tk;
+    if (!make_tmap_3d_sw128(&a.tv, L.v, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
+    a.rec = rec;
+    a.cbase = cbase;
+    a.o = L.o;
+    a.h0 = L.h0;
+    a.ht = L.ht;
+    a.ckpt = L.ckpt;
+    a.cu = L.cu;
+    a.err = L.err;
+    a.T = L.T;
+    a.HV = (int)L.HV;
+    a.H = (int)L.H;
+    a.ckpt_every = L.ckpt_every;
+    chunk_state_kernel<<<(unsigned)(L.N * L.HV), cs::NTHR, cs::SMEM_BYTES, s>>>(a);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+}  // namespace gdn

@@ -56,6 +56,17 @@ constexpr size_t kBwdRecT = 49152;
 constexpr size_t kBwdRecDel = 57344;  // Delta^T
 constexpr size_t kBwdRecDdl = 73728;  // Dd^T low part
 
+// Per-(chunk, head) record of the split forward (gdn_chunk_split.cu): the prep pass writes it, the state
+// pass reads it. Shared-memory images in the 128-byte-swizzled operand layouts of -W (bf16 [i][dk], two
+// 8 KB d-blocks), TV = T diag(beta) (bf16 [i][j]), P hi and P lo (bf16 [i][j]), then fp32 vectors:
+// e^(G_C - G_j) nk_j [64], f1 = scale e^G_i nq_i [64], f2 = nq_i [64], e^G_C.
+constexpr size_t kFwdRecordBytes = 41984;
+constexpr size_t kFwdRecW = 0;
+constexpr size_t kFwdRecTV = 16384;
+constexpr size_t kFwdRecP = 24576;  // P hi, then P lo at +8192
+constexpr size_t kFwdRecVec = 40960;
+constexpr uint32_t kFwdRecVecBytes = 784;
+
 // Arguments of the chunked backward.
 struct ChunkBwdLaunch {
     const void *q, *k, *v, *g, *beta, *dout;
@@ -87,6 +98,10 @@ int decode_tma(const void* q, const void* k, const void* v, const void* g, const
 
 bool chunk_fwd_supported(int64_t DK, int64_t DV, int act_dtype);
 int chunk_fwd(const ChunkLaunch& L, cudaStream_t s);
+// The plain forward as two launches (chunk-parallel prep, per-(sequence, head) state pass); `ws` holds the
+// per-chunk records (chunk_fwd_split_workspace bytes, 256-byte aligned).
+size_t chunk_fwd_split_workspace(int64_t B, int64_t T, int64_t N, int64_t HV, bool varlen);
+int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s);
 bool chunk_bwd_supported(int64_t DK, int64_t DV, int act_dtype);
 size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t HV, bool varlen);
 int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s);
