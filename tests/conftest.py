@@ -33,8 +33,12 @@ def pytest_terminal_summary(terminalreporter, exitstatus, config):
     if not PARITY_LOG:
         return
     worst = {}
-    for name, strict, excess, tol in PARITY_LOG:
-        w = worst.setdefault(name, [0.0, None, tol, 0])
+    for name, strict, excess, tol, test in PARITY_LOG:
+        w = worst.setdefault(name, [0.0, None, tol, 0, ""])
+        key = strict if excess is None else excess
+        prev = w[0] if w[1] is None else w[1]
+        if w[3] == 0 or key >= prev:
+            w[4] = test
         w[0] = max(w[0], strict)
         if excess is not None:
             w[1] = excess if w[1] is None else max(w[1], excess)
@@ -42,8 +46,16 @@ def pytest_terminal_summary(terminalreporter, exitstatus, config):
         w[3] += 1
     tr = terminalreporter
     tr.write_sep("-", "parity: worst max-abs error / RMS(reference) per output")
-    tr.write_line(f"{'output':<16}{'checks':>8}{'strict':>12}{'beyond bf16 rounding':>24}{'bar':>8}")
+    tr.write_line(f"{'output':<16}{'checks':>8}{'strict':>12}{'beyond bf16 rounding':>24}{'bar':>8}  worst in")
     for name in sorted(worst):
-        strict, excess, tol, n = worst[name]
+        strict, excess, tol, n, test = worst[name]
         ex = "-" if excess is None else f"{excess:.4f}"
-        tr.write_line(f"{name:<16}{n:>8}{strict:>12.4f}{ex:>24}{tol:>8}")
+        tr.write_line(f"{name:<16}{n:>8}{strict:>12.4f}{ex:>24}{tol:>8}  {test.split('::')[-1]}")
+
+
+@pytest.fixture(autouse=True)
+def _record_test_name(request):
+    from helpers import CURRENT_TEST
+
+    CURRENT_TEST[0] = request.node.nodeid
+    yield

@@ -7,6 +7,7 @@ import numpy as np
 # of the run, so the log shows how far each output is from the literal north-star bar and from the bar
 # applied beyond rounding.
 PARITY_LOG = []
+CURRENT_TEST = [""]  # node id of the running test (set by conftest.py)
 
 
 def rms(x) -> float:
@@ -22,7 +23,7 @@ def assert_rms_close(actual, ref, tol, name=""):
     err = float(np.abs(a - r).max()) if a.size else 0.0
     bound = tol * max(rms(r), 1e-30)
     assert np.isfinite(a).all(), f"{name}: non-finite values"
-    PARITY_LOG.append((name, err / max(rms(r), 1e-30), None, tol))
+    PARITY_LOG.append((name, err / max(rms(r), 1e-30), None, tol, CURRENT_TEST[0]))
     assert err <= bound, f"{name}: max abs err {err:.3e} > {tol} * RMS(ref) = {bound:.3e}"
     return err / max(rms(r), 1e-30)
 
@@ -42,7 +43,7 @@ def assert_bf16_close(actual, ref, tol, name=""):
     rr = max(rms(r), 1e-30)
     err = np.abs(a - r)
     excess = float((err - 2.0 ** -8 * np.abs(r)).max()) if a.size else 0.0
-    PARITY_LOG.append((name, float(err.max() / rr) if a.size else 0.0, excess / rr, tol))
+    PARITY_LOG.append((name, float(err.max() / rr) if a.size else 0.0, excess / rr, tol, CURRENT_TEST[0]))
     assert excess <= tol * rr, (f"{name}: error beyond bf16 output rounding {excess:.3e} > {tol} * RMS(ref) = "
                                 f"{tol * rr:.3e} (strict max-abs/RMS {err.max() / rr:.4f})")
     return float(err.max() / rr), excess / rr
