@@ -67,6 +67,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  "l"((uint64_t)src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+// L2 prefetches: a chunk's operands are brought into L2 two chunks before its shared-memory loads
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((uint64_t)src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_tile_l2(const CUtensorMap* map, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"((uint64_t)map), "r"(c0),
+                 "r"(c1), "r"(c2)
+                 : "memory");
+}
 template <int N>
 __device__ __forceinline__ void vload(const float* v, int base, float (&o)[N]) {
     const float4* p = reinterpret_cast<const float4*>(v + base);
@@ -146,14 +155,6 @@ __global__ void __launch_bounds__(cp::NTHR, 3) chunk_prep_kernel(const __grid_co
         mbar_init(bar_in, 1);
         mbar_init(bar_mma, 1);
         fence_barrier_init();
-    }
-    if (warp == 0) tmem_alloc(tmem_slot, T_COLS);
-    sync_tc();
-    const uint32_t tm = *tmem_slot;
-    const uint32_t lb = (uint32_t)(32 * lg) << 16;
-    const uint32_t sb = smem_u32(sm);
-    bool ok = true;
-    if (tid == 0) {
         mbar_arrive_expect_tx(bar_in, 4 * 8192);
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb) {
@@ -161,6 +162,12 @@ __global__ void __launch_bounds__(cp::NTHR, 3) chunk_prep_kernel(const __grid_co
             tma_load_3d(sm + OFF_QK + kb * 16384 + 8192, &a.tk, bar_in, kb * 64, hq, (int)tok0);
         }
     }
+    if (warp == 0) tmem_alloc(tmem_slot, T_COLS);
+    sync_tc();
+    const uint32_t tm = *tmem_slot;
+    const uint32_t lb = (uint32_t)(32 * lg) << 16;
+    const uint32_t sb = smem_u32(sm);
+    bool ok = true;
     // gates: Gamma = inclusive cumsum of g in the chunk; rows past the sequence end carry g = 0, beta = 0
     if (tid < 64) {
         float x = 0.f, bt = 0.f;
@@ -433,7 +440,9 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     }
 
     auto recp = [&](int c) { return a.rec + ((cb + c) * a.HV + hv) * kFwdRecordBytes; };
-    auto issue_l1 = [&](int c) {  // Q, -W, TV, V, vectors of chunk c
+    // Chunk c's Q, -W, TV, V tiles (issued once G1 of chunk c-1 has read them) and its vectors (issued once the
+    // output step of chunk c-2 has read that vector buffer) complete one phase of bar_l1 together.
+    auto issue_l1_tiles = [&](int c) {
         const int tok0 = (int)(bos + 64 * c);
         const uint8_t* r = recp(c);
         mbar_arrive_expect_tx(bar_l1, TX_L1);
@@ -444,7 +453,19 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             tma_load_3d(sm + OFF_V + kb * 8192, &a.tv, bar_l1, kb * 64, hv, tok0);
         }
         bulk_g2s(sm + OFF_TV, r + kFwdRecTV, 8192, bar_l1);
-        bulk_g2s(sm + OFF_VEC + (c & 1) * kFwdRecVecBytes, r + kFwdRecVec, kFwdRecVecBytes, bar_l1);
+    };
+    auto issue_l1_vec = [&](int c) {
+        bulk_g2s(sm + OFF_VEC + (c & 1) * kFwdRecVecBytes, recp(c) + kFwdRecVec, kFwdRecVecBytes, bar_l1);
+    };
+    auto prefetch_chunk = [&](int c) {  // everything chunk c reads from global memory, into L2
+        const int tok0 = (int)(bos + 64 * c);
+        prefetch_l2(recp(c), (uint32_t)kFwdRecordBytes);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+            prefetch_tile_l2(&a.tq, kb * 64, hq, tok0);
+            prefetch_tile_l2(&a.tk, kb * 64, hq, tok0);
+            prefetch_tile_l2(&a.tv, kb * 64, hv, tok0);
+        }
     };
     auto issue_l2 = [&](int c) {  // K of chunk c
         const int tok0 = (int)(bos + 64 * c);
@@ -483,9 +504,11 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     };
 
     if (tid == 0 && nchunks > 0) {
-        issue_l1(0);
+        issue_l1_tiles(0);
+        issue_l1_vec(0);
         issue_l2(0);
         issue_l3(0);
+        if (nchunks > 1) prefetch_chunk(1);
     }
 
     for (int c = 0; c < nchunks; ++c) {
@@ -493,6 +516,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         const uint32_t tD = tm + T_D + par * 128;
         const float* vec = (const float*)(sm + OFF_VEC + par * kFwdRecVecBytes);
         // A. this chunk's Q, -W, TV, V and vectors; U = TV V into D (rows 64-127), zeros into rows 0-63
+        if (tid == 0 && c + 2 < nchunks) prefetch_chunk(c + 2);
         wait_bar(bar_l1, par, a.err, 51, ok);
         if (tid == 0) {
             tc_fence_after();
@@ -557,6 +581,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         // D. Delta (lanes 64-127) -> Delta and Dd tiles; meanwhile lanes 0-63 emit the previous chunk's outputs
         wait_bar(bar_g, par, a.err, 54, ok);
         tc_fence_after();
+        if (tid == 0 && c + 1 < nchunks) issue_l1_tiles(c + 1);  // G1 has read Q, -W, TV, V
         if (lg >= 2) {
             const int j = row - 64;
             const float x = vec[j];  // e^(G_C - G_j) nk_j
@@ -607,7 +632,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
                 umma_bf16(tE, desc_kmajor(sb + OFF_PH + ks * 32), dl, idE, 1);
             }
             umma_commit(bar_o);
-            if (c + 1 < nchunks) issue_l1(c + 1);  // G1 has read Q, -W, TV, V; the other vector buffer is free
+            if (c + 1 < nchunks) issue_l1_vec(c + 1);  // the output step of chunk c-1 has read that buffer
         }
     }
     // the last chunk's outputs and the final state
