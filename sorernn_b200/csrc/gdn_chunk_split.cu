@@ -219,16 +219,32 @@ __global__ void __launch_bounds__(cp::NTHR, 3) chunk_prep_kernel(const __grid_co
         if (kb == 0) (r < 64 ? vNQ : vNK)[i] = inv;
     }
     __syncthreads();
-    if (tid < 64) {  // record vectors: vX = e^(G_C - G) nk, f1 = scale e^G nq, f2 = nq, e^G_C
-        const float eg = __expf(vG[tid]);
-        vEG[tid] = eg;
+    if (tid < 64) {  // record vectors: vX = e^(G_C - G) nk, nq, e^G_C
+        vEG[tid] = __expf(vG[tid]);
         float* rv = (float*)(rec + kFwdRecVec);
         rv[tid] = __expf(vG[63] - vG[tid]) * vNK[tid];
-        rv[64 + tid] = a.scale * eg * vNQ[tid];
-        rv[128 + tid] = vNQ[tid];
-        if (tid == 0) rv[192] = __expf(vG[63]);
+        rv[64 + tid] = vNQ[tid];
+        if (tid == 0) rv[128] = __expf(vG[63]);
     }
     __syncthreads();
+    // Qg = diag(scale e^G) Q (raw q rows) to the record, in the tile's own swizzled layout: 16-byte chunks,
+    // each scaled by its row's factor
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const int e = tid + 256 * it, i = e >> 4, kb = (e >> 3) & 1, ch = e & 7;
+        const uint32_t off = kb * 16384 + i * 128 + ch * 16;
+        const uint4 u = *reinterpret_cast<const uint4*>(sm + OFF_QK + off);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+        const float f = a.scale * vEG[i];
+        float y[8];
+#pragma unroll
+        for (int k2 = 0; k2 < 4; ++k2) {
+            const float2 z = __bfloat1622float2(h[k2]);
+            y[2 * k2] = z.x * f;
+            y[2 * k2 + 1] = z.y * f;
+        }
+        *reinterpret_cast<uint4*>(rec + kFwdRecQg + kb * 8192 + i * 128 + ch * 16) = pack8(y);
+    }
     wait_bar(bar_mma, 0, a.err, 42, ok);
     tc_fence_after();
     // D1 rows 0-63 -> P hi/lo (straight to the record), rows 64-127 -> A (fp32, shared memory)
@@ -327,34 +343,39 @@ __global__ void __launch_bounds__(cp::NTHR, 3) chunk_prep_kernel(const __grid_co
 }
 
 // ================================================================================================
-// chunk_state_kernel: one CTA (512 threads) per (sequence, value head), chunks in order
+// chunk_state_kernel: one CTA per (sequence, value head), chunks in order. Warps 0-15 move data between
+// tensor memory and operand tiles; warp 16 only issues the loads and the MMAs, so that issue (about one
+// 128 x 128 x 16 MMA per 70 cycles) overlaps the other warps' work.
 // ================================================================================================
 namespace cs {
-constexpr int NTHR = 512;
-constexpr uint32_t OFF_QW = 0;         // per d-block kb (16 KB apart): [Q 8 KB | -W 8 KB] = MMA G1's A
-constexpr uint32_t OFF_PH = 32768;     // P hi [i][j]; [P hi; P lo] and [P lo; Z] are G2's 128-row A operands
-constexpr uint32_t OFF_PL = 40960;
-constexpr uint32_t OFF_Z = 49152;      // zeros: [Z; TV] puts U on rows 64-127 and zeros on 0-63
-constexpr uint32_t OFF_TV = 57344;
-constexpr uint32_t OFF_V = 65536;      // V [token][dv], 2 x 8 KB
-constexpr uint32_t OFF_K = 81920;      // K [token][dk], 2 x 8 KB
-constexpr uint32_t OFF_S0 = 98304;     // S0^T hi bf16 [dv][dk], 2 dk-blocks x 16 KB
-constexpr uint32_t OFF_S0L = 131072;   // S0^T lo
-constexpr uint32_t OFF_DH = 163840;    // Delta hi [token][dv], 2 x 8 KB
-constexpr uint32_t OFF_DL = 180224;    // Delta lo
-constexpr uint32_t OFF_DDH = 196608;   // Dd hi
-constexpr uint32_t OFF_DDL = 212992;   // Dd lo
-constexpr uint32_t OFF_VEC = 229376;   // record vectors, two buffers of kFwdRecVecBytes
+constexpr int NWORK = 512;              // warps 0-15: TMEM lane quadrant w % 4, column quarter w / 4
+constexpr int NTHR = NWORK + 32;        // + warp 16: load and MMA issue
+constexpr uint32_t OFF_W = 0;           // -W bf16 [i][dk], two 8 KB d-blocks: G1's B (N = 64 tokens)
+constexpr uint32_t OFF_PH = 16384;      // P hi [i][j]; [P hi; P lo] and [P lo; Z] are the 128-row A operands
+constexpr uint32_t OFF_PL = 24576;      //   of the output products (rows 0-63 used)
+constexpr uint32_t OFF_Z = 32768;       // zeros
+constexpr uint32_t OFF_TV = 40960;      // TV [i][j]: B of U^T = V^T TV^T
+constexpr uint32_t OFF_V = 49152;       // V [token][dv], 2 x 8 KB
+constexpr uint32_t OFF_K = 65536;       // K [token][dk], 2 x 8 KB
+constexpr uint32_t OFF_S0 = 81920;      // S0^T hi [dv][dk], 2 dk-blocks x 16 KB (A of G1, B of the output MMA)
+// per d-block kb (24 KB apart): [Qg_kb 8 KB | S0^T lo block kb 16 KB]: [Qg; S0lo rows] is the output MMA's A
+constexpr uint32_t OFF_QL = 114688;
+constexpr uint32_t QL_BLK = 24576;
+constexpr uint32_t OFF_DH = 163840;     // Delta^T hi [dv][j] (128 rows x 128 B)
+constexpr uint32_t OFF_DL = 180224;
+constexpr uint32_t OFF_DDH = 196608;    // Dd^T = Delta^T diag(e^(G_C - G) nk), hi
+constexpr uint32_t OFF_DDL = 212992;
+constexpr uint32_t OFF_VEC = 229376;    // record vectors, two buffers
 constexpr uint32_t OFF_BAR = OFF_VEC + 2 * kFwdRecVecBytes;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 128 + 1024;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-// TMEM columns: S^T, the two D buffers (G1 output, M = 128), E (P Delta, rows 0-63)
-constexpr uint32_t T_S = 0, T_D = 128, T_E = 384, T_COLS = 512;
-constexpr uint32_t TX_L1 = 2 * 8192 + 2 * 8192 + 8192 + 2 * 8192 + kFwdRecVecBytes;  // Q, -W, TV, V, vectors
+// TMEM columns: S^T [dv][dk], Delta^T [dv][j] (64), two output accumulators (rows 0-63 used)
+constexpr uint32_t T_S = 0, T_DT = 128, T_O = 256, T_COLS = 512;
+constexpr uint32_t TX_L1 = 2 * 8192 + 8192 + 2 * 8192 + 2 * 8192 + kFwdRecVecBytes;  // W, TV, V, Qg, vectors
 }  // namespace cs
 
 struct ChunkStateArgs {
-    CUtensorMap tq, tk, tv;
+    CUtensorMap tk, tv;
     const uint8_t* rec;
     const int64_t* cbase;
     void* o;
@@ -367,22 +388,39 @@ struct ChunkStateArgs {
     int HV, H, ckpt_every;
 };
 
+// hi = the upper 16 bits of each fp32 (bf16 truncation), lo = bf16(x - hi): the pair carries ~16 bits
+__device__ __forceinline__ void split2_trunc(float a0, float a1, uint32_t& hi, uint32_t& lo) {
+    const uint32_t u0 = __float_as_uint(a0), u1 = __float_as_uint(a1);
+    hi = __byte_perm(u0, u1, 0x7632);
+    const __nv_bfloat162 l =
+        __floats2bfloat162_rn(a0 - __uint_as_float(u0 & 0xffff0000u), a1 - __uint_as_float(u1 & 0xffff0000u));
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+__device__ __forceinline__ void split8_trunc(const float* v, uint4& hi, uint4& lo) {
+    split2_trunc(v[0], v[1], hi.x, lo.x);
+    split2_trunc(v[2], v[3], hi.y, lo.y);
+    split2_trunc(v[4], v[5], hi.z, lo.z);
+    split2_trunc(v[6], v[7], hi.w, lo.w);
+}
+
 __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_constant__ ChunkStateArgs a) {
     using namespace cs;
     using namespace split;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bar = (uint64_t*)(sm + OFF_BAR);
-    uint64_t* bar_l1 = bar;      // Q, -W, TV, V, vectors of a chunk
+    uint64_t* bar_l1 = bar;      // -W, TV, V, Qg, vectors of a chunk
     uint64_t* bar_l2 = bar + 1;  // K
     uint64_t* bar_l3 = bar + 2;  // P hi/lo
-    uint64_t* bar_g = bar + 3;   // G1 done
-    uint64_t* bar_s = bar + 4;   // state update done
-    uint64_t* bar_o = bar + 5;   // E products done
-    uint32_t* tmem_slot = (uint32_t*)(bar + 6);
+    uint64_t* bar_g = bar + 3;   // Delta^T products done
+    uint64_t* bar_q = bar + 4;   // Qg S0 done
+    uint64_t* bar_s = bar + 5;   // state update done
+    uint64_t* bar_o = bar + 6;   // P Delta done
+    uint32_t* tmem_slot = (uint32_t*)(bar + 7);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int lg = warp & 3, cq = warp >> 2;
+    const bool issuer = tid == NWORK;  // warp 16, lane 0
+    const int lg = warp & 3, cq = (warp >> 2) & 3;
     const int row = 32 * lg + lane;
     const int n = blockIdx.x / a.HV, hv = blockIdx.x % a.HV, hq = hv / (a.HV / a.H);
     int64_t bos, eos;
@@ -409,10 +447,9 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         }
     }
 
-    if (tid == 0) {
-        for (int i = 0; i < 6; ++i) mbar_init(&bar[i], 1);
+    if (issuer) {
+        for (int i = 0; i < 7; ++i) mbar_init(&bar[i], 1);
         fence_barrier_init();
-        prefetch_tmap(&a.tq);
         prefetch_tmap(&a.tk);
         prefetch_tmap(&a.tv);
     }
@@ -421,13 +458,13 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     fence_async_smem();
     sync_tc();
     const uint32_t tm = *tmem_slot;
-    const uint32_t tS = tm + T_S, tE = tm + T_E;
+    const uint32_t tS = tm + T_S, tDT = tm + T_DT;
     const uint32_t lb = (uint32_t)(32 * lg) << 16;
     const uint32_t sb = smem_u32(sm);
     bool ok = true;
 
     // initial state -> TMEM: thread (row = dv, quarter cq) holds S^T[dv][dk] for dk in [32 cq, 32 cq + 32)
-    {
+    if (!issuer && tid < NWORK) {
         const float* h0 = a.h0 ? a.h0 + ((int64_t)n * a.HV + hv) * 16384 : nullptr;
 #pragma unroll
         for (int c0 = 0; c0 < 32; c0 += 16) {
@@ -440,32 +477,23 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     }
 
     auto recp = [&](int c) { return a.rec + ((cb + c) * a.HV + hv) * kFwdRecordBytes; };
-    // Chunk c's Q, -W, TV, V tiles (issued once G1 of chunk c-1 has read them) and its vectors (issued once the
-    // output step of chunk c-2 has read that vector buffer) complete one phase of bar_l1 together.
-    auto issue_l1_tiles = [&](int c) {
+    // bar_l1 phase of chunk c: -W, TV, V (issued once the Delta^T products of chunk c-1 have read them), then
+    // Qg (once the output product of chunk c-1 has read it) and the vectors (once the output step of chunk c-2
+    // has read that buffer)
+    auto issue_l1_a = [&](int c) {
         const int tok0 = (int)(bos + 64 * c);
         const uint8_t* r = recp(c);
         mbar_arrive_expect_tx(bar_l1, TX_L1);
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {
-            tma_load_3d(sm + OFF_QW + kb * 16384, &a.tq, bar_l1, kb * 64, hq, tok0);
-            bulk_g2s(sm + OFF_QW + kb * 16384 + 8192, r + kFwdRecW + kb * 8192, 8192, bar_l1);
-            tma_load_3d(sm + OFF_V + kb * 8192, &a.tv, bar_l1, kb * 64, hv, tok0);
-        }
+        bulk_g2s(sm + OFF_W, r + kFwdRecW, 16384, bar_l1);
         bulk_g2s(sm + OFF_TV, r + kFwdRecTV, 8192, bar_l1);
-    };
-    auto issue_l1_vec = [&](int c) {
-        bulk_g2s(sm + OFF_VEC + (c & 1) * kFwdRecVecBytes, recp(c) + kFwdRecVec, kFwdRecVecBytes, bar_l1);
-    };
-    auto prefetch_chunk = [&](int c) {  // everything chunk c reads from global memory, into L2
-        const int tok0 = (int)(bos + 64 * c);
-        prefetch_l2(recp(c), (uint32_t)kFwdRecordBytes);
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {
-            prefetch_tile_l2(&a.tq, kb * 64, hq, tok0);
-            prefetch_tile_l2(&a.tk, kb * 64, hq, tok0);
-            prefetch_tile_l2(&a.tv, kb * 64, hv, tok0);
-        }
+        for (int kb = 0; kb < 2; ++kb) tma_load_3d(sm + OFF_V + kb * 8192, &a.tv, bar_l1, kb * 64, hv, tok0);
+    };
+    auto issue_l1_b = [&](int c) {
+        const uint8_t* r = recp(c);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) bulk_g2s(sm + OFF_QL + kb * QL_BLK, r + kFwdRecQg + kb * 8192, 8192, bar_l1);
+        bulk_g2s(sm + OFF_VEC + (c & 1) * kFwdRecVecBytes, r + kFwdRecVec, kFwdRecVecBytes, bar_l1);
     };
     auto issue_l2 = [&](int c) {  // K of chunk c
         const int tok0 = (int)(bos + 64 * c);
@@ -477,35 +505,44 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         mbar_arrive_expect_tx(bar_l3, 16384);
         bulk_g2s(sm + OFF_PH, recp(c) + kFwdRecP, 16384, bar_l3);
     };
-    // output step of chunk c (warps of lanes 0-63): O = f1 (Q S0) + f2 (P Delta) -> o[token][hv][dv]
+    auto prefetch_chunk = [&](int c) {  // everything chunk c reads from global memory, into L2
+        const int tok0 = (int)(bos + 64 * c);
+        prefetch_l2(recp(c), (uint32_t)kFwdRecordBytes);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+            prefetch_tile_l2(&a.tk, kb * 64, hq, tok0);
+            prefetch_tile_l2(&a.tv, kb * 64, hv, tok0);
+        }
+    };
+    // output step of chunk c on warps 8, 9, 12, 13 (lanes 0-63, 64 columns each): o = nq (Qg S0 + P Delta)
     auto output_step = [&](int c) {
         const int i = row;
         const float* vec = (const float*)(sm + OFF_VEC + (c & 1) * kFwdRecVecBytes);
-        const float f1 = vec[64 + i], f2 = vec[128 + i];
+        const float f = vec[64 + i];
         const int nv = (len - 64 * (int64_t)c) < 64 ? (int)(len - 64 * (int64_t)c) : 64;
-        float v1[32], v2[32];
-        const uint32_t tD = tm + T_D + (uint32_t)(c & 1) * 128;
-        tmem_ld16(tD + lb + 32 * cq, *reinterpret_cast<float(*)[16]>(v1));
-        tmem_ld16(tD + lb + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v1 + 16));
-        tmem_ld16(tE + lb + 32 * cq, *reinterpret_cast<float(*)[16]>(v2));
-        tmem_ld16(tE + lb + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v2 + 16));
-        tmem_wait_ld();
-        if (i < nv) {
-            uint4* dst = reinterpret_cast<uint4*>((__nv_bfloat16*)a.o + ((bos + 64 * (int64_t)c + i) * a.HV + hv) * 128 +
-                                                  32 * cq);
+        const uint32_t tO = tm + T_O + (uint32_t)(c & 1) * 128 + lb + 64 * ((warp >> 2) & 1);
+        __nv_bfloat16* orow = (__nv_bfloat16*)a.o + ((bos + 64 * (int64_t)c + i) * a.HV + hv) * 128 +
+                              64 * ((warp >> 2) & 1);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                float y[8];
+        for (int h = 0; h < 2; ++h) {
+            float v[32];
+            tmem_ld16(tO + 32 * h, *reinterpret_cast<float(*)[16]>(v));
+            tmem_ld16(tO + 32 * h + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+            tmem_wait_ld();
+            if (i < nv) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) y[e] = fmaf(f1, v1[8 * q + e], f2 * v2[8 * q + e]);
-                dst[q] = pack8(y);
+                for (int e = 0; e < 32; ++e) v[e] *= f;
+                uint4* dst = reinterpret_cast<uint4*>(orow + 32 * h);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) dst[q] = pack8(v + 8 * q);
             }
         }
     };
+    const bool out_warp = warp >= 8 && warp < 16 && lg < 2;  // warps 8, 9, 12, 13
 
-    if (tid == 0 && nchunks > 0) {
-        issue_l1_tiles(0);
-        issue_l1_vec(0);
+    if (issuer && nchunks > 0) {
+        issue_l1_a(0);
+        issue_l1_b(0);
         issue_l2(0);
         issue_l3(0);
         if (nchunks > 1) prefetch_chunk(1);
@@ -513,26 +550,21 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
 
     for (int c = 0; c < nchunks; ++c) {
         const uint32_t par = (uint32_t)c & 1u;
-        const uint32_t tD = tm + T_D + par * 128;
         const float* vec = (const float*)(sm + OFF_VEC + par * kFwdRecVecBytes);
-        // A. this chunk's Q, -W, TV, V and vectors; U = TV V into D (rows 64-127), zeros into rows 0-63
-        if (tid == 0 && c + 2 < nchunks) prefetch_chunk(c + 2);
+        // A. this chunk's tiles and vectors; the previous chunk's state update and output product have landed
         wait_bar(bar_l1, par, a.err, 51, ok);
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t id = idesc_bf16(128, 128, 0, 1);
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tD, desc_kmajor(sb + OFF_Z + ks * 32), desc_mnmajor(sb + OFF_V + ks * 2048, 8192), id, ks > 0);
-        }
-        // B. the previous chunk's state update has landed: K of this chunk may overwrite the K tile; read S out
         if (c > 0) {
             wait_bar(bar_s, par ^ 1u, a.err, 52, ok);
+            wait_bar(bar_q, par ^ 1u, a.err, 53, ok);
             tc_fence_after();
         }
-        if (tid == 0 && c > 0) issue_l2(c);
-        {
-            const float eGC = vec[192];
+        if (issuer) {
+            if (c > 0) issue_l2(c);  // the state update of chunk c-1 has read K
+            if (c + 2 < nchunks) prefetch_chunk(c + 2);
+        }
+        // B. S^T -> S0^T hi/lo operand tiles; TMEM state <- e^G_C S0; checkpoint
+        if (tid < NWORK) {
+            const float eGC = vec[128];
             const bool ck = a.ckpt && (c % a.ckpt_every == 0);
             float* ckp = ck ? a.ckpt + ((ck_base + c / a.ckpt_every) * a.HV + hv) * 16384 : nullptr;
             float v[32];
@@ -543,14 +575,14 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
 #pragma unroll
                 for (int i = 0; i < 32; ++i) ckp[(32 * cq + i) * 128 + row] = v[i];
             }
-            const uint32_t blk = (uint32_t)(cq >> 1) * 16384;
+            const uint32_t kb = (uint32_t)(cq >> 1);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 uint4 hi, lo;
-                split8(v + 8 * q, hi, lo);
-                const uint32_t off = blk + sw128_off(row, 32 * (cq & 1) + 8 * q);
-                *reinterpret_cast<uint4*>(sm + OFF_S0 + off) = hi;
-                *reinterpret_cast<uint4*>(sm + OFF_S0L + off) = lo;
+                split8_trunc(v + 8 * q, hi, lo);
+                const uint32_t off = sw128_off(row, 32 * (cq & 1) + 8 * q);
+                *reinterpret_cast<uint4*>(sm + OFF_S0 + kb * 16384 + off) = hi;
+                *reinterpret_cast<uint4*>(sm + OFF_QL + kb * QL_BLK + 8192 + off) = lo;
             }
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= eGC;
@@ -560,90 +592,110 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         }
         fence_async_smem();
         sync_tc();
-        // C. G1: D += [Q; -W] (S0hi + S0lo)  (K = dk = 128); then P of this chunk may replace the previous one
-        if (tid == 0) {
-            const uint32_t id = idesc_bf16(128, 128, 0, 0);
+        // C. issuer: Delta^T = V^T TV^T + S0^T (-W)^T (hi + lo) -> bar_g; O = [Qg; -] S0hi -> bar_q; the next loads.
+        //    Warps 8, 9, 12, 13 meanwhile emit the previous chunk's outputs.
+        if (issuer) {
+            const uint32_t idU = idesc_bf16(128, 64, 1, 0), idD = idesc_bf16(128, 64, 0, 0);
+            const uint32_t idO = idesc_bf16(128, 128, 0, 0);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+                umma_bf16(tDT, desc_mnmajor(sb + OFF_V + ks * 2048, 8192), desc_kmajor(sb + OFF_TV + ks * 32), idU,
+                          ks > 0);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const uint32_t s0 = sb + (h ? OFF_S0L : OFF_S0);
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
                     const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                    umma_bf16(tD, desc_kmajor(sb + OFF_QW + kb * 16384 + ko), desc_kmajor(s0 + kb * 16384 + ko), id, 1);
+                    const uint32_t s0 = h ? sb + OFF_QL + kb * QL_BLK + 8192 : sb + OFF_S0 + kb * 16384;
+                    umma_bf16(tDT, desc_kmajor(s0 + ko), desc_kmajor(sb + OFF_W + kb * 8192 + ko), idD, 1);
                 }
             }
             umma_commit(bar_g);
+            const uint32_t tO = tm + T_O + par * 128;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                umma_bf16(tO, desc_kmajor(sb + OFF_QL + kb * QL_BLK + ko), desc_kmajor(sb + OFF_S0 + kb * 16384 + ko),
+                          idO, ks > 0);
+            }
+            umma_commit(bar_q);
             if (c > 0) {
-                wait_bar(bar_o, par ^ 1u, a.err, 53, ok);
+                wait_bar(bar_o, par ^ 1u, a.err, 54, ok);  // the P tiles of chunk c-1 have been read
                 issue_l3(c);
             }
+            wait_bar(bar_g, par, a.err, 55, ok);
+            if (c + 1 < nchunks) issue_l1_a(c + 1);  // -W, TV, V have been read
+        } else if (out_warp && c > 0) {
+            wait_bar(bar_o, par ^ 1u, a.err, 56, ok);
+            tc_fence_after();
+            output_step(c - 1);
         }
-        // D. Delta (lanes 64-127) -> Delta and Dd tiles; meanwhile lanes 0-63 emit the previous chunk's outputs
-        wait_bar(bar_g, par, a.err, 54, ok);
-        tc_fence_after();
-        if (tid == 0 && c + 1 < nchunks) issue_l1_tiles(c + 1);  // G1 has read Q, -W, TV, V
-        if (lg >= 2) {
-            const int j = row - 64;
-            const float x = vec[j];  // e^(G_C - G_j) nk_j
-            float v[32];
-            tmem_ld16(tD + lb + 32 * cq, *reinterpret_cast<float(*)[16]>(v));
-            tmem_ld16(tD + lb + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+        // D. Delta^T (TMEM, lanes = dv) -> Delta^T and Dd^T hi/lo tiles (all 16 warps, 16 tokens each)
+        if (tid < NWORK) {
+            if (c > 0) wait_bar(bar_o, par ^ 1u, a.err, 57, ok);  // the previous P Delta has read the tiles
+            wait_bar(bar_g, par, a.err, 58, ok);
+            tc_fence_after();
+            float v[16], x[16];
+            tmem_ld16(tDT + lb + 16 * cq, v);
+            vload(vec, 16 * cq, x);
             tmem_wait_ld();
-            const uint32_t blk = (uint32_t)(cq >> 1) * 8192;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < 2; ++q) {
                 float d[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) d[e] = v[8 * q + e] * x;
+                for (int e = 0; e < 8; ++e) d[e] = v[8 * q + e] * x[8 * q + e];
                 uint4 hi, lo, dhi, dlo;
-                split8(v + 8 * q, hi, lo);
-                split8(d, dhi, dlo);
-                const uint32_t off = blk + sw128_off(j, 32 * (cq & 1) + 8 * q);
+                split8_trunc(v + 8 * q, hi, lo);
+                split8_trunc(d, dhi, dlo);
+                const uint32_t off = sw128_off(row, 16 * cq + 8 * q);
                 *reinterpret_cast<uint4*>(sm + OFF_DH + off) = hi;
                 *reinterpret_cast<uint4*>(sm + OFF_DL + off) = lo;
                 *reinterpret_cast<uint4*>(sm + OFF_DDH + off) = dhi;
                 *reinterpret_cast<uint4*>(sm + OFF_DDL + off) = dlo;
             }
-        } else if (c > 0) {
-            output_step(c - 1);
         }
         fence_async_smem();
         sync_tc();
-        // E. G2: S^T += Dd^T K (hi + lo) -> bar_s; E = P Delta (hi.hi + lo.hi + hi.lo) -> bar_o; next loads
-        if (tid == 0) {
-            wait_bar(bar_l2, par, a.err, 55, ok);
-            wait_bar(bar_l3, par, a.err, 56, ok);
+        // E. issuer: S^T += Dd^T K (hi + lo) -> bar_s; O += P Delta (hi.hi + lo.hi + hi.lo) -> bar_o; Qg and
+        //    vectors of the next chunk
+        if (issuer) {
+            wait_bar(bar_l2, par, a.err, 59, ok);
             tc_fence_after();
-            const uint32_t idS = idesc_bf16(128, 128, 1, 1), idE = idesc_bf16(128, 128, 0, 1);
+            const uint32_t idS = idesc_bf16(128, 128, 0, 1), idO = idesc_bf16(128, 128, 0, 0);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const uint32_t dd = sb + (h ? OFF_DDL : OFF_DDH);
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks)
-                    umma_bf16(tS, desc_mnmajor(dd + ks * 2048, 8192), desc_mnmajor(sb + OFF_K + ks * 2048, 8192), idS, 1);
+                    umma_bf16(tS, desc_kmajor(dd + ks * 32), desc_mnmajor(sb + OFF_K + ks * 2048, 8192), idS, 1);
             }
             umma_commit(bar_s);
+            wait_bar(bar_l3, par, a.err, 60, ok);
+            tc_fence_after();
+            const uint32_t tO = tm + T_O + par * 128;
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-                const uint64_t dh = desc_mnmajor(sb + OFF_DH + ks * 2048, 8192);
-                const uint64_t dl = desc_mnmajor(sb + OFF_DL + ks * 2048, 8192);
-                umma_bf16(tE, desc_kmajor(sb + OFF_PH + ks * 32), dh, idE, ks > 0);
-                umma_bf16(tE, desc_kmajor(sb + OFF_PL + ks * 32), dh, idE, 1);
-                umma_bf16(tE, desc_kmajor(sb + OFF_PH + ks * 32), dl, idE, 1);
+                const uint64_t dh = desc_kmajor(sb + OFF_DH + ks * 32), dl = desc_kmajor(sb + OFF_DL + ks * 32);
+                umma_bf16(tO, desc_kmajor(sb + OFF_PH + ks * 32), dh, idO, 1);
+                umma_bf16(tO, desc_kmajor(sb + OFF_PL + ks * 32), dh, idO, 1);
+                umma_bf16(tO, desc_kmajor(sb + OFF_PH + ks * 32), dl, idO, 1);
             }
             umma_commit(bar_o);
-            if (c + 1 < nchunks) issue_l1_vec(c + 1);  // the output step of chunk c-1 has read that buffer
+            if (c + 1 < nchunks) {
+                wait_bar(bar_q, par, a.err, 61, ok);  // Qg of chunk c has been read
+                issue_l1_b(c + 1);
+            }
         }
     }
     // the last chunk's outputs and the final state
     if (nchunks > 0) {
         const uint32_t par = (uint32_t)(nchunks - 1) & 1u;
-        wait_bar(bar_o, par, a.err, 57, ok);
-        wait_bar(bar_s, par, a.err, 58, ok);
+        wait_bar(bar_o, par, a.err, 62, ok);
+        wait_bar(bar_s, par, a.err, 63, ok);
         tc_fence_after();
-        if (lg < 2) output_step(nchunks - 1);
+        if (out_warp) output_step(nchunks - 1);
     }
-    if (ok && a.ht) {
+    if (ok && a.ht && tid < NWORK) {
         float* ht = a.ht + ((int64_t)n * a.HV + hv) * 16384;
         float v[32];
         tmem_ld16(tS + lb + 32 * cq, *reinterpret_cast<float(*)[16]>(v));
@@ -739,7 +791,6 @@ int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s) {
     }
     ChunkStateArgs a;
     memset(&a, 0, sizeof(a));
-    a.tq = p.tq;
     a.tk = p.tk;
     if (!make_tmap_3d_sw128(&a.tv, L.v, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
     a.rec = rec;

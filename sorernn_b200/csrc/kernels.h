@@ -57,15 +57,16 @@ constexpr size_t kBwdRecDel = 57344;  // Delta^T
 constexpr size_t kBwdRecDdl = 73728;  // Dd^T low part
 
 // Per-(chunk, head) record of the split forward (gdn_chunk_split.cu): the prep pass writes it, the state
-// pass reads it. Shared-memory images in the 128-byte-swizzled operand layouts of -W (bf16 [i][dk], two
-// 8 KB d-blocks), TV = T diag(beta) (bf16 [i][j]), P hi and P lo (bf16 [i][j]), then fp32 vectors:
-// e^(G_C - G_j) nk_j [64], f1 = scale e^G_i nq_i [64], f2 = nq_i [64], e^G_C.
-constexpr size_t kFwdRecordBytes = 41984;
-constexpr size_t kFwdRecW = 0;
-constexpr size_t kFwdRecTV = 16384;
-constexpr size_t kFwdRecP = 24576;  // P hi, then P lo at +8192
-constexpr size_t kFwdRecVec = 40960;
-constexpr uint32_t kFwdRecVecBytes = 784;
+// pass reads it. Shared-memory images in the 128-byte-swizzled operand layouts of Qg = diag(scale e^G) Q
+// (bf16 [i][dk], two 8 KB d-blocks), -W (bf16 [i][dk], two 8 KB d-blocks), TV = T diag(beta) (bf16 [i][j]),
+// P hi and P lo (bf16 [i][j]), then fp32 vectors: e^(G_C - G_j) nk_j [64], nq_i [64], e^G_C.
+constexpr size_t kFwdRecordBytes = 58368;
+constexpr size_t kFwdRecQg = 0;
+constexpr size_t kFwdRecW = 16384;
+constexpr size_t kFwdRecTV = 32768;
+constexpr size_t kFwdRecP = 40960;  // P hi, then P lo at +8192
+constexpr size_t kFwdRecVec = 57344;
+constexpr uint32_t kFwdRecVecBytes = 528;
 
 // Arguments of the chunked backward.
 struct ChunkBwdLaunch {
