@@ -344,12 +344,14 @@ __global__ void __launch_bounds__(cp::NTHR, 3) chunk_prep_kernel(const __grid_co
 
 // ================================================================================================
 // chunk_state_kernel: one CTA per (sequence, value head), chunks in order. Warps 0-15 move data between
-// tensor memory and operand tiles; warp 16 only issues the loads and the MMAs, so that issue (about one
-// 128 x 128 x 16 MMA per 70 cycles) overlaps the other warps' work.
+// tensor memory and operand tiles; warps 16 and 17 only issue loads and MMAs (one thread issues a tcgen05.mma
+// about every 70-85 cycles), so that issue overlaps the other warps' work: warp 16 the state chain (the
+// Delta^T products with S0 hi, the state update), warp 17 the rest (the Delta^T products with S0 lo into a
+// second accumulator, the output products) and the loads those read.
 // ================================================================================================
 namespace cs {
 constexpr int NWORK = 512;              // warps 0-15: TMEM lane quadrant w % 4, column quarter w / 4
-constexpr int NTHR = NWORK + 32;        // + warp 16: load and MMA issue
+constexpr int NTHR = NWORK + 64;        // + warps 16, 17: load and MMA issue
 constexpr uint32_t OFF_W = 0;           // -W bf16 [i][dk], two 8 KB d-blocks: G1's B (N = 64 tokens)
 constexpr uint32_t OFF_PH = 16384;      // P hi [i][j]; [P hi; P lo] and [P lo; Z] are the 128-row A operands
 constexpr uint32_t OFF_PL = 24576;      //   of the output products (rows 0-63 used)
@@ -369,8 +371,9 @@ constexpr uint32_t OFF_VEC = 229376;    // record vectors, two buffers
 constexpr uint32_t OFF_BAR = OFF_VEC + 2 * kFwdRecVecBytes;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 128 + 1024;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-// TMEM columns: S^T [dv][dk], Delta^T [dv][j] (64), two output accumulators (rows 0-63 used)
-constexpr uint32_t T_S = 0, T_DT = 128, T_O = 256, T_COLS = 512;
+// TMEM columns: S^T [dv][dk], Delta^T [dv][j] (the S0 hi part, and the S0 lo part: 64 each), two output
+// accumulators (rows 0-63 used)
+constexpr uint32_t T_S = 0, T_DT = 128, T_DT2 = 192, T_O = 256, T_COLS = 512;
 constexpr uint32_t TX_L1 = 2 * 8192 + 8192 + 2 * 8192 + 2 * 8192 + kFwdRecVecBytes;  // W, TV, V, Qg, vectors
 }  // namespace cs
 
@@ -416,10 +419,12 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     uint64_t* bar_q = bar + 4;   // Qg S0 done
     uint64_t* bar_s = bar + 5;   // state update done
     uint64_t* bar_o = bar + 6;   // P Delta done
-    uint32_t* tmem_slot = (uint32_t*)(bar + 7);
+    uint64_t* bar_g2 = bar + 7;  // Delta^T product with S0 lo done
+    uint32_t* tmem_slot = (uint32_t*)(bar + 8);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool issuer = tid == NWORK;  // warp 16, lane 0
+    const bool issuer = tid == NWORK;        // warp 16, lane 0: the state chain
+    const bool issuer2 = tid == NWORK + 32;  // warp 17, lane 0: the rest
     const int lg = warp & 3, cq = (warp >> 2) & 3;
     const int row = 32 * lg + lane;
     const int n = blockIdx.x / a.HV, hv = blockIdx.x % a.HV, hq = hv / (a.HV / a.H);
@@ -448,7 +453,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     }
 
     if (issuer) {
-        for (int i = 0; i < 7; ++i) mbar_init(&bar[i], 1);
+        for (int i = 0; i < 8; ++i) mbar_init(&bar[i], 1);
         fence_barrier_init();
         prefetch_tmap(&a.tk);
         prefetch_tmap(&a.tv);
@@ -458,7 +463,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     fence_async_smem();
     sync_tc();
     const uint32_t tm = *tmem_slot;
-    const uint32_t tS = tm + T_S, tDT = tm + T_DT;
+    const uint32_t tS = tm + T_S, tDT = tm + T_DT, tDT2 = tm + T_DT2;
     const uint32_t lb = (uint32_t)(32 * lg) << 16;
     const uint32_t sb = smem_u32(sm);
     bool ok = true;
@@ -592,25 +597,34 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         }
         fence_async_smem();
         sync_tc();
-        // C. issuer: Delta^T = V^T TV^T + S0^T (-W)^T (hi + lo) -> bar_g; O = [Qg; -] S0hi -> bar_q; the next loads.
+        // C. warp 16: Delta^T = V^T TV^T + S0hi^T (-W)^T -> bar_g, then the next -W, TV, V; warp 17:
+        //    Delta2^T = S0lo^T (-W)^T -> bar_g2, O = [Qg; -] S0hi -> bar_q, then this chunk's P.
         //    Warps 8, 9, 12, 13 meanwhile emit the previous chunk's outputs.
         if (issuer) {
             const uint32_t idU = idesc_bf16(128, 64, 1, 0), idD = idesc_bf16(128, 64, 0, 0);
-            const uint32_t idO = idesc_bf16(128, 128, 0, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tDT, desc_mnmajor(sb + OFF_V + ks * 2048, 8192), desc_kmajor(sb + OFF_TV + ks * 32), idU,
                           ks > 0);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks) {
-                    const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                    const uint32_t s0 = h ? sb + OFF_QL + kb * QL_BLK + 8192 : sb + OFF_S0 + kb * 16384;
-                    umma_bf16(tDT, desc_kmajor(s0 + ko), desc_kmajor(sb + OFF_W + kb * 8192 + ko), idD, 1);
-                }
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                umma_bf16(tDT, desc_kmajor(sb + OFF_S0 + kb * 16384 + ko), desc_kmajor(sb + OFF_W + kb * 8192 + ko),
+                          idD, 1);
             }
             umma_commit(bar_g);
+            wait_bar(bar_g, par, a.err, 55, ok);
+            wait_bar(bar_g2, par, a.err, 64, ok);
+            if (c + 1 < nchunks) issue_l1_a(c + 1);  // -W, TV, V have been read
+        } else if (issuer2) {
+            const uint32_t idD = idesc_bf16(128, 64, 0, 0), idO = idesc_bf16(128, 128, 0, 0);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                umma_bf16(tDT2, desc_kmajor(sb + OFF_QL + kb * QL_BLK + 8192 + ko),
+                          desc_kmajor(sb + OFF_W + kb * 8192 + ko), idD, ks > 0);
+            }
+            umma_commit(bar_g2);
             const uint32_t tO = tm + T_O + par * 128;
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
@@ -623,8 +637,6 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
                 wait_bar(bar_o, par ^ 1u, a.err, 54, ok);  // the P tiles of chunk c-1 have been read
                 issue_l3(c);
             }
-            wait_bar(bar_g, par, a.err, 55, ok);
-            if (c + 1 < nchunks) issue_l1_a(c + 1);  // -W, TV, V have been read
         } else if (out_warp && c > 0) {
             wait_bar(bar_o, par ^ 1u, a.err, 56, ok);
             tc_fence_after();
@@ -634,11 +646,15 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         if (tid < NWORK) {
             if (c > 0) wait_bar(bar_o, par ^ 1u, a.err, 57, ok);  // the previous P Delta has read the tiles
             wait_bar(bar_g, par, a.err, 58, ok);
+            wait_bar(bar_g2, par, a.err, 65, ok);
             tc_fence_after();
-            float v[16], x[16];
+            float v[16], v2[16], x[16];
             tmem_ld16(tDT + lb + 16 * cq, v);
+            tmem_ld16(tDT2 + lb + 16 * cq, v2);
             vload(vec, 16 * cq, x);
             tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] += v2[e];
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 float d[8];
@@ -656,12 +672,12 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         }
         fence_async_smem();
         sync_tc();
-        // E. issuer: S^T += Dd^T K (hi + lo) -> bar_s; O += P Delta (hi.hi + lo.hi + hi.lo) -> bar_o; Qg and
-        //    vectors of the next chunk
+        // E. warp 16: S^T += Dd^T K (hi + lo) -> bar_s; warp 17: the next chunk's Qg and vectors, then
+        //    O += P Delta (hi.hi + lo.hi + hi.lo) -> bar_o
         if (issuer) {
             wait_bar(bar_l2, par, a.err, 59, ok);
             tc_fence_after();
-            const uint32_t idS = idesc_bf16(128, 128, 0, 1), idO = idesc_bf16(128, 128, 0, 0);
+            const uint32_t idS = idesc_bf16(128, 128, 0, 1);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const uint32_t dd = sb + (h ? OFF_DDL : OFF_DDH);
@@ -670,8 +686,14 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
                     umma_bf16(tS, desc_kmajor(dd + ks * 32), desc_mnmajor(sb + OFF_K + ks * 2048, 8192), idS, 1);
             }
             umma_commit(bar_s);
+        } else if (issuer2) {
+            if (c + 1 < nchunks) {
+                wait_bar(bar_q, par, a.err, 61, ok);  // Qg of chunk c has been read
+                issue_l1_b(c + 1);
+            }
             wait_bar(bar_l3, par, a.err, 60, ok);
             tc_fence_after();
+            const uint32_t idO = idesc_bf16(128, 128, 0, 0);
             const uint32_t tO = tm + T_O + par * 128;
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
@@ -681,10 +703,6 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
                 umma_bf16(tO, desc_kmajor(sb + OFF_PH + ks * 32), dl, idO, 1);
             }
             umma_commit(bar_o);
-            if (c + 1 < nchunks) {
-                wait_bar(bar_q, par, a.err, 61, ok);  // Qg of chunk c has been read
-                issue_l1_b(c + 1);
-            }
         }
     }
     // the last chunk's outputs and the final state
