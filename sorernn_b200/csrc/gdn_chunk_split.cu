@@ -374,7 +374,8 @@ static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 // TMEM columns: S^T [dv][dk], Delta^T [dv][j] (the S0 hi part, and the S0 lo part: 64 each), two output
 // accumulators (rows 0-63 used)
 constexpr uint32_t T_S = 0, T_DT = 128, T_DT2 = 192, T_O = 256, T_COLS = 512;
-constexpr uint32_t TX_L1 = 2 * 8192 + 8192 + 2 * 8192 + 2 * 8192 + kFwdRecVecBytes;  // W, TV, V, Qg, vectors
+constexpr uint32_t TX_L1 = 2 * 8192 + 8192 + 2 * 8192;  // -W, TV, V
+constexpr uint32_t TX_LB = 2 * 8192 + kFwdRecVecBytes;  // Qg, vectors
 }  // namespace cs
 
 struct ChunkStateArgs {
@@ -412,7 +413,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bar = (uint64_t*)(sm + OFF_BAR);
-    uint64_t* bar_l1 = bar;      // -W, TV, V, Qg, vectors of a chunk
+    uint64_t* bar_l1 = bar;      // -W, TV, V of a chunk
     uint64_t* bar_l2 = bar + 1;  // K
     uint64_t* bar_l3 = bar + 2;  // P hi/lo
     uint64_t* bar_g = bar + 3;   // Delta^T products done
@@ -420,7 +421,9 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     uint64_t* bar_s = bar + 5;   // state update done
     uint64_t* bar_o = bar + 6;   // P Delta done
     uint64_t* bar_g2 = bar + 7;  // Delta^T product with S0 lo done
-    uint32_t* tmem_slot = (uint32_t*)(bar + 8);
+    uint64_t* bar_lb = bar + 8;  // Qg and vectors of a chunk
+    uint64_t* bar_od = bar + 9;  // the output step of a chunk has read its vector buffer (4 warps arrive)
+    uint32_t* tmem_slot = (uint32_t*)(bar + 10);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool issuer = tid == NWORK;        // warp 16, lane 0: the state chain
@@ -453,7 +456,8 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     }
 
     if (issuer) {
-        for (int i = 0; i < 8; ++i) mbar_init(&bar[i], 1);
+        for (int i = 0; i < 9; ++i) mbar_init(&bar[i], 1);
+        mbar_init(bar_od, 4);
         fence_barrier_init();
         prefetch_tmap(&a.tk);
         prefetch_tmap(&a.tv);
@@ -482,9 +486,9 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     }
 
     auto recp = [&](int c) { return a.rec + ((cb + c) * a.HV + hv) * kFwdRecordBytes; };
-    // bar_l1 phase of chunk c: -W, TV, V (issued once the Delta^T products of chunk c-1 have read them), then
-    // Qg (once the output product of chunk c-1 has read it) and the vectors (once the output step of chunk c-2
-    // has read that buffer)
+    // -W, TV, V of chunk c (bar_l1; issued once the Delta^T products of chunk c-1 have read them) and Qg and
+    // the vectors (bar_lb; once the output product of chunk c-1 has read Qg and the output step of chunk c-2
+    // has read that vector buffer)
     auto issue_l1_a = [&](int c) {
         const int tok0 = (int)(bos + 64 * c);
         const uint8_t* r = recp(c);
@@ -496,6 +500,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     };
     auto issue_l1_b = [&](int c) {
         const uint8_t* r = recp(c);
+        mbar_arrive_expect_tx(bar_lb, TX_LB);
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb) bulk_g2s(sm + OFF_QL + kb * QL_BLK, r + kFwdRecQg + kb * 8192, 8192, bar_l1);
         bulk_g2s(sm + OFF_VEC + (c & 1) * kFwdRecVecBytes, r + kFwdRecVec, kFwdRecVecBytes, bar_l1);
@@ -556,8 +561,8 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     for (int c = 0; c < nchunks; ++c) {
         const uint32_t par = (uint32_t)c & 1u;
         const float* vec = (const float*)(sm + OFF_VEC + par * kFwdRecVecBytes);
-        // A. this chunk's tiles and vectors; the previous chunk's state update and output product have landed
-        wait_bar(bar_l1, par, a.err, 51, ok);
+        // A. this chunk's Qg and vectors; the previous chunk's state update and output product have landed
+        wait_bar(bar_lb, par, a.err, 51, ok);
         if (c > 0) {
             wait_bar(bar_s, par ^ 1u, a.err, 52, ok);
             wait_bar(bar_q, par ^ 1u, a.err, 53, ok);
@@ -601,6 +606,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         //    Delta2^T = S0lo^T (-W)^T -> bar_g2, O = [Qg; -] S0hi -> bar_q, then this chunk's P.
         //    Warps 8, 9, 12, 13 meanwhile emit the previous chunk's outputs.
         if (issuer) {
+            wait_bar(bar_l1, par, a.err, 66, ok);
             const uint32_t idU = idesc_bf16(128, 64, 1, 0), idD = idesc_bf16(128, 64, 0, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
@@ -613,10 +619,8 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
                           idD, 1);
             }
             umma_commit(bar_g);
-            wait_bar(bar_g, par, a.err, 55, ok);
-            wait_bar(bar_g2, par, a.err, 64, ok);
-            if (c + 1 < nchunks) issue_l1_a(c + 1);  // -W, TV, V have been read
         } else if (issuer2) {
+            wait_bar(bar_l1, par, a.err, 67, ok);
             const uint32_t idD = idesc_bf16(128, 64, 0, 0), idO = idesc_bf16(128, 128, 0, 0);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
@@ -637,10 +641,17 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
                 wait_bar(bar_o, par ^ 1u, a.err, 54, ok);  // the P tiles of chunk c-1 have been read
                 issue_l3(c);
             }
+            if (c + 1 < nchunks) {  // Qg of chunk c read by the output product, vectors of c-1 by the output step
+                wait_bar(bar_q, par, a.err, 61, ok);
+                if (c > 0) wait_bar(bar_od, par ^ 1u, a.err, 68, ok);
+                issue_l1_b(c + 1);
+            }
         } else if (out_warp && c > 0) {
             wait_bar(bar_o, par ^ 1u, a.err, 56, ok);
             tc_fence_after();
             output_step(c - 1);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_od);
         }
         // D. Delta^T (TMEM, lanes = dv) -> Delta^T and Dd^T hi/lo tiles (all 16 warps, 16 tokens each)
         if (tid < NWORK) {
@@ -686,11 +697,8 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
                     umma_bf16(tS, desc_kmajor(dd + ks * 32), desc_mnmajor(sb + OFF_K + ks * 2048, 8192), idS, 1);
             }
             umma_commit(bar_s);
+            if (c + 1 < nchunks) issue_l1_a(c + 1);  // the Delta^T products (bar_g, bar_g2 waited) read -W, TV, V
         } else if (issuer2) {
-            if (c + 1 < nchunks) {
-                wait_bar(bar_q, par, a.err, 61, ok);  // Qg of chunk c has been read
-                issue_l1_b(c + 1);
-            }
             wait_bar(bar_l3, par, a.err, 60, ok);
             tc_fence_after();
             const uint32_t idO = idesc_bf16(128, 128, 0, 0);
