@@ -502,8 +502,8 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         const uint8_t* r = recp(c);
         mbar_arrive_expect_tx(bar_lb, TX_LB);
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb) bulk_g2s(sm + OFF_QL + kb * QL_BLK, r + kFwdRecQg + kb * 8192, 8192, bar_l1);
-        bulk_g2s(sm + OFF_VEC + (c & 1) * kFwdRecVecBytes, r + kFwdRecVec, kFwdRecVecBytes, bar_l1);
+        for (int kb = 0; kb < 2; ++kb) bulk_g2s(sm + OFF_QL + kb * QL_BLK, r + kFwdRecQg + kb * 8192, 8192, bar_lb);
+        bulk_g2s(sm + OFF_VEC + (c & 1) * kFwdRecVecBytes, r + kFwdRecVec, kFwdRecVecBytes, bar_lb);
     };
     auto issue_l2 = [&](int c) {  // K of chunk c
         const int tok0 = (int)(bos + 64 * c);
