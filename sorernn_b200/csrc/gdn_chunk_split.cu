@@ -100,12 +100,13 @@ constexpr uint32_t OFF_QK = 0;       // per d-block kb (16 KB apart): [Q 8 KB | 
 constexpr uint32_t OFF_A = 32768;    // fp32 A / T, 64 x AST
 constexpr int AST = 68;
 constexpr uint32_t OFF_Y = OFF_A + 64 * AST * 4;       // solve scratch
-constexpr uint32_t OFF_TB = 55296;                     // TB bf16 [i][j] 8 KB, then TV: [TB; TV] is MMA2's A
-constexpr uint32_t OFF_VEC = OFF_TB + 16384;           // G, EG, B, NQ, NK: 5 x 64 fp32
+constexpr uint32_t OFF_TB = OFF_A;                     // after the solve: TB bf16 [i][j] 8 KB, then TV: [TB; TV]
+                                                       // is MMA2's A (T is read into registers first)
+constexpr uint32_t OFF_VEC = OFF_Y + 32 * kSolveYStride * 4;  // G, EG, B, NQ, NK: 5 x 64 fp32
 constexpr uint32_t OFF_BAR = OFF_VEC + 5 * 256;
-constexpr uint32_t SMEM_BYTES = OFF_BAR + 64 + 1024;   // three CTAs per SM
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 64 + 1024;   // four CTAs per SM
 constexpr uint32_t T_COLS = 128;                       // D1 in columns 0-63, then W in 0-127
-static_assert(OFF_Y + 32 * kSolveYStride * 4 <= OFF_TB, "solve scratch overlaps TB");
+static_assert(SMEM_BYTES + 1024 <= 233472 / 4, "four CTAs per SM");
 }  // namespace cp
 
 struct ChunkPrepArgs {
@@ -121,7 +122,7 @@ struct ChunkPrepArgs {
     float scale;
 };
 
-__global__ void __launch_bounds__(cp::NTHR, 3) chunk_prep_kernel(const __grid_constant__ ChunkPrepArgs a) {
+__global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_constant__ ChunkPrepArgs a) {
     using namespace cp;
     using namespace split;
     extern __shared__ uint8_t smem_raw[];
@@ -255,11 +256,13 @@ __global__ void __launch_bounds__(cp::NTHR, 3) chunk_prep_kernel(const __grid_co
         tmem_wait_ld();
         const int i = row & 63;
         const float gi = vG[i];
+        // rows 32 lg' .. (lg' = lg & 1) against columns 32 hf ..: the block above the diagonal is all zero
+        const bool zero_blk = hf > (lg & 1);
         if (lg < 2) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 const int jj = 32 * hf + j;
-                v[j] = (jj <= i) ? a.scale * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
+                v[j] = (!zero_blk && jj <= i) ? a.scale * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
             }
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -274,7 +277,7 @@ __global__ void __launch_bounds__(cp::NTHR, 3) chunk_prep_kernel(const __grid_co
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 const int jj = 32 * hf + j;
-                v[j] = (jj < i) ? bi * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
+                v[j] = (!zero_blk && jj < i) ? bi * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
             }
             float4* dst = reinterpret_cast<float4*>(Am + i * AST + 32 * hf);
 #pragma unroll
@@ -285,15 +288,24 @@ __global__ void __launch_bounds__(cp::NTHR, 3) chunk_prep_kernel(const __grid_co
     // T = (I + A)^-1 in place (all 8 warps)
     tri_inverse64<AST>(Am, Yb);
     __syncthreads();
-    // TB = T diag(beta e^G nk), TV = T diag(beta): bf16 K-major [i][j] tiles in shared memory (MMA2's A);
-    // TV also to the record
+    // TB = T diag(beta e^G nk), TV = T diag(beta): bf16 K-major [i][j] tiles in shared memory (MMA2's A, over
+    // the T region: every thread reads its T elements first); TV also to the record
+    float tr[2][8];
 #pragma unroll
     for (int it = 0; it < 2; ++it) {
         const int wl = tid & 31, qq = wl >> 3, sub = wl & 7;
         const int i = 32 * it + 4 * warp + 2 * (qq & 1) + (sub >> 2), c8 = 8 * ((sub & 3) + 4 * (qq >> 1));
         const float4 t0 = *reinterpret_cast<const float4*>(Am + i * AST + c8);
         const float4 t1 = *reinterpret_cast<const float4*>(Am + i * AST + c8 + 4);
-        const float t[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+        tr[it][0] = t0.x; tr[it][1] = t0.y; tr[it][2] = t0.z; tr[it][3] = t0.w;
+        tr[it][4] = t1.x; tr[it][5] = t1.y; tr[it][6] = t1.z; tr[it][7] = t1.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+        const int wl = tid & 31, qq = wl >> 3, sub = wl & 7;
+        const int i = 32 * it + 4 * warp + 2 * (qq & 1) + (sub >> 2), c8 = 8 * ((sub & 3) + 4 * (qq >> 1));
+        const float* t = tr[it];
         float b8[8], e8[8], n8[8], tb[8], tv[8];
         vload(vB, c8, b8);
         vload(vEG, c8, e8);
