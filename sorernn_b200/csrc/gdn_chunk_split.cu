@@ -67,6 +67,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  "l"((uint64_t)src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+// bulk (TMA engine) copy shared -> global in this thread's bulk group; wait until the group's reads are done
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"((uint64_t)dst), "r"(smem_u32(src)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // L2 prefetches: a chunk's operands are brought into L2 two chunks before its shared-memory loads
 __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((uint64_t)src), "r"(bytes) : "memory");
@@ -228,13 +237,15 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
         if (tid == 0) rv[128] = __expf(vG[63]);
     }
     __syncthreads();
-    // Qg = diag(scale e^G) Q (raw q rows) to the record, in the tile's own swizzled layout: 16-byte chunks,
-    // each scaled by its row's factor
+    wait_bar(bar_mma, 0, a.err, 42, ok);
+    tc_fence_after();
+    // Qg = diag(scale e^G) Q (raw q rows), in place in the Q tile (MMA1 has read it), then one bulk store per
+    // d-block: 16-byte chunks keep the tile's swizzled layout, each scaled by its row's factor
 #pragma unroll
     for (int it = 0; it < 4; ++it) {
         const int e = tid + 256 * it, i = e >> 4, kb = (e >> 3) & 1, ch = e & 7;
-        const uint32_t off = kb * 16384 + i * 128 + ch * 16;
-        const uint4 u = *reinterpret_cast<const uint4*>(sm + OFF_QK + off);
+        uint4* pc = reinterpret_cast<uint4*>(sm + OFF_QK + kb * 16384 + i * 128 + ch * 16);
+        const uint4 u = *pc;
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
         const float f = a.scale * vEG[i];
         float y[8];
@@ -244,11 +255,16 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
             y[2 * k2] = z.x * f;
             y[2 * k2 + 1] = z.y * f;
         }
-        *reinterpret_cast<uint4*>(rec + kFwdRecQg + kb * 8192 + i * 128 + ch * 16) = pack8(y);
+        *pc = pack8(y);
     }
-    wait_bar(bar_mma, 0, a.err, 42, ok);
-    tc_fence_after();
-    // D1 rows 0-63 -> P hi/lo (straight to the record), rows 64-127 -> A (fp32, shared memory)
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+        bulk_s2g(rec + kFwdRecQg, sm + OFF_QK, 8192);
+        bulk_s2g(rec + kFwdRecQg + 8192, sm + OFF_QK + 16384, 8192);
+        bulk_commit();
+    }
+    // D1 rows 0-63 -> P hi/lo (staged in the Q slots once Qg has left), rows 64-127 -> A (fp32, shared memory)
     {
         float v[32];
         tmem_ld16(tm + lb + 32 * hf, *reinterpret_cast<float(*)[16]>(v));
@@ -264,14 +280,6 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
                 const int jj = 32 * hf + j;
                 v[j] = (!zero_blk && jj <= i) ? a.scale * v[j] * vNK[jj] * __expf(gi - vG[jj]) : 0.f;
             }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint4 hi, lo;
-                split8(v + 8 * q, hi, lo);
-                const uint32_t off = sw128_off(i, 32 * hf + 8 * q);
-                *reinterpret_cast<uint4*>(rec + kFwdRecP + off) = hi;
-                *reinterpret_cast<uint4*>(rec + kFwdRecP + 8192 + off) = lo;
-            }
         } else {
             const float bi = vB[i] * vNK[i];
 #pragma unroll
@@ -282,6 +290,25 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
             float4* dst = reinterpret_cast<float4*>(Am + i * AST + 32 * hf);
 #pragma unroll
             for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+        if (tid == 0) bulk_wait_read();  // the Qg stores have read the Q slots
+        __syncthreads();
+        if (lg < 2) {  // P hi into the d-block-0 Q slot, P lo into the d-block-1 Q slot
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint4 hi, lo;
+                split8(v + 8 * q, hi, lo);
+                const uint32_t off = sw128_off(i, 32 * hf + 8 * q);
+                *reinterpret_cast<uint4*>(sm + OFF_QK + off) = hi;
+                *reinterpret_cast<uint4*>(sm + OFF_QK + 16384 + off) = lo;
+            }
+        }
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            bulk_s2g(rec + kFwdRecP, sm + OFF_QK, 8192);
+            bulk_s2g(rec + kFwdRecP + 8192, sm + OFF_QK + 16384, 8192);
+            bulk_commit();
         }
     }
     sync_tc();
@@ -316,13 +343,15 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
             tb[j] = tv[j] * e8[j] * n8[j];
         }
         const uint32_t off = sw128_off(i, c8);
-        const uint4 uv = pack8(tv);
         *reinterpret_cast<uint4*>(sm + OFF_TB + off) = pack8(tb);
-        *reinterpret_cast<uint4*>(sm + OFF_TB + 8192 + off) = uv;
-        *reinterpret_cast<uint4*>(rec + kFwdRecTV + off) = uv;
+        *reinterpret_cast<uint4*>(sm + OFF_TB + 8192 + off) = pack8(tv);
     }
     fence_async_smem();
     sync_tc();
+    if (tid == 0) {
+        bulk_s2g(rec + kFwdRecTV, sm + OFF_TB + 8192, 8192);
+        bulk_commit();
+    }
     // MMA2: [W; TV K] = [TB; TV] K  (M = 128, N = 128 = dk, K = 64 tokens); W rows on lanes 0-63
     if (tid == 0) {
         const uint32_t id = idesc_bf16(128, 128, 0, 1);
@@ -334,11 +363,14 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
     }
     wait_bar(bar_mma, 1, a.err, 43, ok);
     tc_fence_after();
-    // -W (bf16, K-major [i][dk]) to the record: warps of lanes 0-63, 64 columns each
+    // -W (bf16, K-major [i][dk]) staged in the Q slots (the P stores have read them), then bulk-stored:
+    // warps of lanes 0-63, 64 columns (one d-block) each
+    if (tid == 0) bulk_wait_read();
+    __syncthreads();
     if (lg < 2) {
-        uint8_t* dst = rec + kFwdRecW + hf * 8192;
+        uint8_t* dst = sm + OFF_QK + hf * 16384;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {  // two halves of 32 columns (the register cap of three CTAs per SM)
+        for (int h = 0; h < 2; ++h) {  // two halves of 32 columns (the register cap of four CTAs per SM)
             float v[32];
             tmem_ld16(tm + lb + 64 * hf + 32 * h, *reinterpret_cast<float(*)[16]>(v));
             tmem_ld16(tm + lb + 64 * hf + 32 * h + 16, *reinterpret_cast<float(*)[16]>(v + 16));
@@ -349,6 +381,14 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
             for (int q = 0; q < 4; ++q)
                 *reinterpret_cast<uint4*>(dst + sw128_off(row, 32 * h + 8 * q)) = pack8(v + 8 * q);
         }
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+        bulk_s2g(rec + kFwdRecW, sm + OFF_QK, 8192);
+        bulk_s2g(rec + kFwdRecW + 8192, sm + OFF_QK + 16384, 8192);
+        bulk_commit();
+        bulk_wait_all();  // the record is in global memory before the CTA ends
     }
     sync_tc();
     if (warp == 0) tmem_dealloc(tm, T_COLS);
