@@ -141,6 +141,15 @@ __device__ __forceinline__ void ld16x2(uint32_t ta, float (&va)[16], uint32_t tb
     tmem_ld16(tb, vb);
     tmem_wait_ld();
 }
+// L2 prefetches: a chunk's tiles and record are brought into L2 two chunks before their shared-memory loads
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((uint64_t)src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_tile_l2(const CUtensorMap* map, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"((uint64_t)map), "r"(c0),
+                 "r"(c1), "r"(c2)
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_u32(dst)),
@@ -311,9 +320,21 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         bulk_load(sm + OFF_W, rec + kBwdRecW, 24576, bar_in);  // -W | T, contiguous here and there
         bulk_load(sm + OFF_DEL, rec + kBwdRecDel, 16384, bar_in);
     };
+    auto prefetch_chunk = [&](int c) {  // every tile and the record chunk c reads, into L2
+        const int tok0 = (int)(bos + 64 * c);
+#pragma unroll 1
+        for (int kb = 0; kb < 2; ++kb) {
+            prefetch_tile_l2(&a.tq, kb * 64, hq, tok0);
+            prefetch_tile_l2(&a.tk, kb * 64, hq, tok0);
+            prefetch_tile_l2(&a.tdo, kb * 64, hv, tok0);
+            prefetch_tile_l2(&a.tv, kb * 64, hv, tok0);
+        }
+        prefetch_l2(a.s0_tiles + ((cbase + c) * a.HV + hv) * kBwdRecordBytes, (uint32_t)kBwdRecordBytes);
+    };
     if (tid == 0 && nchunks > 0) {
         issue_inputs_a(nchunks - 1);
         issue_inputs_b(nchunks - 1);
+        if (nchunks > 1) prefetch_chunk(nchunks - 2);
     }
     uint32_t in_phase = 0, v_phase = 0;
     const uint32_t aQ = sb + OFF_QK, aK = sb + OFF_QK + 8192, aV = sb + OFF_V, aDO = sb + OFF_DO;
@@ -330,6 +351,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
     for (int c = nchunks - 1; c >= 0; --c) {
         const int64_t tok0 = bos + 64 * (int64_t)c;
         const int nv = (len - 64 * (int64_t)c) < 64 ? (int)(len - 64 * (int64_t)c) : 64;
+        if (tid == 0 && c >= 2) prefetch_chunk(c - 2);
 
         // ---- 1. gates; wait for this chunk's tiles ------------------------------------------------------
         if (tid < 64) {
