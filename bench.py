@@ -321,6 +321,53 @@ def activation_memory(leaf, do, step, zero):
             "note": "torch.cuda.memory_allocated / max_memory_allocated around one call"}
 
 
+def config2_layer_bench(dev, world, reps=5):
+    """Config 2's GDN mixer layer (d_model 1536, 16 q/k heads and 16 v heads of 128, short conv K = 4,
+    gate and beta activations in kernel, fused RMSNorm(o)*silu(gate)) through sorernn_b200.layer, fwd+bwd
+    under bf16 autocast at batch 8 x 4096 (packed as one 32,768-token micro-batch of 8 documents, as the
+    reference's trainer and bench pack, scripts/bench.py:84-111). The model's other layers (6 attention
+    layers, SwiGLU FFNs, embeddings, MTP head) belong to the reference and are not built here; 18 of its
+    24 layers are this one. Returns ms per layer call, tokens/s and the peak device memory of one call."""
+    import torch
+
+    from sorernn_b200.layer import GatedDeltaNet
+
+    B, T, d = 8, 4096, 1536
+    gen = torch.Generator(device=dev).manual_seed(9)
+    torch.manual_seed(9)
+    layer = GatedDeltaNet(d, 16, 16, 128).to(dev)
+    x = (torch.randn(1, B * T, d, device=dev, generator=gen) * 0.5).requires_grad_(True)
+    dy = torch.randn(1, B * T, d, device=dev, generator=gen)
+    cu_cpu = torch.arange(0, B * T + 1, T, dtype=torch.int64)
+    cu = cu_cpu.to(dev)
+
+    def call():
+        x.grad = None
+        layer.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = layer(x, cu_seqlens=cu, cu_seqlens_cpu=cu_cpu)
+        y.backward(dy)
+
+    call()
+    barrier(world)
+    torch.cuda.reset_peak_memory_stats(dev)
+    base = torch.cuda.memory_allocated(dev)
+    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(reps):
+        call()
+    e0.record()
+    barrier(world)
+    ms = max_over_ranks(s0.elapsed_time(e0) / reps, world)
+    peak = torch.cuda.max_memory_allocated(dev) - base
+    return {"workload": "config2 GDN layer: d_model 1536, 16+16 heads x 128, conv 4, gate in kernel, fused "
+                        "norm-gate, 8 documents x 4096 packed, bf16 autocast, fwd+bwd",
+            "ms_per_layer": round(ms, 3), "tokens_per_s_per_layer": round(B * T / (ms / 1e3), 1),
+            "gdn_layers_in_model": 18, "ms_gdn_share_of_step": round(18 * ms, 2),
+            "peak_bytes_per_call": int(peak),
+            "not_built": "attention, FFN, embedding and MTP layers of SoreLM (reference code, out of scope)"}
+
+
 def strong_scaling_bench(dev, rank, world, step, steps):
     """Config 1 with its total work fixed: the B=8 rows (x 16 heads) are split across the ranks (B/N rows
     per rank, i.e. 128/N (sequence, head) units) and every rank times fwd+bwd of its share; value = the
@@ -482,6 +529,7 @@ def run_ours(args):
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e2e_steps, world)
 
     strong = strong_scaling_bench(dev, rank, world, step, args.steps)
+    config2 = config2_layer_bench(dev, world)
     dec_ms, dec_bytes = decode_bench(dev, rank, world)
     long_prefill = long_prefill_bench(dev, rank, world)
     peaks, peak_kind = load_peaks()
@@ -527,6 +575,7 @@ def run_ours(args):
         "layer_ops": layer_ops,
         "activation_memory": mem,
         "config1_strong": strong,
+        "config2_gdn_layer": config2,
     }
     if rank == 0:
         if world == 1:  # the host-core baseline is timed at N=1 only
