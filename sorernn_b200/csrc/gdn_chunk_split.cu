@@ -654,8 +654,8 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         }
         fence_async_smem();
         sync_tc();
-        // C. warp 16: Delta^T = V^T TV^T + S0hi^T (-W)^T -> bar_g, then the next -W, TV, V; warp 17:
-        //    Delta2^T = S0lo^T (-W)^T -> bar_g2, O = [Qg; -] S0hi -> bar_q, then this chunk's P.
+        // C. warp 16: Delta^T = V^T TV^T + S0hi^T (-W)^T -> bar_g; warp 17: Delta2^T = S0lo^T (-W)^T -> bar_g2,
+        //    O = [Qg; -] (S0hi + S0lo) -> bar_q, then this chunk's P and the next chunk's Qg and vectors.
         //    Warps 8, 9, 12, 13 meanwhile emit the previous chunk's outputs.
         if (issuer) {
             wait_bar(bar_l1, par, a.err, 66, ok);
@@ -683,10 +683,14 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             umma_commit(bar_g2);
             const uint32_t tO = tm + T_O + par * 128;
 #pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tO, desc_kmajor(sb + OFF_QL + kb * QL_BLK + ko), desc_kmajor(sb + OFF_S0 + kb * 16384 + ko),
-                          idO, ks > 0);
+            for (int h = 0; h < 2; ++h) {  // Qg (S0hi + S0lo)
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                    const uint32_t s0 = h ? sb + OFF_QL + kb * QL_BLK + 8192 : sb + OFF_S0 + kb * 16384;
+                    umma_bf16(tO, desc_kmajor(sb + OFF_QL + kb * QL_BLK + ko), desc_kmajor(s0 + ko), idO,
+                              h > 0 || ks > 0);
+                }
             }
             umma_commit(bar_q);
             if (c > 0) {
