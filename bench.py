@@ -237,8 +237,9 @@ def layer_ops_bench(dev, world, hbm_peak, reps=10):
     """The layer's neighbouring steps at config-1 sizes (B=8, T=4096, H=16, d=128, bf16): the output step
     RMSNorm(o)*silu(gate) over o [8, 4096, 16, 128] and the q-projection's causal conv + SiLU over
     [8, 4096, 2048] (K = 4), forward and backward through the public ops (torch.autograd.grad, so no
-    gradient accumulation kernels run). HBM-bound: reports GB/s of the algorithmic bytes (each tensor read
-    or written once) per call and its fraction of the measured HBM peak, max over ranks."""
+    gradient accumulation kernels run), one call captured as a CUDA graph and replayed. HBM-bound: reports
+    GB/s of the algorithmic bytes (each tensor read or written once) per call and its fraction of the
+    measured HBM peak, max over ranks."""
     import torch
 
     from sorernn_b200.layer_ops import causal_conv1d, rms_norm_gated
@@ -255,14 +256,26 @@ def layer_ops_bench(dev, world, hbm_peak, reps=10):
     nb = o.numel() * 2  # bytes of one bf16 tensor of this size
 
     def timed(fn):
-        fn()
+        # one fwd+bwd call captured as a CUDA graph and replayed: device time of the kernels, without the
+        # per-call host dispatch of the Python autograd path (which a short op like these can be bound by)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        graph.replay()
         barrier(world)
         s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s0.record()
         for _ in range(reps):
-            fn()
+            graph.replay()
         e0.record()
         barrier(world)
+        del graph
         return max_over_ranks(s0.elapsed_time(e0) / reps, world)
 
     def ng():
