@@ -3,23 +3,30 @@
 //
 // Notation (the algebra of tests/test_chunk_algebra.py, the same as gdn_chunk_fwd.cu): Gamma = in-chunk
 // cumsum of g, E_ij = exp(Gamma_i - Gamma_j), nq_i, nk_j the inverse L2 norms of the raw q/k rows (1 without
-// the norm, 0 on rows past the sequence end), S0 the state at the chunk start.
+// the norm, 0 on rows past the sequence end), S0 the state at the chunk start, S^T its transpose [dv][dk].
 //   A  = strict_lower(diag(beta) (K K^T . nk nk^T) . E)       T = (I + A)^-1
 //   W  = T diag(beta e^Gamma nk) K      U = T diag(beta) V      Delta = U - W S0
-//   O_i = f1_i (Q S0)_i + f2_i (P Delta)_i,   f1 = scale e^Gamma nq,  f2 = nq,
-//         P_ij = scale (q_i . k_j) nk_j E_ij  (j <= i)
+//   O_i = nq_i [ (Qg S0)_i + (P Delta)_i ],   Qg = diag(scale e^Gamma) Q,   P_ij = scale (q_i . k_j) nk_j E_ij
+//         (j <= i)
 //   S1 = e^Gamma_C S0 + K^T diag(e^(Gamma_C - Gamma) nk) Delta
-// Everything except Delta, O and S1 is independent of the state, so it is computed for all (chunk, head)
-// pairs at once by chunk_prep_kernel (8,192 CTAs at B8 T4096 H16, three per SM) and handed to the state pass
-// as one record per (chunk, head) in the workspace: the bf16 operand tiles -W, TV = T diag(beta), P (hi and
-// lo parts) as shared-memory images in the 128-byte-swizzled layout, and the vectors the state pass needs.
-// chunk_state_kernel then runs one CTA per (sequence, value head) that keeps S^T (fp32) in tensor memory and
-// per chunk only forms the S0 operand, Delta and Dd = diag(e^(Gamma_C - Gamma) nk) Delta, and the outputs:
-//   G1:  D = [Z; TV] V + [Q; -W] (S0hi + S0lo)    (M = 128: rows 0-63 Q S0, rows 64-127 U - W S0 = Delta)
-//   G2:  S^T += Dd^T K (hi + lo)                   E = P Delta  (rows 0-63; P and Delta in hi + lo parts)
-// The output step of chunk c-1 (rows 0-63 of D and E, on warps 0-7 of lanes 0-63) runs while warps of lanes
-// 64-127 turn chunk c's Delta into operand tiles, and the E products of chunk c execute on the tensor core
-// while chunk c+1 reads the state out. The raw bf16 q, k, v tiles feed the tensor cores unmodified.
+// Everything except Delta, O and S1 is independent of the state, so chunk_prep_kernel computes it for all
+// (chunk, head) pairs at once (8,192 CTAs of 256 threads at B8 T4096 H16, four per SM: Gram matrix, norms,
+// gates, P, the triangular solve, W) and hands it to the state pass as one record per (chunk, head) in the
+// workspace (kFwdRecordBytes, kernels.h): the bf16 operand tiles Qg, -W, TV = T diag(beta), P hi and lo as
+// shared-memory images in the 128-byte-swizzled layout, staged in shared memory and written by bulk copies,
+// and the vectors e^(Gamma_C - Gamma) nk, nq, e^Gamma_C.
+// chunk_state_kernel runs one CTA per (sequence, value head) that keeps S^T (fp32) in tensor memory. Per
+// chunk, 16 warps turn S into the S0^T hi/lo operand tiles (and scale the TMEM state by e^Gamma_C), then
+//   Delta^T = V^T TV^T + S0hi^T (-W)^T  [+ S0lo^T (-W)^T in a second accumulator]     (M = dv = 128, N = 64)
+//   O      = [Qg; -] (S0hi + S0lo)                                                   (rows 0-63 used)
+// 16 warps turn Delta^T (all 128 TMEM lanes) into the Delta^T and Dd^T = Delta^T diag(e^(Gamma_C - Gamma) nk)
+// hi/lo tiles, and
+//   S^T += Dd^T K (hi + lo)        O += P Delta (hi.hi + lo.hi + hi.lo)
+// Two extra warps only issue the loads and MMAs (a tcgen05.mma every 70-85 cycles from one thread): warp 16
+// the state chain, warp 17 the output products and the loads they read, so issue overlaps the data phases;
+// four warps emit chunk c-1's outputs while the Delta^T products of chunk c run, and every chunk's operands
+// are prefetched into L2 two chunks ahead. The raw bf16 q, k, v tiles feed the tensor cores unmodified;
+// Qg is the one operand rounded from a scaled q.
 #include <cstring>
 
 #include "chunk_common.cuh"
