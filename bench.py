@@ -37,9 +37,10 @@ FWD_FLOP_PER_TOKEN_HEAD = 10 * C * 128 + 6 * 128 * 128 + C * C / 3  # chunked fw
 STRONG_LIMITER = ("each (sequence, head) unit walks its 64 chunks serially in one CTA: with {units} units per "
                   "rank, {units} SMs work and the step time stays the per-unit chain time")
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
-# DRAM bytes (read + write) per launch from ncu captures of this build: the backward pass (recompute +
-# sweep launches) captured at batch 2 and scaled by 4 to batch 8; the decode step at full config-3 size.
-BWD_PASS_TRAFFIC_BYTES = (211.7e6 + 405.3e6) * 4
+# DRAM bytes (read + write) per launch from ncu captures of this build: the backward pass (the reverse-sweep
+# launch over the records the forward saved) captured at batch 2 and scaled by 4 to batch 8; the decode step
+# at full config-3 size.
+BWD_PASS_TRAFFIC_BYTES = (322.8e6 + 81.2e6) * 4
 DECODE_TRAFFIC_BYTES = 271.6e6 + 210.9e6
 
 
@@ -298,39 +299,45 @@ def layer_ops_bench(dev, world, hbm_peak, reps=10):
 
 
 def activation_memory(leaf, do, step, zero):
-    """Device memory of one config-1 fwd+bwd, from the caching allocator's counters: the bytes the forward
-    leaves allocated until the backward (its output o, the final state and the op's own saved tensors:
-    the fp32 state checkpoints every 8 chunks; q, k, v, g, beta are the caller's and not counted) and the
-    backward's peak above that (its transient workspace plus the gradients). Beside them, what storing
-    every chunk's fp32 state would take (FLA's chunk_fwd_h materialises [B, NT, H, 128, 128] in its
-    backward), so that the bytes the checkpoint recompute saves are a measured figure."""
+    """Device memory of one config-1 fwd+bwd in each backward mode, from the caching allocator's counters:
+    the bytes the forward leaves allocated until the backward (its output o, the final state and the op's
+    own saved tensors; q, k, v, g, beta are the caller's and not counted) and the backward's peak above
+    that (its transient workspace plus the gradients). Modes: the default (every chunk's backward record
+    saved, the backward runs the reverse sweep alone) and the recompute mode (fp32 state checkpoints every
+    8 chunks, the backward rebuilds the records first). Beside them, what storing every chunk's fp32 state
+    would take (FLA's chunk_fwd_h materialises [B, NT, H, 128, 128] in its backward)."""
     import torch
 
-    from sorernn_b200.gated_delta_rule import DEFAULT_CKPT_EVERY, chunk_gated_delta_rule
+    from sorernn_b200.gated_delta_rule import DEFAULT_CKPT_EVERY, SAVE_RECORDS, chunk_gated_delta_rule
 
-    zero()
-    torch.cuda.synchronize()
-    base = torch.cuda.memory_allocated()
-    o, _ = chunk_gated_delta_rule(leaf["q"], leaf["k"], leaf["v"], leaf["g"], leaf["beta"],
-                                  use_qk_l2norm_in_kernel=True)
-    torch.cuda.synchronize()
-    held = torch.cuda.memory_allocated() - base
-    o_bytes = o.numel() * o.element_size()
-    torch.cuda.reset_peak_memory_stats()
-    after_fwd = torch.cuda.memory_allocated()
-    o.backward(do)
-    torch.cuda.synchronize()
-    bwd_peak = torch.cuda.max_memory_allocated() - after_fwd
-    grads = sum(t.grad.numel() * t.grad.element_size() for t in leaf.values())
-    del o
-    zero()
+    def one(ckpt_every):
+        zero()
+        torch.cuda.synchronize()
+        base = torch.cuda.memory_allocated()
+        o, _ = chunk_gated_delta_rule(leaf["q"], leaf["k"], leaf["v"], leaf["g"], leaf["beta"],
+                                      use_qk_l2norm_in_kernel=True, ckpt_every=ckpt_every)
+        torch.cuda.synchronize()
+        held = torch.cuda.memory_allocated() - base
+        o_bytes = o.numel() * o.element_size()
+        torch.cuda.reset_peak_memory_stats()
+        after_fwd = torch.cuda.memory_allocated()
+        o.backward(do)
+        torch.cuda.synchronize()
+        bwd_peak = torch.cuda.max_memory_allocated() - after_fwd
+        grads = sum(t.grad.numel() * t.grad.element_size() for t in leaf.values())
+        del o
+        zero()
+        return {"held_fwd_to_bwd_bytes": held, "of_which_output_o": o_bytes, "op_saved_bytes": held - o_bytes,
+                "bwd_peak_above_fwd_bytes": bwd_peak, "of_which_gradients": grads,
+                "bwd_transient_bytes": bwd_peak - grads}
+
     B, T, H, D = leaf["q"].shape
     per_chunk_states = B * H * ((T + 63) // 64) * D * D * 4
-    return {"held_fwd_to_bwd_bytes": held, "of_which_output_o": o_bytes, "op_saved_bytes": held - o_bytes,
-            "bwd_peak_above_fwd_bytes": bwd_peak, "of_which_gradients": grads,
-            "bwd_transient_bytes": bwd_peak - grads, "ckpt_every_chunks": DEFAULT_CKPT_EVERY,
+    saved, recompute = one(SAVE_RECORDS), one(DEFAULT_CKPT_EVERY)
+    recompute["ckpt_every_chunks"] = DEFAULT_CKPT_EVERY
+    return {"saved_records (default)": saved, "recompute": recompute,
             "per_chunk_fp32_states_bytes": per_chunk_states,
-            "saved_vs_per_chunk_states_bytes": per_chunk_states - (held - o_bytes),
+            "recompute_saves_vs_per_chunk_states_bytes": per_chunk_states - recompute["op_saved_bytes"],
             "note": "torch.cuda.memory_allocated / max_memory_allocated around one call"}
 
 
@@ -570,7 +577,7 @@ def run_ours(args):
         "gpu_launches": int(launches),
         "kernels": {"fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
                     "fwd_tflops": round(fwd_flop / (fwd_ms / 1e3) / 1e12, 2)},
-        "roofline": {"bound": "tensor", "kernel": "backward pass (recompute + reverse-sweep launches)",
+        "roofline": {"bound": "tensor", "kernel": "backward pass (reverse-sweep launch over the saved records)",
                      "achieved": round(achieved_bwd, 2), "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": round(achieved_bwd / peak_tf, 4),
                      "peak_source": f"{peak_kind} bf16_tflops_sustained (of {peak_kind})",

@@ -109,6 +109,29 @@ int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void
                   const float* dht, void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0,
                   void* workspace, size_t workspace_bytes, gdn_stream_t stream);
 
+/*
+ * Saved-record variant of the pair above, for problems with gdn_uses_chunk_kernels(p) == 1 (others get
+ * GDN_ERR_SHAPE). gdn_chunk_fwd_save is gdn_chunk_fwd that, in place of the sparse checkpoints, also writes
+ * the backward's per-(64-token chunk, value head) record into `saved` (gdn_chunk_saved_bytes(p) bytes,
+ * 16-byte aligned; 88 KB per chunk-head, e.g. 704 MB for 8 x 4,096 tokens x 16 heads): the chunk-start
+ * state S0^T, -W, T = (I + A)^-1, Delta^T and the low part of Dd^T, as bf16 operand tiles. Given those
+ * records, gdn_chunk_bwd_saved (workspace: gdn_chunk_bwd_saved_workspace_size) runs the reverse sweep
+ * without the recompute pass that gdn_chunk_bwd needs. Same results as the checkpoint pair within bf16
+ * rounding of the records; the trade is memory held between the two calls for one pass less.
+ * p->ckpt_every is not used by this pair but must be valid (>= 1). With cu_seqlens the buffer is sized for
+ * the worst split of the tokens; the forward zeroes the slots past the last sequence's chunks.
+ * Replaces: the same two calls as gdn_chunk_fwd / gdn_chunk_bwd (fla chunk.py:365-380, 117-236).
+ */
+size_t gdn_chunk_saved_bytes(const gdn_problem* p);
+size_t gdn_chunk_bwd_saved_workspace_size(const gdn_problem* p);
+int gdn_chunk_fwd_save(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                       const void* beta, const float* initial_state, void* o, float* final_state, void* saved,
+                       void* workspace, size_t workspace_bytes, gdn_stream_t stream);
+int gdn_chunk_bwd_saved(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                        const void* beta, const void* saved, const void* dout, const float* dht, void* dq, void* dk,
+                        void* dv, float* dg, float* dbeta, float* dh0, void* workspace, size_t workspace_bytes,
+                        gdn_stream_t stream);
+
 /* Size of gdn_chunk_bwd_noalloc's fixed scratch array (36 MiB). */
 #define GDN_NOALLOC_SCRATCH_BYTES ((size_t)36 << 20)
 

@@ -36,6 +36,10 @@ SIGNATURES = {
     "gdn_chunk_bwd_workspace_size": (_sz, [_P]),
     "gdn_chunk_fwd": (ctypes.c_int, [_P] + [_vp] * 10 + [_sz, _vp]),
     "gdn_chunk_bwd": (ctypes.c_int, [_P] + [_vp] * 16 + [_sz, _vp]),
+    "gdn_chunk_saved_bytes": (_sz, [_P]),
+    "gdn_chunk_bwd_saved_workspace_size": (_sz, [_P]),
+    "gdn_chunk_fwd_save": (ctypes.c_int, [_P] + [_vp] * 10 + [_sz, _vp]),
+    "gdn_chunk_bwd_saved": (ctypes.c_int, [_P] + [_vp] * 15 + [_sz, _vp]),
     "gdn_decode_step": (ctypes.c_int, [_i64] * 5 + [_f32] + [_i32] * 4 + [_vp] * 7 + [_vp]),
     "gdn_segment_transition": (ctypes.c_int, [_P] + [_vp] * 5 + [_sz, _vp]),
     "gdn_segment_apply_state": (ctypes.c_int, [_P] + [_vp] * 8 + [_sz, _vp]),

@@ -120,13 +120,26 @@ size_t gdn_chunk_fwd_workspace_size(const gdn_problem* p) {
 
 size_t gdn_chunk_bwd_workspace_size(const gdn_problem* p) {
     if (check_problem(p) != GDN_OK) return 0;
-    if (gdn_uses_chunk_kernels(p)) return kErrBytes + chunk_bwd_workspace(p->B, p->T, p->N, p->H, p->HV, p->cu_seqlens);
+    if (gdn_uses_chunk_kernels(p))
+        return kErrBytes + chunk_bwd_workspace(p->B, p->T, p->N, p->H, p->HV, p->cu_seqlens, false);
     return kErrBytes + rec_bwd_workspace(p->N, p->HV, p->DK, p->DV, max_len(p), p->B * p->T, p->H);
 }
 
-int gdn_chunk_fwd(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
-                  const void* beta, const float* initial_state, void* o, float* final_state, float* checkpoints,
-                  void* workspace, size_t workspace_bytes, gdn_stream_t stream) {
+size_t gdn_chunk_saved_bytes(const gdn_problem* p) {
+    if (!gdn_uses_chunk_kernels(p)) return 0;
+    return chunk_saved_bytes(p->B, p->T, p->N, p->HV, p->cu_seqlens != nullptr);
+}
+
+size_t gdn_chunk_bwd_saved_workspace_size(const gdn_problem* p) {
+    if (!gdn_uses_chunk_kernels(p)) return 0;
+    return kErrBytes + chunk_bwd_workspace(p->B, p->T, p->N, p->H, p->HV, p->cu_seqlens, true);
+}
+
+// gdn_chunk_fwd (checkpoints) and gdn_chunk_fwd_save (saved: the backward's per-chunk records)
+static int forward_impl(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                        const void* beta, const float* initial_state, void* o, float* final_state,
+                        float* checkpoints, void* saved, void* workspace, size_t workspace_bytes,
+                        gdn_stream_t stream) {
     int st = check_problem(p);
     if (st != GDN_OK) return st;
     cudaStream_t s = (cudaStream_t)stream;
@@ -154,15 +167,37 @@ int gdn_chunk_fwd(const gdn_problem* p, const void* q, const void* k, const void
         C.B = p->B; C.T = p->T; C.N = p->N; C.H = p->H; C.HV = p->HV; C.max_seqlen = max_len(p);
         C.scale = p->scale; C.g_dtype = p->g_dtype; C.beta_dtype = p->beta_dtype; C.l2norm = p->use_qk_l2norm;
         C.ckpt_every = p->ckpt_every;
+        C.bwd_rec = saved;
         return chunk_fwd_split(C, (char*)workspace + kErrBytes, s);
     }
     return dispatch_forward(p, L, checkpoints, workspace, s);
 }
 
-int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
-                  const void* beta, const float* initial_state, const float* checkpoints, const void* dout,
-                  const float* dht, void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0,
+int gdn_chunk_fwd(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                  const void* beta, const float* initial_state, void* o, float* final_state, float* checkpoints,
                   void* workspace, size_t workspace_bytes, gdn_stream_t stream) {
+    return forward_impl(p, q, k, v, g, beta, initial_state, o, final_state, checkpoints, nullptr, workspace,
+                        workspace_bytes, stream);
+}
+
+int gdn_chunk_fwd_save(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                       const void* beta, const float* initial_state, void* o, float* final_state, void* saved,
+                       void* workspace, size_t workspace_bytes, gdn_stream_t stream) {
+    int st = check_problem(p);
+    if (st != GDN_OK) return st;
+    if (!gdn_uses_chunk_kernels(p)) return GDN_ERR_SHAPE;
+    if (p->B * p->T > 0 && !saved) return GDN_ERR_ARGUMENT;
+    if (saved && !aligned16(saved)) return GDN_ERR_ALIGN;
+    return forward_impl(p, q, k, v, g, beta, initial_state, o, final_state, nullptr, saved, workspace,
+                        workspace_bytes, stream);
+}
+
+// gdn_chunk_bwd (from checkpoints) and gdn_chunk_bwd_saved (from the records gdn_chunk_fwd_save wrote)
+static int backward_impl(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                         const void* beta, const float* initial_state, const float* checkpoints, const void* saved,
+                         const void* dout, const float* dht, void* dq, void* dk, void* dv, float* dg,
+                         float* dbeta, float* dh0, void* workspace, size_t workspace_bytes, size_t workspace_need,
+                         gdn_stream_t stream) {
     int st = check_problem(p);
     if (st != GDN_OK) return st;
     cudaStream_t s = (cudaStream_t)stream;
@@ -175,11 +210,12 @@ int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void
         return e == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
     }
     if (!q || !k || !v || !g || !beta || !dout || !dq || !dk || !dv || !dg || !dbeta) return GDN_ERR_ARGUMENT;
-    if (!workspace || workspace_bytes < gdn_chunk_bwd_workspace_size(p)) return GDN_ERR_WORKSPACE;
+    if (!workspace || workspace_bytes < workspace_need) return GDN_ERR_WORKSPACE;
     if (!aligned16(workspace)) return GDN_ERR_ALIGN;
     if (cudaMemsetAsync(workspace, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
     if (gdn_uses_chunk_kernels(p)) {
-        if (!checkpoints) return GDN_ERR_ARGUMENT;  // the chunked backward restarts from the forward's checkpoints
+        // the chunked backward reads the forward's saved records, or restarts from its checkpoints
+        if (!checkpoints && !saved) return GDN_ERR_ARGUMENT;
         ChunkBwdLaunch C{};
         C.q = q; C.k = k; C.v = v; C.g = g; C.beta = beta; C.dout = dout;
         C.h0 = initial_state; C.ckpt = checkpoints; C.dht = dht;
@@ -188,6 +224,7 @@ int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void
         C.B = p->B; C.T = p->T; C.N = p->N; C.H = p->H; C.HV = p->HV; C.max_seqlen = max_len(p);
         C.scale = p->scale; C.g_dtype = p->g_dtype; C.beta_dtype = p->beta_dtype; C.l2norm = p->use_qk_l2norm;
         C.ckpt_every = p->ckpt_every;
+        C.saved_rec = saved;
         return chunk_bwd(C, s);
     }
     RecLaunch L = rec_launch(p);
@@ -195,6 +232,27 @@ int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void
     L.h0 = initial_state;
     return rec_bwd(L, dout, dht, dq, dk, dv, dg, dbeta, dh0, (char*)workspace + kErrBytes, max_len(p),
                    p->B * p->T, s);
+}
+
+int gdn_chunk_bwd(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                  const void* beta, const float* initial_state, const float* checkpoints, const void* dout,
+                  const float* dht, void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0,
+                  void* workspace, size_t workspace_bytes, gdn_stream_t stream) {
+    return backward_impl(p, q, k, v, g, beta, initial_state, checkpoints, nullptr, dout, dht, dq, dk, dv, dg, dbeta,
+                         dh0, workspace, workspace_bytes, gdn_chunk_bwd_workspace_size(p), stream);
+}
+
+int gdn_chunk_bwd_saved(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                        const void* beta, const void* saved, const void* dout, const float* dht, void* dq, void* dk,
+                        void* dv, float* dg, float* dbeta, float* dh0, void* workspace, size_t workspace_bytes,
+                        gdn_stream_t stream) {
+    int st = check_problem(p);
+    if (st != GDN_OK) return st;
+    if (!gdn_uses_chunk_kernels(p)) return GDN_ERR_SHAPE;
+    if (p->B * p->T > 0 && !saved) return GDN_ERR_ARGUMENT;
+    if (saved && !aligned16(saved)) return GDN_ERR_ALIGN;
+    return backward_impl(p, q, k, v, g, beta, nullptr, nullptr, saved, dout, dht, dq, dk, dv, dg, dbeta, dh0,
+                         workspace, workspace_bytes, gdn_chunk_bwd_saved_workspace_size(p), stream);
 }
 
 int gdn_decode_step(int64_t N, int64_t H, int64_t HV, int64_t DK, int64_t DV, float scale, int32_t act_dtype,

@@ -1005,9 +1005,14 @@ bool chunk_bwd_supported(int64_t DK, int64_t DV, int act_dtype) {
     return DK == 128 && DV == 128 && act_dtype == GDN_BF16;
 }
 
-size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t HV, bool varlen) {
+size_t chunk_saved_bytes(int64_t B, int64_t T, int64_t N, int64_t HV, bool varlen) {
     const int64_t chunks = varlen ? (B * T + 63 * N) / 64 + N : N * ((T + 63) / 64);
-    size_t bytes = (size_t)chunks * HV * kBwdRecordBytes;  // S0^T, TB, TV, T tiles from the recompute pass
+    return (size_t)chunks * HV * kBwdRecordBytes;
+}
+
+size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t HV, bool varlen, bool saved) {
+    // the records of the recompute pass, unless the forward saved them
+    size_t bytes = saved ? 0 : chunk_saved_bytes(B, T, N, HV, varlen);
     if (HV > H) bytes += (size_t)B * T * H * 128 * 4 * 2;  // fp32 dq/dk accumulators (grouped value heads)
     return bytes;
 }
@@ -1015,17 +1020,24 @@ size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t H
 int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s) {
     using namespace cb;
     if (smem_optin((const void*)chunk_bwd_kernel, SMEM_BYTES) != cudaSuccess) return GDN_ERR_LAUNCH;
-    // 1. rebuild every chunk-start state from the checkpoints (segment-parallel forward, no outputs)
-    ChunkLaunch R{};
-    R.q = L.q; R.k = L.k; R.v = L.v; R.g = L.g; R.beta = L.beta; R.o = nullptr;
-    R.h0 = L.h0; R.ht = nullptr; R.ckpt = const_cast<float*>(L.ckpt); R.cu = L.cu; R.err = L.err;
-    R.B = L.B; R.T = L.T; R.N = L.N; R.H = L.H; R.HV = L.HV; R.scale = L.scale;
-    R.g_dtype = L.g_dtype; R.beta_dtype = L.beta_dtype; R.l2norm = L.l2norm; R.o_mode = 2;
-    R.ckpt_every = L.ckpt_every;
-    R.s0_out = L.ws;
-    R.max_seqlen = L.max_seqlen;
-    int st = chunk_fwd(R, s);
-    if (st != GDN_OK) return st;
+    // 1. rebuild every chunk-start state from the checkpoints (segment-parallel forward, no outputs), unless
+    //    the forward saved the records
+    const uint8_t* records = (const uint8_t*)L.saved_rec;
+    uint8_t* scratch = (uint8_t*)L.ws;
+    if (!records) {
+        ChunkLaunch R{};
+        R.q = L.q; R.k = L.k; R.v = L.v; R.g = L.g; R.beta = L.beta; R.o = nullptr;
+        R.h0 = L.h0; R.ht = nullptr; R.ckpt = const_cast<float*>(L.ckpt); R.cu = L.cu; R.err = L.err;
+        R.B = L.B; R.T = L.T; R.N = L.N; R.H = L.H; R.HV = L.HV; R.scale = L.scale;
+        R.g_dtype = L.g_dtype; R.beta_dtype = L.beta_dtype; R.l2norm = L.l2norm; R.o_mode = 2;
+        R.ckpt_every = L.ckpt_every;
+        R.s0_out = L.ws;
+        R.max_seqlen = L.max_seqlen;
+        int st = chunk_fwd(R, s);
+        if (st != GDN_OK) return st;
+        records = (const uint8_t*)L.ws;
+        scratch += chunk_saved_bytes(L.B, L.T, L.N, L.HV, L.cu != nullptr);
+    }
 
     // 2. reverse sweep
     ChunkBwdArgs a;
@@ -1036,13 +1048,12 @@ int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s) {
     if (!make_tmap_3d_sw128(&a.tv, L.v, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
     if (!make_tmap_3d_sw128(&a.tdo, L.dout, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
     const bool acc = L.HV > L.H;
-    const int64_t chunks = L.cu ? (L.B * L.T + 63 * L.N) / 64 + L.N : L.N * ((L.T + 63) / 64);
-    float* acc_q = acc ? (float*)((uint8_t*)L.ws + (size_t)chunks * L.HV * kBwdRecordBytes) : nullptr;
+    float* acc_q = acc ? (float*)scratch : nullptr;
     float* acc_k = acc ? acc_q + Ttot * L.H * 128 : nullptr;
     if (acc && cudaMemsetAsync(acc_q, 0, (size_t)Ttot * L.H * 128 * 4 * 2, s) != cudaSuccess) return GDN_ERR_LAUNCH;
     a.g = L.g;
     a.beta = L.beta;
-    a.s0_tiles = (const uint8_t*)L.ws;
+    a.s0_tiles = records;
     a.dht = L.dht;
     a.dq = acc ? (void*)acc_q : L.dq;
     a.dk = acc ? (void*)acc_k : L.dk;

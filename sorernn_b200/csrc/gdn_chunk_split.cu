@@ -27,6 +27,12 @@
 // four warps emit chunk c-1's outputs while the Delta^T products of chunk c run, and every chunk's operands
 // are prefetched into L2 two chunks ahead. The raw bf16 q, k, v tiles feed the tensor cores unmodified;
 // Qg is the one operand rounded from a scaled q.
+// Saved-record mode (ChunkLaunch::bwd_rec set): the two passes also write the backward sweep's record of every
+// (chunk, head) (kBwdRecordBytes, kernels.h) from what they already hold: the prep pass -W (bulk copies of its
+// staged tile) and T (16-byte stores from registers), the state pass S0^T, Delta^T and the low part of Dd^T:
+// its hi/lo splits round the hi part to nearest, so those staged operand tiles are the record's tiles as they
+// are, and thread 0 bulk-copies them out after each phase's barrier. The backward then skips its recompute
+// pass.
 #include <cstring>
 
 #include "chunk_common.cuh"
@@ -132,6 +138,7 @@ struct ChunkPrepArgs {
     const int64_t* cu;
     const int64_t* cbase;  // varlen: first flattened chunk of each sequence (NULL: n * ceil(T / 64))
     uint8_t* rec;          // kFwdRecordBytes per (flattened chunk, value head)
+    uint8_t* rec_bwd;      // NULL, or the backward's kBwdRecordBytes records: -W and T are written here too
     int* err;
     int64_t T;
     int H, HV, g_dtype, beta_dtype, l2norm;
@@ -352,6 +359,9 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
         const uint32_t off = sw128_off(i, c8);
         *reinterpret_cast<uint4*>(sm + OFF_TB + off) = pack8(tb);
         *reinterpret_cast<uint4*>(sm + OFF_TB + 8192 + off) = pack8(tv);
+        if (a.rec_bwd)  // the backward's T tile (same image layout), straight from registers
+            *reinterpret_cast<uint4*>(a.rec_bwd + ((cb + c) * a.HV + hv) * kBwdRecordBytes + kBwdRecT + off) =
+                pack8(t);
     }
     fence_async_smem();
     sync_tc();
@@ -394,8 +404,13 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
     if (tid == 0) {
         bulk_s2g(rec + kFwdRecW, sm + OFF_QK, 8192);
         bulk_s2g(rec + kFwdRecW + 8192, sm + OFF_QK + 16384, 8192);
+        if (a.rec_bwd) {  // -W for the backward's record too
+            uint8_t* rb = a.rec_bwd + ((cb + c) * a.HV + hv) * kBwdRecordBytes + kBwdRecW;
+            bulk_s2g(rb, sm + OFF_QK, 8192);
+            bulk_s2g(rb + 8192, sm + OFF_QK + 16384, 8192);
+        }
         bulk_commit();
-        bulk_wait_all();  // the record is in global memory before the CTA ends
+        bulk_wait_all();  // the records are in global memory before the CTA ends
     }
     sync_tc();
     if (warp == 0) tmem_dealloc(tm, T_COLS);
@@ -441,6 +456,7 @@ struct ChunkStateArgs {
     CUtensorMap tk, tv;
     const uint8_t* rec;
     const int64_t* cbase;
+    uint8_t* rec_bwd;  // NULL, or the backward's records: S0^T, Delta^T and the low part of Dd^T are written here
     void* o;
     const float* h0;
     float* ht;
@@ -451,20 +467,7 @@ struct ChunkStateArgs {
     int HV, H, ckpt_every;
 };
 
-// hi = the upper 16 bits of each fp32 (bf16 truncation), lo = bf16(x - hi): the pair carries ~16 bits
-__device__ __forceinline__ void split2_trunc(float a0, float a1, uint32_t& hi, uint32_t& lo) {
-    const uint32_t u0 = __float_as_uint(a0), u1 = __float_as_uint(a1);
-    hi = __byte_perm(u0, u1, 0x7632);
-    const __nv_bfloat162 l =
-        __floats2bfloat162_rn(a0 - __uint_as_float(u0 & 0xffff0000u), a1 - __uint_as_float(u1 & 0xffff0000u));
-    lo = *reinterpret_cast<const uint32_t*>(&l);
-}
-__device__ __forceinline__ void split8_trunc(const float* v, uint4& hi, uint4& lo) {
-    split2_trunc(v[0], v[1], hi.x, lo.x);
-    split2_trunc(v[2], v[3], hi.y, lo.y);
-    split2_trunc(v[4], v[5], hi.z, lo.z);
-    split2_trunc(v[6], v[7], hi.w, lo.w);
-}
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_constant__ ChunkStateArgs a) {
     using namespace cs;
@@ -545,6 +548,9 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     }
 
     auto recp = [&](int c) { return a.rec + ((cb + c) * a.HV + hv) * kFwdRecordBytes; };
+    // saved-record mode: thread 0 bulk-copies the staged tiles into the backward's record of each chunk
+    const bool rec_copier = a.rec_bwd != nullptr && tid == 0;
+    auto recb = [&](int c) { return a.rec_bwd + ((cb + c) * a.HV + hv) * kBwdRecordBytes; };
     // -W, TV, V of chunk c (bar_l1; issued once the Delta^T products of chunk c-1 have read them) and Qg and
     // the vectors (bar_lb; once the output product of chunk c-1 has read Qg and the output step of chunk c-2
     // has read that vector buffer)
@@ -631,7 +637,8 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             if (c > 0) issue_l2(c);  // the state update of chunk c-1 has read K
             if (c + 2 < nchunks) prefetch_chunk(c + 2);
         }
-        // B. S^T -> S0^T hi/lo operand tiles; TMEM state <- e^G_C S0; checkpoint
+        // B. S^T -> S0^T hi/lo operand tiles (hi = bf16(S0), round to nearest: the backward record's S0^T
+        //    tile as it is); TMEM state <- e^G_C S0; checkpoint
         if (tid < NWORK) {
             const float eGC = vec[128];
             const bool ck = a.ckpt && (c % a.ckpt_every == 0);
@@ -647,11 +654,15 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             const uint32_t kb = (uint32_t)(cq >> 1);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                uint4 hi, lo;
-                split8_trunc(v + 8 * q, hi, lo);
+                float h[8], l[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    h[e] = bf16r(v[8 * q + e]);
+                    l[e] = v[8 * q + e] - h[e];
+                }
                 const uint32_t off = sw128_off(row, 32 * (cq & 1) + 8 * q);
-                *reinterpret_cast<uint4*>(sm + OFF_S0 + kb * 16384 + off) = hi;
-                *reinterpret_cast<uint4*>(sm + OFF_QL + kb * QL_BLK + 8192 + off) = lo;
+                *reinterpret_cast<uint4*>(sm + OFF_S0 + kb * 16384 + off) = pack8(h);
+                *reinterpret_cast<uint4*>(sm + OFF_QL + kb * QL_BLK + 8192 + off) = pack8(l);
             }
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= eGC;
@@ -659,8 +670,15 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             tmem_st16(tS + lb + 32 * cq + 16, *reinterpret_cast<float(*)[16]>(v + 16));
             tmem_wait_st();
         }
+        // saved-record mode: thread 0 copies tiles into the backward record with bulk copies; the copy of the
+        // previous chunk's Delta^T / Dd^T low tiles has read them before anyone passes this barrier towards D
+        if (rec_copier && c > 0) bulk_wait_read();
         fence_async_smem();
         sync_tc();
+        if (rec_copier) {  // S0^T hi (= the record's bf16 S0^T), 32 KB contiguous here and there
+            bulk_s2g(recb(c), sm + OFF_S0, 32768);
+            bulk_commit();
+        }
         // C. warp 16: Delta^T = V^T TV^T + S0hi^T (-W)^T -> bar_g; warp 17: Delta2^T = S0lo^T (-W)^T -> bar_g2,
         //    O = [Qg; -] (S0hi + S0lo) -> bar_q, then this chunk's P and the next chunk's Qg and vectors.
         //    Warps 8, 9, 12, 13 meanwhile emit the previous chunk's outputs.
@@ -729,23 +747,34 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 16; ++e) v[e] += v2[e];
+            // Delta hi = bf16(Delta), lo = Delta - hi; Dd = Delta x as hi = bf16(hi x), lo = Dd - that hi: the hi
+            // tile and the Dd^T lo tile are the backward record's Delta^T and Dd^T low part as they are
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
-                float d[8];
+                float h[8], l[8], dh[8], dl[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) d[e] = v[8 * q + e] * x[8 * q + e];
-                uint4 hi, lo, dhi, dlo;
-                split8_trunc(v + 8 * q, hi, lo);
-                split8_trunc(d, dhi, dlo);
+                for (int e = 0; e < 8; ++e) {
+                    const float ve = v[8 * q + e], xe = x[8 * q + e];
+                    h[e] = bf16r(ve);
+                    l[e] = ve - h[e];
+                    dh[e] = bf16r(h[e] * xe);
+                    dl[e] = ve * xe - dh[e];
+                }
                 const uint32_t off = sw128_off(row, 16 * cq + 8 * q);
-                *reinterpret_cast<uint4*>(sm + OFF_DH + off) = hi;
-                *reinterpret_cast<uint4*>(sm + OFF_DL + off) = lo;
-                *reinterpret_cast<uint4*>(sm + OFF_DDH + off) = dhi;
-                *reinterpret_cast<uint4*>(sm + OFF_DDL + off) = dlo;
+                *reinterpret_cast<uint4*>(sm + OFF_DH + off) = pack8(h);
+                *reinterpret_cast<uint4*>(sm + OFF_DL + off) = pack8(l);
+                *reinterpret_cast<uint4*>(sm + OFF_DDH + off) = pack8(dh);
+                *reinterpret_cast<uint4*>(sm + OFF_DDL + off) = pack8(dl);
             }
         }
+        if (rec_copier) bulk_wait_read();  // the S0^T copy has read its tiles before the next chunk's B
         fence_async_smem();
         sync_tc();
+        if (rec_copier) {  // Delta^T hi and the Dd^T low part into the record
+            bulk_s2g(recb(c) + kBwdRecDel, sm + OFF_DH, 16384);
+            bulk_s2g(recb(c) + kBwdRecDdl, sm + OFF_DDL, 16384);
+            bulk_commit();
+        }
         // E. warp 16: S^T += Dd^T K (hi + lo) -> bar_s; warp 17: the next chunk's Qg and vectors, then
         //    O += P Delta (hi.hi + lo.hi + hi.lo) -> bar_o
         if (issuer) {
@@ -793,11 +822,13 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
 #pragma unroll
         for (int i = 0; i < 32; ++i) ht[(32 * cq + i) * 128 + row] = v[i];
     }
+    if (rec_copier) bulk_wait_all();  // the last records are in global memory before the CTA ends
     sync_tc();
     if (warp == 0) tmem_dealloc(tm, T_COLS);
 }
 
-// First flattened chunk of every sequence: exclusive scan of ceil(len_n / 64) over cu_seqlens (one CTA).
+// First flattened chunk of every sequence: exclusive scan of ceil(len_n / 64) over cu_seqlens (one CTA);
+// cbase[N] = the total.
 __global__ void __launch_bounds__(1024) chunk_base_kernel(const int64_t* __restrict__ cu, int64_t N,
                                                           int64_t* __restrict__ cbase) {
     __shared__ int64_t wsum[32];
@@ -832,6 +863,19 @@ __global__ void __launch_bounds__(1024) chunk_base_kernel(const int64_t* __restr
         if (tid == 1023) carry = incl;
         __syncthreads();
     }
+    if (tid == 0) cbase[N] = carry;
+}
+
+// Zero the backward-record slots past the last sequence's chunks (the record buffer is sized for the worst
+// split of the packed tokens): the saved buffer is then the same bytes on every call with these inputs.
+__global__ void record_tail_zero_kernel(uint8_t* __restrict__ rec, const int64_t* __restrict__ total_chunks,
+                                        int64_t HV, int64_t capacity_chunks) {
+    const int64_t begin = total_chunks[0] * HV * (int64_t)(kBwdRecordBytes / 16);
+    const int64_t end = capacity_chunks * HV * (int64_t)(kBwdRecordBytes / 16);
+    uint4* p = reinterpret_cast<uint4*>(rec);
+    for (int64_t i = begin + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < end;
+         i += (int64_t)gridDim.x * blockDim.x)
+        p[i] = make_uint4(0, 0, 0, 0);
 }
 
 size_t chunk_fwd_split_workspace(int64_t B, int64_t T, int64_t N, int64_t HV, bool varlen) {
@@ -854,6 +898,11 @@ int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s) {
         rec = (uint8_t*)ws + ((size_t)(L.N + 1) * 8 + 255) / 256 * 256;
         chunk_base_kernel<<<1, 1024, 0, s>>>(L.cu, L.N, cbase);
         count_launch();
+        if (L.bwd_rec) {
+            const int64_t capacity = (Ttot + 63 * L.N) / 64 + L.N;  // chunk_saved_bytes' chunk count
+            record_tail_zero_kernel<<<148, 256, 0, s>>>((uint8_t*)L.bwd_rec, cbase + L.N, L.HV, capacity);
+            count_launch();
+        }
     }
     ChunkPrepArgs p;
     memset(&p, 0, sizeof(p));
@@ -864,6 +913,7 @@ int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s) {
     p.cu = L.cu;
     p.cbase = cbase;
     p.rec = rec;
+    p.rec_bwd = (uint8_t*)L.bwd_rec;
     p.err = L.err;
     p.T = L.T;
     p.H = (int)L.H;
@@ -884,6 +934,7 @@ int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s) {
     if (!make_tmap_3d_sw128(&a.tv, L.v, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
     a.rec = rec;
     a.cbase = cbase;
+    a.rec_bwd = (uint8_t*)L.bwd_rec;
     a.o = L.o;
     a.h0 = L.h0;
     a.ht = L.ht;

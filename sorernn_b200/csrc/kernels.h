@@ -44,9 +44,13 @@ struct ChunkLaunch {
     // final state.
     void* s0_out;
     int64_t max_seqlen;
+    // split forward only: when set, the prep and state passes also write the backward's kBwdRecordBytes record
+    // of every (chunk, head) here (chunk_saved_bytes), so that the backward skips its recompute pass
+    void* bwd_rec;
 };
 
-// Per-(chunk, head) record the recompute pass writes for the backward sweep: shared-memory images, in the
+// Per-(chunk, head) record the backward sweep reads, written by the recompute pass or, in the saved-record
+// mode, by the split forward (prep pass: -W, T; state pass: S0^T, Delta^T, Dd^T low): shared-memory images, in the
 // 128-byte-swizzled operand layouts, of the chunk's S0^T (bf16 [dv][dk], 32 KB), -W (bf16 [j][dk], 16 KB),
 // T = (I + A)^-1 (bf16 [i][j], 8 KB), Delta^T (bf16 [dv][j], 16 KB) and the low part of
 // Dd^T = Delta^T diag(e^(G_C - G) / nk) relative to bf16(bf16(Delta^T) diag(...)) (16 KB).
@@ -80,6 +84,8 @@ struct ChunkBwdLaunch {
     int64_t B, T, N, H, HV, max_seqlen;
     float scale;
     int g_dtype, beta_dtype, l2norm, ckpt_every;
+    // records the split forward saved (chunk_saved_bytes); NULL: rebuild them from ckpt in a recompute pass
+    const void* saved_rec;
 };
 
 // Codes the workspace-less streaming kernels leave in their device error words when a stage wait gives up
@@ -104,7 +110,10 @@ int chunk_fwd(const ChunkLaunch& L, cudaStream_t s);
 size_t chunk_fwd_split_workspace(int64_t B, int64_t T, int64_t N, int64_t HV, bool varlen);
 int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s);
 bool chunk_bwd_supported(int64_t DK, int64_t DV, int act_dtype);
-size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t HV, bool varlen);
+// workspace of chunk_bwd: the records (unless saved by the forward) and the fp32 dq/dk accumulators (HV > H)
+size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t HV, bool varlen, bool saved);
+// bytes of the backward records of every (chunk, head), as the split forward saves them
+size_t chunk_saved_bytes(int64_t B, int64_t T, int64_t N, int64_t HV, bool varlen);
 int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s);
 
 int rec_fwd(const RecLaunch& L, cudaStream_t s);

@@ -26,7 +26,14 @@ from torch import Tensor
 from . import _lib
 
 _DT = {torch.bfloat16: _lib.BF16, torch.float16: _lib.FP16, torch.float32: _lib.FP32}
-DEFAULT_CKPT_EVERY = 8  # chunks of 64 tokens between forward state checkpoints kept for the backward
+# Backward modes of the chunked kernels, chosen by ``ckpt_every``:
+#   SAVE_RECORDS (0): the forward saves every chunk's backward record (88 KB per 64-token chunk and value head:
+#     the chunk-start state and the chunk's operand tiles), the backward runs the reverse sweep alone;
+#   k >= 1: the forward keeps one fp32 state every k chunks (64 KB each), the backward rebuilds the records from
+#     them in a recompute pass first (less memory held between the passes, one pass more).
+SAVE_RECORDS = 0
+DEFAULT_CKPT_EVERY = 8  # the checkpoint interval of the recompute mode
+_BWD_RECORD_BYTES = 90112  # kBwdRecordBytes (csrc/kernels.h)
 
 
 def _ptr(t: Optional[Tensor]):
@@ -58,6 +65,23 @@ def checkpoint_count(B: int, T: int, N: int, ckpt_every: int, varlen: bool) -> i
     return nc // ckpt_every + N + 1
 
 
+def _uses_chunk_kernels(q: Tensor, v: Tensor) -> bool:
+    """The library's kernel-family choice (``gdn_uses_chunk_kernels``): chunked tcgen05 kernels for bf16 with
+    dk = dv = 128, recurrent kernels otherwise."""
+    return q.dtype == torch.bfloat16 and q.shape[-1] == 128 and v.shape[-1] == 128
+
+
+def _saves_records(q: Tensor, v: Tensor, ckpt_every: int) -> bool:
+    return ckpt_every == SAVE_RECORDS and _uses_chunk_kernels(q, v)
+
+
+def saved_record_bytes(B: int, T: int, N: int, HV: int, varlen: bool) -> int:
+    """Bytes of the backward records the forward saves (``gdn_chunk_saved_bytes``): one per 64-token chunk and
+    value head; with ``cu_seqlens`` sized for the worst split of the packed tokens into N sequences."""
+    chunks = (B * T + 63 * N) // 64 + N if varlen else N * ((T + 63) // 64)
+    return chunks * HV * _BWD_RECORD_BYTES
+
+
 def _check_inputs(q, k, v, g, beta, cu_seqlens):
     if not q.is_cuda:
         raise RuntimeError("sorernn_b200 runs on CUDA tensors only (no CPU fallback)")
@@ -83,21 +107,28 @@ def _check_inputs(q, k, v, g, beta, cu_seqlens):
 def gdn_fwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, initial_state: Optional[Tensor],
             cu_seqlens: Optional[Tensor], scale: float, use_qk_l2norm: bool, max_seqlen: int,
             ckpt_every: int) -> tuple[Tensor, Tensor, Tensor]:
-    """Returns ``(o, final_state, checkpoints)``; checkpoints feed :func:`gdn_bwd`."""
-    p = _problem(q, k, v, g, beta, scale, cu_seqlens, max_seqlen, use_qk_l2norm, ckpt_every)
+    """Returns ``(o, final_state, saved)``; ``saved`` feeds :func:`gdn_bwd`: the backward records (uint8) when
+    ``ckpt_every == SAVE_RECORDS`` and the chunked kernels run, else fp32 state checkpoints."""
+    saves = _saves_records(q, v, ckpt_every)
+    p = _problem(q, k, v, g, beta, scale, cu_seqlens, max_seqlen, use_qk_l2norm,
+                 DEFAULT_CKPT_EVERY if ckpt_every == SAVE_RECORDS else ckpt_every)
     L = _lib.lib()
     o = torch.empty_like(v)
     final = torch.empty(p.N, p.HV, p.DK, p.DV, dtype=torch.float32, device=q.device)
-    n_ck = L.gdn_checkpoint_count(ctypes.byref(p))
-    # with cu_seqlens the count is an upper bound: the slots no sequence fills are zeros, so the output is
-    # deterministic (the same in eager mode and under tracing)
-    alloc = torch.zeros if cu_seqlens is not None else torch.empty
-    ck = alloc(max(n_ck, 0), p.HV, p.DK, p.DV, dtype=torch.float32, device=q.device)
+    # with cu_seqlens the sizes are upper bounds: the slots no sequence fills are zeros (the library zeroes
+    # the records' unused tail itself), so the output is deterministic (the same in eager mode and under tracing)
+    if saves:
+        ck = torch.empty(L.gdn_chunk_saved_bytes(ctypes.byref(p)), dtype=torch.uint8, device=q.device)
+    else:
+        alloc = torch.zeros if cu_seqlens is not None else torch.empty
+        n_ck = L.gdn_checkpoint_count(ctypes.byref(p))
+        ck = alloc(max(n_ck, 0), p.HV, p.DK, p.DV, dtype=torch.float32, device=q.device)
     ws_bytes = L.gdn_chunk_fwd_workspace_size(ctypes.byref(p))
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
     h0 = None if initial_state is None else initial_state.float().contiguous()
-    _lib.check(L.gdn_chunk_fwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0), _ptr(o),
-                               _ptr(final), _ptr(ck), _ptr(ws), ws_bytes, _stream(q)), "gdn_chunk_fwd")
+    fn, name = (L.gdn_chunk_fwd_save, "gdn_chunk_fwd_save") if saves else (L.gdn_chunk_fwd, "gdn_chunk_fwd")
+    _lib.check(fn(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0), _ptr(o), _ptr(final),
+                  _ptr(ck), _ptr(ws), ws_bytes, _stream(q)), name)
     return o, final, ck
 
 
@@ -106,9 +137,13 @@ def _(q, k, v, g, beta, initial_state, cu_seqlens, scale, use_qk_l2norm, max_seq
     B, T, H, DK = q.shape
     HV, DV = v.shape[2], v.shape[3]
     N = B if cu_seqlens is None else cu_seqlens.shape[0] - 1
-    n_ck = checkpoint_count(B, T, N, ckpt_every, cu_seqlens is not None)  # no library call while tracing
-    return (torch.empty_like(v), q.new_empty(N, HV, DK, DV, dtype=torch.float32),
-            q.new_empty(max(n_ck, 0), HV, DK, DV, dtype=torch.float32))
+    varlen = cu_seqlens is not None
+    if _saves_records(q, v, ckpt_every):  # no library call while tracing
+        saved = q.new_empty(saved_record_bytes(B, T, N, HV, varlen), dtype=torch.uint8)
+    else:
+        k_ = DEFAULT_CKPT_EVERY if ckpt_every == SAVE_RECORDS else ckpt_every
+        saved = q.new_empty(max(checkpoint_count(B, T, N, k_, varlen), 0), HV, DK, DV, dtype=torch.float32)
+    return torch.empty_like(v), q.new_empty(N, HV, DK, DV, dtype=torch.float32), saved
 
 
 @torch.library.custom_op("sorernn_b200::gdn_bwd", mutates_args=())
@@ -116,20 +151,32 @@ def gdn_bwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, initial_st
             checkpoints: Tensor, do: Tensor, dht: Optional[Tensor], cu_seqlens: Optional[Tensor], scale: float,
             use_qk_l2norm: bool, max_seqlen: int, ckpt_every: int) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor,
                                                                              Tensor]:
-    """Returns ``(dq, dk, dv, dg, dbeta, dh0)``; dg, dbeta in the dtypes of g, beta; dh0 fp32."""
-    p = _problem(q, k, v, g, beta, scale, cu_seqlens, max_seqlen, use_qk_l2norm, ckpt_every)
+    """Returns ``(dq, dk, dv, dg, dbeta, dh0)``; dg, dbeta in the dtypes of g, beta; dh0 fp32.
+    ``checkpoints`` is the third output of :func:`gdn_fwd` called with the same ``ckpt_every``."""
+    saves = _saves_records(q, v, ckpt_every)
+    p = _problem(q, k, v, g, beta, scale, cu_seqlens, max_seqlen, use_qk_l2norm,
+                 DEFAULT_CKPT_EVERY if ckpt_every == SAVE_RECORDS else ckpt_every)
     L = _lib.lib()
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     dg = torch.empty(g.shape, dtype=torch.float32, device=q.device)
     db = torch.empty(beta.shape, dtype=torch.float32, device=q.device)
     dh0 = torch.empty(p.N, p.HV, p.DK, p.DV, dtype=torch.float32, device=q.device)
-    ws_bytes = L.gdn_chunk_bwd_workspace_size(ctypes.byref(p))
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
-    h0 = None if initial_state is None else initial_state.float().contiguous()
     dht_ = None if dht is None else dht.float().contiguous()
-    _lib.check(L.gdn_chunk_bwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0),
-                               _ptr(checkpoints), _ptr(do.contiguous()), _ptr(dht_), _ptr(dq), _ptr(dk), _ptr(dv),
-                               _ptr(dg), _ptr(db), _ptr(dh0), _ptr(ws), ws_bytes, _stream(q)), "gdn_chunk_bwd")
+    if saves:  # the reverse sweep over the records the forward saved
+        ws_bytes = L.gdn_chunk_bwd_saved_workspace_size(ctypes.byref(p))
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+        _lib.check(L.gdn_chunk_bwd_saved(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta),
+                                         _ptr(checkpoints), _ptr(do.contiguous()), _ptr(dht_), _ptr(dq), _ptr(dk),
+                                         _ptr(dv), _ptr(dg), _ptr(db), _ptr(dh0), _ptr(ws), ws_bytes, _stream(q)),
+                   "gdn_chunk_bwd_saved")
+    else:
+        ws_bytes = L.gdn_chunk_bwd_workspace_size(ctypes.byref(p))
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+        h0 = None if initial_state is None else initial_state.float().contiguous()
+        _lib.check(L.gdn_chunk_bwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0),
+                                   _ptr(checkpoints), _ptr(do.contiguous()), _ptr(dht_), _ptr(dq), _ptr(dk),
+                                   _ptr(dv), _ptr(dg), _ptr(db), _ptr(dh0), _ptr(ws), ws_bytes, _stream(q)),
+                   "gdn_chunk_bwd")
     return dq, dk, dv, dg.to(g.dtype), db.to(beta.dtype), dh0
 
 
@@ -144,15 +191,21 @@ def _(q, k, v, g, beta, initial_state, checkpoints, do, dht, cu_seqlens, scale, 
 
 def _setup_context(ctx, inputs, output):
     q, k, v, g, beta, initial_state, cu_seqlens, scale, use_qk_l2norm, max_seqlen, ckpt_every = inputs
-    _, _, ck = output
+    o, _, ck = output
     ctx.save_for_backward(q, k, v, g, beta, initial_state, ck, cu_seqlens)
     ctx.args = (scale, use_qk_l2norm, max_seqlen, ckpt_every)
     ctx.has_h0 = initial_state is not None
+    ctx.o_meta = (o.shape, o.dtype)
+    # outputs the loss does not reach get None, not zero tensors: no zero fill of the saved records (hundreds
+    # of MB) or of the final-state gradient on every backward
+    ctx.set_materialize_grads(False)
 
 
 def _backward(ctx, do, dht, _dck):
     q, k, v, g, beta, initial_state, ck, cu_seqlens = ctx.saved_tensors
     scale, l2, max_seqlen, ckpt_every = ctx.args
+    if do is None:  # only the final state reaches the loss
+        do = q.new_zeros(ctx.o_meta[0], dtype=ctx.o_meta[1])
     dq, dk, dv, dg, db, dh0 = gdn_bwd(q, k, v, g, beta, initial_state, ck, do, dht, cu_seqlens, scale, l2,
                                       max_seqlen, ckpt_every)
     return dq, dk, dv, dg, db, (dh0 if ctx.has_h0 else None), None, None, None, None, None
@@ -261,7 +314,7 @@ torch.library.register_autograd("sorernn_b200::gdn_beta_sigmoid", _beta_backward
 def chunk_gated_delta_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: Optional[float] = None,
                            initial_state: Optional[Tensor] = None, output_final_state: bool = False,
                            use_qk_l2norm_in_kernel: bool = False, cu_seqlens: Optional[Tensor] = None,
-                           cu_seqlens_cpu: Optional[Tensor] = None, ckpt_every: int = DEFAULT_CKPT_EVERY,
+                           cu_seqlens_cpu: Optional[Tensor] = None, ckpt_every: Optional[int] = None,
                            **kwargs):
     """Gated delta rule, same contract as FLA's ``chunk_gated_delta_rule`` (q, k, v, g, beta order).
 
@@ -276,6 +329,13 @@ def chunk_gated_delta_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Ten
     ``use_beta_sigmoid_in_kernel=True``, ``beta`` is the raw b_proj output and ``sigmoid(beta)`` is used.
     Both activations run as fused CUDA kernels with their own backward (gradients reach a, b, A_log,
     dt_bias).
+
+    ``ckpt_every`` picks what the chunked kernels keep for the backward: ``SAVE_RECORDS`` (0) saves every
+    chunk's backward record (88 KB per 64-token chunk and value head) and the backward runs its reverse sweep
+    alone; k >= 1 keeps one fp32 state every k chunks and the backward first rebuilds the records from them
+    (less memory held between the passes, one pass more). ``None`` (the default): ``SAVE_RECORDS`` when
+    autograd will need the backward, else ``DEFAULT_CKPT_EVERY`` (nothing per chunk is written for a
+    forward without gradients).
     """
     use_gate = bool(kwargs.pop("use_gate_in_kernel", False))
     A_log, dt_bias = kwargs.pop("A_log", None), kwargs.pop("dt_bias", None)
@@ -306,6 +366,12 @@ def chunk_gated_delta_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Ten
     else:
         max_seqlen = q.shape[1]
     q, k, v, g, beta = (x.contiguous() for x in (q, k, v, g, beta))
+    if ckpt_every is None:
+        grads = torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (q, k, v, g, beta, initial_state))
+        ckpt_every = SAVE_RECORDS if grads else DEFAULT_CKPT_EVERY
+    elif ckpt_every < 0:
+        raise ValueError(f"ckpt_every must be >= 0, got {ckpt_every}")
     o, final, _ = gdn_fwd(q, k, v, g, beta, initial_state, cu_seqlens, scale, bool(use_qk_l2norm_in_kernel),
                           int(max_seqlen), int(ckpt_every))
     return o, (final if output_final_state else None)

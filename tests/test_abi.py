@@ -63,6 +63,31 @@ def test_checkpoint_count_and_workspace_queries():
     assert lib.gdn_checkpoint_count(ctypes.byref(p)) >= 5
 
 
+def test_saved_record_queries_and_checks():
+    """The saved-record pair: 88 KB (90,112 B) per chunk-head for chunk-kernel problems, nothing for the
+    recurrent family (which the pair refuses with GDN_ERR_SHAPE); missing or misaligned record buffers are
+    refused before any launch."""
+    lib = _lib.lib()
+    p = _chunk_problem(4096, 16, B=8)
+    assert lib.gdn_chunk_saved_bytes(ctypes.byref(p)) == 8 * 64 * 16 * 90112
+    ws_saved = lib.gdn_chunk_bwd_saved_workspace_size(ctypes.byref(p))
+    assert 0 < ws_saved < lib.gdn_chunk_bwd_workspace_size(ctypes.byref(p))
+    pv = _chunk_problem(1000, 2)
+    pv.N, pv.cu_seqlens = 5, 16
+    assert lib.gdn_chunk_saved_bytes(ctypes.byref(pv)) == ((1000 + 63 * 5) // 64 + 5) * 2 * 90112
+    rec = _problem()  # fp32, head size 64: the recurrent kernels
+    assert lib.gdn_chunk_saved_bytes(ctypes.byref(rec)) == 0
+    vp = ctypes.c_void_p(16)
+    fwd = lambda prob, saved: lib.gdn_chunk_fwd_save(ctypes.byref(prob), vp, vp, vp, vp, vp, None, vp, None,  # noqa
+                                                     saved, vp, 1 << 30, None)
+    bwd = lambda prob, saved: lib.gdn_chunk_bwd_saved(ctypes.byref(prob), vp, vp, vp, vp, vp, saved, vp, None,  # noqa
+                                                      vp, vp, vp, vp, vp, None, vp, 1 << 30, None)
+    for call in (fwd, bwd):
+        assert call(rec, vp) == 1
+        assert call(p, None) == 7
+        assert call(p, ctypes.c_void_p(24)) == 3
+
+
 @pytest.mark.parametrize("bad", [dict(HV=6), dict(DK=256), dict(act_dtype=7), dict(N=3), dict(ckpt_every=0),
                                  dict(B=2, cu_seqlens=16)])
 def test_invalid_problems_are_rejected_before_launch(bad):

@@ -54,6 +54,20 @@ def test_python_checkpoint_count_matches_library(B, T, N, K, varlen):
     assert checkpoint_count(B, T, N, K, varlen) == _lib.lib().gdn_checkpoint_count(ctypes.byref(p))
 
 
+@pytest.mark.parametrize("B,T,N,HV,varlen", [(8, 4096, 8, 16, False), (2, 300, 2, 4, False), (1, 1000, 5, 2, True),
+                                             (1, 0, 3, 2, True)])
+def test_python_saved_record_bytes_match_library(B, T, N, HV, varlen):
+    import ctypes
+
+    from sorernn_b200 import _lib
+    from sorernn_b200.gated_delta_rule import saved_record_bytes
+
+    p = _lib.Problem(B=B, T=T, H=HV, HV=HV, DK=128, DV=128, N=N, cu_seqlens=16 if varlen else None,
+                     max_seqlen=T, scale=1.0, act_dtype=_lib.BF16, g_dtype=_lib.FP32, beta_dtype=_lib.BF16,
+                     use_qk_l2norm=1, ckpt_every=8)
+    assert saved_record_bytes(B, T, N, HV, varlen) == _lib.lib().gdn_chunk_saved_bytes(ctypes.byref(p))
+
+
 def test_fake_kernels_trace_without_the_library(monkeypatch):
     """The custom ops' fake (meta) kernels compute output shapes in Python, so tracing (torch.compile,
     activation-checkpoint policies) needs neither a GPU nor the CUDA library."""
@@ -78,3 +92,8 @@ def test_fake_kernels_trace_without_the_library(monkeypatch):
         dq, dk, dv, dg, db, dh0 = torch.ops.sorernn_b200.gdn_bwd(q, q, v, g, b, None, ck, v, None, cu, 0.1, True,
                                                                  300, 8)
         assert dq.shape == q.shape and dv.shape == v.shape and dh0.shape == (3, 4, 128, 128)
+        # saved-record mode (ckpt_every 0): the third output is the byte buffer of the backward records
+        o, ht, rec = torch.ops.sorernn_b200.gdn_fwd(q, q, v, g, b, None, cu, 0.1, True, 300, 0)
+        assert rec.dtype == torch.uint8 and rec.shape == (((300 + 63 * 3) // 64 + 3) * 4 * 90112,)
+        dq, *_ = torch.ops.sorernn_b200.gdn_bwd(q, q, v, g, b, None, rec, v, None, cu, 0.1, True, 300, 0)
+        assert dq.shape == q.shape

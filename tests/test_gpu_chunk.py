@@ -155,7 +155,12 @@ def test_sequence_split_passes_bf16():
     assert_bf16_close(to_np(torch.cat([o1, o2], 1)), to_np(o_full), 2e-2, "o")
 
 
-def _grads_vs_oracle(x, h0, dht, l2, cu=None, tol=3e-2):
+# the two backward modes: records saved by the forward (the default when gradients are needed), and the
+# recompute pass from state checkpoints (every 4 chunks here: several segments per sequence)
+MODES = {"saved": 0, "recompute": 4}
+
+
+def _grads_vs_oracle(x, h0, dht, l2, cu=None, tol=3e-2, mode="saved"):
     """fwd+bwd through the public op; compare every gradient with the oracle on the same inputs."""
     from sorernn_b200 import chunk_gated_delta_rule
 
@@ -164,7 +169,8 @@ def _grads_vs_oracle(x, h0, dht, l2, cu=None, tol=3e-2):
     cu_t = None if cu is None else torch.tensor(cu, device="cuda")
     o, ht = chunk_gated_delta_rule(t["q"], t["k"], t["v"], t["g"], t["beta"], initial_state=h0t,
                                    output_final_state=True, use_qk_l2norm_in_kernel=l2, cu_seqlens=cu_t,
-                                   cu_seqlens_cpu=None if cu is None else torch.tensor(cu))
+                                   cu_seqlens_cpu=None if cu is None else torch.tensor(cu),
+                                   ckpt_every=MODES[mode])
     loss = (o.float() * t["do"].float()).sum() + (0 if dht is None else (ht * dht).sum())
     loss.backward()
     xn = _np(x)
@@ -180,25 +186,71 @@ def _grads_vs_oracle(x, h0, dht, l2, cu=None, tol=3e-2):
         assert_rms_close(to_np(h0t.grad), ref[5], tol, "dh0")
 
 
+@pytest.mark.parametrize("mode", sorted(MODES))
 @pytest.mark.parametrize("B,T,H,HV,l2", [(1, 64, 1, 1, False), (2, 300, 2, 2, True), (1, 200, 1, 2, True),
                                          (1, 130, 2, 2, False)])
-def test_chunk_backward_matches_oracle(B, T, H, HV, l2):
+def test_chunk_backward_matches_oracle(B, T, H, HV, l2, mode):
     x = _inputs(B * 7 + T, B, T, H, HV, normalized=not l2)
     gen = torch.Generator(device="cuda").manual_seed(B * 7 + T + 1)
     h0 = torch.randn(B, HV, D, D, device="cuda", generator=gen) * 0.05
     dht = torch.randn(B, HV, D, D, device="cuda", generator=gen) * 0.1
-    _grads_vs_oracle(x, h0, dht, l2)
+    _grads_vs_oracle(x, h0, dht, l2, mode=mode)
 
 
-def test_chunk_backward_varlen_short_documents():
+@pytest.mark.parametrize("mode", sorted(MODES))
+def test_chunk_backward_varlen_short_documents(mode):
     cu = [0, 1, 3, 4, 70, 200, 512]
     x = _inputs(21, 1, 512, 2, 2, normalized=False)
-    _grads_vs_oracle(x, None, None, True, cu=cu)
+    _grads_vs_oracle(x, None, None, True, cu=cu, mode=mode)
 
 
-def test_chunk_backward_large_row_config1_shape():
+@pytest.mark.parametrize("mode", sorted(MODES))
+def test_chunk_backward_large_row_config1_shape(mode):
     x = _inputs(22, 1, 4096, 16, 16, normalized=False)
-    _grads_vs_oracle(x, None, None, True)
+    _grads_vs_oracle(x, None, None, True, mode=mode)
+
+
+def test_backward_mode_follows_autograd():
+    """Without ckpt_every the op saves per-chunk records only when a backward will run: a forward without
+    gradients keeps the small checkpoints, and both modes give the same gradients within the bf16 bar."""
+    from sorernn_b200 import chunk_gated_delta_rule
+
+    x = _inputs(31, 1, 640, 2, 2, normalized=False)
+    with torch.no_grad():
+        base = torch.cuda.memory_allocated()
+        o, _ = chunk_gated_delta_rule(x["q"], x["k"], x["v"], x["g"], x["beta"], use_qk_l2norm_in_kernel=True)
+        held_nograd = torch.cuda.memory_allocated() - base - o.numel() * o.element_size()
+    del o
+    assert held_nograd < 10 * 2 * 128 * 128 * 4  # no records (88 KB per chunk-head would be 1.8 MB here)
+    grads = {}
+    for mode, ck in (("auto", None), ("recompute", 8)):
+        t = {n: x[n].clone().requires_grad_(n != "do") for n in x}
+        o, _ = chunk_gated_delta_rule(t["q"], t["k"], t["v"], t["g"], t["beta"], use_qk_l2norm_in_kernel=True,
+                                      ckpt_every=ck)
+        o.backward(t["do"])
+        grads[mode] = [to_np(t[n].grad) for n in ("q", "k", "v", "g", "beta")]
+    for name, a, r in zip(("dq", "dk", "dv", "dg", "dbeta"), grads["auto"], grads["recompute"]):
+        assert_rms_close(a, r, 2e-2, f"{name} saved vs recompute")
+
+
+def test_saved_records_tail_is_zeroed_varlen():
+    """With cu_seqlens the record buffer is sized for the worst split; the slots past the last sequence's
+    chunks come back zero even when the allocator hands out a dirty block, so the op's outputs are a
+    function of its inputs."""
+    from sorernn_b200.gated_delta_rule import SAVE_RECORDS, gdn_fwd, saved_record_bytes
+
+    cu = [0, 1, 3, 4, 70, 200, 512]
+    x = _inputs(32, 1, 512, 2, 2, normalized=False)
+    cu_t = torch.tensor(cu, device="cuda")
+    nbytes = saved_record_bytes(1, 512, len(cu) - 1, 2, True)
+    dirty = torch.full((nbytes,), 0xA5, dtype=torch.uint8, device="cuda")
+    del dirty  # the caching allocator hands this block to the op's buffer of the same size
+    _, _, rec = gdn_fwd(x["q"], x["k"], x["v"], x["g"], x["beta"], None, cu_t, D ** -0.5, True, 312, SAVE_RECORDS)
+    assert rec.dtype == torch.uint8 and rec.numel() == nbytes
+    used = sum((b - a + 63) // 64 for a, b in zip(cu[:-1], cu[1:])) * 2 * 90112
+    assert used < nbytes
+    assert int(rec[used:].count_nonzero()) == 0
+    assert int(rec[:used].count_nonzero()) > 0
 
 
 @pytest.mark.parametrize("P,with_h0", [(4, True), (8, False), (1, True)])
@@ -219,7 +271,8 @@ def test_segmented_prefill_matches_one_forward(P, with_h0):
     assert_rms_close(to_np(s), to_np(s_ref), 2e-2, "final state")
 
 
-def test_chunk_varlen_empty_documents_fwd_bwd():
+@pytest.mark.parametrize("mode", sorted(MODES))
+def test_chunk_varlen_empty_documents_fwd_bwd(mode):
     """Zero-length documents at the start, middle and end: their final state is their initial state, their
     dh0 is their dht, and the neighbours are unaffected (forward and backward against the oracle)."""
     cu = [0, 0, 5, 5, 70, 70, 200, 200]
@@ -228,7 +281,7 @@ def test_chunk_varlen_empty_documents_fwd_bwd():
     gen = torch.Generator(device="cuda").manual_seed(24)
     h0 = torch.randn(N, 2, D, D, device="cuda", generator=gen) * 0.05
     dht = torch.randn(N, 2, D, D, device="cuda", generator=gen) * 0.1
-    _grads_vs_oracle(x, h0, dht, True, cu=cu)
+    _grads_vs_oracle(x, h0, dht, True, cu=cu, mode=mode)
 
 
 def test_zero_length_sequences():

@@ -62,17 +62,18 @@ def test_packed_fwd_bwd_has_no_host_sync(gate_in_kernel):
     assert all(t.grad is not None and torch.isfinite(t.grad.float()).all() for t in x.values())
 
 
-def test_custom_ops_pass_opcheck():
+@pytest.mark.parametrize("ckpt_every", [4, 0], ids=["checkpoints", "saved_records"])
+def test_custom_ops_pass_opcheck(ckpt_every):
     import sorernn_b200.gated_delta_rule  # noqa: F401  (registers the ops)
 
     x, do = _packed(3, [0, 130, 300], requires_grad=False)
     cu = torch.tensor([0, 130, 300], device="cuda")
     h0 = torch.randn(2, 4, D, D, device="cuda") * 0.05
-    fwd_args = (x["q"], x["k"], x["v"], x["g"], x["beta"], h0, cu, D ** -0.5, True, 170, 4)
+    fwd_args = (x["q"], x["k"], x["v"], x["g"], x["beta"], h0, cu, D ** -0.5, True, 170, ckpt_every)
     torch.library.opcheck(torch.ops.sorernn_b200.gdn_fwd.default, fwd_args)
     _, _, ck = torch.ops.sorernn_b200.gdn_fwd(*fwd_args)
     dht = torch.randn(2, 4, D, D, device="cuda") * 0.1
-    bwd_args = (x["q"], x["k"], x["v"], x["g"], x["beta"], h0, ck, do, dht, cu, D ** -0.5, True, 170, 4)
+    bwd_args = (x["q"], x["k"], x["v"], x["g"], x["beta"], h0, ck, do, dht, cu, D ** -0.5, True, 170, ckpt_every)
     torch.library.opcheck(torch.ops.sorernn_b200.gdn_bwd.default, bwd_args)
 
 
