@@ -467,7 +467,22 @@ struct ChunkStateArgs {
     int HV, H, ckpt_every;
 };
 
-__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// (a0, a1) -> hi = bf16x2(a0, a1) rounded to nearest, lo = bf16x2(a - hi); hf0, hf1 = hi as floats
+__device__ __forceinline__ void split2_rn(float a0, float a1, uint32_t& hi, uint32_t& lo, float& hf0, float& hf1) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    hf0 = __uint_as_float(hi << 16);
+    hf1 = __uint_as_float(hi & 0xffff0000u);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a0 - hf0, a1 - hf1);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+// 8 values: hi/lo words as above, hf = hi as floats
+__device__ __forceinline__ void split8_rn(const float* v, uint4& hi, uint4& lo, float* hf) {
+    split2_rn(v[0], v[1], hi.x, lo.x, hf[0], hf[1]);
+    split2_rn(v[2], v[3], hi.y, lo.y, hf[2], hf[3]);
+    split2_rn(v[4], v[5], hi.z, lo.z, hf[4], hf[5]);
+    split2_rn(v[6], v[7], hi.w, lo.w, hf[6], hf[7]);
+}
 
 __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_constant__ ChunkStateArgs a) {
     using namespace cs;
@@ -654,15 +669,12 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             const uint32_t kb = (uint32_t)(cq >> 1);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                float h[8], l[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    h[e] = bf16r(v[8 * q + e]);
-                    l[e] = v[8 * q + e] - h[e];
-                }
+                uint4 hi, lo;
+                float hf[8];
+                split8_rn(v + 8 * q, hi, lo, hf);
                 const uint32_t off = sw128_off(row, 32 * (cq & 1) + 8 * q);
-                *reinterpret_cast<uint4*>(sm + OFF_S0 + kb * 16384 + off) = pack8(h);
-                *reinterpret_cast<uint4*>(sm + OFF_QL + kb * QL_BLK + 8192 + off) = pack8(l);
+                *reinterpret_cast<uint4*>(sm + OFF_S0 + kb * 16384 + off) = hi;
+                *reinterpret_cast<uint4*>(sm + OFF_QL + kb * QL_BLK + 8192 + off) = lo;
             }
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= eGC;
@@ -751,20 +763,23 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             // tile and the Dd^T lo tile are the backward record's Delta^T and Dd^T low part as they are
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
-                float h[8], l[8], dh[8], dl[8];
+                uint4 hi, lo, dhi, dlo;
+                float hf[8], hx[8], dhf[8];
+                split8_rn(v + 8 * q, hi, lo, hf);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float ve = v[8 * q + e], xe = x[8 * q + e];
-                    h[e] = bf16r(ve);
-                    l[e] = ve - h[e];
-                    dh[e] = bf16r(h[e] * xe);
-                    dl[e] = ve * xe - dh[e];
+                for (int e = 0; e < 8; ++e) hx[e] = hf[e] * x[8 * q + e];
+                split8_rn(hx, dhi, dlo, dhf);  // dhi = bf16(hi x); dlo below is taken against the exact Delta x
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                    const __nv_bfloat162 l = __floats2bfloat162_rn(v[8 * q + e] * x[8 * q + e] - dhf[e],
+                                                                   v[8 * q + e + 1] * x[8 * q + e + 1] - dhf[e + 1]);
+                    (&dlo.x)[e / 2] = *reinterpret_cast<const uint32_t*>(&l);
                 }
                 const uint32_t off = sw128_off(row, 16 * cq + 8 * q);
-                *reinterpret_cast<uint4*>(sm + OFF_DH + off) = pack8(h);
-                *reinterpret_cast<uint4*>(sm + OFF_DL + off) = pack8(l);
-                *reinterpret_cast<uint4*>(sm + OFF_DDH + off) = pack8(dh);
-                *reinterpret_cast<uint4*>(sm + OFF_DDL + off) = pack8(dl);
+                *reinterpret_cast<uint4*>(sm + OFF_DH + off) = hi;
+                *reinterpret_cast<uint4*>(sm + OFF_DL + off) = lo;
+                *reinterpret_cast<uint4*>(sm + OFF_DDH + off) = dhi;
+                *reinterpret_cast<uint4*>(sm + OFF_DDL + off) = dlo;
             }
         }
         if (rec_copier) bulk_wait_read();  // the S0^T copy has read its tiles before the next chunk's B
