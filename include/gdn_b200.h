@@ -241,6 +241,28 @@ int gdn_segment_apply_state(const gdn_problem* p, const void* q, const void* k, 
 /* Workspace bytes for the two sequence-split calls (same for both). */
 size_t gdn_segment_workspace_size(const gdn_problem* p);
 
+/*
+ * The same sequence split on the chunked kernels (problems with gdn_uses_chunk_kernels(p) == 1; others get
+ * GDN_ERR_SHAPE and use the two calls above). The chunk-parallel prep work of every (chunk, head) runs once
+ * into `records` (gdn_segment_records_size(p) bytes, 16-byte aligned, kept by the caller between the calls),
+ * and the per-sequence state passes reuse it:
+ *   gdn_segment_maps    C = final_state of each sequence from initial_state (NULL = zeros), and, when
+ *                       transition != NULL (needs DK == DV), M = the transition map [N, HV, DK, DK];
+ *                       no outputs;
+ *   gdn_segment_outputs o (and final_state, NULL = not wanted) of each sequence started from
+ *                       incoming_state (NULL = zeros): the segment's true outputs once the caller has
+ *                       composed its incoming state from the other segments' maps.
+ * Three state passes in all, over one prep pass.
+ * Replaces: the per-segment forward, gdn_segment_transition and gdn_segment_apply_state above.
+ */
+size_t gdn_segment_records_size(const gdn_problem* p);
+int gdn_segment_maps(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                     const void* beta, const float* initial_state, float* final_state, float* transition,
+                     void* records, size_t records_bytes, gdn_stream_t stream);
+int gdn_segment_outputs(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                        const void* beta, const float* incoming_state, void* o, float* final_state, void* records,
+                        size_t records_bytes, gdn_stream_t stream);
+
 /* Reads the error word that device-side bounded waits leave in `workspace` (0 = none; the word is
  * cleared at the start of every call that takes the workspace). Synchronises `stream`. */
 int gdn_workspace_error(const void* workspace, gdn_stream_t stream, int32_t* error_out);

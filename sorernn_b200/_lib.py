@@ -37,6 +37,9 @@ SIGNATURES = {
     "gdn_chunk_fwd": (ctypes.c_int, [_P] + [_vp] * 10 + [_sz, _vp]),
     "gdn_chunk_bwd": (ctypes.c_int, [_P] + [_vp] * 16 + [_sz, _vp]),
     "gdn_chunk_saved_bytes": (_sz, [_P]),
+    "gdn_segment_records_size": (_sz, [_P]),
+    "gdn_segment_maps": (ctypes.c_int, [_P] + [_vp] * 9 + [_sz, _vp]),
+    "gdn_segment_outputs": (ctypes.c_int, [_P] + [_vp] * 9 + [_sz, _vp]),
     "gdn_chunk_bwd_saved_workspace_size": (_sz, [_P]),
     "gdn_chunk_fwd_save": (ctypes.c_int, [_P] + [_vp] * 10 + [_sz, _vp]),
     "gdn_chunk_bwd_saved": (ctypes.c_int, [_P] + [_vp] * 15 + [_sz, _vp]),

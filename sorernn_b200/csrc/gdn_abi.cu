@@ -319,6 +319,87 @@ int gdn_segment_apply_state(const gdn_problem* p, const void* q, const void* k, 
     return dispatch_forward(p, L, nullptr, workspace, s);
 }
 
+// count matrices [D, D] set to the identity (the transition map of an empty segment)
+__global__ void identity_states_kernel(float* m, int64_t count, int64_t D) {
+    const int64_t n = count * D * D;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i % (D * D);
+        m[i] = r / D == r % D ? 1.f : 0.f;
+    }
+}
+
+size_t gdn_segment_records_size(const gdn_problem* p) {
+    if (!gdn_uses_chunk_kernels(p)) return 0;
+    return kErrBytes + chunk_fwd_split_workspace(p->B, p->T, p->N, p->HV, p->cu_seqlens != nullptr);
+}
+
+static ChunkLaunch segment_launch(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                                  const void* beta, void* records) {
+    ChunkLaunch C{};
+    C.q = q; C.k = k; C.v = v; C.g = g; C.beta = beta; C.cu = p->cu_seqlens;
+    C.err = (int*)records;
+    C.B = p->B; C.T = p->T; C.N = p->N; C.H = p->H; C.HV = p->HV; C.max_seqlen = max_len(p);
+    C.scale = p->scale; C.g_dtype = p->g_dtype; C.beta_dtype = p->beta_dtype; C.l2norm = p->use_qk_l2norm;
+    C.ckpt_every = p->ckpt_every;
+    return C;
+}
+
+int gdn_segment_maps(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                     const void* beta, const float* initial_state, float* final_state, float* transition,
+                     void* records, size_t records_bytes, gdn_stream_t stream) {
+    int st = check_problem(p);
+    if (st != GDN_OK) return st;
+    if (!gdn_uses_chunk_kernels(p)) return GDN_ERR_SHAPE;
+    if (!q || !k || !v || !g || !beta || !final_state) return GDN_ERR_ARGUMENT;
+    if (!records || records_bytes < gdn_segment_records_size(p)) return GDN_ERR_WORKSPACE;
+    if (!aligned16(records)) return GDN_ERR_ALIGN;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(records, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
+    if (p->B * p->T == 0) {  // no tokens: C is the initial state and M the identity
+        const size_t bytes = (size_t)p->N * p->HV * p->DK * p->DV * sizeof(float);
+        if (bytes == 0) return GDN_OK;
+        const cudaError_t e = initial_state ? cudaMemcpyAsync(final_state, initial_state, bytes,
+                                                              cudaMemcpyDeviceToDevice, s)
+                                            : cudaMemsetAsync(final_state, 0, bytes, s);
+        if (e != cudaSuccess) return GDN_ERR_LAUNCH;
+        if (transition) {
+            identity_states_kernel<<<148, 256, 0, s>>>(transition, p->N * p->HV, p->DK);
+            count_launch();
+            if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
+        }
+        return GDN_OK;
+    }
+    void* ws = (char*)records + kErrBytes;
+    ChunkLaunch C = segment_launch(p, q, k, v, g, beta, records);
+    if ((st = chunk_prep_pass(C, ws, s)) != GDN_OK) return st;
+    C.h0 = initial_state;  // C: the final state from the initial state, no outputs
+    C.ht = final_state;
+    if ((st = chunk_state_pass(C, ws, s)) != GDN_OK) return st;
+    if (!transition) return GDN_OK;
+    C.h0 = nullptr;  // M: the state from the identity with v = 0
+    C.h0_identity = 1;
+    C.zero_v = 1;
+    C.ht = transition;
+    return chunk_state_pass(C, ws, s);
+}
+
+int gdn_segment_outputs(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                        const void* beta, const float* incoming_state, void* o, float* final_state, void* records,
+                        size_t records_bytes, gdn_stream_t stream) {
+    int st = check_problem(p);
+    if (st != GDN_OK) return st;
+    if (!gdn_uses_chunk_kernels(p)) return GDN_ERR_SHAPE;
+    if (p->B * p->T == 0) return GDN_OK;
+    if (!q || !k || !v || !g || !beta || !o) return GDN_ERR_ARGUMENT;
+    if (!records || records_bytes < gdn_segment_records_size(p)) return GDN_ERR_WORKSPACE;
+    if (!aligned16(records)) return GDN_ERR_ALIGN;
+    ChunkLaunch C = segment_launch(p, q, k, v, g, beta, records);
+    C.o = o;
+    C.h0 = incoming_state;
+    C.ht = final_state;
+    return chunk_state_pass(C, (char*)records + kErrBytes, (cudaStream_t)stream);
+}
+
 uint64_t gdn_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int gdn_stream_kernels_error(gdn_stream_t stream, int32_t* error_out) {

@@ -457,7 +457,7 @@ struct ChunkStateArgs {
     const uint8_t* rec;
     const int64_t* cbase;
     uint8_t* rec_bwd;  // NULL, or the backward's records: S0^T, Delta^T and the low part of Dd^T are written here
-    void* o;
+    void* o;           // NULL: no outputs (the output products and stores are skipped; the final state is kept)
     const float* h0;
     float* ht;
     float* ckpt;
@@ -465,6 +465,8 @@ struct ChunkStateArgs {
     int* err;
     int64_t T;
     int HV, H, ckpt_every;
+    int zero_v;       // 1: v = 0 (no U term, V not loaded): the state evolves by its homogeneous part only
+    int h0_identity;  // 1: the state starts as the identity (dk = dv): the final state is the transition map
 };
 
 // (a0, a1) -> hi = bf16x2(a0, a1) rounded to nearest, lo = bf16x2(a - hi); hf0, hf1 = hi as floats
@@ -556,7 +558,8 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         for (int c0 = 0; c0 < 32; c0 += 16) {
             float v[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = h0 ? h0[(32 * cq + c0 + i) * 128 + row] : 0.f;
+            for (int i = 0; i < 16; ++i)
+                v[i] = h0 ? h0[(32 * cq + c0 + i) * 128 + row] : (a.h0_identity && 32 * cq + c0 + i == row ? 1.f : 0.f);
             tmem_st16(tS + lb + 32 * cq + c0, v);
         }
         tmem_wait_st();
@@ -572,11 +575,13 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
     auto issue_l1_a = [&](int c) {
         const int tok0 = (int)(bos + 64 * c);
         const uint8_t* r = recp(c);
-        mbar_arrive_expect_tx(bar_l1, TX_L1);
+        mbar_arrive_expect_tx(bar_l1, a.zero_v ? TX_L1 - 2 * 8192 : TX_L1);
         bulk_g2s(sm + OFF_W, r + kFwdRecW, 16384, bar_l1);
         bulk_g2s(sm + OFF_TV, r + kFwdRecTV, 8192, bar_l1);
+        if (!a.zero_v) {
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb) tma_load_3d(sm + OFF_V + kb * 8192, &a.tv, bar_l1, kb * 64, hv, tok0);
+            for (int kb = 0; kb < 2; ++kb) tma_load_3d(sm + OFF_V + kb * 8192, &a.tv, bar_l1, kb * 64, hv, tok0);
+        }
     };
     auto issue_l1_b = [&](int c) {
         const uint8_t* r = recp(c);
@@ -601,7 +606,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb) {
             prefetch_tile_l2(&a.tk, kb * 64, hq, tok0);
-            prefetch_tile_l2(&a.tv, kb * 64, hv, tok0);
+            if (!a.zero_v) prefetch_tile_l2(&a.tv, kb * 64, hv, tok0);
         }
     };
     // output step of chunk c on warps 8, 9, 12, 13 (lanes 0-63, 64 columns each): o = nq (Qg S0 + P Delta)
@@ -629,12 +634,15 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         }
     };
     const bool out_warp = warp >= 8 && warp < 16 && lg < 2;  // warps 8, 9, 12, 13
+    // without outputs warp 17 issues no output products but keeps committing bar_q / bar_o (a commit with no new
+    // MMAs arrives once the thread's earlier ones are done), so every wait below keeps its meaning
+    const bool outs = a.o != nullptr;
 
     if (issuer && nchunks > 0) {
         issue_l1_a(0);
         issue_l1_b(0);
         issue_l2(0);
-        issue_l3(0);
+        if (outs) issue_l3(0);
         if (nchunks > 1) prefetch_chunk(1);
     }
 
@@ -697,15 +705,17 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         if (issuer) {
             wait_bar(bar_l1, par, a.err, 66, ok);
             const uint32_t idU = idesc_bf16(128, 64, 1, 0), idD = idesc_bf16(128, 64, 0, 0);
+            if (!a.zero_v) {
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tDT, desc_mnmajor(sb + OFF_V + ks * 2048, 8192), desc_kmajor(sb + OFF_TV + ks * 32), idU,
-                          ks > 0);
+                for (int ks = 0; ks < 4; ++ks)
+                    umma_bf16(tDT, desc_mnmajor(sb + OFF_V + ks * 2048, 8192), desc_kmajor(sb + OFF_TV + ks * 32),
+                              idU, ks > 0);
+            }
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
                 umma_bf16(tDT, desc_kmajor(sb + OFF_S0 + kb * 16384 + ko), desc_kmajor(sb + OFF_W + kb * 8192 + ko),
-                          idD, 1);
+                          idD, !a.zero_v || ks > 0);
             }
             umma_commit(bar_g);
         } else if (issuer2) {
@@ -719,18 +729,20 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             }
             umma_commit(bar_g2);
             const uint32_t tO = tm + T_O + par * 128;
+            if (outs) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {  // Qg (S0hi + S0lo)
+                for (int h = 0; h < 2; ++h) {  // Qg (S0hi + S0lo)
 #pragma unroll
-                for (int ks = 0; ks < 8; ++ks) {
-                    const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                    const uint32_t s0 = h ? sb + OFF_QL + kb * QL_BLK + 8192 : sb + OFF_S0 + kb * 16384;
-                    umma_bf16(tO, desc_kmajor(sb + OFF_QL + kb * QL_BLK + ko), desc_kmajor(s0 + ko), idO,
-                              h > 0 || ks > 0);
+                    for (int ks = 0; ks < 8; ++ks) {
+                        const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
+                        const uint32_t s0 = h ? sb + OFF_QL + kb * QL_BLK + 8192 : sb + OFF_S0 + kb * 16384;
+                        umma_bf16(tO, desc_kmajor(sb + OFF_QL + kb * QL_BLK + ko), desc_kmajor(s0 + ko), idO,
+                                  h > 0 || ks > 0);
+                    }
                 }
             }
             umma_commit(bar_q);
-            if (c > 0) {
+            if (c > 0 && outs) {
                 wait_bar(bar_o, par ^ 1u, a.err, 54, ok);  // the P tiles of chunk c-1 have been read
                 issue_l3(c);
             }
@@ -742,7 +754,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         } else if (out_warp && c > 0) {
             wait_bar(bar_o, par ^ 1u, a.err, 56, ok);
             tc_fence_after();
-            output_step(c - 1);
+            if (outs) output_step(c - 1);
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_od);
         }
@@ -806,16 +818,18 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             umma_commit(bar_s);
             if (c + 1 < nchunks) issue_l1_a(c + 1);  // the Delta^T products (bar_g, bar_g2 waited) read -W, TV, V
         } else if (issuer2) {
-            wait_bar(bar_l3, par, a.err, 60, ok);
-            tc_fence_after();
-            const uint32_t idO = idesc_bf16(128, 128, 0, 0);
-            const uint32_t tO = tm + T_O + par * 128;
+            if (outs) {
+                wait_bar(bar_l3, par, a.err, 60, ok);
+                tc_fence_after();
+                const uint32_t idO = idesc_bf16(128, 128, 0, 0);
+                const uint32_t tO = tm + T_O + par * 128;
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                const uint64_t dh = desc_kmajor(sb + OFF_DH + ks * 32), dl = desc_kmajor(sb + OFF_DL + ks * 32);
-                umma_bf16(tO, desc_kmajor(sb + OFF_PH + ks * 32), dh, idO, 1);
-                umma_bf16(tO, desc_kmajor(sb + OFF_PL + ks * 32), dh, idO, 1);
-                umma_bf16(tO, desc_kmajor(sb + OFF_PH + ks * 32), dl, idO, 1);
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint64_t dh = desc_kmajor(sb + OFF_DH + ks * 32), dl = desc_kmajor(sb + OFF_DL + ks * 32);
+                    umma_bf16(tO, desc_kmajor(sb + OFF_PH + ks * 32), dh, idO, 1);
+                    umma_bf16(tO, desc_kmajor(sb + OFF_PL + ks * 32), dh, idO, 1);
+                    umma_bf16(tO, desc_kmajor(sb + OFF_PH + ks * 32), dl, idO, 1);
+                }
             }
             umma_commit(bar_o);
         }
@@ -826,7 +840,7 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
         wait_bar(bar_o, par, a.err, 62, ok);
         wait_bar(bar_s, par, a.err, 63, ok);
         tc_fence_after();
-        if (out_warp) output_step(nchunks - 1);
+        if (out_warp && outs) output_step(nchunks - 1);
     }
     if (ok && a.ht && tid < NWORK) {
         float* ht = a.ht + ((int64_t)n * a.HV + hv) * 16384;
@@ -900,17 +914,24 @@ size_t chunk_fwd_split_workspace(int64_t B, int64_t T, int64_t N, int64_t HV, bo
     return bytes;
 }
 
-int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s) {
-    if (L.N * L.HV == 0) return GDN_OK;
-    if (smem_optin((const void*)chunk_prep_kernel, (int)cp::SMEM_BYTES) != cudaSuccess ||
-        smem_optin((const void*)chunk_state_kernel, (int)cs::SMEM_BYTES) != cudaSuccess)
-        return GDN_ERR_LAUNCH;
-    const int64_t Ttot = L.B * L.T;
-    uint8_t* rec = (uint8_t*)ws;
-    int64_t* cbase = nullptr;
+// Workspace layout of chunk_fwd_split: varlen: cbase [N + 1] (256-byte aligned), then the records.
+static void split_ws(const ChunkLaunch& L, void* ws, uint8_t*& rec, int64_t*& cbase) {
+    rec = (uint8_t*)ws;
+    cbase = nullptr;
     if (L.cu) {
         cbase = (int64_t*)ws;
         rec = (uint8_t*)ws + ((size_t)(L.N + 1) * 8 + 255) / 256 * 256;
+    }
+}
+
+int chunk_prep_pass(const ChunkLaunch& L, void* ws, cudaStream_t s) {
+    if (L.N * L.HV == 0) return GDN_OK;
+    if (smem_optin((const void*)chunk_prep_kernel, (int)cp::SMEM_BYTES) != cudaSuccess) return GDN_ERR_LAUNCH;
+    const int64_t Ttot = L.B * L.T;
+    uint8_t* rec;
+    int64_t* cbase;
+    split_ws(L, ws, rec, cbase);
+    if (L.cu) {
         chunk_base_kernel<<<1, 1024, 0, s>>>(L.cu, L.N, cbase);
         count_launch();
         if (L.bwd_rec) {
@@ -943,9 +964,19 @@ int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s) {
         chunk_prep_kernel<<<dim3((unsigned)maxchunks, (unsigned)(L.N * L.HV)), cp::NTHR, cp::SMEM_BYTES, s>>>(p);
         count_launch();
     }
+    return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+int chunk_state_pass(const ChunkLaunch& L, void* ws, cudaStream_t s) {
+    if (L.N * L.HV == 0) return GDN_OK;
+    if (smem_optin((const void*)chunk_state_kernel, (int)cs::SMEM_BYTES) != cudaSuccess) return GDN_ERR_LAUNCH;
+    const int64_t Ttot = L.B * L.T;
+    uint8_t* rec;
+    int64_t* cbase;
+    split_ws(L, ws, rec, cbase);
     ChunkStateArgs a;
     memset(&a, 0, sizeof(a));
-    a.tk = p.tk;
+    if (!make_tmap_3d_sw128(&a.tk, L.k, 128, L.H, Ttot, 128, L.H * 128, 64)) return GDN_ERR_ALIGN;
     if (!make_tmap_3d_sw128(&a.tv, L.v, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
     a.rec = rec;
     a.cbase = cbase;
@@ -960,9 +991,16 @@ int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s) {
     a.HV = (int)L.HV;
     a.H = (int)L.H;
     a.ckpt_every = L.ckpt_every;
+    a.zero_v = L.zero_v;
+    a.h0_identity = L.h0_identity;
     chunk_state_kernel<<<(unsigned)(L.N * L.HV), cs::NTHR, cs::SMEM_BYTES, s>>>(a);
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s) {
+    const int st = chunk_prep_pass(L, ws, s);
+    return st != GDN_OK ? st : chunk_state_pass(L, ws, s);
 }
 
 }  // namespace gdn

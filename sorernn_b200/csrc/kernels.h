@@ -109,6 +109,11 @@ int chunk_fwd(const ChunkLaunch& L, cudaStream_t s);
 // per-chunk records (chunk_fwd_split_workspace bytes, 256-byte aligned).
 size_t chunk_fwd_split_workspace(int64_t B, int64_t T, int64_t N, int64_t HV, bool varlen);
 int chunk_fwd_split(const ChunkLaunch& L, void* ws, cudaStream_t s);
+// The two launches of chunk_fwd_split on their own, over the same workspace: the prep pass writes the records
+// (and, with cu_seqlens, each sequence's first chunk); the state pass reads them and may run several times
+// (the sequence-split passes). The state pass honours zero_v, h0_identity and o == NULL (no outputs).
+int chunk_prep_pass(const ChunkLaunch& L, void* ws, cudaStream_t s);
+int chunk_state_pass(const ChunkLaunch& L, void* ws, cudaStream_t s);
 bool chunk_bwd_supported(int64_t DK, int64_t DV, int act_dtype);
 // workspace of chunk_bwd: the records (unless saved by the forward) and the fp32 dq/dk accumulators (HV > H)
 size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t HV, bool varlen, bool saved);

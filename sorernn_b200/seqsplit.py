@@ -14,6 +14,10 @@ A segment of tokens is an affine map on the state entering it (gdn_ref.py:18-21 
 3. ranks r > 0 add the incoming state's contribution to their outputs (``gdn_segment_apply_state``:
    the recurrence with v = 0 from ``S_in``), and the last rank's ``S_out`` is the sequence's final state.
 
+On the chunked kernels (bf16, d = 128) steps 1 and 3 share one chunk-parallel prep pass: ``gdn_segment_maps``
+writes its records and runs the C and M state passes over them, and ``gdn_segment_outputs`` reruns the state
+pass from the true incoming state with outputs, in place of the zero-state outputs plus a correction.
+
 Only step 2 crosses GPUs: one ``[N, HV, dk, dk]`` map and one ``[N, HV, dk, dv]`` state per rank (2 MiB at
 HV=16, d=128), gathered into this GPU's memory by NCCL before any kernel reads them.
 """
@@ -116,6 +120,39 @@ def exchange_boundary_states(C: Tensor, M: Optional[Tensor], group=None) -> tupl
     return Cin[rank - 1].to(C.dtype), Cin[rank].to(C.dtype)
 
 
+class _Records:
+    """Prep records of one sequence-split problem, kept between ``gdn_segment_maps`` and
+    ``gdn_segment_outputs`` (chunked kernels only)."""
+
+    def __init__(self, q, v, g, beta, scale, l2):
+        self.p = _problem(q, v.shape, g, beta, scale, l2)
+        n = _lib.lib().gdn_segment_records_size(ctypes.byref(self.p))
+        self.buf = torch.empty(max(n, 1), dtype=torch.uint8, device=q.device)
+        self.n = n
+
+    def maps(self, q, k, v, g, beta, h0, want_m):
+        B, HV, dk, dv = q.shape[0], v.shape[2], q.shape[3], v.shape[3]
+        C = torch.empty(B, HV, dk, dv, dtype=torch.float32, device=q.device)
+        M = torch.empty(B, HV, dk, dk, dtype=torch.float32, device=q.device) if want_m else None
+        h0 = None if h0 is None else h0.float().contiguous()
+        _lib.check(_lib.lib().gdn_segment_maps(ctypes.byref(self.p), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta),
+                                               _ptr(h0), _ptr(C), _ptr(M), _ptr(self.buf), self.n, _stream(q)),
+                   "gdn_segment_maps")
+        return C, M
+
+    def outputs(self, q, k, v, g, beta, incoming):
+        o = torch.empty_like(v)
+        inc = None if incoming is None else incoming.float().contiguous()
+        _lib.check(_lib.lib().gdn_segment_outputs(ctypes.byref(self.p), _ptr(q), _ptr(k), _ptr(v), _ptr(g),
+                                                  _ptr(beta), _ptr(inc), _ptr(o), None, _ptr(self.buf), self.n,
+                                                  _stream(q)), "gdn_segment_outputs")
+        return o
+
+
+def _chunk_path(q, v) -> bool:
+    return q.dtype == torch.bfloat16 and q.shape[-1] == 128 and v.shape[-1] == 128
+
+
 def _local_split(q, k, v, g, beta, scale, l2, P, h0):
     """Forward of one rank's sequence cut into P sub-segments run side by side as a batch of P (the
     tensors are [1, T, ...] and contiguous, so the cut is a view). Sub-segment 0 starts from h0, the
@@ -164,6 +201,9 @@ def segmented_prefill(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, 
         raise ValueError(f"slice length {q.shape[1]} is not a multiple of local_segments = {P}")
     q, k, v, g, beta = (x.contiguous() for x in (q, k, v, g, beta))
     h0 = initial_state if rank == 0 else None
+    if _chunk_path(q, v):
+        return _segmented_prefill_chunked(q, k, v, g, beta, scale, use_qk_l2norm_in_kernel, P, h0, rank, world,
+                                          group)
     qs, ks, gs, bs, o, S_loc, Mpre, M_r, C_r = _local_split(q, k, v, g, beta, scale, use_qk_l2norm_in_kernel,
                                                            P, h0)
     if world > 1:
@@ -178,6 +218,45 @@ def segmented_prefill(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, 
     return o, (S_out if rank == world - 1 else None)
 
 
+def _segmented_prefill_chunked(q, k, v, g, beta, scale, l2, P, h0, rank, world, group):
+    """segmented_prefill on the chunked kernels: one prep pass for all pieces, then three state passes over
+    its records: each piece's C (from zero; piece 0 of rank 0 from h0) and M, the scans and the exchange,
+    and each piece's outputs from its true incoming state."""
+    T = q.shape[1]
+    Ts = T // P
+    seg = lambda x: x.view(P, Ts, *x.shape[2:])  # noqa: E731
+    qs, ks, vs, gs, bs = (seg(x) for x in (q, k, v, g, beta))
+    HV, dk, dv = v.shape[2], q.shape[3], v.shape[3]
+    init = None
+    if h0 is not None:
+        init = torch.zeros(P, HV, dk, dv, dtype=torch.float32, device=q.device)
+        init[0] = h0[0].float()
+    rec = _Records(qs, vs, gs, bs, scale, l2)
+    need_m = P > 1 or (world > 1 and rank > 0)
+    C, M = rec.maps(qs, ks, vs, gs, bs, init, need_m)
+    if need_m:
+        Mi, Ci = affine_inclusive_scan(M, C)
+        M_r, C_r = Mi[P - 1:], Ci[P - 1:]
+        S_loc = torch.cat([torch.zeros_like(C[:1]), Ci[:-1]])
+    else:
+        M_r, C_r, S_loc = None, C, torch.zeros_like(C)
+    if world > 1:
+        S_in, S_out = exchange_boundary_states(C_r, M_r if rank > 0 else None, group)
+    else:
+        S_in, S_out = None, C_r
+    # every piece's true incoming state: the local prefix, the rank's input carried through the pieces before
+    # it, and h0 for the first piece
+    inc = S_loc
+    if S_in is not None:
+        eye = torch.eye(dk, dtype=torch.float32, device=q.device).expand(1, HV, dk, dk)
+        Mpre = torch.cat([eye, Mi[:-1]]) if P > 1 else eye
+        inc = inc + torch.matmul(Mpre, S_in.float().expand(P, -1, -1, -1))
+    if init is not None:
+        inc = inc + init
+    o = rec.outputs(qs, ks, vs, gs, bs, inc)
+    return o.view(1, T, *o.shape[2:]), (S_out if rank == world - 1 else None)
+
+
 def sequence_split_prefill(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: Optional[float] = None,
                            use_qk_l2norm_in_kernel: bool = False, group=None,
                            initial_state: Optional[Tensor] = None) -> tuple[Tensor, Optional[Tensor]]:
@@ -190,6 +269,13 @@ def sequence_split_prefill(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Ten
     world = dist.get_world_size(group)
     scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
     h0 = initial_state if rank == 0 else None
+    if rank > 0 and _chunk_path(q, v):  # one prep pass; C and M, then the outputs from the incoming state
+        q, k, v, g, beta = (x.contiguous() for x in (q, k, v, g, beta))
+        rec = _Records(q, v, g, beta, scale, use_qk_l2norm_in_kernel)
+        C, M = rec.maps(q, k, v, g, beta, None, True)
+        S_in, S_out = exchange_boundary_states(C, M, group)
+        o = rec.outputs(q, k, v, g, beta, S_in)
+        return o, (S_out if rank == world - 1 else None)
     o, C = chunk_gated_delta_rule(q, k, v, g, beta, scale=scale, initial_state=h0, output_final_state=True,
                                   use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
     if world == 1:

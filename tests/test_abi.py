@@ -88,6 +88,28 @@ def test_saved_record_queries_and_checks():
         assert call(p, ctypes.c_void_p(24)) == 3
 
 
+def test_segment_record_queries_and_checks():
+    """The shared-record sequence-split pair: records sized like the forward's workspace for chunk-kernel
+    problems, refused with GDN_ERR_SHAPE for the recurrent family; missing, short or misaligned record
+    buffers are refused before any launch."""
+    lib = _lib.lib()
+    p = _chunk_problem(4096, 16, B=8)
+    n = lib.gdn_segment_records_size(ctypes.byref(p))
+    assert n >= 8 * 64 * 16 * 58368
+    rec = _problem()
+    assert lib.gdn_segment_records_size(ctypes.byref(rec)) == 0
+    vp = ctypes.c_void_p(16)
+    maps = lambda prob, buf, nb: lib.gdn_segment_maps(ctypes.byref(prob), vp, vp, vp, vp, vp, None, vp, vp,  # noqa
+                                                      buf, nb, None)
+    outs = lambda prob, buf, nb: lib.gdn_segment_outputs(ctypes.byref(prob), vp, vp, vp, vp, vp, None, vp,  # noqa
+                                                         None, buf, nb, None)
+    for call in (maps, outs):
+        assert call(rec, vp, 1 << 20) == 1
+        assert call(p, None, n) == 6
+        assert call(p, vp, n - 1) == 6
+        assert call(p, ctypes.c_void_p(24), n) == 3
+
+
 @pytest.mark.parametrize("bad", [dict(HV=6), dict(DK=256), dict(act_dtype=7), dict(N=3), dict(ckpt_every=0),
                                  dict(B=2, cu_seqlens=16)])
 def test_invalid_problems_are_rejected_before_launch(bad):

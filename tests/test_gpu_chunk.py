@@ -253,6 +253,39 @@ def test_saved_records_tail_is_zeroed_varlen():
     assert int(rec[:used].count_nonzero()) > 0
 
 
+@pytest.mark.parametrize("l2", [True, False])
+def test_segment_maps_and_outputs_share_one_prep(l2):
+    """gdn_segment_maps / gdn_segment_outputs over one set of prep records: the C pass and the output pass
+    are the forward's own state pass, so C and o equal the plain forward's bit for bit; M matches the
+    transition map of the fused kernel (gdn_segment_transition) within the fp32 bar."""
+    from sorernn_b200 import chunk_gated_delta_rule, seqsplit
+
+    B, T, H, HV = 3, 300, 2, 4
+    # weak decay (g / 256): M keeps entries of order 0.1 over 300 tokens, so the 2e-2 bar relative to its RMS
+    # measures the kernel, not noise on a matrix that has decayed to ~1e-8
+    x = _inputs(41, B, T, H, HV, normalized=not l2, g_scale=256.0)
+    gen = torch.Generator(device="cuda").manual_seed(42)
+    h0 = torch.randn(B, HV, D, D, device="cuda", generator=gen) * 0.05
+    rec = seqsplit._Records(x["q"], x["v"], x["g"], x["beta"], D ** -0.5, l2)
+    C, M = rec.maps(x["q"], x["k"], x["v"], x["g"], x["beta"], h0, True)
+    o = rec.outputs(x["q"], x["k"], x["v"], x["g"], x["beta"], h0)
+    o_ref, C_ref = chunk_gated_delta_rule(x["q"], x["k"], x["v"], x["g"], x["beta"], initial_state=h0,
+                                          output_final_state=True, use_qk_l2norm_in_kernel=l2)
+    assert torch.equal(C, C_ref)
+    assert torch.equal(o, o_ref)
+    M_ref = seqsplit.segment_transition(x["k"], x["g"], x["beta"], l2, HV)
+    assert_rms_close(to_np(M), to_np(M_ref), 2e-2, "transition")
+    xn = _np(x)  # M against the oracle: the final state of the recurrence from the identity with v = 0
+    Mo = []
+    for b in range(B):
+        _, s_b = cgdn.forward(xn["q"][b:b + 1], xn["k"][b:b + 1], np.zeros_like(xn["v"][b:b + 1]),
+                              xn["g"][b:b + 1], xn["beta"][b:b + 1], D ** -0.5,
+                              initial_state=np.broadcast_to(np.eye(D, dtype=np.float32), (1, HV, D, D)).copy(),
+                              use_qk_l2norm=l2)
+        Mo.append(s_b)
+    assert_rms_close(to_np(M), np.concatenate(Mo), 2e-2, "transition vs oracle")
+
+
 @pytest.mark.parametrize("P,with_h0", [(4, True), (8, False), (1, True)])
 def test_segmented_prefill_matches_one_forward(P, with_h0):
     """The sequence cut into P local pieces joined by affine maps == one chunk forward (bf16 bar)."""
