@@ -23,9 +23,10 @@
 //            - kn.dKst_j  (+ sum_j kn.dKst_j + e^Gamma_C <dS, S0> on the last row);  dg = reverse cumsum
 //   dq = (dqn - qn (qn.dqn)) / nq,  dk likewise (chain rule through the L2 norm)
 // MMAs are issued by two threads, 0 and 32, each committing its groups to its own mbarriers (thread 0:
-// bar_mma; thread 32: bar_mma2, and bar_mma3 for its share of step 6's first group): one thread issues a
-// tcgen05.mma about every 70 cycles, so two issuers halve the issue time of the larger steps, and a phase
-// waits only for the groups it reads. Products that accumulate into one TMEM region stay on one thread.
+// bar_mma; thread 32: bar_mma2, and bar_mma3 for its share of step 6's first group), so two issuers halve the
+// issue time of the larger steps, and a phase waits only for the groups it reads. Issue loops are unrolled
+// over hoisted descriptors (one N = 64 UMMA per ~50 cycles against ~100 rolled), except step 10's, whose
+// unrolled form raised the kernel's register spills (its issuers hold the dq operands live). Products that accumulate into one TMEM region stay on one thread.
 // Every GEMM is an M = 128 UMMA with a 128-wide dimension on the TMEM lanes. The three 64 x 64 x K
 // products (dP, Z, dA) use a 128-row A operand of which one 64-row half is ignored; Z and dA put their
 // rows on lanes 64-127, where the same threads also hold the K K^T rows of the recomputed Gram matrix.
@@ -378,10 +379,11 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id = idesc_bf16(128, 64, 0, 0);
-#pragma unroll 1
+            const uint64_t dQ = desc_kmajor(aQ), dK = desc_kmajor(aK);
+#pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tD1, desc_kmajor(aQ + kb * QK_BLK + ko), desc_kmajor(aK + kb * QK_BLK + ko), id, ks > 0);
+                const uint32_t o = (ks >> 2) * QK_BLK + (ks & 3) * 32;
+                umma_bf16(tD1, desc_at(dQ, o), desc_at(dK, o), id, ks > 0);
             }
             umma_commit(bar_mma);
         }
@@ -478,33 +480,34 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         // ---- 6. dO^T P''^T (320); dS^T K^T, hi and lo (384); dP = [dO;-] Delta^T (448); QA = S0 dO^T (192)
         if (tid == 0) {
             const uint32_t id_kk = idesc_bf16(128, 64, 0, 0);
-#pragma unroll 1
+            const uint64_t dDS = desc_kmajor(sb + OFF_DS), dK = desc_kmajor(aK);
+            const uint64_t dLo0 = desc_kmajor(sb + OFF_DD), dLo1 = desc_kmajor(sb + OFF_A);
+#pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tm + C384, desc_kmajor(sb + OFF_DS + kb * 16384 + ko), desc_kmajor(aK + kb * QK_BLK + ko),
-                          id_kk, ks > 0);
-                umma_bf16(tm + C384, desc_kmajor(sb + (kb ? OFF_A : OFF_DD) + ko), desc_kmajor(aK + kb * QK_BLK + ko),
-                          id_kk, 1);  // dS lo . K
+                umma_bf16(tm + C384, desc_at(dDS, kb * 16384 + ko), desc_at(dK, kb * QK_BLK + ko), id_kk, ks > 0);
+                umma_bf16(tm + C384, desc_at(kb ? dLo1 : dLo0, ko), desc_at(dK, kb * QK_BLK + ko), id_kk,
+                          1);  // dS lo . K
             }
             umma_commit(bar_mma);  // dDelta's two products: step 7 starts on them
         } else if (tid == 32) {  // a second issuing thread: its MMAs and commits are tracked apart from thread 0's
             const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mk = idesc_bf16(128, 64, 1, 0);
             const uint32_t id_mm = idesc_bf16(128, 64, 1, 1);
-#pragma unroll 1
+            const uint64_t dDOm = desc_mnmajor(aDO, 8192), dPS = desc_mnmajor(sb + OFF_PS, 8192),
+                           dPS2 = desc_mnmajor(sb + OFF_PS2, 8192);
+#pragma unroll
             for (int ks = 0; ks < 4; ++ks) {  // K = i: dDelta's first product
-                umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS + ks * 2048, 8192),
-                          id_mm, ks > 0);
-                umma_bf16(tm + C320, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
-                          id_mm, 1);
+                umma_bf16(tm + C320, desc_at(dDOm, ks * 2048), desc_at(dPS, ks * 2048), id_mm, ks > 0);
+                umma_bf16(tm + C320, desc_at(dDOm, ks * 2048), desc_at(dPS2, ks * 2048), id_mm, 1);
             }
             umma_commit(bar_mma3);
-#pragma unroll 1
+            const uint64_t dDOk = desc_kmajor(aDO), dDEL = desc_mnmajor(sb + OFF_DEL, 8192),
+                           dS0 = desc_mnmajor(sb + OFF_S0, 16384);
+#pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tm + C448, desc_kmajor(aDO + kb * 8192 + ko), desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192),
-                          id_km, ks > 0);
-                umma_bf16(tm + C192, desc_mnmajor(sb + OFF_S0 + ks * 2048, 16384), desc_kmajor(aDO + kb * 8192 + ko),
-                          id_mk, ks > 0);
+                const uint32_t ok_ = (ks >> 2) * 8192 + (ks & 3) * 32;
+                umma_bf16(tm + C448, desc_at(dDOk, ok_), desc_at(dDEL, ks * 2048), id_km, ks > 0);
+                umma_bf16(tm + C192, desc_at(dS0, ks * 2048), desc_at(dDOk, ok_), id_mk, ks > 0);
             }
             umma_commit(bar_mma2);  // dP and QA: run while step 7 forms dDelta
         }
@@ -628,34 +631,33 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         //         dK' = Q^T dPs2 + dS Dd^T (448). Thread 0 issues QB and dK', thread 32 dVb and -dW^T.
         if (tid == 0) {
             const uint32_t id_mm = idesc_bf16(128, 64, 1, 1);
-#pragma unroll 1
+            const uint64_t dQm = desc_mnmajor(aQ, QK_BLK), dPS2 = desc_mnmajor(sb + OFF_PS2, 8192);
+#pragma unroll
             for (int ks = 0; ks < 4; ++ks)  // K = tokens
-                umma_bf16(tm + C448, desc_mnmajor(aQ + ks * 2048, QK_BLK), desc_mnmajor(sb + OFF_PS2 + ks * 2048, 8192),
-                          id_mm, ks > 0);
-#pragma unroll 1
+                umma_bf16(tm + C448, desc_at(dQm, ks * 2048), desc_at(dPS2, ks * 2048), id_mm, ks > 0);
+            const uint64_t dDSm = desc_mnmajor(sb + OFF_DS, 16384), dDEL = desc_mnmajor(sb + OFF_DEL, 8192),
+                           dVm = desc_mnmajor(sb + OFF_V, 8192);
+#pragma unroll
             for (int ks = 0; ks < 8; ++ks) {  // K = dv
-                umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
-                          desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192), id_mm, 1);
-                umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
-                          desc_mnmajor(sb + OFF_V + ks * 2048, 8192), id_mm, 1);  // dS hi . Dd lo
+                umma_bf16(tm + C448, desc_at(dDSm, ks * 2048), desc_at(dDEL, ks * 2048), id_mm, 1);
+                umma_bf16(tm + C448, desc_at(dDSm, ks * 2048), desc_at(dVm, ks * 2048), id_mm, 1);  // dS hi . Dd lo
             }
             umma_commit(bar_mma);
         } else if (tid == 32) {
             const uint32_t id_km = idesc_bf16(128, 64, 0, 1), id_mm = idesc_bf16(128, 64, 1, 1);
             const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
-#pragma unroll 1
+            const uint64_t dKm = desc_mnmajor(aK, QK_BLK), dPSk = desc_kmajor(sb + OFF_PS), dDDk = desc_kmajor(sb + OFF_DD),
+                           dDDLk = desc_kmajor(sb + OFF_DDL), dTm = desc_mnmajor(sb + OFF_T, 8192);
+#pragma unroll
             for (int ks = 0; ks < 4; ++ks) {  // K = tokens
-                umma_bf16(tm + C384, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_PS + ks * 32), id_mk,
-                          ks > 0);
-                umma_bf16(tm + C256, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
-                          id_km, ks > 0);
-                umma_bf16(tm + C256, desc_kmajor(sb + OFF_DDL + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
-                          id_km, 1);
+                umma_bf16(tm + C384, desc_at(dKm, ks * 2048), desc_at(dPSk, ks * 32), id_mk, ks > 0);
+                umma_bf16(tm + C256, desc_at(dDDk, ks * 32), desc_at(dTm, ks * 2048), id_km, ks > 0);
+                umma_bf16(tm + C256, desc_at(dDDLk, ks * 32), desc_at(dTm, ks * 2048), id_km, 1);
             }
-#pragma unroll 1
+            const uint64_t dS0m = desc_mnmajor(sb + OFF_S0, 16384), dDDm = desc_mnmajor(sb + OFF_DD, 8192);
+#pragma unroll
             for (int ks = 0; ks < 8; ++ks)  // K = dv
-                umma_bf16(tm + C320, desc_mnmajor(sb + OFF_S0 + ks * 2048, 16384),
-                          desc_mnmajor(sb + OFF_DD + ks * 2048, 8192), id_mm, ks > 0);
+                umma_bf16(tm + C320, desc_at(dS0m, ks * 2048), desc_at(dDDm, ks * 2048), id_mm, ks > 0);
             umma_commit(bar_mma2);
         }
         mwait(bar_mma, mph, a.err, 16, ok);
@@ -693,19 +695,19 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         sync_tc();
         if (tid == 0) {  // dK' (thread 0, after its other dK' products) and the dS update (thread 32)
             const uint32_t id_mm = idesc_bf16(128, 64, 1, 1);
-#pragma unroll 1
+            const uint64_t dDSm = desc_mnmajor(sb + OFF_DS, 16384), dDEL = desc_mnmajor(sb + OFF_DEL, 8192);
+#pragma unroll
             for (int ks = 0; ks < 8; ++ks)  // K = dv
-                umma_bf16(tm + C448, desc_mnmajor(sb + OFF_DS + ks * 2048, 16384),
-                          desc_mnmajor(sb + OFF_DEL + ks * 2048, 8192), id_mm, 1);
+                umma_bf16(tm + C448, desc_at(dDSm, ks * 2048), desc_at(dDEL, ks * 2048), id_mm, 1);
         } else if (tid == 32) {
             const uint32_t id_mm128 = idesc_bf16(128, 128, 1, 1), id_km128 = idesc_bf16(128, 128, 0, 1);
-#pragma unroll 1
+            const uint64_t dDOm = desc_mnmajor(aDO, 8192), dQm = desc_mnmajor(aQ, QK_BLK), dDDk = desc_kmajor(sb + OFF_DD),
+                           dDDLk = desc_kmajor(sb + OFF_DDL), dWm = desc_mnmajor(sb + OFF_W, 8192);
+#pragma unroll
             for (int ks = 0; ks < 4; ++ks) {  // K = tokens
-                umma_bf16(tS, desc_mnmajor(aDO + ks * 2048, 8192), desc_mnmajor(aQ + ks * 2048, QK_BLK), id_mm128, 1);
-                umma_bf16(tS, desc_kmajor(sb + OFF_DD + ks * 32), desc_mnmajor(sb + OFF_W + ks * 2048, 8192), id_km128,
-                          1);
-                umma_bf16(tS, desc_kmajor(sb + OFF_DDL + ks * 32), desc_mnmajor(sb + OFF_W + ks * 2048, 8192), id_km128,
-                          1);
+                umma_bf16(tS, desc_at(dDOm, ks * 2048), desc_at(dQm, ks * 2048), id_mm128, 1);
+                umma_bf16(tS, desc_at(dDDk, ks * 32), desc_at(dWm, ks * 2048), id_km128, 1);
+                umma_bf16(tS, desc_at(dDDLk, ks * 32), desc_at(dWm, ks * 2048), id_km128, 1);
             }
         }
 
@@ -754,19 +756,18 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         // ---- 10. dKb^T = dW^T T (192) ; Z1 = [-; dVb] V^T (256, rows j on lanes 64-127) ------------------
         if (tid == 0) {  // dKb (thread 0) and Z1 (thread 32); each commit also covers that thread's step-8b MMAs
             const uint32_t id_km = idesc_bf16(128, 64, 0, 1);
+            const uint64_t dDWk = desc_kmajor(sb + OFF_DWT), dTm = desc_mnmajor(sb + OFF_T, 8192);
 #pragma unroll 1
             for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tm + C192, desc_kmajor(sb + OFF_DWT + ks * 32), desc_mnmajor(sb + OFF_T + ks * 2048, 8192),
-                          id_km, ks > 0);
+                umma_bf16(tm + C192, desc_at(dDWk, ks * 32), desc_at(dTm, ks * 2048), id_km, ks > 0);
             umma_commit(bar_mma);
         } else if (tid == 32) {
             const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
+            const uint64_t dDVBm = desc_mnmajor(sb + OFF_DVB - 16384, 16384), dVk = desc_kmajor(aV);
 #pragma unroll 1
-            for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tm + C256, desc_mnmajor(sb + OFF_DVB - 16384 + ks * 2048, 16384),
-                          desc_kmajor(aV + kb * 8192 + ko), id_mk, ks > 0);
-            }
+            for (int ks = 0; ks < 8; ++ks)
+                umma_bf16(tm + C256, desc_at(dDVBm, ks * 2048), desc_at(dVk, (ks >> 2) * 8192 + (ks & 3) * 32), id_mk,
+                          ks > 0);
             umma_commit(bar_mma2);
         }
         if (tid < 64) {  // per-column terms of the dq epilogue; dGamma and dbeta contributions
@@ -822,12 +823,11 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         sync_tc();
         if (tid == 0) {
             const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
-#pragma unroll 1
-            for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tm + C320, desc_mnmajor(sb + OFF_DKB - 16384 + ks * 2048, 16384),
-                          desc_kmajor(aK + kb * QK_BLK + ko), id_mk, ks > 0);
-            }
+            const uint64_t dDKBm = desc_mnmajor(sb + OFF_DKB - 16384, 16384), dKk = desc_kmajor(aK);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+                umma_bf16(tm + C320, desc_at(dDKBm, ks * 2048), desc_at(dKk, (ks >> 2) * QK_BLK + (ks & 3) * 32), id_mk,
+                          ks > 0);
             umma_commit(bar_mma);
         }
         if (tid < 64) {
@@ -854,9 +854,10 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         sync_tc();
         if (tid == 0) {
             const uint32_t id = idesc_bf16(128, 64, 0, 0);
-#pragma unroll 1
+            const uint64_t dPSk = desc_kmajor(sb + OFF_PS), dTk = desc_kmajor(sb + OFF_T);
+#pragma unroll
             for (int ks = 0; ks < 4; ++ks)  // A rows 0-63 = the dPs1 tile (ignored), 64-127 = Z
-                umma_bf16(tm + C256, desc_kmajor(sb + OFF_PS + ks * 32), desc_kmajor(sb + OFF_T + ks * 32), id, ks > 0);
+                umma_bf16(tm + C256, desc_at(dPSk, ks * 32), desc_at(dTk, ks * 32), id, ks > 0);
             umma_commit(bar_mma);
         }
         mwait(bar_mma, mph, a.err, 19, ok);
@@ -913,9 +914,9 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         // ---- 13. dK' += K^T Gs (448) ----------------------------------------------------------------
         if (tid == 0) {
             const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
-#pragma unroll 1
-            for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tm + C448, desc_mnmajor(aK + ks * 2048, QK_BLK), desc_kmajor(sb + OFF_GS + ks * 32), id_mk, 1);
+            const uint64_t dKm = desc_mnmajor(aK, QK_BLK), dGSk = desc_kmajor(sb + OFF_GS);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) umma_bf16(tm + C448, desc_at(dKm, ks * 2048), desc_at(dGSk, ks * 32), id_mk, 1);
             umma_commit(bar_mma);
         }
         float kr[16], w16[16];  // step 14's shared-memory operands, loaded while the MMAs run

@@ -22,7 +22,7 @@
 // 16 warps turn Delta^T (all 128 TMEM lanes) into the Delta^T and Dd^T = Delta^T diag(e^(Gamma_C - Gamma) nk)
 // hi/lo tiles, and
 //   S^T += Dd^T K (hi + lo)        O += P Delta (hi.hi + lo.hi + hi.lo)
-// Two extra warps only issue the loads and MMAs (a tcgen05.mma every 70-85 cycles from one thread): warp 16
+// Two extra warps only issue the loads and MMAs (unrolled, one N = 64 UMMA per ~50 cycles from a thread): warp 16
 // the state chain, warp 17 the output products and the loads they read, so issue overlaps the data phases;
 // four warps emit chunk c-1's outputs while the Delta^T products of chunk c run, and every chunk's operands
 // are prefetched into L2 two chunks ahead. The raw bf16 q, k, v tiles feed the tensor cores unmodified;
@@ -213,11 +213,11 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
     if (tid == 0) {
         tc_fence_after();
         const uint32_t id = idesc_bf16(128, 64, 0, 0);
+        const uint64_t dA = desc_kmajor(sb + OFF_QK), dB = desc_kmajor(sb + OFF_QK + 8192);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
-            const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-            umma_bf16(tm, desc_kmajor(sb + OFF_QK + kb * 16384 + ko), desc_kmajor(sb + OFF_QK + kb * 16384 + 8192 + ko),
-                      id, ks > 0);
+            const uint32_t o = (ks >> 2) * 16384 + (ks & 3) * 32;
+            umma_bf16(tm, desc_at(dA, o), desc_at(dB, o), id, ks > 0);
         }
         umma_commit(bar_mma);
     }
@@ -372,10 +372,9 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
     // MMA2: [W; TV K] = [TB; TV] K  (M = 128, N = 128 = dk, K = 64 tokens); W rows on lanes 0-63
     if (tid == 0) {
         const uint32_t id = idesc_bf16(128, 128, 0, 1);
+        const uint64_t dTB = desc_kmajor(sb + OFF_TB), dK = desc_mnmajor(sb + OFF_QK + 8192, 16384);
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-            umma_bf16(tm, desc_kmajor(sb + OFF_TB + ks * 32), desc_mnmajor(sb + OFF_QK + 8192 + ks * 2048, 16384), id,
-                      ks > 0);
+        for (int ks = 0; ks < 4; ++ks) umma_bf16(tm, desc_at(dTB, ks * 32), desc_at(dK, ks * 2048), id, ks > 0);
         umma_commit(bar_mma);
     }
     wait_bar(bar_mma, 1, a.err, 43, ok);
@@ -418,8 +417,8 @@ __global__ void __launch_bounds__(cp::NTHR, 4) chunk_prep_kernel(const __grid_co
 
 // ================================================================================================
 // chunk_state_kernel: one CTA per (sequence, value head), chunks in order. Warps 0-15 move data between
-// tensor memory and operand tiles; warps 16 and 17 only issue loads and MMAs (one thread issues a tcgen05.mma
-// about every 70-85 cycles), so that issue overlaps the other warps' work: warp 16 the state chain (the
+// tensor memory and operand tiles; warps 16 and 17 only issue loads and MMAs (one thread issues an N = 64
+// tcgen05.mma about every 50 cycles), so that issue overlaps the other warps' work: warp 16 the state chain (the
 // Delta^T products with S0 hi, the state update), warp 17 the rest (the Delta^T products with S0 lo into a
 // second accumulator, the output products) and the loads those read.
 // ================================================================================================
@@ -706,38 +705,38 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             wait_bar(bar_l1, par, a.err, 66, ok);
             const uint32_t idU = idesc_bf16(128, 64, 1, 0), idD = idesc_bf16(128, 64, 0, 0);
             if (!a.zero_v) {
+                const uint64_t dV = desc_mnmajor(sb + OFF_V, 8192), dTV = desc_kmajor(sb + OFF_TV);
 #pragma unroll
-                for (int ks = 0; ks < 4; ++ks)
-                    umma_bf16(tDT, desc_mnmajor(sb + OFF_V + ks * 2048, 8192), desc_kmajor(sb + OFF_TV + ks * 32),
-                              idU, ks > 0);
+                for (int ks = 0; ks < 4; ++ks) umma_bf16(tDT, desc_at(dV, ks * 2048), desc_at(dTV, ks * 32), idU, ks > 0);
             }
+            const uint64_t dS0 = desc_kmajor(sb + OFF_S0), dW = desc_kmajor(sb + OFF_W);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tDT, desc_kmajor(sb + OFF_S0 + kb * 16384 + ko), desc_kmajor(sb + OFF_W + kb * 8192 + ko),
-                          idD, !a.zero_v || ks > 0);
+                umma_bf16(tDT, desc_at(dS0, kb * 16384 + ko), desc_at(dW, kb * 8192 + ko), idD, !a.zero_v || ks > 0);
             }
             umma_commit(bar_g);
         } else if (issuer2) {
             wait_bar(bar_l1, par, a.err, 67, ok);
             const uint32_t idD = idesc_bf16(128, 64, 0, 0), idO = idesc_bf16(128, 128, 0, 0);
+            const uint64_t dSL = desc_kmajor(sb + OFF_QL + 8192), dW = desc_kmajor(sb + OFF_W);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                umma_bf16(tDT2, desc_kmajor(sb + OFF_QL + kb * QL_BLK + 8192 + ko),
-                          desc_kmajor(sb + OFF_W + kb * 8192 + ko), idD, ks > 0);
+                umma_bf16(tDT2, desc_at(dSL, kb * QL_BLK + ko), desc_at(dW, kb * 8192 + ko), idD, ks > 0);
             }
             umma_commit(bar_g2);
             const uint32_t tO = tm + T_O + par * 128;
             if (outs) {
+                const uint64_t dQg = desc_kmajor(sb + OFF_QL), dHi = desc_kmajor(sb + OFF_S0),
+                               dLo = desc_kmajor(sb + OFF_QL + 8192);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {  // Qg (S0hi + S0lo)
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks) {
                         const uint32_t kb = ks >> 2, ko = (ks & 3) * 32;
-                        const uint32_t s0 = h ? sb + OFF_QL + kb * QL_BLK + 8192 : sb + OFF_S0 + kb * 16384;
-                        umma_bf16(tO, desc_kmajor(sb + OFF_QL + kb * QL_BLK + ko), desc_kmajor(s0 + ko), idO,
-                                  h > 0 || ks > 0);
+                        const uint64_t s0 = h ? desc_at(dLo, kb * QL_BLK + ko) : desc_at(dHi, kb * 16384 + ko);
+                        umma_bf16(tO, desc_at(dQg, kb * QL_BLK + ko), s0, idO, h > 0 || ks > 0);
                     }
                 }
             }
@@ -808,12 +807,12 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
             wait_bar(bar_l2, par, a.err, 59, ok);
             tc_fence_after();
             const uint32_t idS = idesc_bf16(128, 128, 0, 1);
+            const uint64_t dK = desc_mnmajor(sb + OFF_K, 8192);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const uint32_t dd = sb + (h ? OFF_DDL : OFF_DDH);
+                const uint64_t dd = desc_kmajor(sb + (h ? OFF_DDL : OFF_DDH));
 #pragma unroll
-                for (int ks = 0; ks < 4; ++ks)
-                    umma_bf16(tS, desc_kmajor(dd + ks * 32), desc_mnmajor(sb + OFF_K + ks * 2048, 8192), idS, 1);
+                for (int ks = 0; ks < 4; ++ks) umma_bf16(tS, desc_at(dd, ks * 32), desc_at(dK, ks * 2048), idS, 1);
             }
             umma_commit(bar_s);
             if (c + 1 < nchunks) issue_l1_a(c + 1);  // the Delta^T products (bar_g, bar_g2 waited) read -W, TV, V
@@ -823,12 +822,14 @@ __global__ void __launch_bounds__(cs::NTHR, 1) chunk_state_kernel(const __grid_c
                 tc_fence_after();
                 const uint32_t idO = idesc_bf16(128, 128, 0, 0);
                 const uint32_t tO = tm + T_O + par * 128;
+                const uint64_t dDH = desc_kmajor(sb + OFF_DH), dDL = desc_kmajor(sb + OFF_DL),
+                               dPH = desc_kmajor(sb + OFF_PH), dPL = desc_kmajor(sb + OFF_PL);
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks) {
-                    const uint64_t dh = desc_kmajor(sb + OFF_DH + ks * 32), dl = desc_kmajor(sb + OFF_DL + ks * 32);
-                    umma_bf16(tO, desc_kmajor(sb + OFF_PH + ks * 32), dh, idO, 1);
-                    umma_bf16(tO, desc_kmajor(sb + OFF_PL + ks * 32), dh, idO, 1);
-                    umma_bf16(tO, desc_kmajor(sb + OFF_PH + ks * 32), dl, idO, 1);
+                    const uint64_t dh = desc_at(dDH, ks * 32), dl = desc_at(dDL, ks * 32);
+                    umma_bf16(tO, desc_at(dPH, ks * 32), dh, idO, 1);
+                    umma_bf16(tO, desc_at(dPL, ks * 32), dh, idO, 1);
+                    umma_bf16(tO, desc_at(dPH, ks * 32), dl, idO, 1);
                 }
             }
             umma_commit(bar_o);
