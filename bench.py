@@ -36,11 +36,14 @@ FWD_FLOP_PER_TOKEN_HEAD = 10 * C * 128 + 6 * 128 * 128 + C * C / 3  # chunked fw
 # What bounds the strong-scaling side line (the serial part of the step at few units per GPU).
 STRONG_LIMITER = ("each (sequence, head) unit walks its 64 chunks serially in one CTA: with {units} units per "
                   "rank, {units} SMs work and the step time stays the per-unit chain time")
+STRONG_LIMITER_PIECES = ("{units} units per rank, each cut into {P} pieces of {chunks} chunks: three state passes, "
+                         "a dS-only sweep and a full sweep of {chunks} chunks per step (the pieces' maps and "
+                         "end-state gradients), each still one CTA per piece walking its chunks serially")
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
 # DRAM bytes (read + write) per launch from ncu captures of this build: the backward pass (the reverse-sweep
 # launch over the records the forward saved) captured at batch 2 and scaled by 4 to batch 8; the decode step
 # at full config-3 size.
-BWD_PASS_TRAFFIC_BYTES = (322.8e6 + 81.2e6) * 4
+BWD_PASS_TRAFFIC_BYTES = (319.8e6 + 83.8e6) * 4
 DECODE_TRAFFIC_BYTES = 271.6e6 + 210.9e6
 
 
@@ -392,36 +395,67 @@ def strong_scaling_bench(dev, rank, world, step, steps):
     """Config 1 with its total work fixed: the B=8 rows (x 16 heads) are split across the ranks (B/N rows
     per rank, i.e. 128/N (sequence, head) units) and every rank times fwd+bwd of its share; value = the
     8 x 4096 tokens / the slowest rank's time per step (strong scaling). The main line is the weak one
-    (every rank a full B=8 problem)."""
+    (every rank a full B=8 problem). With fewer than 128 units per rank the rank's sequences are also run
+    cut into P = 128 / units pieces side by side (sorernn_b200.pieces, no collective); both paths are timed
+    and the line reports each and the faster."""
     import torch
+
+    from sorernn_b200.pieces import chunk_gated_delta_rule_pieces
 
     B, T, H, D = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["D"]
     if B % world:
         return {"skipped": f"B={B} rows do not split over {world} ranks"}
     Br = B // world
+    units = Br * H
     x = make_inputs(Br, T, H, D, dev, seed=77 + rank)
     leaf = {n: x[n].clone().requires_grad_(n != "do") for n in ("q", "k", "v", "g", "beta")}
+    P = 1
+    while units * P * 2 <= 128 and T % (64 * P * 2) == 0:
+        P *= 2
+
+    def pieces_step_of(Pn):
+        def pieces_step(inp, do):
+            o, _ = chunk_gated_delta_rule_pieces(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"], pieces=Pn,
+                                                 use_qk_l2norm_in_kernel=True)
+            o.backward(do)
+        return pieces_step
 
     def zero_s():
         for t in leaf.values():
             t.grad = None
 
-    for _ in range(3):
-        zero_s()
-        step(leaf, x["do"])
-    barrier(world)
-    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s0.record()
-    for _ in range(steps):
-        zero_s()
-        step(leaf, x["do"])
-    e0.record()
-    barrier(world)
-    ms = max_over_ranks(s0.elapsed_time(e0) / steps, world)
-    return {"workload": f"config1 B{B} T{T} H{H} d{D} fwd+bwd split by batch rows over {world} rank(s)",
-            "per_rank_batch": Br, "units_per_rank": Br * H, "ms_per_step": round(ms, 4),
-            "tokens_per_s": round(B * T / (ms / 1e3), 1), "scaling": "strong",
-            "limiter": STRONG_LIMITER.format(units=Br * H)}
+    def timed(fn):
+        for _ in range(3):
+            zero_s()
+            fn(leaf, x["do"])
+        barrier(world)
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(steps):
+            zero_s()
+            fn(leaf, x["do"])
+        e0.record()
+        barrier(world)
+        return max_over_ranks(s0.elapsed_time(e0) / steps, world)
+
+    ms_plain = timed(step)
+    ms_pieces = None
+    if P > 1:  # the largest piece count that keeps the CTAs within one wave, and half of it
+        tried = {Pn: timed(pieces_step_of(Pn)) for Pn in sorted({P, max(2, P // 2)})}
+        P = min(tried, key=tried.get)
+        ms_pieces = tried[P]
+    ms = ms_plain if ms_pieces is None else min(ms_plain, ms_pieces)
+    out = {"workload": f"config1 B{B} T{T} H{H} d{D} fwd+bwd split by batch rows over {world} rank(s)",
+           "per_rank_batch": Br, "units_per_rank": units, "ms_per_step": round(ms, 4),
+           "tokens_per_s": round(B * T / (ms / 1e3), 1), "scaling": "strong",
+           "ms_per_step_one_piece": round(ms_plain, 4)}
+    if ms_pieces is not None:
+        out.update({"pieces_per_sequence": P, "ms_per_step_pieces": round(ms_pieces, 4),
+                    "pieces_tried_ms": {str(k): round(v, 4) for k, v in tried.items()},
+                    "path": "pieces" if ms_pieces < ms_plain else "one piece"})
+    out["limiter"] = STRONG_LIMITER.format(units=units) if P == 1 else STRONG_LIMITER_PIECES.format(
+        units=units, P=P, chunks=T // (64 * P))
+    return out
 
 
 def run_ours(args):

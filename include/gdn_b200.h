@@ -132,6 +132,18 @@ int gdn_chunk_bwd_saved(const gdn_problem* p, const void* q, const void* k, cons
                         void* dv, float* dg, float* dbeta, float* dh0, void* workspace, size_t workspace_bytes,
                         gdn_stream_t stream);
 
+/*
+ * The state-gradient half of gdn_chunk_bwd_saved: dh0 (fp32 [N, HV, DK, DV], required) = the gradient of every
+ * sequence's initial state given do and dht (NULL = zero), with no token gradients. The reverse sweep then
+ * carries dS alone and skips the per-chunk gradient steps (about half of its work per chunk). Workspace:
+ * gdn_chunk_bwd_saved_workspace_size(p) bytes. Used to join pieces of sequences (gdn_piece_chain): the
+ * gradient each piece passes back from a zero end-state gradient.
+ * Replaces: part of ChunkGatedDeltaRuleFunction.backward (fla chunk.py:117-236): its dh0 output alone.
+ */
+int gdn_chunk_state_grad_saved(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                               const void* beta, const void* saved, const void* dout, const float* dht, float* dh0,
+                               void* workspace, size_t workspace_bytes, gdn_stream_t stream);
+
 /* Size of gdn_chunk_bwd_noalloc's fixed scratch array (36 MiB). */
 #define GDN_NOALLOC_SCRATCH_BYTES ((size_t)36 << 20)
 
@@ -262,6 +274,41 @@ int gdn_segment_maps(const gdn_problem* p, const void* q, const void* k, const v
 int gdn_segment_outputs(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
                         const void* beta, const float* incoming_state, void* o, float* final_state, void* records,
                         size_t records_bytes, gdn_stream_t stream);
+
+/*
+ * The two calls above for training on pieces: each also writes its share of the backward's per-(chunk, head)
+ * records into `saved` (gdn_chunk_saved_bytes(p) bytes, 16-byte aligned, the same buffer for both calls):
+ * gdn_segment_maps_save the -W and T parts (prep pass), gdn_segment_outputs_save the S0^T, Delta^T and
+ * Dd^T low parts from each sequence's true incoming state. After both, `saved` is what gdn_chunk_fwd_save
+ * writes for the same problem started from those incoming states, so gdn_chunk_bwd_saved runs the reverse
+ * sweep of any piece from a given end-state gradient (dht). This lets a caller cut long sequences into
+ * pieces that run side by side when there are too few (sequence, head) pairs to fill the GPU.
+ * Replaces: the same forward as gdn_chunk_fwd_save (fla chunk.py:365-380), split across pieces.
+ */
+int gdn_segment_maps_save(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                          const void* beta, const float* initial_state, float* final_state, float* transition,
+                          void* saved, void* records, size_t records_bytes, gdn_stream_t stream);
+int gdn_segment_outputs_save(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                             const void* beta, const float* incoming_state, void* o, float* final_state, void* saved,
+                             void* records, size_t records_bytes, gdn_stream_t stream);
+
+/*
+ * The chain of piece maps along each of n_seq sequences cut into `pieces` pieces (training on pieces, with
+ * gdn_segment_maps_save / gdn_segment_outputs_save / gdn_chunk_bwd_saved on the pieces as sequences). maps
+ * [n_seq * pieces, HV, DK, DK] and terms, out [n_seq * pieces, HV, DK, DV] are fp32 with piece p of
+ * sequence n at index n * pieces + p; start and final_state [n_seq, HV, DK, DV] (NULL = zeros / not wanted).
+ *   reverse = 0: out[p] = the state entering piece p, given each piece's map (M_p, C_p = terms[p], the
+ *                piece's final state from its own start, piece 0 from `start`): out[0] = start,
+ *                out[p] = M_{p-1} out[p-1] + C_{p-1} for p >= 1 (as a chain: Y = C_0, Y <- M_p Y + C_p);
+ *                final_state = the state leaving the last piece.
+ *   reverse = 1: out[p] = the gradient of the state leaving piece p, given R_p = terms[p], the gradient
+ *                entering piece p for a zero end-state gradient: out[pieces-1] = start (the gradient of
+ *                the sequence's final state), out[p] = M_{p+1}^T out[p+1] + R_{p+1}.
+ * DK = DV = 128. fp32 throughout. No counterpart in the reference (it has no sequence split).
+ */
+int gdn_piece_chain(int64_t n_seq, int64_t pieces, int64_t HV, int64_t DK, int64_t DV, const float* maps,
+                    const float* terms, const float* start, float* out, float* final_state, int32_t reverse,
+                    gdn_stream_t stream);
 
 /* Reads the error word that device-side bounded waits leave in `workspace` (0 = none; the word is
  * cleared at the start of every call that takes the workspace). Synchronises `stream`. */

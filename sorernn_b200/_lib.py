@@ -40,6 +40,10 @@ SIGNATURES = {
     "gdn_segment_records_size": (_sz, [_P]),
     "gdn_segment_maps": (ctypes.c_int, [_P] + [_vp] * 9 + [_sz, _vp]),
     "gdn_segment_outputs": (ctypes.c_int, [_P] + [_vp] * 9 + [_sz, _vp]),
+    "gdn_segment_maps_save": (ctypes.c_int, [_P] + [_vp] * 10 + [_sz, _vp]),
+    "gdn_segment_outputs_save": (ctypes.c_int, [_P] + [_vp] * 10 + [_sz, _vp]),
+    "gdn_piece_chain": (ctypes.c_int, [_i64] * 5 + [_vp] * 5 + [_i32, _vp]),
+    "gdn_chunk_state_grad_saved": (ctypes.c_int, [_P] + [_vp] * 10 + [_sz, _vp]),
     "gdn_chunk_bwd_saved_workspace_size": (_sz, [_P]),
     "gdn_chunk_fwd_save": (ctypes.c_int, [_P] + [_vp] * 10 + [_sz, _vp]),
     "gdn_chunk_bwd_saved": (ctypes.c_int, [_P] + [_vp] * 15 + [_sz, _vp]),

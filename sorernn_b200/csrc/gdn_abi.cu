@@ -255,6 +255,37 @@ int gdn_chunk_bwd_saved(const gdn_problem* p, const void* q, const void* k, cons
                          workspace, workspace_bytes, gdn_chunk_bwd_saved_workspace_size(p), stream);
 }
 
+int gdn_chunk_state_grad_saved(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                               const void* beta, const void* saved, const void* dout, const float* dht, float* dh0,
+                               void* workspace, size_t workspace_bytes, gdn_stream_t stream) {
+    int st = check_problem(p);
+    if (st != GDN_OK) return st;
+    if (!gdn_uses_chunk_kernels(p)) return GDN_ERR_SHAPE;
+    if (!dh0) return GDN_ERR_ARGUMENT;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (p->B * p->T == 0) {  // no tokens: dh0 is dht
+        const size_t bytes = (size_t)p->N * p->HV * p->DK * p->DV * sizeof(float);
+        if (bytes == 0) return GDN_OK;
+        const cudaError_t e = dht ? cudaMemcpyAsync(dh0, dht, bytes, cudaMemcpyDeviceToDevice, s)
+                                  : cudaMemsetAsync(dh0, 0, bytes, s);
+        return e == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+    }
+    if (!q || !k || !v || !g || !beta || !dout || !saved) return GDN_ERR_ARGUMENT;
+    if (!aligned16(saved)) return GDN_ERR_ALIGN;
+    if (!workspace || workspace_bytes < gdn_chunk_bwd_saved_workspace_size(p)) return GDN_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return GDN_ERR_ALIGN;
+    if (cudaMemsetAsync(workspace, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
+    ChunkBwdLaunch C{};
+    C.q = q; C.k = k; C.v = v; C.g = g; C.beta = beta; C.dout = dout; C.dht = dht; C.dh0 = dh0;
+    C.ws = (char*)workspace + kErrBytes; C.cu = p->cu_seqlens; C.err = (int*)workspace;
+    C.B = p->B; C.T = p->T; C.N = p->N; C.H = p->H; C.HV = p->HV; C.max_seqlen = max_len(p);
+    C.scale = p->scale; C.g_dtype = p->g_dtype; C.beta_dtype = p->beta_dtype; C.l2norm = p->use_qk_l2norm;
+    C.ckpt_every = p->ckpt_every;
+    C.saved_rec = saved;
+    C.state_grad_only = 1;
+    return chunk_bwd(C, s);
+}
+
 int gdn_decode_step(int64_t N, int64_t H, int64_t HV, int64_t DK, int64_t DV, float scale, int32_t act_dtype,
                     int32_t g_dtype, int32_t beta_dtype, int32_t use_qk_l2norm, const void* q, const void* k,
                     const void* v, const void* g, const void* beta, float* state, void* o, gdn_stream_t stream) {
@@ -344,15 +375,15 @@ static ChunkLaunch segment_launch(const gdn_problem* p, const void* q, const voi
     return C;
 }
 
-int gdn_segment_maps(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
-                     const void* beta, const float* initial_state, float* final_state, float* transition,
-                     void* records, size_t records_bytes, gdn_stream_t stream) {
+static int segment_maps_impl(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                             const void* beta, const float* initial_state, float* final_state, float* transition,
+                             void* saved, void* records, size_t records_bytes, gdn_stream_t stream) {
     int st = check_problem(p);
     if (st != GDN_OK) return st;
     if (!gdn_uses_chunk_kernels(p)) return GDN_ERR_SHAPE;
     if (!q || !k || !v || !g || !beta || !final_state) return GDN_ERR_ARGUMENT;
     if (!records || records_bytes < gdn_segment_records_size(p)) return GDN_ERR_WORKSPACE;
-    if (!aligned16(records)) return GDN_ERR_ALIGN;
+    if (!aligned16(records) || (saved && !aligned16(saved))) return GDN_ERR_ALIGN;
     cudaStream_t s = (cudaStream_t)stream;
     if (cudaMemsetAsync(records, 0, kErrBytes, s) != cudaSuccess) return GDN_ERR_LAUNCH;
     if (p->B * p->T == 0) {  // no tokens: C is the initial state and M the identity
@@ -371,7 +402,9 @@ int gdn_segment_maps(const gdn_problem* p, const void* q, const void* k, const v
     }
     void* ws = (char*)records + kErrBytes;
     ChunkLaunch C = segment_launch(p, q, k, v, g, beta, records);
+    C.bwd_rec = saved;  // the prep pass writes the records' -W and T parts; the state passes below write nothing
     if ((st = chunk_prep_pass(C, ws, s)) != GDN_OK) return st;
+    C.bwd_rec = nullptr;
     C.h0 = initial_state;  // C: the final state from the initial state, no outputs
     C.ht = final_state;
     if ((st = chunk_state_pass(C, ws, s)) != GDN_OK) return st;
@@ -383,21 +416,65 @@ int gdn_segment_maps(const gdn_problem* p, const void* q, const void* k, const v
     return chunk_state_pass(C, ws, s);
 }
 
-int gdn_segment_outputs(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
-                        const void* beta, const float* incoming_state, void* o, float* final_state, void* records,
-                        size_t records_bytes, gdn_stream_t stream) {
+static int segment_outputs_impl(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                                const void* beta, const float* incoming_state, void* o, float* final_state,
+                                void* saved, void* records, size_t records_bytes, gdn_stream_t stream) {
     int st = check_problem(p);
     if (st != GDN_OK) return st;
     if (!gdn_uses_chunk_kernels(p)) return GDN_ERR_SHAPE;
     if (p->B * p->T == 0) return GDN_OK;
     if (!q || !k || !v || !g || !beta || !o) return GDN_ERR_ARGUMENT;
     if (!records || records_bytes < gdn_segment_records_size(p)) return GDN_ERR_WORKSPACE;
-    if (!aligned16(records)) return GDN_ERR_ALIGN;
+    if (!aligned16(records) || (saved && !aligned16(saved))) return GDN_ERR_ALIGN;
     ChunkLaunch C = segment_launch(p, q, k, v, g, beta, records);
     C.o = o;
     C.h0 = incoming_state;
     C.ht = final_state;
+    C.bwd_rec = saved;  // S0^T, Delta^T and the Dd^T low part of every chunk, from the true incoming state
     return chunk_state_pass(C, (char*)records + kErrBytes, (cudaStream_t)stream);
+}
+
+int gdn_segment_maps(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                     const void* beta, const float* initial_state, float* final_state, float* transition,
+                     void* records, size_t records_bytes, gdn_stream_t stream) {
+    return segment_maps_impl(p, q, k, v, g, beta, initial_state, final_state, transition, nullptr, records,
+                             records_bytes, stream);
+}
+
+int gdn_segment_outputs(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                        const void* beta, const float* incoming_state, void* o, float* final_state, void* records,
+                        size_t records_bytes, gdn_stream_t stream) {
+    return segment_outputs_impl(p, q, k, v, g, beta, incoming_state, o, final_state, nullptr, records,
+                                records_bytes, stream);
+}
+
+int gdn_segment_maps_save(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                          const void* beta, const float* initial_state, float* final_state, float* transition,
+                          void* saved, void* records, size_t records_bytes, gdn_stream_t stream) {
+    if (p && p->B * p->T > 0 && !saved) return GDN_ERR_ARGUMENT;
+    return segment_maps_impl(p, q, k, v, g, beta, initial_state, final_state, transition, saved, records,
+                             records_bytes, stream);
+}
+
+int gdn_segment_outputs_save(const gdn_problem* p, const void* q, const void* k, const void* v, const void* g,
+                             const void* beta, const float* incoming_state, void* o, float* final_state, void* saved,
+                             void* records, size_t records_bytes, gdn_stream_t stream) {
+    if (p && p->B * p->T > 0 && !saved) return GDN_ERR_ARGUMENT;
+    return segment_outputs_impl(p, q, k, v, g, beta, incoming_state, o, final_state, saved, records, records_bytes,
+                                stream);
+}
+
+int gdn_piece_chain(int64_t n_seq, int64_t pieces, int64_t HV, int64_t DK, int64_t DV, const float* maps,
+                    const float* terms, const float* start, float* out, float* final_state, int32_t reverse,
+                    gdn_stream_t stream) {
+    if (n_seq < 0 || pieces < 0 || HV < 0) return GDN_ERR_SHAPE;
+    if (DK != 128 || DV != 128) return GDN_ERR_SHAPE;
+    if (reverse != 0 && reverse != 1) return GDN_ERR_ARGUMENT;
+    if (n_seq * pieces * HV == 0) return GDN_OK;
+    if (!terms || !out || (pieces > 1 && !maps)) return GDN_ERR_ARGUMENT;
+    if (!aligned16(maps) || !aligned16(terms) || !aligned16(out) || !aligned16(start) || !aligned16(final_state))
+        return GDN_ERR_ALIGN;
+    return piece_chain(n_seq, pieces, HV, maps, terms, start, out, final_state, reverse, (cudaStream_t)stream);
 }
 
 uint64_t gdn_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }

@@ -94,6 +94,7 @@ struct ChunkBwdArgs {
     int N, H, HV, g_dtype, beta_dtype;
     float scale;
     int l2norm, accumulate_qk;
+    int state_grad_only;  // 1: only dS is carried (steps 1-8b) and dh0 written; no token gradients
 };
 
 __device__ __forceinline__ uint32_t pk_bf16(float a, float b) {
@@ -662,7 +663,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         mwait(bar_mma, mph, a.err, 16, ok);
         mwait(bar_mma2, mph2, a.err, 25, ok);
-        if (tid == 0) {  // the Dd lo tile is consumed: bring V back for Z1 (step 10)
+        if (tid == 0 && !a.state_grad_only) {  // the Dd lo tile is consumed: bring V back for Z1 (step 10)
             const int tok0i = (int)tok0;
             mbar_arrive_expect_tx(bar_v, 2 * 8192);
             tma_load_3d(sm + OFF_V, &a.tv, bar_v, 0, hv, tok0i);
@@ -693,7 +694,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         }
         fence_async_smem();
         sync_tc();
-        if (tid == 0) {  // dK' (thread 0, after its other dK' products) and the dS update (thread 32)
+        if (tid == 0 && !a.state_grad_only) {  // dK' (thread 0, after its other dK' products); dS update (thread 32)
             const uint32_t id_mm = idesc_bf16(128, 64, 1, 1);
             const uint64_t dDSm = desc_mnmajor(sb + OFF_DS, 16384), dDEL = desc_mnmajor(sb + OFF_DEL, 8192);
 #pragma unroll
@@ -709,6 +710,16 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 umma_bf16(tS, desc_at(dDDk, ks * 32), desc_at(dWm, ks * 2048), id_km128, 1);
                 umma_bf16(tS, desc_at(dDDLk, ks * 32), desc_at(dWm, ks * 2048), id_km128, 1);
             }
+        }
+
+        if (a.state_grad_only) {  // the dS update lands; every reader of this chunk's tiles is done
+            if (tid == 32) umma_commit(bar_mma2);
+            mwait(bar_mma2, mph2, a.err, 28, ok);
+            if (tid == 0 && c > 0) {
+                issue_inputs_a(c - 1);
+                issue_inputs_b(c - 1);
+            }
+            continue;
         }
 
         // ---- 9. dv, dVb tile, dVb.v; dW^T tile; qn.(S0 dO) and qn.QB -------------------------------------
@@ -1048,7 +1059,7 @@ int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s) {
     if (!make_tmap_3d_sw128(&a.tk, L.k, 128, L.H, Ttot, 128, L.H * 128, 64)) return GDN_ERR_ALIGN;
     if (!make_tmap_3d_sw128(&a.tv, L.v, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
     if (!make_tmap_3d_sw128(&a.tdo, L.dout, 128, L.HV, Ttot, 128, L.HV * 128, 64)) return GDN_ERR_ALIGN;
-    const bool acc = L.HV > L.H;
+    const bool acc = L.HV > L.H && !L.state_grad_only;
     float* acc_q = acc ? (float*)scratch : nullptr;
     float* acc_k = acc ? acc_q + Ttot * L.H * 128 : nullptr;
     if (acc && cudaMemsetAsync(acc_q, 0, (size_t)Ttot * L.H * 128 * 4 * 2, s) != cudaSuccess) return GDN_ERR_LAUNCH;
@@ -1073,6 +1084,7 @@ int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s) {
     a.scale = L.scale;
     a.l2norm = L.l2norm;
     a.accumulate_qk = acc ? 1 : 0;
+    a.state_grad_only = L.state_grad_only;
     const unsigned grid = (unsigned)(L.N * L.HV);
     if (grid > 0) {
         chunk_bwd_kernel<<<grid, NTHR, SMEM_BYTES, s>>>(a);

@@ -110,6 +110,25 @@ def test_segment_record_queries_and_checks():
         assert call(p, ctypes.c_void_p(24), n) == 3
 
 
+def test_segment_save_variants_check_their_record_buffer():
+    """The saving pair (training on pieces) takes the same arguments plus the backward-record buffer: a
+    missing one is GDN_ERR_ARGUMENT, a misaligned one GDN_ERR_ALIGN, both before any launch; the record
+    checks of the plain pair still apply."""
+    lib = _lib.lib()
+    p = _chunk_problem(4096, 16, B=2)
+    n = lib.gdn_segment_records_size(ctypes.byref(p))
+    vp = ctypes.c_void_p(16)
+    maps = lambda saved, buf, nb: lib.gdn_segment_maps_save(ctypes.byref(p), vp, vp, vp, vp, vp, None, vp,  # noqa
+                                                            vp, saved, buf, nb, None)
+    outs = lambda saved, buf, nb: lib.gdn_segment_outputs_save(ctypes.byref(p), vp, vp, vp, vp, vp, None, vp,  # noqa
+                                                               None, saved, buf, nb, None)
+    for call in (maps, outs):
+        assert call(None, vp, n) == _lib.lib().gdn_chunk_fwd_save(ctypes.byref(p), vp, vp, vp, vp, vp, None, vp,
+                                                                  None, None, vp, 1 << 40, None)
+        assert call(ctypes.c_void_p(24), vp, n) == 3
+        assert call(vp, None, n) == 6
+
+
 @pytest.mark.parametrize("bad", [dict(HV=6), dict(DK=256), dict(act_dtype=7), dict(N=3), dict(ckpt_every=0),
                                  dict(B=2, cu_seqlens=16)])
 def test_invalid_problems_are_rejected_before_launch(bad):
@@ -164,3 +183,33 @@ def test_noalloc_reports_the_same_status_as_the_workspace_backward_for_invalid_p
         p = _problem(**bad)
         assert lib.gdn_chunk_bwd_noalloc(ctypes.byref(p), *([vp] * 15), None) == want
         assert lib.gdn_chunk_bwd(ctypes.byref(p), *([vp] * 15), vp, 1 << 30, None) == want
+
+
+def test_piece_chain_checks_its_arguments():
+    """gdn_piece_chain: head sizes other than 128, a bad direction flag, missing tensors and misaligned
+    pointers are refused before any launch; empty problems are a no-op."""
+    lib = _lib.lib()
+    vp = ctypes.c_void_p(256)
+    assert lib.gdn_piece_chain(1, 4, 2, 64, 64, vp, vp, None, vp, None, 0, None) == 1
+    assert lib.gdn_piece_chain(1, 4, 2, 128, 128, vp, vp, None, vp, None, 2, None) == 7
+    assert lib.gdn_piece_chain(1, 4, 2, 128, 128, None, vp, None, vp, None, 0, None) == 7
+    assert lib.gdn_piece_chain(1, 4, 2, 128, 128, vp, vp, None, None, None, 1, None) == 7
+    assert lib.gdn_piece_chain(1, 4, 2, 128, 128, vp, ctypes.c_void_p(260), None, vp, None, 0, None) == 3
+    assert lib.gdn_piece_chain(0, 4, 2, 128, 128, None, None, None, None, None, 0, None) == 0
+
+
+def test_state_grad_sweep_checks_its_arguments():
+    """gdn_chunk_state_grad_saved: dh0 and the records are required, the workspace is the saved backward's,
+    recurrent-family problems are refused; all before any launch."""
+    lib = _lib.lib()
+    p = _chunk_problem(1024, 4, B=2)
+    n = lib.gdn_chunk_bwd_saved_workspace_size(ctypes.byref(p))
+    vp = ctypes.c_void_p(256)
+    call = lambda prob, saved, dh0, ws, nb: lib.gdn_chunk_state_grad_saved(  # noqa: E731
+        ctypes.byref(prob), vp, vp, vp, vp, vp, saved, vp, None, dh0, ws, nb, None)
+    assert call(p, vp, None, vp, n) == 7
+    assert call(p, None, vp, vp, n) == 7
+    assert call(p, ctypes.c_void_p(264), vp, vp, n) == 3
+    assert call(p, vp, vp, None, n) == 6
+    assert call(p, vp, vp, vp, n - 1) == 6
+    assert call(_problem(), vp, vp, vp, 1 << 30) == 1
