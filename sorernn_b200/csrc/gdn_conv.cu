@@ -9,6 +9,8 @@
 // HBM-bound streaming: rows are bulk-copied into a shared-memory ring and each thread slides a window over
 // the taps for its 16-byte channel group (conv_kernel below); fp32 accumulation, weights and weight
 // gradients in registers.
+#include <type_traits>
+
 #include "bulk.cuh"
 #include "common.cuh"
 #include "kernels.h"
@@ -33,7 +35,19 @@ __device__ __forceinline__ float ld_w(const void* p, int dtype, int64_t i) {
     if (dtype == GDN_BF16) return __bfloat162float(((const __nv_bfloat16*)p)[i]);
     return __half2float(((const __half*)p)[i]);
 }
-__device__ __forceinline__ float sig(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+// The sigmoid for activations of type TA. 16-bit activations: sigmoid(x) = (1 + tanh(x / 2)) / 2 with the
+// hardware tanh approximation (tanh.approx.f32, one MUFU operation, relative error ~2^-11, below the 16-bit
+// rounding of y and dx), half the MUFU work of 1 / (1 + exp(-x)); fp32 activations keep the latter.
+template <typename TA>
+__device__ __forceinline__ float sig(float x) {
+    if constexpr (std::is_same<TA, float>::value) {
+        return __fdividef(1.f, 1.f + __expf(-x));
+    } else {
+        float t;
+        asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+        return fmaf(0.5f, t, 0.5f);
+    }
+}
 
 // [start, end) of the document holding flattened token t
 __device__ __forceinline__ void doc_span(const ConvArgs& a, int64_t t, int64_t& s, int64_t& e) {
@@ -164,7 +178,7 @@ __global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t ran
                 float acc = 0.f;
 #pragma unroll
                 for (int j = 0; j < K; ++j) acc = fmaf(w[q][K - 1 - j], xw[j][q], acc);
-                y[q] = a.silu ? acc * sig(acc) : acc;
+                y[q] = a.silu ? acc * sig<TA>(acc) : acc;
             }
             if (active && ok && u >= tb) stv<TA, VEC>(a.y, u * a.C + c0, y);
         } else {
@@ -188,7 +202,7 @@ __global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t ran
                 for (int j = 0; j < K; ++j) z = fmaf(w[q][K - 1 - j], xw[j][q], z);
                 float d = dyv[q];
                 if (a.silu) {
-                    const float sg = sig(z);
+                    const float sg = sig<TA>(z);
                     d *= sg * (1.f + z * (1.f - sg));
                 }
                 const float dd = acc_dw ? d : 0.f;
