@@ -391,7 +391,7 @@ def config2_layer_bench(dev, world, reps=5):
             "not_built": "attention, FFN, embedding and MTP layers of SoreLM (reference code, out of scope)"}
 
 
-def strong_scaling_bench(dev, rank, world, step, steps):
+def strong_scaling_bench(dev, rank, world, steps):
     """Config 1 with its total work fixed: the B=8 rows (x 16 heads) are split across the ranks (B/N rows
     per rank, i.e. 128/N (sequence, head) units) and every rank times fwd+bwd of its share; value = the
     8 x 4096 tokens / the slowest rank's time per step (strong scaling). The main line is the weak one
@@ -400,6 +400,7 @@ def strong_scaling_bench(dev, rank, world, step, steps):
     and the line reports each and the faster."""
     import torch
 
+    from sorernn_b200 import chunk_gated_delta_rule
     from sorernn_b200.pieces import chunk_gated_delta_rule_pieces
 
     B, T, H, D = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["D"]
@@ -412,6 +413,11 @@ def strong_scaling_bench(dev, rank, world, step, steps):
     P = 1
     while units * P * 2 <= 128 and T % (64 * P * 2) == 0:
         P *= 2
+
+    def step(inp, do):  # the sequences whole (the op would otherwise pick pieces by itself below 33 units)
+        o, _ = chunk_gated_delta_rule(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"], use_qk_l2norm_in_kernel=True,
+                                      pieces=1)
+        o.backward(do)
 
     def pieces_step_of(Pn):
         def pieces_step(inp, do):
@@ -582,7 +588,7 @@ def run_ours(args):
     barrier(world)
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / e2e_steps, world)
 
-    strong = strong_scaling_bench(dev, rank, world, step, args.steps)
+    strong = strong_scaling_bench(dev, rank, world, args.steps)
     config2 = config2_layer_bench(dev, world)
     dec_ms, dec_bytes = decode_bench(dev, rank, world)
     long_prefill = long_prefill_bench(dev, rank, world)

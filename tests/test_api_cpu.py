@@ -97,3 +97,23 @@ def test_fake_kernels_trace_without_the_library(monkeypatch):
         assert rec.dtype == torch.uint8 and rec.shape == (((300 + 63 * 3) // 64 + 3) * 4 * 90112,)
         dq, *_ = torch.ops.sorernn_b200.gdn_bwd(q, q, v, g, b, None, rec, v, None, cu, 0.1, True, 300, 0)
         assert dq.shape == q.shape
+
+
+@pytest.mark.parametrize("B,T,H,dtype,D,varlen,want", [
+    (1, 4096, 16, torch.bfloat16, 128, False, 8),   # config 1 over 8 GPUs: 16 pairs
+    (2, 4096, 16, torch.bfloat16, 128, False, 4),   # over 4 GPUs: 32 pairs
+    (4, 4096, 16, torch.bfloat16, 128, False, 1),   # 64 pairs: whole sequences
+    (1, 1024, 16, torch.bfloat16, 128, False, 2),   # pieces of at least 512 tokens
+    (1, 640, 2, torch.bfloat16, 128, False, 1),     # too short to cut
+    (1, 4096, 16, torch.float32, 128, False, 1),    # recurrent kernels
+    (1, 4096, 16, torch.bfloat16, 64, False, 1),    # head size other than 128
+    (1, 4096, 16, torch.bfloat16, 128, True, 1),    # packed documents
+])
+def test_auto_pieces_choice(B, T, H, dtype, D, varlen, want):
+    """The op's own choice of pieces per sequence (shape-only; no kernel runs)."""
+    from sorernn_b200.gated_delta_rule import auto_pieces
+
+    q = torch.empty(B, T, H, D, dtype=dtype, device="meta")
+    v = torch.empty(B, T, H, D, dtype=dtype, device="meta")
+    cu = torch.tensor([0, T // 2, T]) if varlen else None
+    assert auto_pieces(q, v, cu) == want

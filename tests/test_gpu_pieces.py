@@ -67,7 +67,7 @@ def test_pieces_match_the_unsplit_op():
 
     x, _, _ = _inputs(7, 1, 2048, 2, 2)
     res = {}
-    for name, fn in (("one", lambda *a, **kw: chunk_gated_delta_rule(*a, **kw)),
+    for name, fn in (("one", lambda *a, **kw: chunk_gated_delta_rule(*a, pieces=1, **kw)),
                      ("pieces", lambda *a, **kw: chunk_gated_delta_rule_pieces(*a, pieces=4, **kw))):
         t = {n: x[n].clone().requires_grad_(n != "do") for n in x}
         o, _ = fn(t["q"], t["k"], t["v"], t["g"], t["beta"], use_qk_l2norm_in_kernel=True)
@@ -139,3 +139,22 @@ def test_state_grad_sweep_equals_the_full_sweeps_dh0(HV, with_dht):
                                             _stream(x["q"])), "gdn_chunk_state_grad_saved")
     torch.cuda.synchronize()
     assert torch.equal(dh0, full)
+
+
+def test_op_picks_pieces_by_itself_for_few_sequence_heads():
+    """chunk_gated_delta_rule on a padded batch of 16 (sequence, head) pairs with gradients runs on 8 pieces
+    (auto_pieces), and its outputs and gradients match the unsplit op's (pieces=1) within the bf16 bar."""
+    from sorernn_b200 import chunk_gated_delta_rule
+    from sorernn_b200.gated_delta_rule import auto_pieces
+
+    x, _, _ = _inputs(9, 1, 4096, 16, 16)
+    assert auto_pieces(x["q"], x["v"], None) == 8
+    res = {}
+    for name, P in (("auto", None), ("one", 1)):
+        t = {n: x[n].clone().requires_grad_(n != "do") for n in x}
+        o, _ = chunk_gated_delta_rule(t["q"], t["k"], t["v"], t["g"], t["beta"], use_qk_l2norm_in_kernel=True,
+                                      pieces=P)
+        o.backward(t["do"])
+        res[name] = [to_np(o)] + [to_np(t[n].grad) for n in ("q", "k", "v", "g", "beta")]
+    for name, a, r in zip(("o", "dq", "dk", "dv", "dg", "dbeta"), res["auto"], res["one"]):
+        assert_rms_close(a, r, 3e-2, "auto pieces vs one " + name)
