@@ -502,15 +502,17 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 umma_bf16(tm + C320, desc_at(dDOm, ks * 2048), desc_at(dPS2, ks * 2048), id_mm, 1);
             }
             umma_commit(bar_mma3);
-            const uint64_t dDOk = desc_kmajor(aDO), dDEL = desc_mnmajor(sb + OFF_DEL, 8192),
-                           dS0 = desc_mnmajor(sb + OFF_S0, 16384);
+            if (!a.state_grad_only) {  // dP and QA feed only the token gradients
+                const uint64_t dDOk = desc_kmajor(aDO), dDEL = desc_mnmajor(sb + OFF_DEL, 8192),
+                               dS0 = desc_mnmajor(sb + OFF_S0, 16384);
 #pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t ok_ = (ks >> 2) * 8192 + (ks & 3) * 32;
-                umma_bf16(tm + C448, desc_at(dDOk, ok_), desc_at(dDEL, ks * 2048), id_km, ks > 0);
-                umma_bf16(tm + C192, desc_at(dS0, ks * 2048), desc_at(dDOk, ok_), id_mk, ks > 0);
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint32_t ok_ = (ks >> 2) * 8192 + (ks & 3) * 32;
+                    umma_bf16(tm + C448, desc_at(dDOk, ok_), desc_at(dDEL, ks * 2048), id_km, ks > 0);
+                    umma_bf16(tm + C192, desc_at(dS0, ks * 2048), desc_at(dDOk, ok_), id_mk, ks > 0);
+                }
             }
-            umma_commit(bar_mma2);  // dP and QA: run while step 7 forms dDelta
+            umma_commit(bar_mma2);  // dP and QA: run while step 7 forms dDelta (without them: no new MMAs)
         }
         // ---- 7. dDelta^T = (320) + (384) diag(vX) -> tile; r4; dP -> dPs tiles, X_P sums -------------------
         {
@@ -554,7 +556,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             deposit_colsum(de, red0, lg, cq);
         }
         mwait(bar_mma2, mph2, a.err, 24, ok);
-        {
+        if (!a.state_grad_only) {
             float v[16], p[16];
             ld16x2(tm + C448 + lb + 16 * cq, v, tD1 + lb + 16 * cq, p);
             if (lg < 2) {
@@ -608,7 +610,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
             }
             *reinterpret_cast<uint4*>(pp) = u;
         }
-        {  // Delta^T -> Dd^T = Delta^T diag(vX) in place (thread owns row dv, 16 columns)
+        if (!a.state_grad_only) {  // Delta^T -> Dd^T = Delta^T diag(vX) in place (thread owns row dv, 16 columns)
             float x16[16];
             vec16(vX, 16 * cq, x16);
 #pragma unroll
@@ -629,8 +631,10 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         sync_tc();
 
         // ---- 8. dVb^T = dDelta^T T (256); S0 dDelta^T = -dW^T (320); QB = K^T dPs1^T (384);
-        //         dK' = Q^T dPs2 + dS Dd^T (448). Thread 0 issues QB and dK', thread 32 dVb and -dW^T.
-        if (tid == 0) {
+        //         dK' = Q^T dPs2 + dS Dd^T (448). Thread 0 issues QB and dK', thread 32 dVb and -dW^T. All of it
+        //         feeds only the token gradients: without them the chunk goes on to the dS update.
+        if (a.state_grad_only) {
+        } else if (tid == 0) {
             const uint32_t id_mm = idesc_bf16(128, 64, 1, 1);
             const uint64_t dQm = desc_mnmajor(aQ, QK_BLK), dPS2 = desc_mnmajor(sb + OFF_PS2, 8192);
 #pragma unroll
@@ -661,8 +665,10 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
                 umma_bf16(tm + C320, desc_at(dS0m, ks * 2048), desc_at(dDDm, ks * 2048), id_mm, ks > 0);
             umma_commit(bar_mma2);
         }
-        mwait(bar_mma, mph, a.err, 16, ok);
-        mwait(bar_mma2, mph2, a.err, 25, ok);
+        if (!a.state_grad_only) {
+            mwait(bar_mma, mph, a.err, 16, ok);
+            mwait(bar_mma2, mph2, a.err, 25, ok);
+        }
         if (tid == 0 && !a.state_grad_only) {  // the Dd lo tile is consumed: bring V back for Z1 (step 10)
             const int tok0i = (int)tok0;
             mbar_arrive_expect_tx(bar_v, 2 * 8192);

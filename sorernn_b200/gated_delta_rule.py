@@ -315,8 +315,8 @@ def auto_pieces(q: Tensor, v: Tensor, cu_seqlens: Optional[Tensor]) -> int:
     """Pieces per sequence the op picks by itself: 1 unless the problem runs on the chunked kernels as a padded
     batch (no ``cu_seqlens``) of at most 32 (sequence, value head) pairs; then the largest of 2, 4, 8 that keeps
     pairs x pieces <= 128 (one wave of CTAs) and the pieces at least 512 tokens (8 chunks), in whole chunks.
-    Measured on one B200 (config-1 rows, T = 4,096, fwd+bwd): 16 pairs 1.83 -> 0.61 ms on 8 pieces, 32 pairs
-    1.88 -> 1.02 ms on 4. Never under torch.compile (the pieces path is not one of the registered custom
+    Measured on one B200 (config-1 rows, T = 4,096, fwd+bwd): 16 pairs 1.83 -> 0.56 ms on 8 pieces, 32 pairs
+    1.88 -> 0.95 ms on 4. Never under torch.compile (the pieces path is not one of the registered custom
     ops)."""
     if cu_seqlens is not None or not _uses_chunk_kernels(q, v) or torch.compiler.is_compiling():
         return 1
