@@ -28,8 +28,10 @@ def _inputs(seed, B, T, H, HV):
     return dict(q=bf(q), k=bf(k), v=bf(v), g=gg.float(), beta=bf(beta), do=bf(do)), h0, dht
 
 
+# (1, 300, 1, 2, 3): pieces of 100 tokens, so every piece ends in a partial chunk
 @pytest.mark.parametrize("B,T,H,HV,P,with_state", [(2, 1024, 2, 2, 4, True), (1, 4096, 1, 2, 8, False),
-                                                   (2, 640, 2, 4, 5, True), (1, 512, 1, 1, 1, True)])
+                                                   (2, 640, 2, 4, 5, True), (1, 512, 1, 1, 1, True),
+                                                   (1, 300, 1, 2, 3, True)])
 def test_pieces_fwd_bwd_match_oracle(B, T, H, HV, P, with_state):
     from sorernn_b200.pieces import chunk_gated_delta_rule_pieces
 
