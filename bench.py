@@ -207,9 +207,9 @@ def decode_bench(dev, rank, world, n_dec=1024, timed=True):
 def long_prefill_bench(dev, rank, world, reps=3):
     """Config 4: one sequence of T = 262,144 tokens (H=16, d=128, bf16, forward only, in-kernel L2 norm),
     cut into `world` contiguous segments, one per rank (strong scaling: the sequence is fixed), each run as
-    8 local pieces side by side (16 heads alone would fill 16 of 148 SMs): local chunk forward, piece
-    transitions, scan of the affine maps, NCCL send/recv of the boundary state between ranks, and one
-    incoming-state correction pass. Returns ms per call, max over ranks."""
+    8 local pieces side by side (16 heads alone would fill 16 of 148 SMs): one prep pass, the pieces' C and
+    M state passes, the scan of the affine maps with one NCCL all_gather of every rank's map, and the
+    outputs pass from every piece's true incoming state. Returns ms per call, max over ranks."""
     import torch
 
     from sorernn_b200.seqsplit import segmented_prefill
