@@ -485,12 +485,15 @@ def run_ours(args):
         B = args.profile_batch  # profiling mode: a small case, fwd+bwd steps only (no JSON line)
     x = make_inputs(B, T, H, D, dev, seed=1234 + rank)
     leaf = {n: x[n].clone().requires_grad_(n != "do") for n in ("q", "k", "v", "g", "beta")}
+    # profiling mode runs whole sequences unless --profile-pieces asks for pieces (at batch 1 or 2 the op would
+    # otherwise pick pieces by itself); the timed run (batch 8, 128 sequence-heads) never splits
+    pieces = args.profile_pieces if args.profile_batch else None
 
     def step(inp, do, ev=None):
         if ev is not None:
             ev[0].record()
         o, _ = chunk_gated_delta_rule(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"],
-                                      use_qk_l2norm_in_kernel=True)
+                                      use_qk_l2norm_in_kernel=True, pieces=pieces)
         if ev is not None:
             ev[1].record()
         o.backward(do)
@@ -715,6 +718,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--profile-batch", type=int, default=0,
                     help="profiling mode: run only fwd+bwd steps of config 1 with this batch (for ncu captures)")
+    ap.add_argument("--profile-pieces", type=int, default=1,
+                    help="with --profile-batch: pieces per sequence (1: whole sequences)")
     ap.add_argument("--profile-decode", type=int, default=0,
                     help="profiling mode: run only this many decode steps of config 3 (for ncu captures)")
     ap.add_argument("--profile-layer", action="store_true",
