@@ -304,6 +304,9 @@ int gdn_segment_outputs_save(const gdn_problem* p, const void* q, const void* k,
  *   reverse = 1: out[p] = the gradient of the state leaving piece p, given R_p = terms[p], the gradient
  *                entering piece p for a zero end-state gradient: out[pieces-1] = start (the gradient of
  *                the sequence's final state), out[p] = M_{p+1}^T out[p+1] + R_{p+1}.
+ *   reverse = 2: as 0 with every term but terms[0] taken as zero; with terms = maps, final_state (required)
+ *                = M_{pieces-1} ... M_1 M_0, the sequence's composite map; out (NULL = not wanted) = the
+ *                prefix products M_{p-1} ... M_0 for p >= 1.
  * DK = DV = 128. fp32 throughout. No counterpart in the reference (it has no sequence split).
  */
 int gdn_piece_chain(int64_t n_seq, int64_t pieces, int64_t HV, int64_t DK, int64_t DV, const float* maps,

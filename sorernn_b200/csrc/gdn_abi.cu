@@ -467,14 +467,16 @@ int gdn_segment_outputs_save(const gdn_problem* p, const void* q, const void* k,
 int gdn_piece_chain(int64_t n_seq, int64_t pieces, int64_t HV, int64_t DK, int64_t DV, const float* maps,
                     const float* terms, const float* start, float* out, float* final_state, int32_t reverse,
                     gdn_stream_t stream) {
+    const int mode = reverse;  // 0 forward, 1 reverse, 2 composite map
     if (n_seq < 0 || pieces < 0 || HV < 0) return GDN_ERR_SHAPE;
     if (DK != 128 || DV != 128) return GDN_ERR_SHAPE;
-    if (reverse != 0 && reverse != 1) return GDN_ERR_ARGUMENT;
+    if (mode < 0 || mode > 2) return GDN_ERR_ARGUMENT;
     if (n_seq * pieces * HV == 0) return GDN_OK;
-    if (!terms || !out || (pieces > 1 && !maps)) return GDN_ERR_ARGUMENT;
+    if (!terms || (pieces > 1 && !maps)) return GDN_ERR_ARGUMENT;
+    if (mode == 2 ? !final_state : !out) return GDN_ERR_ARGUMENT;
     if (!aligned16(maps) || !aligned16(terms) || !aligned16(out) || !aligned16(start) || !aligned16(final_state))
         return GDN_ERR_ALIGN;
-    return piece_chain(n_seq, pieces, HV, maps, terms, start, out, final_state, reverse, (cudaStream_t)stream);
+    return piece_chain(n_seq, pieces, HV, maps, terms, start, out, final_state, mode, (cudaStream_t)stream);
 }
 
 uint64_t gdn_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }

@@ -45,8 +45,10 @@ __global__ void __launch_bounds__(pc::NTHR) piece_chain_kernel(const float* __re
                                                                 const float* __restrict__ terms,
                                                                 const float* __restrict__ start, float* __restrict__ out,
                                                                 float* __restrict__ final_state, int P, int HV,
-                                                                int reverse) {
+                                                                int mode) {
     using namespace pc;
+    const bool reverse = mode == 1;
+    const bool product = mode == 2;  // the terms of pieces 1 .. P-1 are zero: final = M_{P-1} .. M_1 terms[0]
     extern __shared__ __align__(16) float sm_chain[];
     float* Ms = sm_chain;                // [2][D][LDM]: the maps of this step and the next, staged by cp.async
     float* Y = sm_chain + 2 * D * LDM;  // running value, [k][16 columns]
@@ -81,7 +83,7 @@ __global__ void __launch_bounds__(pc::NTHR) piece_chain_kernel(const float* __re
     for (int r = 0; r < 4; ++r) {
         if (!reverse) {  // Y = C_0; out[0] = start
             y[r] = ld4(terms + at(0, r));
-            st4(out + at(0, r), start ? ld4(start + at0(r)) : zero4);
+            if (out) st4(out + at(0, r), start ? ld4(start + at0(r)) : zero4);
         } else {  // Z = start; out[P - 1] = Z
             y[r] = start ? ld4(start + at0(r)) : zero4;
             st4(out + at(P - 1, r), y[r]);
@@ -89,7 +91,7 @@ __global__ void __launch_bounds__(pc::NTHR) piece_chain_kernel(const float* __re
     }
     for (int s = 1; s < P; ++s) {
         const int p = piece_of(s), m = map_of(s);
-        if (!reverse) {
+        if (!reverse && out) {
 #pragma unroll
             for (int r = 0; r < 4; ++r) st4(out + at(p, r), y[r]);
         }
@@ -100,7 +102,7 @@ __global__ void __launch_bounds__(pc::NTHR) piece_chain_kernel(const float* __re
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             st4(&Y[(rg + 32 * r) * BLK + c0], y[r]);
-            const float4 t = ld4(terms + at(m, r));
+            const float4 t = product ? zero4 : ld4(terms + at(m, r));
             acc[r][0] = t.x;
             acc[r][1] = t.y;
             acc[r][2] = t.z;
@@ -157,11 +159,11 @@ __global__ void __launch_bounds__(pc::NTHR) piece_chain_kernel(const float* __re
 }
 
 int piece_chain(int64_t n_seq, int64_t pieces, int64_t HV, const float* maps, const float* terms, const float* start,
-                float* out, float* final_state, int reverse, cudaStream_t s) {
+                float* out, float* final_state, int mode, cudaStream_t s) {
     if (n_seq * HV == 0 || pieces == 0) return GDN_OK;
     if (smem_optin((const void*)piece_chain_kernel, pc::SMEM_BYTES) != cudaSuccess) return GDN_ERR_LAUNCH;
     piece_chain_kernel<<<dim3((unsigned)(n_seq * HV), pc::D / pc::BLK), pc::NTHR, pc::SMEM_BYTES, s>>>(
-        maps, terms, start, out, final_state, (int)pieces, (int)HV, reverse);
+        maps, terms, start, out, final_state, (int)pieces, (int)HV, mode);
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }

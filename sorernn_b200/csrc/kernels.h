@@ -123,10 +123,10 @@ size_t chunk_bwd_workspace(int64_t B, int64_t T, int64_t N, int64_t H, int64_t H
 size_t chunk_saved_bytes(int64_t B, int64_t T, int64_t N, int64_t HV, bool varlen);
 int chunk_bwd(const ChunkBwdLaunch& L, cudaStream_t s);
 
-// The chain of piece maps along each sequence (gdn_piece_chain): reverse = 0 the states entering the pieces,
-// reverse = 1 the gradients of the pieces' end states (dk = dv = 128).
+// The chain of piece maps along each sequence (gdn_piece_chain): mode 0 the states entering the pieces, mode 1
+// the gradients of the pieces' end states, mode 2 the composite map (dk = dv = 128).
 int piece_chain(int64_t n_seq, int64_t pieces, int64_t HV, const float* maps, const float* terms, const float* start,
-                float* out, float* final_state, int reverse, cudaStream_t s);
+                float* out, float* final_state, int mode, cudaStream_t s);
 
 int rec_fwd(const RecLaunch& L, cudaStream_t s);
 size_t rec_bwd_workspace(int64_t N, int64_t HV, int64_t DK, int64_t DV, int64_t max_len, int64_t total_tokens,

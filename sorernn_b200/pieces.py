@@ -68,7 +68,8 @@ def end_state_grads(MT: Tensor, R: Tensor, dht: Optional[Tensor]) -> Tensor:
 
 def _chain(B, P, HV, maps, terms, start, out, final, reverse, stream):
     """``gdn_piece_chain``: the forward chain of :func:`incoming_states` (reverse = 0) or the reverse chain of
-    :func:`end_state_grads` (reverse = 1) in one launch (fp32 FMAs, one CTA per (sequence, head, 16 columns))."""
+    :func:`end_state_grads` (reverse = 1) in one launch (fp32 FMAs, one CTA per (sequence, head, 16 columns)) on
+    ``stream``."""
     _lib.check(_lib.lib().gdn_piece_chain(B, P, HV, 128, 128, _ptr(maps), _ptr(terms), _ptr(start), _ptr(out),
                                           _ptr(final), reverse, stream), "gdn_piece_chain")
 

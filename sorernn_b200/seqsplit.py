@@ -218,41 +218,63 @@ def segmented_prefill(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, 
     return o, (S_out if rank == world - 1 else None)
 
 
+def piece_chain(n_seq: int, pieces: int, HV: int, maps: Optional[Tensor], terms: Tensor, start: Optional[Tensor],
+                out: Optional[Tensor], final: Optional[Tensor], mode: int) -> None:
+    """``gdn_piece_chain`` on the current stream: the chain of affine maps along ``pieces`` consecutive pieces
+    of each of ``n_seq`` sequences (fp32, one launch). mode 0: ``out[p]`` = the state entering piece p (``start``
+    for piece 0; ``terms[p]`` = piece p's final state from its own start), ``final`` = the state leaving the last
+    piece; mode 1: the reverse chain of the transposed maps (end-state gradients); mode 2: with ``terms`` = the
+    maps, ``final`` = the composite map M_{P-1} ... M_0."""
+    _lib.check(_lib.lib().gdn_piece_chain(n_seq, pieces, HV, 128, 128, _ptr(maps), _ptr(terms), _ptr(start),
+                                          _ptr(out), _ptr(final), mode, _stream(terms)), "gdn_piece_chain")
+
+
+def _gather(x: Tensor, world: int, group) -> Tensor:
+    """all_gather of a contiguous tensor into ``[world, *x.shape]`` (one NCCL collective)."""
+    out = torch.empty(world * x.numel(), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(out, x.reshape(-1), group=group)
+    return out.view(world, *x.shape)
+
+
 def _segmented_prefill_chunked(q, k, v, g, beta, scale, l2, P, h0, rank, world, group):
     """segmented_prefill on the chunked kernels: one prep pass for all pieces, then three state passes over
-    its records: each piece's C (from zero; piece 0 of rank 0 from h0) and M, the scans and the exchange,
-    and each piece's outputs from its true incoming state."""
+    its records: each piece's C (from zero; piece 0 of rank 0 from h0) and M, then each piece's outputs from
+    its true incoming state. The maps are joined by chain kernels (gdn_piece_chain), across ranks after one
+    all_gather of every rank's composite map (M_r, C_r)."""
     T = q.shape[1]
     Ts = T // P
     seg = lambda x: x.view(P, Ts, *x.shape[2:])  # noqa: E731
     qs, ks, vs, gs, bs = (seg(x) for x in (q, k, v, g, beta))
     HV, dk, dv = v.shape[2], q.shape[3], v.shape[3]
+    f32 = dict(dtype=torch.float32, device=q.device)
     init = None
     if h0 is not None:
-        init = torch.zeros(P, HV, dk, dv, dtype=torch.float32, device=q.device)
+        init = torch.zeros(P, HV, dk, dv, **f32)
         init[0] = h0[0].float()
     rec = _Records(qs, vs, gs, bs, scale, l2)
     need_m = P > 1 or (world > 1 and rank > 0)
     C, M = rec.maps(qs, ks, vs, gs, bs, init, need_m)
-    if need_m:
-        Mi, Ci = affine_inclusive_scan(M, C)
-        M_r, C_r = Mi[P - 1:], Ci[P - 1:]
-        S_loc = torch.cat([torch.zeros_like(C[:1]), Ci[:-1]])
-    else:
-        M_r, C_r, S_loc = None, C, torch.zeros_like(C)
-    if world > 1:
-        S_in, S_out = exchange_boundary_states(C_r, M_r if rank > 0 else None, group)
-    else:
-        S_in, S_out = None, C_r
-    # every piece's true incoming state: the local prefix, the rank's input carried through the pieces before
-    # it, and h0 for the first piece
-    inc = S_loc
-    if S_in is not None:
-        eye = torch.eye(dk, dtype=torch.float32, device=q.device).expand(1, HV, dk, dk)
-        Mpre = torch.cat([eye, Mi[:-1]]) if P > 1 else eye
-        inc = inc + torch.matmul(Mpre, S_in.float().expand(P, -1, -1, -1))
-    if init is not None:
-        inc = inc + init
+    inc = torch.empty(P, HV, dk, dv, **f32)  # every piece's true incoming state
+    final = torch.empty(1, HV, dk, dv, **f32)
+    if rank == 0:  # the pieces' incoming states from h0; final: the state leaving this rank (C_r)
+        h0f = None if h0 is None else h0.float().contiguous()
+        piece_chain(1, P, HV, M, C, h0f, inc, final, 0)
+    else:  # this rank's composite map and its final state from a zero input, for the exchange
+        piece_chain(1, P, HV, M, C, None, inc, final, 0)
+    if world == 1:
+        return rec.outputs(qs, ks, vs, gs, bs, inc).view(1, T, HV, dv), final
+    M_r = torch.zeros(1, HV, dk, dk, **f32)  # rank 0's map is never read (it starts the sequence)
+    if rank > 0:
+        piece_chain(1, P, HV, M, M, None, None, M_r, 2)
+    Ms, Cs = _gather(M_r, world, group), _gather(final, world, group)
+    # the state entering every rank: the chain of the ranks' maps (rank 0's C_r already holds h0)
+    S_ranks = torch.empty(world, HV, dk, dv, **f32)
+    S_out = torch.empty(1, HV, dk, dv, **f32)
+    piece_chain(1, world, HV, Ms.view(world, HV, dk, dk), Cs.view(world, HV, dk, dv), None, S_ranks, S_out, 0)
+    if rank > 0:  # piece 0 leaves with M_0 S_in + C_0; the pieces' chain from S_in
+        S_in = S_ranks[rank:rank + 1]
+        C[0] = torch.baddbmm(C[0], M[0], S_in[0])
+        piece_chain(1, P, HV, M, C, S_in, inc, None, 0)
     o = rec.outputs(qs, ks, vs, gs, bs, inc)
     return o.view(1, T, *o.shape[2:]), (S_out if rank == world - 1 else None)
 
