@@ -1,9 +1,10 @@
 """Sequence-split prefill over NCCL: one sequence cut into per-rank segments on 2 GPUs.
 
-Each rank runs ``sequence_split_prefill`` on its own slice (chunk kernels + transition + NCCL send/recv of
-the boundary state + incoming-state correction). The outputs of every rank and the last rank's final
-state must match the oracle (the reference recurrence) on the whole sequence, within the bf16 bar.
-Needs 2 GPUs; skipped otherwise. NVLS is off (NCCL_NVLS_ENABLE=0): the path uses send/recv only.
+Each rank runs ``sequence_split_prefill`` (one segment per rank) or ``segmented_prefill`` (local pieces too)
+on its own slice: the segment maps on the chunk kernels, one NCCL all_gather of every rank's map, the
+composition of the maps before it, and the outputs from its true incoming state. The outputs of every rank
+and the last rank's final state must match the oracle (the reference recurrence) on the whole sequence,
+within the bf16 bar. Needs 2 GPUs; skipped otherwise. NVLS is off (NCCL_NVLS_ENABLE=0).
 """
 import os
 import socket
