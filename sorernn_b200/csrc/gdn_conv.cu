@@ -171,14 +171,32 @@ __global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t ran
 #pragma unroll
             for (int q = 0; q < VEC; ++q) xw[0][q] = 0.f;
         }
+        // 16-bit activations: the K-tap sums run on channel pairs as packed fp32 FMAs (__ffma2_rn, fmaf's
+        // rounding in each lane), half the FMA instructions of these issue-bound rows. fp32 activations keep
+        // scalar FMAs, as ptxas spills their paired form.
+        constexpr bool PAIRS = sizeof(TA) == 2;
         if constexpr (!BWD) {
             float y[VEC];
+            if constexpr (PAIRS) {
 #pragma unroll
-            for (int q = 0; q < VEC; ++q) {
-                float acc = 0.f;
+                for (int q = 0; q < VEC; q += 2) {
+                    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int j = 0; j < K; ++j) acc = fmaf(w[q][K - 1 - j], xw[j][q], acc);
-                y[q] = a.silu ? acc * sig<TA>(acc) : acc;
+                    for (int j = 0; j < K; ++j) {
+                        const float2 wj = make_float2(w[q][K - 1 - j], w[q + 1][K - 1 - j]);
+                        acc = __ffma2_rn(wj, make_float2(xw[j][q], xw[j][q + 1]), acc);
+                    }
+                    y[q] = a.silu ? acc.x * sig<TA>(acc.x) : acc.x;
+                    y[q + 1] = a.silu ? acc.y * sig<TA>(acc.y) : acc.y;
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < VEC; ++q) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int j = 0; j < K; ++j) acc = fmaf(w[q][K - 1 - j], xw[j][q], acc);
+                    y[q] = a.silu ? acc * sig<TA>(acc) : acc;
+                }
             }
             if (active && ok && u >= tb) stv<TA, VEC>(a.y, u * a.C + c0, y);
         } else {
@@ -195,30 +213,73 @@ __global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t ran
                 for (int q = 0; q < VEC; ++q) dzw[j][q] = dzw[j + 1][q];
             }
             const bool acc_dw = u < te && ok;  // rows past the range feed dx only
+            if constexpr (PAIRS) {
 #pragma unroll
-            for (int q = 0; q < VEC; ++q) {
-                float z = 0.f;
+                for (int q = 0; q < VEC; q += 2) {
+                    float2 z = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int j = 0; j < K; ++j) z = fmaf(w[q][K - 1 - j], xw[j][q], z);
-                float d = dyv[q];
-                if (a.silu) {
-                    const float sg = sig<TA>(z);
-                    d *= sg * (1.f + z * (1.f - sg));
+                    for (int j = 0; j < K; ++j) {
+                        const float2 wj = make_float2(w[q][K - 1 - j], w[q + 1][K - 1 - j]);
+                        z = __ffma2_rn(wj, make_float2(xw[j][q], xw[j][q + 1]), z);
+                    }
+                    float d0 = dyv[q], d1 = dyv[q + 1];
+                    if (a.silu) {
+                        const float s0 = sig<TA>(z.x), s1 = sig<TA>(z.y);
+                        d0 *= s0 * (1.f + z.x * (1.f - s0));
+                        d1 *= s1 * (1.f + z.y * (1.f - s1));
+                    }
+                    const float2 dd = acc_dw ? make_float2(d0, d1) : make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int j = 0; j < K; ++j) {
+                        const float2 dwj = make_float2(dw[q][K - 1 - j], dw[q + 1][K - 1 - j]);
+                        const float2 r = __ffma2_rn(make_float2(xw[j][q], xw[j][q + 1]), dd, dwj);
+                        dw[q][K - 1 - j] = r.x;
+                        dw[q + 1][K - 1 - j] = r.y;
+                    }
+                    dzw[K - 1][q] = d0;
+                    dzw[K - 1][q + 1] = d1;
                 }
-                const float dd = acc_dw ? d : 0.f;
+            } else {
 #pragma unroll
-                for (int j = 0; j < K; ++j) dw[q][K - 1 - j] = fmaf(xw[j][q], dd, dw[q][K - 1 - j]);
-                dzw[K - 1][q] = d;
+                for (int q = 0; q < VEC; ++q) {
+                    float z = 0.f;
+#pragma unroll
+                    for (int j = 0; j < K; ++j) z = fmaf(w[q][K - 1 - j], xw[j][q], z);
+                    float d = dyv[q];
+                    if (a.silu) {
+                        const float sg = sig<TA>(z);
+                        d *= sg * (1.f + z * (1.f - sg));
+                    }
+                    const float dd = acc_dw ? d : 0.f;
+#pragma unroll
+                    for (int j = 0; j < K; ++j) dw[q][K - 1 - j] = fmaf(xw[j][q], dd, dw[q][K - 1 - j]);
+                    dzw[K - 1][q] = d;
+                }
             }
             ew[K - 1] = have ? e_doc : 0;
             const int64_t t = u - (K - 1);  // < te, as u < te + K - 1
             float dx[VEC];
+            if constexpr (PAIRS) {
 #pragma unroll
-            for (int q = 0; q < VEC; ++q) {
-                float acc = 0.f;
+                for (int q = 0; q < VEC; q += 2) {
+                    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int j = 0; j < K; ++j) acc = fmaf(t + j < ew[0] ? w[q][K - 1 - j] : 0.f, dzw[j][q], acc);
-                dx[q] = acc;
+                    for (int j = 0; j < K; ++j) {
+                        const bool in = t + j < ew[0];
+                        const float2 wj = in ? make_float2(w[q][K - 1 - j], w[q + 1][K - 1 - j]) : make_float2(0.f, 0.f);
+                        acc = __ffma2_rn(wj, make_float2(dzw[j][q], dzw[j][q + 1]), acc);
+                    }
+                    dx[q] = acc.x;
+                    dx[q + 1] = acc.y;
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < VEC; ++q) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int j = 0; j < K; ++j) acc = fmaf(t + j < ew[0] ? w[q][K - 1 - j] : 0.f, dzw[j][q], acc);
+                    dx[q] = acc;
+                }
             }
             if (active && ok && t >= tb) stv<TA, VEC>(a.dx, t * a.C + c0, dx);
         }
