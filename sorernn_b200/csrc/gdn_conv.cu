@@ -67,31 +67,34 @@ __device__ __forceinline__ void doc_span(const ConvArgs& a, int64_t t, int64_t& 
 }
 
 namespace cvs {
-constexpr int STAGES = 3;
-// one stage: TT rows of the slab of every staged input (backward: one block per SM, so larger stages)
-template <bool BWD> __host__ __device__ constexpr uint32_t stage_bytes() { return BWD ? 65536 : 32768; }
+// One 512-thread block per SM with two 96 KB stages, a stage holding TT rows of the slab of every staged
+// input (24 rows forward, 12 backward: multiples of the 4-row unroll). At config-1 sizes this measured
+// fastest of 2-3 stages of 32-112 KB with 4-, 8- or 16-byte channel groups (fwd 58 -> 51 us, bwd 113 ->
+// 107 us against three stages of 32 KB / 64 KB with 16- / 8-byte groups).
+constexpr int STAGES = 2;
+constexpr uint32_t STAGE_BYTES = 98304;
 constexpr uint32_t SLAB_BYTES = 4096;    // bytes of a row one block covers
-// bytes of a row one thread covers: 16 forward; 8 backward, whose windows hold twice the state per channel
-template <bool BWD> __host__ __device__ constexpr int group_bytes() { return BWD ? 8 : 16; }
+constexpr int GROUP_BYTES = 8;  // bytes of a row one thread covers
 }  // namespace cvs
 
 // Block = (slab of channels, contiguous range [tb, te) of the flattened token axis). The block streams the
 // rows u of its range, plus the K-1 rows before it (and, backward, the K-1 after it), through a STAGES-deep
 // ring: tile i of TT rows lands in stage i % STAGES by bulk copies (one per input when the slab is the whole
-// row, else one per row, issued by warp 0). Each thread owns one channel group of the slab (16 bytes
-// forward, 8 backward) and slides a window over the rows in order:
+// row, else one per row, issued by warp 0). Each thread owns one 8-byte channel group of the slab and slides
+// a window over the rows in order:
 //   forward:  x window [u-K+1, u] -> y[u] for u in [tb, te)
 //   backward: x window -> z[u], dz[u] for u in [tb, te+K-1); dz window [t, t+K-1] -> dx[t], t = u-K+1 in
 //             [tb, te); dw += x[u-j] dz[u] for u in [tb, te), kept in registers and added once per block.
 // Window rows from before the current document are zero, and dz rows past the document end of t are masked.
+// __maxnreg__(128): 512 threads per block fit the register file; under __launch_bounds__(512) ptxas chose 64
+// registers and spills for the K = 3 kernels
 template <typename TA, int K, bool BWD>
-__global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t range_len, int nslabs) {
+__global__ void __maxnreg__(128) conv_kernel(const ConvArgs a, int64_t range_len, int nslabs) {
     using namespace cvs;
-    constexpr int VEC = group_bytes<BWD>() / (int)sizeof(TA);  // channels per thread
-    constexpr int MAX_GROUPS = SLAB_BYTES / group_bytes<BWD>();
+    constexpr int VEC = GROUP_BYTES / (int)sizeof(TA);  // channels per thread
+    constexpr int MAX_GROUPS = SLAB_BYTES / GROUP_BYTES;
     constexpr int NTN = BWD ? 2 : 1;                              // staged inputs: x (and dy)
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr uint32_t STAGE_BYTES = stage_bytes<BWD>();
     uint64_t* bar = (uint64_t*)(smem + STAGES * STAGE_BYTES);
     const int tid = threadIdx.x;
     const int64_t BT = a.B * a.T;
@@ -292,7 +295,7 @@ __global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t ran
         const int64_t u0 = u_lo + tile * TT;
         const int n = (int)(u_hi - u0 < TT ? u_hi - u0 : TT);
         // inactive threads (past a narrow slab's last group) read the group-0 column and store nothing
-        const uint8_t* st = smem + s * STAGE_BYTES + (active ? (uint32_t)tid * group_bytes<BWD>() : 0u);
+        const uint8_t* st = smem + s * STAGE_BYTES + (active ? (uint32_t)tid * GROUP_BYTES : 0u);
         int r = 0;
         while (r < n) {
             if (u0 + r >= e_doc) {  // a new document starts here: no taps before it
@@ -338,13 +341,13 @@ __global__ void __launch_bounds__(512) conv_kernel(const ConvArgs a, int64_t ran
 template <typename TA>
 static int conv_launch(const ConvArgs& a, int K, bool bwd, cudaStream_t s) {
     using namespace cvs;
-    const int VEC = (bwd ? group_bytes<true>() : group_bytes<false>()) / (int)sizeof(TA);
-    const int MAX_GROUPS = (int)SLAB_BYTES / (bwd ? group_bytes<true>() : group_bytes<false>());
+    const int VEC = GROUP_BYTES / (int)sizeof(TA);
+    const int MAX_GROUPS = (int)SLAB_BYTES / GROUP_BYTES;
     const int64_t BT = a.B * a.T;
     const int nslabs = (int)((a.C + MAX_GROUPS * VEC - 1) / (MAX_GROUPS * VEC));
     const int64_t g0 = (a.C < MAX_GROUPS * VEC ? a.C : MAX_GROUPS * VEC) / VEC;  // groups of the widest slab
     const int nthr = (int)((g0 + 31) / 32 * 32);
-    const size_t smem = (size_t)STAGES * (bwd ? stage_bytes<true>() : stage_bytes<false>()) + bulk::kBarBytes;
+    const size_t smem = (size_t)STAGES * STAGE_BYTES + bulk::kBarBytes;
     const void* k = nullptr;
     switch (K * 2 + (bwd ? 1 : 0)) {
         case 2: k = (const void*)conv_kernel<TA, 1, false>; break;
