@@ -7,8 +7,9 @@
 //   dg = dy a s'(g),  s'(g) = sigmoid(g) (1 + g (1 - sigmoid(g)))
 //   dn = dy s w,  dx = r (dn - n mean(dn n)),  dw = sum over rows of dy s n
 // HBM-bound streaming: each block walks tiles of whole rows (8 KB of each input per tile), bulk-copied into
-// a 3-stage shared-memory ring by one thread, so two tiles per block are in flight while the block computes
-// the third. A row of D features is held by LPR = min(32, D / VEC) consecutive lanes, PER = D / LPR features
+// a 4-stage shared-memory ring by one thread, so three tiles per block are in flight while the block computes
+// the fourth (at config-1 sizes the fastest of 3-8 stages of 4-16 KB tiles: backward 127 -> 115 us against
+// 3 stages). A row of D features is held by LPR = min(32, D / VEC) consecutive lanes, PER = D / LPR features
 // each (VEC = the elements of 16 bytes: at D = 128 bf16, 16 lanes of 8 features). Outputs go straight from
 // registers to global memory in 16-byte stores. dw is reduced across the lanes that share features, then
 // per block in shared memory, then added to global memory with one atomic add per feature per block.
@@ -24,7 +25,7 @@ static __device__ int g_norm_gate_err;
 
 namespace ngs {
 constexpr int NTHR = 256;
-constexpr int STAGES = 3;
+constexpr int STAGES = 4;
 constexpr uint32_t TILE = 8192;  // bytes of one input per tile (whole rows)
 }  // namespace ngs
 
