@@ -82,3 +82,54 @@ def test_causal_conv1d_silu_forward_backward(dtype, K, varlen, C):
     grad_check = assert_rms_close if dtype == torch.float32 else assert_bf16_close
     grad_check(to_np(x.grad), x64.grad.numpy(), tol, "dx")
     assert_rms_close(to_np(w.grad), w64.grad.numpy(), 1e-4 if dtype == torch.float32 else 3e-2, "dweight")
+
+
+@pytest.mark.parametrize("K", [4, 3])
+def test_causal_conv1d_ranges_over_many_tiles(K):
+    """Rows of 4 KB (2,048 bf16 channels) over 8,880 tokens: every block's token range spans several tiles of
+    its two-stage ring (stages refilled), with document boundaries at arbitrary rows, inside tiles and across
+    ranges."""
+    from oracle.gdn_oracle import causal_conv1d as conv_ref
+    from sorernn_b200.layer_ops import causal_conv1d
+
+    gen = torch.Generator(device="cuda").manual_seed(100 + K)
+    T, C = 8880, 2048
+    rng = np.random.default_rng(K)
+    cu = [0] + sorted(rng.choice(np.arange(1, T), 40, replace=False).tolist()) + [T]
+    x = torch.randn(1, T, C, device="cuda", generator=gen).bfloat16().requires_grad_(True)
+    w = (torch.randn(C, K, device="cuda", generator=gen) * K ** -0.5).requires_grad_(True)
+    y, _ = causal_conv1d(x, w, activation="silu", cu_seqlens=torch.tensor(cu, device="cuda"))
+    ids = _doc_ids(cu, T)
+    assert_bf16_close(to_np(y), conv_ref(to_np(x), to_np(w), ids), 2e-2, "y")
+    dy = torch.randn(y.shape, device="cuda", generator=gen).bfloat16()
+    y.backward(dy)
+    x64, w64 = (t.detach().double().cpu().requires_grad_(True) for t in (x, w))
+    z = x64 * w64[:, K - 1]
+    for j in range(1, K):
+        same = torch.tensor(ids[j:] == ids[: T - j])
+        z = z + torch.nn.functional.pad((x64[:, : T - j] * w64[:, K - 1 - j]).masked_fill(~same[None, :, None], 0.0),
+                                        (0, 0, j, 0))
+    torch.nn.functional.silu(z).backward(dy.double().cpu())
+    assert_bf16_close(to_np(x.grad), x64.grad.numpy(), 3e-2, "dx")
+    assert_rms_close(to_np(w.grad), w64.grad.numpy(), 3e-2, "dweight")
+
+
+def test_rms_norm_gated_blocks_over_many_tiles():
+    """94,720 rows of 128 bf16 features: every block walks about ten 32-row tiles, so its four-stage ring is
+    refilled several times, in both directions."""
+    from sorernn_b200.layer_ops import rms_norm_gated
+
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(94720, 128, device="cuda", generator=gen).bfloat16().requires_grad_(True)
+    g = torch.randn(94720, 128, device="cuda", generator=gen).bfloat16().requires_grad_(True)
+    w = (1.0 + 0.2 * torch.randn(128, device="cuda", generator=gen)).requires_grad_(True)
+    y = rms_norm_gated(x, g, w, None, activation="swish", eps=1e-6)
+    assert_bf16_close(to_np(y), rms_norm_gated_ref(to_np(x), to_np(g), to_np(w), 1e-6), 2e-2, "y")
+    dy = torch.randn(y.shape, device="cuda", generator=gen).bfloat16()
+    y.backward(dy)
+    x64, g64, w64 = (t.detach().double().cpu().requires_grad_(True) for t in (x, g, w))
+    r = torch.rsqrt(x64.pow(2).mean(-1, keepdim=True) + 1e-6)
+    (x64 * r * w64 * torch.nn.functional.silu(g64)).backward(dy.double().cpu())
+    assert_bf16_close(to_np(x.grad), x64.grad.numpy(), 3e-2, "dx")
+    assert_bf16_close(to_np(g.grad), g64.grad.numpy(), 3e-2, "dgate")
+    assert_rms_close(to_np(w.grad), w64.grad.numpy(), 3e-2, "dweight")
