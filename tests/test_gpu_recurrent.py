@@ -124,7 +124,7 @@ def test_decode_many_heads_per_cta(dtype, tol):
         xr = {n: to_np(t) for n, t in dev.items()}
         o_ref = cgdn.decode_step(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], st_ref, d ** -0.5,
                                  use_qk_l2norm=True)
-        if dtype == torch.bfloat16:  # o is rounded to bf16: judge the error beyond that rounding
+        if dtype == torch.bfloat16:  # o is rounded to bf16: check the error beyond that rounding
             assert_bf16_close(to_np(o), o_ref, tol, f"o step {step}")
         else:
             assert_rms_close(to_np(o), o_ref, tol, f"o step {step}")
