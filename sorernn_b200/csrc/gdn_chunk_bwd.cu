@@ -25,8 +25,9 @@
 // MMAs are issued by two threads, 0 and 32, each committing its groups to its own mbarriers (thread 0:
 // bar_mma; thread 32: bar_mma2, and bar_mma3 for its share of step 6's first group), so two issuers halve the
 // issue time of the larger steps, and a phase waits only for the groups it reads. Issue loops are unrolled
-// over hoisted descriptors (one N = 64 UMMA per ~50 cycles against ~100 rolled), except step 10's, whose
-// unrolled form raised the kernel's register spills (its issuers hold the dq operands live). Products that accumulate into one TMEM region stay on one thread.
+// over hoisted descriptors (one N = 64 UMMA per ~50 cycles against ~100 rolled), except thread 0's in step 10,
+// whose unrolled form spills registers (its issuers hold the dq operands live); thread 32's step-10 loop is
+// unrolled (sweep 1.440 -> 1.429 ms at config 1). Products that accumulate into one TMEM region stay on one thread.
 // Every GEMM is an M = 128 UMMA with a 128-wide dimension on the TMEM lanes. The three 64 x 64 x K
 // products (dP, Z, dA) use a 128-row A operand of which one 64-row half is ignored; Z and dA put their
 // rows on lanes 64-127, where the same threads also hold the K K^T rows of the recomputed Gram matrix.
@@ -781,7 +782,7 @@ __global__ void __launch_bounds__(cb::NTHR, 1) chunk_bwd_kernel(const __grid_con
         } else if (tid == 32) {
             const uint32_t id_mk = idesc_bf16(128, 64, 1, 0);
             const uint64_t dDVBm = desc_mnmajor(sb + OFF_DVB - 16384, 16384), dVk = desc_kmajor(aV);
-#pragma unroll 1
+#pragma unroll
             for (int ks = 0; ks < 8; ++ks)
                 umma_bf16(tm + C256, desc_at(dDVBm, ks * 2048), desc_at(dVk, (ks >> 2) * 8192 + (ks & 3) * 32), id_mk,
                           ks > 0);
