@@ -698,8 +698,10 @@ def run_reference(args):
     v = statistics.median(x["value"] for x in vals)
     cb = dict(vals[-1])
     cb["value"] = v
+    # ms_per_step: one config-1 step (B x T tokens) at the sampled rate
     rec = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-           "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(CFG1["B"] * CFG1["T"] / v * 1e3, 1),
+           "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
            "config": {"workload": "config1 on host cores: reference recurrence fwd+bwd (C port of "
                                   "sore/model/gdn_ref.py) of B8 T4096 H16 d128 rows, each step a bounded "
