@@ -213,3 +213,43 @@ def test_state_grad_sweep_checks_its_arguments():
     assert call(p, vp, vp, None, n) == 6
     assert call(p, vp, vp, vp, n - 1) == 6
     assert call(_problem(), vp, vp, vp, 1 << 30) == 1
+
+
+def test_header_compiles_as_c_and_a_c_program_links_and_calls_the_queries(tmp_path):
+    """A plain C99 caller (what a cgo, JNI or other C FFI binding compiles against): the header builds with gcc
+    without C++, the program links against the library, and the host-side queries answer as documented."""
+    import shutil
+    import subprocess
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no gcc")
+    root = Path(__file__).resolve().parents[1]
+    src = tmp_path / "caller.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "gdn_b200.h"
+int main(void) {
+    gdn_problem p;
+    memset(&p, 0, sizeof p);
+    p.B = 8; p.T = 4096; p.H = 16; p.HV = 16; p.DK = 128; p.DV = 128; p.N = 8; p.max_seqlen = 4096;
+    p.scale = 0.08838834764831845f; p.act_dtype = GDN_BF16; p.g_dtype = GDN_FP32; p.beta_dtype = GDN_BF16;
+    p.use_qk_l2norm = 1; p.ckpt_every = 4;
+    if (gdn_checkpoint_count(&p) != 8 * 16) return 1;
+    if (gdn_chunk_fwd_workspace_size(&p) < 256) return 2;
+    if (gdn_chunk_saved_bytes(&p) != (size_t)8 * 64 * 16 * 90112) return 3;
+    if (strlen(gdn_status_string(GDN_OK)) == 0) return 4;
+    p.DK = 256;  /* rejected by the shape check, before any pointer is used or any kernel launched */
+    if (gdn_chunk_fwd(&p, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0) != GDN_ERR_SHAPE) return 5;
+    printf("ok\n");
+    return 0;
+}
+''')
+    lib_dir = root / "sorernn_b200" / "_lib"
+    exe = tmp_path / "caller"
+    r = subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-I", str(root / "include"), str(src), "-o", str(exe),
+                        "-L", str(lib_dir), "-lgdn_b200", f"-Wl,-rpath,{lib_dir}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", (r.returncode, r.stdout, r.stderr)
