@@ -313,16 +313,16 @@ torch.library.register_autograd("sorernn_b200::gdn_beta_sigmoid", _beta_backward
 # ------------------------------------------------------------------------------------------------
 def auto_pieces(q: Tensor, v: Tensor, cu_seqlens: Optional[Tensor]) -> int:
     """Pieces per sequence the op picks by itself: 1 unless the problem runs on the chunked kernels as a padded
-    batch (no ``cu_seqlens``) of at most 32 (sequence, value head) pairs; then the largest of 2, 4, 8 that keeps
+    batch (no ``cu_seqlens``) of at most 64 (sequence, value head) pairs; then the largest of 2, 4, 8 that keeps
     pairs x pieces <= 128 (one wave of CTAs) and the pieces at least 512 tokens (8 chunks), in whole chunks.
     Measured on one B200 (config-1 rows, T = 4,096, fwd+bwd): 16 pairs 1.83 -> 0.56 ms on 8 pieces, 32 pairs
-    1.88 -> 0.95 ms on 4. Never under torch.compile (the pieces path is not one of the registered custom
+    1.88 -> 0.95 ms on 4, 64 pairs 1.98 -> 1.70 ms on 2. Never under torch.compile (the pieces path is not one of the registered custom
     ops)."""
     if cu_seqlens is not None or not _uses_chunk_kernels(q, v) or torch.compiler.is_compiling():
         return 1
     B, T = q.shape[:2]
     units = B * v.shape[2]
-    if units > 32:
+    if units > 64:
         return 1
     P = 1
     while P < 8 and units * P * 2 <= 128 and T % (64 * P * 2) == 0 and T // (P * 2) >= 512:
@@ -359,7 +359,7 @@ def chunk_gated_delta_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Ten
     ``pieces`` (extra keyword): cut every sequence into that many pieces that run side by side, forward and
     backward (:mod:`sorernn_b200.pieces`), for problems with few (sequence, value head) pairs per GPU, whose
     serial per-pair chains would leave most SMs idle. ``None`` (the default) picks it when autograd will run
-    a backward on a padded batch (no ``cu_seqlens``) of at most 32 pairs on the chunked kernels, with pieces
+    a backward on a padded batch (no ``cu_seqlens``) of at most 64 pairs on the chunked kernels, with pieces
     of at least 512 tokens (``auto_pieces``); ``1`` never splits.
     """
     use_gate = bool(kwargs.pop("use_gate_in_kernel", False))

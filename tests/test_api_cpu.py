@@ -102,7 +102,8 @@ def test_fake_kernels_trace_without_the_library(monkeypatch):
 @pytest.mark.parametrize("B,T,H,dtype,D,varlen,want", [
     (1, 4096, 16, torch.bfloat16, 128, False, 8),   # config 1 over 8 GPUs: 16 pairs
     (2, 4096, 16, torch.bfloat16, 128, False, 4),   # over 4 GPUs: 32 pairs
-    (4, 4096, 16, torch.bfloat16, 128, False, 1),   # 64 pairs: whole sequences
+    (4, 4096, 16, torch.bfloat16, 128, False, 2),   # over 2 GPUs: 64 pairs
+    (8, 4096, 16, torch.bfloat16, 128, False, 1),   # 128 pairs (one GPU): whole sequences
     (1, 1024, 16, torch.bfloat16, 128, False, 2),   # pieces of at least 512 tokens
     (1, 640, 2, torch.bfloat16, 128, False, 1),     # too short to cut
     (1, 4096, 16, torch.float32, 128, False, 1),    # recurrent kernels

@@ -143,14 +143,16 @@ def test_state_grad_sweep_equals_the_full_sweeps_dh0(HV, with_dht):
     assert torch.equal(dh0, full)
 
 
-def test_op_picks_pieces_by_itself_for_few_sequence_heads():
-    """chunk_gated_delta_rule on a padded batch of 16 (sequence, head) pairs with gradients runs on 8 pieces
-    (auto_pieces), and its outputs and gradients match the unsplit op's (pieces=1) within the bf16 bar."""
+@pytest.mark.parametrize("B,T,want", [(1, 4096, 8), (4, 1024, 2)])
+def test_op_picks_pieces_by_itself_for_few_sequence_heads(B, T, want):
+    """chunk_gated_delta_rule on a padded batch of 16 or 64 (sequence, head) pairs with gradients runs on 8 or
+    2 pieces (auto_pieces), and its outputs and gradients match the unsplit op's (pieces=1) within the bf16
+    bar."""
     from sorernn_b200 import chunk_gated_delta_rule
     from sorernn_b200.gated_delta_rule import auto_pieces
 
-    x, _, _ = _inputs(9, 1, 4096, 16, 16)
-    assert auto_pieces(x["q"], x["v"], None) == 8
+    x, _, _ = _inputs(9 + B, B, T, 16, 16)
+    assert auto_pieces(x["q"], x["v"], None) == want
     res = {}
     for name, P in (("auto", None), ("one", 1)):
         t = {n: x[n].clone().requires_grad_(n != "do") for n in x}
